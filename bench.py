@@ -1,0 +1,260 @@
+#!/usr/bin/env python
+"""Headline benchmark: transformer-LM DDP training throughput on B200.
+
+Config: decoder-only LM, 6 layers, d_model 512,
+8 heads, MLP 2048 GELU, pre-LayerNorm, vocab 256 (uniform random byte tokens),
+seq 256, batch 64 per GPU, bf16 compute / f32 master weights, AdamW lr 3e-4
+wd 0.1. Weak scaling: global batch = 64 x N.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flodl|reference|torch]
+
+N > 1 runs under torchrun (one rank per GPU, NCCL bootstrap). The timed region
+is exactly K steps bracketed by barrier + synchronize, timed with CUDA events
+on the launching stream, max over ranks; rank 0 prints one JSON line.
+
+``value`` is the device-timed whole-step throughput of the captured step (CUDA
+graph replay: forward, backward, gradient all-reduce, AdamW). ``e2e`` runs the
+public training API (``flodl_b200.train.StepRunner``) with the step's inputs
+copied from pinned host memory and the loss read back every step.
+
+``--impl reference`` runs the unmodified reference (fab2s/floDl) if it is
+installed under baseline/_ref; it is a Rust/cargo workspace that this image
+cannot build, so the arm reports ``unavailable``. ``--impl torch`` is an extra
+proxy arm: the same model written with stock PyTorch modules (cuBLAS, SDPA
+flash attention, fused AdamW, NCCL DDP) — the library calls the reference
+itself makes through libtorch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DDP samples/s & tok/s, 1/2/4/8 B200, max-over-ranks vs ref NCCL build"
+MODEL_DESC = "transformer-lm 6L d512 h8 ff2048 vocab256 pre-LN GELU"
+B_PER_GPU, SEQ, VOCAB = 64, 256, 256
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="flodl", choices=["flodl", "reference", "torch"])
+    ap.add_argument("--engine", default="auto", choices=["auto", "nccl", "peer"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    msg = ("reference fab2s/floDl is a Rust/cargo workspace (no setup.py/pyproject); "
+           "pip install of /root/reference fails and this image has no Rust toolchain")
+    if not os.path.isdir(ref) or not os.listdir(ref):
+        print(json.dumps({"impl": "reference", "unavailable": msg}))
+        return 0
+    print(json.dumps({"impl": "reference", "unavailable": msg + " (baseline/_ref holds no runnable build)"}))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    import torch.distributed as dist
+
+    from flodl_b200.parallel.ddp import init_from_env
+
+    rank, world, local = init_from_env("nccl", timeout_s=300)
+    if world != args.gpus and args.gpus > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(1234)
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    if args.impl == "torch":
+        from flodl_b200.bench_support import torch_arm_step
+        step, state = torch_arm_step(dev, world, B_PER_GPU, SEQ, VOCAB)
+        engine = "nccl(torch DDP)"
+        launches_fn = None
+    else:
+        from flodl_b200.bench_support import flodl_arm_step
+        engine = args.engine
+        if engine == "auto":
+            engine = "peer" if world > 1 else "none"
+        step, state = flodl_arm_step(dev, world, B_PER_GPU, SEQ, VOCAB, engine)
+        from flodl_b200._ext import cuda_ext
+        launches_fn = cuda_ext().launch_count
+
+    ids, tgt = state["ids"], state["tgt"]
+    # warm-up (eager; builds arenas, workspaces)
+    for _ in range(max(args.warmup, 3)):
+        loss = step()
+    torch.cuda.synchronize()
+
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        c0 = launches_fn() if launches_fn else 0
+        with torch.cuda.graph(graph):
+            static_loss = step()
+        per_step_launches = (launches_fn() - c0) if launches_fn else None
+        run = graph.replay
+        for _ in range(2):
+            run()
+    else:
+        c0 = launches_fn() if launches_fn else 0
+        step()
+        per_step_launches = (launches_fn() - c0) if launches_fn else None
+        run = step
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- timed (device)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # ---------------------------------------------------------------- e2e (public API)
+    e2e = None
+    if args.impl == "flodl":
+        from flodl_b200.train import StepRunner
+        runner = StepRunner.for_state(state, graph_step=(graph, static_loss) if graph else None,
+                                      eager_step=step)
+        ids_host = torch.randint(0, VOCAB, (B_PER_GPU, SEQ), dtype=torch.int64).pin_memory()
+        tgt_host = torch.randint(0, VOCAB, (B_PER_GPU, SEQ), dtype=torch.int64).pin_memory()
+        n_e2e = args.e2e_steps or args.steps
+        runner.step(ids_host, tgt_host)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(n_e2e):
+            runner.step(ids_host, tgt_host)  # H2D inputs, replay, D2H loss
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - w0) * 1e3 / n_e2e
+        te = torch.tensor([e2e_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item())
+        e2e = {"value": world * B_PER_GPU * SEQ / (e2e_ms / 1e3), "unit": "tok/s",
+               "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": ids_host.numel() * 8 + tgt_host.numel() * 8,
+               "d2h_bytes_per_step": 4, "api": "flodl_b200.train.StepRunner.step"}
+
+    tok_s = world * B_PER_GPU * SEQ / (ms / 1e3)
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "samples_per_s": world * B_PER_GPU / (ms / 1e3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (uniform random byte tokens), random-init weights",
+            "config": {"model": MODEL_DESC, "global_batch": B_PER_GPU * world, "seq_len": SEQ,
+                       "parallelism": f"dp{world}", "optimizer": "AdamW lr3e-4 wd0.1",
+                       "grad_allreduce": engine, "cuda_graph": graph is not None,
+                       "l2": "inputs larger than L2: ~2 GB of activations per step per GPU"},
+            "impl": args.impl,
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": (per_step_launches * args.steps) if per_step_launches is not None else None,
+        }
+        print(json.dumps(out), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,486 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
+//
+//   C[M,N] = epilogue( sum_k A[m,k] * B[n,k] )
+//
+// Operand storage (all bf16, row-major in memory):
+//   A K-major : [M, K]   (activations x, upstream grads dY)
+//   A MN-major: [K, M]   (dY viewed transposed for the weight gradient)
+//   B K-major : [N, K]   (nn.Linear weight W[out,in])
+//   B MN-major: [K, N]   (W used as [in,out] for the input gradient, x for wgrad)
+//
+// This one engine serves the three GEMMs of a Linear layer (the reference calls
+// torch::linear / cuBLAS for these: flodl-sys/ops_training.cpp:400-414):
+//   forward   y  = x  W^T       A=x  (K-major), B=W (K-major)
+//   dgrad     dx = dy W         A=dy (K-major), B=W (MN-major)
+//   wgrad     dW = dy^T x       A=dy (MN-major), B=x (MN-major), f32 accumulate
+//
+// Warp roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0   : TMA producer (one elected lane)
+//   warp 1   : TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5: epilogue (TMEM -> registers -> bias/GELU/residual -> global)
+// Two TMEM accumulator buffers let the epilogue of tile i overlap the MMAs of
+// tile i+1. No TMA multicast is used anywhere.
+#include "sm100_ptx.cuh"
+#include "gemm_sm100.h"
+
+#include <cstdio>
+#include <atomic>
+#include <mutex>
+
+namespace flodl {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+__device__ uint64_t g_wait_limit_ns = 2000000000ull;  // 2 s
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
+  static constexpr int kBTileBytes = BN * kBK * 2;   // 32 KB or 16 KB
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct SmemCtl {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+__device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, int col0,
+                                               int M, int N, const uint32_t (&acc)[32]) {
+  if (row >= M) return;
+  float v[32];
+  const float alpha = ep.alpha_ptr ? ep.alpha * __ldg(ep.alpha_ptr) : ep.alpha;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) * alpha;
+
+  const bool full_cols = (col0 + 32 <= N);
+  if (ep.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      int c = col0 + i;
+      v[i] += (c < N) ? __ldg(ep.bias + c) : 0.f;
+    }
+  }
+  if (ep.flags & kEpiGelu) {
+    if (ep.aux) {  // keep the pre-activation for the backward pass
+      __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
+      if (full_cols && ((ep.ld_aux & 7) == 0)) {
+        uint4* dst = reinterpret_cast<uint4*>(aux + col0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+          w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+          w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+          w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+          dst[q] = w;
+        }
+      } else {
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < N) aux[col0 + i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+  }
+  if (ep.flags & kEpiDGelu) {  // multiply by GELU'(pre-activation)
+    const __nv_bfloat16* aux =
+        reinterpret_cast<const __nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
+    if (full_cols && ((ep.ld_aux & 7) == 0)) {
+      const uint4* src = reinterpret_cast<const uint4*>(aux + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w = src[q];
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2 f = unpack_bf16x2(ws[h]);
+          v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
+          v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] *= gelu_erf_grad(__bfloat162float(aux[col0 + i]));
+    }
+  }
+  if (ep.residual) {
+    const float* res = ep.residual + (size_t)row * ep.ld_res;
+    if (full_cols && ((ep.ld_res & 3) == 0)) {
+      const float4* src = reinterpret_cast<const float4*>(res + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 r = src[q];
+        v[4 * q + 0] += r.x;
+        v[4 * q + 1] += r.y;
+        v[4 * q + 2] += r.z;
+        v[4 * q + 3] += r.w;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] += res[col0 + i];
+    }
+  }
+
+  if (ep.out_f32) {
+    float* out = reinterpret_cast<float*>(ep.out) + (size_t)row * ep.ld_out;
+    if (full_cols && ((ep.ld_out & 3) == 0)) {
+      if (ep.flags & kEpiAccumulate) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          red_add_v4(out + col0 + 4 * q, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+        float4* dst = reinterpret_cast<float4*>(out + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    } else {
+      for (int i = 0; i < 32; ++i) {
+        int c = col0 + i;
+        if (c >= N) break;
+        if (ep.flags & kEpiAccumulate)
+          atomicAdd(out + c, v[i]);
+        else
+          out[c] = v[i];
+      }
+    }
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + (size_t)row * ep.ld_out;
+    if (full_cols && ((ep.ld_out & 7) == 0)) {
+      uint4* dst = reinterpret_cast<uint4*>(out + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+        dst[q] = w;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) out[col0 + i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, GemmEpilogue ep, int M, int N,
+                      int K, int k_splits, uint32_t* err) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 128B-swizzled tiles need 1024-byte alignment.
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + S * Cfg::kStageBytes);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int k_blocks_total = (K + kBK - 1) / kBK;
+  const int kb_per_split = (k_blocks_total + k_splits - 1) / k_splits;
+  const int num_tiles = tiles_m * tiles_n * k_splits;
+  const uint64_t limit = g_wait_limit_ns;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->tmem_full[a], 1);
+      mbar_init(&ctl->tmem_empty[a], 4);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc<Cfg::kTmemCols>(&ctl->tmem_base);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  volatile uint32_t* abort_flag = &ctl->abort;
+
+  auto tile_coords = [&](int t, int& tm, int& tn, int& ks) {
+    ks = t % k_splits;
+    int mn = t / k_splits;
+    tn = mn % tiles_n;
+    tm = mn / tiles_n;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn, ks;
+        tile_coords(t, tm, tn, ks);
+        const int kb0 = ks * kb_per_split;
+        const int kb1 = min(k_blocks_total, kb0 + kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait_bounded(&ctl->empty[s], ph ^ 1, abort_flag, err, limit)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + s * Cfg::kStageBytes;
+          uint8_t* b_dst = a_dst + Cfg::kATileBytes;
+          mbar_arrive_expect_tx(&ctl->full[s], Cfg::kStageBytes);
+          const int k0 = kb * kBK;
+          if (A_MN) {
+            tma_load_2d(a_dst, &tmA, &ctl->full[s], tm * kBM, k0);
+            tma_load_2d(a_dst + 64 * 128, &tmA, &ctl->full[s], tm * kBM + 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &ctl->full[s], k0, tm * kBM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(b_dst + c * 64 * 128, &tmB, &ctl->full[s], tn * BN + c * 64, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, &ctl->full[s], k0, tn * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) for copies already in flight before leaving.
+        for (int s = 0; s < S; ++s) {
+          uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&ctl->full[s], ((it - 1 - s) / S) & 1)) {
+            if (global_timer_ns() - t0 > 100000000ull) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      uint32_t it = 0;
+      uint32_t local_tile = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local_tile) {
+        int tm, tn, ks;
+        tile_coords(t, tm, tn, ks);
+        const int kb0 = ks * kb_per_split;
+        const int kb1 = min(k_blocks_total, kb0 + kb_per_split);
+        const uint32_t acc = local_tile & 1;
+        const uint32_t acc_ph = (local_tile >> 1) & 1;
+        if (!mbar_wait_bounded(&ctl->tmem_empty[acc], acc_ph ^ 1, abort_flag, err, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait_bounded(&ctl->full[s], ph, abort_flag, err, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t b_addr = a_addr + Cfg::kATileBytes;
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            uint64_t adesc, bdesc;
+            if (A_MN)
+              adesc = make_sdesc_sw128(a_addr + j * 2048, 64 * 128, 1024);
+            else
+              adesc = make_sdesc_sw128(a_addr + j * 32, 16, 1024);
+            if (B_MN)
+              bdesc = make_sdesc_sw128(b_addr + j * 2048, 64 * 128, 1024);
+            else
+              bdesc = make_sdesc_sw128(b_addr + j * 32, 16, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            issued = true;
+          }
+          umma_commit(&ctl->empty[s]);  // smem stage free once these MMAs finish
+        }
+        if (!ok) break;
+        umma_commit(&ctl->tmem_full[acc]);  // accumulator ready for the epilogue
+      }
+      if (!ok && issued) {
+        umma_commit(&ctl->drain);
+        uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&ctl->drain, 0)) {
+          if (global_timer_ns() - t0 > 100000000ull) break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint32_t local_tile = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local_tile) {
+      int tm, tn, ks;
+      tile_coords(t, tm, tn, ks);
+      const uint32_t acc = local_tile & 1;
+      const uint32_t acc_ph = (local_tile >> 1) & 1;
+      bool ok = mbar_wait_bounded(&ctl->tmem_full[acc], acc_ph, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, ok)) break;  // keep the warp converged for tcgen05.ld
+      tc_fence_after();
+      const int row = tm * kBM + q * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const int kb0 = ks * kb_per_split;
+      const bool empty_split = kb0 >= k_blocks_total;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = tn * BN + c * 32;
+        uint32_t r[32];
+        tmem_ld_32cols(t_row + c * 32, r);
+        tmem_ld_wait();
+        if (c == BN / 32 - 1) {
+          // Last read of this accumulator: hand it back to the MMA warp early.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
+        }
+        if (col0 < N && !empty_split) epilogue_chunk(ep, row, col0, M, N, r);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+// 2D bf16 tensor map: inner dimension `inner` (contiguous), `outer` rows with
+// row pitch `ld` elements; box = box_inner x box_outer, 128-byte swizzle.
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t ld, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  });
+  return n;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void reset_launch_count() { g_launches.store(0); }
+
+void set_wait_limit_ns(uint64_t ns) {
+  cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap tmA, tmB;
+  // A tile: 128 (M) x 64 (K)
+  bool ok;
+  if (A_MN)
+    ok = make_tmap_bf16_2d(&tmA, g.A, g.M, g.K, g.lda, 64, kBK);
+  else
+    ok = make_tmap_bf16_2d(&tmA, g.A, g.K, g.M, g.lda, kBK, kBM);
+  if (!ok) return cudaErrorInvalidValue;
+  if (B_MN)
+    ok = make_tmap_bf16_2d(&tmB, g.B, g.N, g.K, g.ldb, 64, kBK);
+  else
+    ok = make_tmap_bf16_2d(&tmB, g.B, g.K, g.N, g.ldb, kBK, BN);
+  if (!ok) return cudaErrorInvalidValue;
+
+  auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    attr_set = true;
+  }
+  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.k_splits;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, g.ep, g.M, g.N, g.K, g.k_splits,
+                                                     g.err);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.k_splits < 1) return cudaErrorInvalidValue;
+  const bool wide = g.N >= 256 && g.bn != 128;
+#define FL_GEMM_CASE(AMN, BMN)                                                   \
+  if (g.a_mn == AMN && g.b_mn == BMN)                                           \
+    return wide ? launch_gemm_t<256, AMN, BMN>(g, stream)                      \
+                : launch_gemm_t<128, AMN, BMN>(g, stream);
+  FL_GEMM_CASE(false, false)
+  FL_GEMM_CASE(false, true)
+  FL_GEMM_CASE(true, false)
+  FL_GEMM_CASE(true, true)
+#undef FL_GEMM_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace flodl

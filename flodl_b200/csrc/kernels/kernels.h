@@ -1,0 +1,121 @@
+// Host launchers of the non-GEMM sm_100a kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gemm_sm100.h"
+
+namespace flodl {
+
+// ------------------------------------------------------------- LayerNorm
+struct LnFwdArgs {
+  const void* x = nullptr;  // [rows, C] f32 or bf16
+  bool x_bf16 = false;
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  __nv_bfloat16* y_bf16 = nullptr;
+  float* y_f32 = nullptr;
+  float* mean = nullptr;
+  float* rstd = nullptr;
+  int rows = 0, C = 0;
+  float eps = 1e-5f;
+};
+struct LnBwdArgs {
+  const __nv_bfloat16* dy = nullptr;
+  const void* x = nullptr;
+  bool x_bf16 = false;
+  const float* mean = nullptr;
+  const float* rstd = nullptr;
+  const float* gamma = nullptr;
+  const float* dres = nullptr;  // f32 [rows, C] added to dx
+  float* dx_f32 = nullptr;
+  __nv_bfloat16* dx_bf16 = nullptr;
+  float* dgamma = nullptr;  // accumulated
+  float* dbeta = nullptr;   // accumulated
+  float* colsum = nullptr;  // accumulated sum over rows of dx
+  int rows = 0, C = 0;
+};
+cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st);
+cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);
+cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
+                          const float* scale = nullptr);
+
+// ------------------------------------------------------------- cross entropy
+struct CeArgs {
+  const __nv_bfloat16* logits = nullptr;  // [T, V] (row pitch ld)
+  int ld = 0;
+  const int64_t* targets = nullptr;       // [T]
+  int T = 0, V = 0;
+  int64_t ignore_index = -100;
+  float smoothing = 0.f;
+  const float* inv_count = nullptr;       // device scalar: 1 / #valid rows
+  float* loss = nullptr;                  // device scalar, accumulated mean loss
+  __nv_bfloat16* dlogits = nullptr;       // [T, V] gradient of the mean loss (nullable)
+};
+cudaError_t launch_ce_count(const int64_t* targets, int T, int64_t ignore_index, float* inv_count,
+                            float* loss_zero, cudaStream_t st);
+cudaError_t launch_softmax_ce(const CeArgs& a, cudaStream_t st);
+
+// ------------------------------------------------------------- embedding
+cudaError_t launch_embed_fwd(const int64_t* ids, const float* tok, const float* pos,
+                             const int64_t* type_ids, const float* type_tab, float* out,
+                             __nv_bfloat16* out_bf16, int T, int S, int C, int V,
+                             cudaStream_t st);
+cudaError_t launch_embed_bwd_atomic(const int64_t* ids, const float* dy, float* dtok, int T, int C,
+                                    cudaStream_t st);
+cudaError_t launch_pos_grad(const float* dy, float* dpos, int B, int S, int C, cudaStream_t st);
+cudaError_t launch_onehot_bf16(const int64_t* ids, __nv_bfloat16* out, int T, int V,
+                               cudaStream_t st);
+
+// ------------------------------------------------------------- optimizers
+struct AdamWArgs {
+  float* p = nullptr;
+  float* g = nullptr;
+  float* m = nullptr;
+  float* v = nullptr;
+  __nv_bfloat16* shadow = nullptr;  // bf16 copy of p for the forward GEMMs (nullable)
+  int64_t n = 0;
+  const float* lr = nullptr;     // device scalar
+  const float* step = nullptr;   // device scalar (already incremented)
+  const float* gscale = nullptr; // device scalar multiplier on g (clip / 1/world), nullable
+  float beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, wd = 0.f;
+  bool decoupled = true;  // AdamW (true) vs Adam with L2 (false)
+  bool zero_grad = false;
+};
+cudaError_t launch_adamw(const AdamWArgs& a, cudaStream_t st);
+
+struct SgdArgs {
+  float* p = nullptr;
+  float* g = nullptr;
+  float* buf = nullptr;  // momentum buffer (nullable when momentum == 0)
+  __nv_bfloat16* shadow = nullptr;
+  int64_t n = 0;
+  const float* lr = nullptr;
+  const float* gscale = nullptr;
+  const float* first = nullptr;  // device scalar: 1 on the first step (buf = g)
+  float momentum = 0.f, dampening = 0.f, wd = 0.f;
+  bool nesterov = false;
+  bool zero_grad = false;
+};
+cudaError_t launch_sgd(const SgdArgs& a, cudaStream_t st);
+
+// Sum of squares of x[0..n) accumulated into *out (f32).
+cudaError_t launch_sumsq(const float* x, int64_t n, float* out, cudaStream_t st);
+// *coef = min(1, max_norm / (sqrt(*sumsq) + 1e-6)); also writes the norm.
+cudaError_t launch_clip_coef(const float* sumsq, float max_norm, float* coef, float* norm,
+                             cudaStream_t st);
+cudaError_t launch_add_scalar(float* x, float v, cudaStream_t st);
+
+// ------------------------------------------------------------- elementwise
+cudaError_t launch_cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t st);
+
+}  // namespace flodl
+
+namespace flodl {
+// dh = dy * gelu'(h), all bf16 [n]
+cudaError_t launch_gelu_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* h, __nv_bfloat16* dh,
+                            int64_t n, cudaStream_t st);
+// y = gelu(x) bf16 -> bf16
+cudaError_t launch_gelu_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n, cudaStream_t st);
+}  // namespace flodl

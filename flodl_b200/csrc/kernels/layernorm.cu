@@ -1,0 +1,295 @@
+// Fused LayerNorm forward/backward for sm_100a (memory-bound, one warp per row).
+//
+// Forward (reference: at::native_layer_norm, flodl-sys/ops_tensor.cpp:580-600):
+//   y = (x - mean) * rstd * gamma + beta,  rstd = 1/sqrt(var + eps)
+//   x is the f32 (or bf16) residual stream; y is written in bf16 so it feeds the
+//   tcgen05 GEMM directly (or in f32), mean/rstd are kept for backward.
+//
+// Backward, fused in one pass over the rows:
+//   dx    = rstd * (g - mean(g) - xhat * mean(g * xhat)),  g = dy * gamma
+//   dx   += dres                         (gradient arriving on the skip path)
+//   dgamma += sum_rows dy * xhat,  dbeta += sum_rows dy     (f32, atomics per block)
+//   colsum += sum_rows dx                (bias gradient of the Linear whose output
+//                                         was added into this residual stream)
+//   dx is written in f32 (the residual chain) and/or bf16 (the GEMM operand).
+#include "sm100_ptx.cuh"
+#include "kernels.h"
+
+namespace flodl {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  float4 f = *reinterpret_cast<const float4*>(p);
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+__device__ __forceinline__ void store4_bf16(__nv_bfloat16* p, const float (&v)[4]) {
+  uint2 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+__device__ __forceinline__ void store4_f32(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kWarps = 8;
+
+// NV = number of 128-element column groups (C <= NV*128); lane owns columns
+// lane*4 + 128*j .. +3 for j < NV.
+template <typename TIn, int NV>
+__global__ void __launch_bounds__(kWarps * 32) ln_fwd_kernel(
+    const TIn* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+    __nv_bfloat16* __restrict__ y_bf16, float* __restrict__ y_f32, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int rows, int C, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int warp_global = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int nwarps = gridDim.x * kWarps;
+  float g[NV][4], b[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane * 4 + 128 * j;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      g[j][e] = (c + e < C) ? (gamma ? gamma[c + e] : 1.f) : 0.f;
+      b[j][e] = (c + e < C) ? (beta ? beta[c + e] : 0.f) : 0.f;
+    }
+  }
+  for (int r = warp_global; r < rows; r += nwarps) {
+    const TIn* xr = x + (size_t)r * C;
+    float v[NV][4];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+        load4<TIn>(xr + c, v[j]);
+      } else {
+        v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+      }
+      s += v[j][0] + v[j][1] + v[j][2] + v[j][3];
+    }
+    const float mean = warp_sum(s) / C;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float d = v[j][e] - mean;
+          ss += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / C + eps);
+    if (lane == 0) {
+      if (mean_out) mean_out[r] = mean;
+      if (rstd_out) rstd_out[r] = rstd;
+    }
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = (v[j][e] - mean) * rstd * g[j][e] + b[j][e];
+        if (y_bf16) store4_bf16(y_bf16 + (size_t)r * C + c, o);
+        if (y_f32) store4_f32(y_f32 + (size_t)r * C + c, o);
+      }
+    }
+  }
+}
+
+template <typename TIn, int NV>
+__global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dy, const TIn* __restrict__ x,
+    const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+    const float* __restrict__ gamma, const float* __restrict__ dres, float* __restrict__ dx_f32,
+    __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dgamma, float* __restrict__ dbeta,
+    float* __restrict__ colsum, int rows, int C) {
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int warp_global = blockIdx.x * kWarps + wib;
+  const int nwarps = gridDim.x * kWarps;
+  float g[NV][4];
+  float acc_dg[NV][4], acc_db[NV][4], acc_cs[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane * 4 + 128 * j;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      g[j][e] = (c + e < C) ? (gamma ? gamma[c + e] : 1.f) : 0.f;
+      acc_dg[j][e] = acc_db[j][e] = acc_cs[j][e] = 0.f;
+    }
+  }
+  for (int r = warp_global; r < rows; r += nwarps) {
+    const float mean = mean_in[r];
+    const float rstd = rstd_in[r];
+    float xh[NV][4], dyv[NV][4];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+        float xv[4];
+        load4<TIn>(x + (size_t)r * C + c, xv);
+        load4<__nv_bfloat16>(dy + (size_t)r * C + c, dyv[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          xh[j][e] = (xv[e] - mean) * rstd;
+          const float gg = dyv[j][e] * g[j][e];
+          s1 += gg;
+          s2 += gg * xh[j][e];
+          acc_dg[j][e] += dyv[j][e] * xh[j][e];
+          acc_db[j][e] += dyv[j][e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
+      }
+    }
+    const float m1 = warp_sum(s1) / C;
+    const float m2 = warp_sum(s2) / C;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = rstd * (dyv[j][e] * g[j][e] - m1 - xh[j][e] * m2);
+        if (dres) {
+          float rv[4];
+          load4<float>(dres + (size_t)r * C + c, rv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[e] += rv[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc_cs[j][e] += o[e];
+        if (dx_f32) store4_f32(dx_f32 + (size_t)r * C + c, o);
+        if (dx_bf16) store4_bf16(dx_bf16 + (size_t)r * C + c, o);
+      }
+    }
+  }
+  // Block reduction of the per-column partials, then one atomic per column.
+  __shared__ float red[kWarps][128];
+  auto flush = [&](float (&acc)[NV][4], float* out) {
+    if (!out) return;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[wib][lane * 4 + e] = acc[j][e];
+      __syncthreads();
+      if (threadIdx.x < 128) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += red[w][threadIdx.x];
+        const int c = threadIdx.x + 128 * j;
+        if (c < C) atomicAdd(out + c, s);
+      }
+      __syncthreads();
+    }
+  };
+  flush(acc_dg, dgamma);
+  flush(acc_db, dbeta);
+  flush(acc_cs, colsum);
+}
+
+// Column sums of a [rows, C] matrix into f32 out[C] (accumulating).
+template <typename T>
+__global__ void colsum_kernel(const T* __restrict__ m, float* __restrict__ out, int rows, int C,
+                              int rows_per_block, const float* __restrict__ scale) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += to_f32(m[(size_t)r * C + c]);
+  if (scale) s *= *scale;
+  atomicAdd(out + c, s);
+}
+
+int grid_for_rows(int rows) {
+  int blocks = (rows + kWarps - 1) / kWarps;
+  int cap = num_sms() * 8;
+  return blocks < cap ? blocks : cap;
+}
+
+}  // namespace
+
+#define FL_LN_DISPATCH_NV(C, KERNEL_CALL) \
+  do {                                   \
+    int nv_ = ((C) + 127) / 128;         \
+    if (nv_ <= 1) { constexpr int NV = 1; KERNEL_CALL; } \
+    else if (nv_ <= 2) { constexpr int NV = 2; KERNEL_CALL; } \
+    else if (nv_ <= 4) { constexpr int NV = 4; KERNEL_CALL; } \
+    else if (nv_ <= 6) { constexpr int NV = 6; KERNEL_CALL; } \
+    else if (nv_ <= 8) { constexpr int NV = 8; KERNEL_CALL; } \
+    else if (nv_ <= 16) { constexpr int NV = 16; KERNEL_CALL; } \
+    else return cudaErrorInvalidValue;   \
+  } while (0)
+
+cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st) {
+  if (a.C % 4 != 0) return cudaErrorInvalidValue;
+  const int grid = grid_for_rows(a.rows);
+  if (a.x_bf16) {
+    FL_LN_DISPATCH_NV(a.C, (ln_fwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
+                               (const __nv_bfloat16*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32,
+                               a.mean, a.rstd, a.rows, a.C, a.eps)));
+  } else {
+    FL_LN_DISPATCH_NV(a.C, (ln_fwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
+                               (const float*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean,
+                               a.rstd, a.rows, a.C, a.eps)));
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
+  if (a.C % 4 != 0) return cudaErrorInvalidValue;
+  const int grid = grid_for_rows(a.rows);
+  if (a.x_bf16) {
+    FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
+                               a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma, a.dres,
+                               a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C)));
+  } else {
+    FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
+                               a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres, a.dx_f32,
+                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C)));
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
+                          const float* scale) {
+  const int threads = 128;
+  const int rows_per_block = 256;
+  dim3 grid((C + threads - 1) / threads, (rows + rows_per_block - 1) / rows_per_block);
+  if (bf16)
+    colsum_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>((const __nv_bfloat16*)m, out, rows, C,
+                                                           rows_per_block, scale);
+  else
+    colsum_kernel<float><<<grid, threads, 0, st>>>((const float*)m, out, rows, C, rows_per_block,
+                                                   scale);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace flodl

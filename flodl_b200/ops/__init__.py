@@ -1,0 +1,7 @@
+"""Fused op layer: autograd Functions over the sm_100a kernel library."""
+from .attention import attention_packed, scaled_dot_product_attention  # noqa: F401
+from .linear import linear  # noqa: F401
+from .loss import cross_entropy  # noqa: F401
+from .misc import batch_norm2d, conv2d, embedding, gelu  # noqa: F401
+from .norm import layer_norm  # noqa: F401
+from .transformer import lm_train_loss  # noqa: F401,E402

@@ -1,0 +1,113 @@
+"""Fused Linear: ``y = act(x W^T + b) [+ residual]`` on the tcgen05 GEMM engine.
+
+Reference: ``autograd::linear`` -> ``torch::linear`` (flodl/src/autograd/ops.rs:576,
+flodl-sys/ops_training.cpp:400-414). On CUDA the forward is one GEMM whose
+epilogue adds the bias, applies GELU (keeping the pre-activation for backward)
+and adds the residual; backward is two GEMMs (dgrad with the GELU derivative in
+its epilogue, split-K wgrad accumulating into ``weight.grad``) plus the bias
+column sum.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ._common import (C, as_bf16_2d, bf16_shadow, grad_buffer, grad_ready, splitk_for,
+                      use_kernels, wants_grad)
+
+
+def wgrad_accumulate(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor,
+                     alpha_t: Optional[torch.Tensor] = None) -> None:
+    """weight.grad += dy2^T @ x2  (dy2 [T, N] bf16, x2 [T, K] bf16)."""
+    T, N = dy2.shape
+    K = x2.shape[1]
+    g = grad_buffer(weight)
+    ks = splitk_for(N, K, T)
+    C().gemm(dy2, x2, g, N, K, T, True, True, flags=C().EPI_ACCUMULATE, k_splits=ks,
+             alpha_t=alpha_t)
+
+
+def bias_grad_accumulate(dy2: torch.Tensor, bias: torch.Tensor) -> None:
+    C().colsum(dy2, grad_buffer(bias))
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, act, residual):
+        K = x.shape[-1]
+        N = weight.shape[0]
+        x2 = as_bf16_2d(x)
+        T = x2.shape[0]
+        w16 = bf16_shadow(weight)
+        out_f32 = residual is not None
+        out = torch.empty((T, N), device=x.device,
+                          dtype=torch.float32 if out_f32 else torch.bfloat16)
+        flags = 0
+        aux = None
+        if act == "gelu":
+            flags |= C().EPI_GELU
+            aux = torch.empty((T, N), device=x.device, dtype=torch.bfloat16)
+        res2 = residual.reshape(T, N).float().contiguous() if residual is not None else None
+        C().gemm(x2, w16, out, T, N, K, False, False, bias=bias.detach() if bias is not None else None,
+                 residual=res2, aux=aux, flags=flags)
+        ctx.save_for_backward(x2, weight, bias, aux)
+        ctx.act = act
+        ctx.x_shape = x.shape
+        ctx.x_dtype = x.dtype
+        ctx.has_res = residual is not None
+        return out.reshape(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight, bias, aux = ctx.saved_tensors
+        N, K = weight.shape
+        dy2 = as_bf16_2d(dy)
+        T = dy2.shape[0]
+        if ctx.act == "gelu":
+            # dy of the pre-activation: dy * gelu'(h), materialised once (bf16).
+            dh = torch.empty((T, N), device=dy.device, dtype=torch.bfloat16)
+            C().gelu_bwd(dy2, aux, dh)
+            dy2 = dh
+        dx = None
+        if ctx.needs_input_grad[0]:
+            w16 = bf16_shadow(weight)
+            out_dtype = torch.float32 if ctx.x_dtype == torch.float32 else torch.bfloat16
+            dx2 = torch.empty((T, K), device=dy.device, dtype=out_dtype)
+            C().gemm(dy2, w16, dx2, T, K, N, False, True)
+            dx = dx2.reshape(ctx.x_shape)
+        if wants_grad(weight):
+            wgrad_accumulate(dy2, x2, weight)
+            grad_ready(weight)
+        if bias is not None and wants_grad(bias):
+            bias_grad_accumulate(dy2, bias)
+            grad_ready(bias)
+        dres = dy if ctx.has_res else None
+        return dx, None, None, None, dres
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           act: Optional[str] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``act(x @ weight.T + bias) + residual``.
+
+    CUDA inputs run the fused tcgen05 path (bf16 operands, f32 accumulation;
+    the output is bf16, or f32 when a residual is added). CPU inputs run the
+    plain PyTorch composition in the input dtype.
+    """
+    if not use_kernels(x):
+        y = F.linear(x, weight, bias)
+        if act == "gelu":
+            y = F.gelu(y)
+        elif act == "relu":
+            y = F.relu(y)
+        elif act is not None:
+            raise ValueError(f"unsupported fused activation {act!r}")
+        if residual is not None:
+            y = residual + y
+        return y
+    if act not in (None, "gelu"):
+        y = _LinearFn.apply(x, weight, bias, None, None)
+        y = F.relu(y) if act == "relu" else y
+        return y if residual is None else residual + y
+    return _LinearFn.apply(x, weight, bias, act, residual)

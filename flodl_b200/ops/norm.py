@@ -1,0 +1,77 @@
+"""Fused LayerNorm on CUDA (one kernel forward, one kernel backward).
+
+Reference: ``autograd::layer_norm`` -> ``at::native_layer_norm``
+(flodl/src/autograd/ops.rs:629, flodl-sys/ops_tensor.cpp:580-600).
+The backward accumulates ``weight.grad``/``bias.grad`` in the same pass as the
+input gradient and notifies the gradient-ready listeners.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ._common import C, grad_buffer, grad_ready, use_kernels, wants_grad
+
+
+class _LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps, out_bf16):
+        xc = x.contiguous()
+        Cdim = xc.shape[-1]
+        rows = xc.numel() // Cdim
+        mean = torch.empty(rows, device=x.device, dtype=torch.float32)
+        rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+        if out_bf16 or x.dtype == torch.bfloat16:
+            y = torch.empty(xc.shape, device=x.device, dtype=torch.bfloat16)
+            C().ln_fwd(xc, weight.detach() if weight is not None else None,
+                       bias.detach() if bias is not None else None, y, None, mean, rstd, eps)
+        else:
+            y = torch.empty(xc.shape, device=x.device, dtype=torch.float32)
+            C().ln_fwd(xc, weight.detach() if weight is not None else None,
+                       bias.detach() if bias is not None else None, None, y, mean, rstd, eps)
+        ctx.save_for_backward(xc, weight, bias, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xc, weight, bias, mean, rstd = ctx.saved_tensors
+        dy16 = dy.contiguous()
+        if dy16.dtype != torch.bfloat16:
+            t = torch.empty(dy16.shape, device=dy.device, dtype=torch.bfloat16)
+            C().cast_f32_bf16(dy16.float(), t)
+            dy16 = t
+        dx_f32 = dx_bf16 = None
+        if xc.dtype == torch.bfloat16:
+            dx_bf16 = torch.empty_like(xc)
+            dx = dx_bf16
+        else:
+            dx_f32 = torch.empty(xc.shape, device=xc.device, dtype=torch.float32)
+            dx = dx_f32
+        dg = grad_buffer(weight) if wants_grad(weight) else None
+        db = grad_buffer(bias) if wants_grad(bias) else None
+        C().ln_bwd(dy16, xc, mean, rstd, weight.detach() if weight is not None else None, None,
+                   dx_f32, dx_bf16, dg, db, None)
+        if dg is not None:
+            grad_ready(weight)
+        if db is not None:
+            grad_ready(bias)
+        return dx, None, None, None, None
+
+
+def layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+               eps: float = 1e-5, out_bf16: bool = False) -> torch.Tensor:
+    """LayerNorm over the last dimension.
+
+    On CUDA, ``out_bf16=True`` writes the normalised output in bf16 (the operand
+    format of the tcgen05 GEMMs) while statistics stay in f32.
+    """
+    if not use_kernels(x) or x.shape[-1] % 4 != 0 or x.shape[-1] > 2048 or x.dtype not in (
+            torch.float32, torch.bfloat16):
+        if x.is_cuda:
+            raise RuntimeError(
+                f"flodl_b200 layer_norm kernel supports f32/bf16 with C%4==0 and C<=2048 "
+                f"(got {x.dtype}, C={x.shape[-1]})")
+        return F.layer_norm(x, (x.shape[-1],), weight, bias, eps)
+    return _LayerNormFn.apply(x, weight, bias, float(eps), bool(out_bf16))

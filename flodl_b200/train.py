@@ -1,0 +1,56 @@
+"""Host-fed training step runner (public API).
+
+``StepRunner`` owns static device input buffers and a training-step callable,
+optionally captured once as a CUDA graph. ``step(*host_tensors)`` copies the
+step's inputs from (pinned) host memory into the static buffers on the
+current stream, runs the step (graph replay or eager), and returns the loss
+read back to the host. This is the end-to-end path a user runs; the device
+copy/replay/readback are the only per-step work besides the kernels.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Sequence
+
+import torch
+
+
+class StepRunner:
+    def __init__(self, step_fn: Callable[[], torch.Tensor], inputs: Sequence[torch.Tensor],
+                 graph: Optional[torch.cuda.CUDAGraph] = None,
+                 graph_loss: Optional[torch.Tensor] = None):
+        self.step_fn = step_fn
+        self.inputs = list(inputs)
+        self.graph = graph
+        self.graph_loss = graph_loss
+
+    @classmethod
+    def for_state(cls, state, graph_step=None, eager_step=None) -> "StepRunner":
+        g, l = graph_step if graph_step is not None else (None, None)
+        return cls(eager_step, [state["ids"], state["tgt"]], g, l)
+
+    @classmethod
+    def capture(cls, step_fn: Callable[[], torch.Tensor], inputs: Sequence[torch.Tensor],
+                warmup: int = 3) -> "StepRunner":
+        """Warm up ``step_fn`` then capture it as a CUDA graph."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                step_fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            loss = step_fn()
+        return cls(step_fn, inputs, g, loss)
+
+    def step(self, *host_inputs: torch.Tensor) -> float:
+        if len(host_inputs) != len(self.inputs):
+            raise ValueError(f"expected {len(self.inputs)} inputs, got {len(host_inputs)}")
+        for dst, src in zip(self.inputs, host_inputs):
+            dst.copy_(src, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            loss = self.graph_loss
+        else:
+            loss = self.step_fn()
+        return float(loss.item())

@@ -1,0 +1,80 @@
+"""Numerics of the tcgen05 GEMM engine against an fp32 PyTorch reference."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from flodl_b200._ext import cuda_ext
+    return cuda_ext()
+
+
+def _ref(A, B, a_mn, b_mn):
+    a = A.float().t() if a_mn else A.float()
+    b = B.float().t() if b_mn else B.float()
+    return a @ b.t()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (300, 200, 136), (1024, 1536, 512)])
+def test_gemm_layouts(a_mn, b_mn, M, N, K):
+    torch.manual_seed(0)
+    C = _C()
+    dev = "cuda"
+    A = torch.randn((K, M) if a_mn else (M, K), device=dev).bfloat16()
+    B = torch.randn((K, N) if b_mn else (N, K), device=dev).bfloat16()
+    if a_mn and M % 8:
+        pytest.skip("MN-major A needs M % 8 == 0")
+    if b_mn and N % 8:
+        pytest.skip("MN-major B needs N % 8 == 0")
+    out = torch.empty(M, N, device=dev, dtype=torch.float32)
+    C.gemm(A, B, out, M, N, K, a_mn, b_mn)
+    torch.cuda.synchronize()
+    ref = _ref(A, B, a_mn, b_mn)
+    torch.testing.assert_close(out, ref, rtol=1e-3, atol=1e-3)
+
+
+def test_gemm_bias_gelu_aux_bf16():
+    torch.manual_seed(1)
+    C = _C()
+    M, N, K = 512, 768, 256
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.1).bfloat16()
+    bias = torch.randn(N, device="cuda")
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    aux = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, M, N, K, False, False, bias=bias, aux=aux, flags=C.EPI_GELU)
+    pre = A.float() @ B.float().t() + bias
+    torch.testing.assert_close(aux.float(), pre, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(out.float(), torch.nn.functional.gelu(pre), rtol=2e-2, atol=2e-2)
+
+
+def test_gemm_residual_and_dgelu():
+    torch.manual_seed(2)
+    C = _C()
+    M, N, K = 256, 512, 384
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.1).bfloat16()
+    res = torch.randn(M, N, device="cuda")
+    out = torch.empty(M, N, device="cuda")
+    C.gemm(A, B, out, M, N, K, False, False, residual=res)
+    torch.testing.assert_close(out, A.float() @ B.float().t() + res, rtol=1e-3, atol=1e-3)
+    h = torch.randn(M, N, device="cuda").bfloat16()
+    out2 = torch.empty(M, N, device="cuda")
+    C.gemm(A, B, out2, M, N, K, False, False, aux=h, flags=C.EPI_DGELU)
+    x = h.float().requires_grad_()
+    torch.nn.functional.gelu(x).backward(torch.ones_like(x))
+    torch.testing.assert_close(out2, (A.float() @ B.float().t()) * x.grad, rtol=1e-3, atol=1e-3)
+
+
+def test_gemm_splitk_accumulate():
+    torch.manual_seed(3)
+    C = _C()
+    M, N, K = 512, 512, 8192
+    A = torch.randn(K, M, device="cuda").bfloat16()  # dY stored [tokens, M]
+    B = torch.randn(K, N, device="cuda").bfloat16()  # x stored [tokens, N]
+    out = torch.ones(M, N, device="cuda")
+    C.gemm(A, B, out, M, N, K, True, True, flags=C.EPI_ACCUMULATE, k_splits=8)
+    ref = A.float().t() @ B.float() + 1.0
+    torch.testing.assert_close(out, ref, rtol=1e-3, atol=5e-2)

@@ -1,0 +1,180 @@
+"""Numerics of the sm_100a kernels against plain fp32 PyTorch references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from flodl_b200._ext import cuda_ext
+    return cuda_ext()
+
+
+@pytest.mark.parametrize("C,dtype", [(512, torch.float32), (768, torch.float32), (64, torch.bfloat16), (1000, torch.float32)])
+def test_layernorm_fwd_bwd(C, dtype):
+    torch.manual_seed(0)
+    from flodl_b200.ops.norm import layer_norm
+    R = 1000
+    x = torch.randn(R, C, device="cuda").to(dtype).requires_grad_()
+    w = torch.randn(C, device="cuda").requires_grad_()
+    b = torch.randn(C, device="cuda").requires_grad_()
+    y = layer_norm(x, w, b, 1e-5, out_bf16=False)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    br = b.detach().clone().requires_grad_()
+    yr = F.layer_norm(xr, (C,), wr, br, 1e-5)
+    yr.backward(dy.float())
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    torch.testing.assert_close(y.float(), yr, rtol=tol, atol=tol)
+    # dy is rounded to bf16 inside the kernel
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=3e-2, atol=3e-1)
+    torch.testing.assert_close(b.grad, br.grad, rtol=3e-2, atol=3e-1)
+
+
+def test_ln_bwd_fused_extras():
+    torch.manual_seed(1)
+    C = _C()
+    R, Cd = 512, 512
+    x = torch.randn(R, Cd, device="cuda")
+    w = torch.randn(Cd, device="cuda")
+    mean = torch.empty(R, device="cuda"); rstd = torch.empty(R, device="cuda")
+    y = torch.empty(R, Cd, device="cuda", dtype=torch.bfloat16)
+    C.ln_fwd(x, w, None, y, None, mean, rstd, 1e-5)
+    dy = torch.randn(R, Cd, device="cuda").bfloat16()
+    dres = torch.randn(R, Cd, device="cuda")
+    dx = torch.empty(R, Cd, device="cuda"); dx16 = torch.empty(R, Cd, device="cuda", dtype=torch.bfloat16)
+    colsum = torch.zeros(Cd, device="cuda")
+    C.ln_bwd(dy, x, mean, rstd, w, dres, dx, dx16, None, None, colsum)
+    xr = x.clone().requires_grad_()
+    yr = F.layer_norm(xr, (Cd,), w, None, 1e-5)
+    yr.backward(dy.float())
+    ref = xr.grad + dres
+    torch.testing.assert_close(dx, ref, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(dx16.float(), ref, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(colsum, ref.sum(0), rtol=1e-3, atol=1e-2)
+
+
+@pytest.mark.parametrize("V,smooth,ignore", [(256, 0.0, False), (30522, 0.1, True), (10, 0.0, False)])
+def test_softmax_ce(V, smooth, ignore):
+    torch.manual_seed(2)
+    from flodl_b200.ops.loss import cross_entropy
+    T = 777
+    logits = (torch.randn(T, V, device="cuda") * 3).bfloat16().requires_grad_()
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    if ignore:
+        tgt[::3] = -100
+    loss = cross_entropy(logits, tgt, ignore_index=-100, label_smoothing=smooth)
+    loss.backward()
+    lr = logits.detach().float().requires_grad_()
+    ref = F.cross_entropy(lr, tgt, ignore_index=-100, label_smoothing=smooth)
+    ref.backward()
+    torch.testing.assert_close(loss, ref, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(logits.grad.float(), lr.grad, rtol=2e-2, atol=2e-5)
+
+
+def _attn_ref(qkv, B, S, H, causal, key_pad=None):
+    D = qkv.shape[1] // (3 * H)
+    q, k, v = qkv.float().view(B, S, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
+    if causal:
+        s = s.masked_fill(~torch.ones(S, S, dtype=torch.bool, device=qkv.device).tril(), float("-inf"))
+    if key_pad is not None:
+        s = s.masked_fill(key_pad[:, None, None, :], float("-inf"))
+    p = s.softmax(-1)
+    return (p @ v).permute(0, 2, 1, 3).reshape(B * S, H * D)
+
+
+@pytest.mark.parametrize("B,S,H,causal", [(2, 256, 2, True), (2, 256, 2, False), (1, 200, 3, True), (2, 512, 2, False), (1, 384, 1, True)])
+def test_flash_attention_fwd_bwd(B, S, H, causal):
+    torch.manual_seed(3)
+    from flodl_b200.ops.attention import attention_packed
+    D = 64
+    qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16().requires_grad_()
+    out = attention_packed(qkv, B, S, H, causal)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    qr = qkv.detach().float().requires_grad_()
+    ref = _attn_ref(qr, B, S, H, causal)
+    ref.backward(dout.float())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(qkv.grad.float(), qr.grad, rtol=5e-2, atol=5e-2)
+
+
+def test_flash_attention_padding_mask():
+    torch.manual_seed(4)
+    from flodl_b200.ops.attention import attention_packed
+    B, S, H, D = 2, 256, 2, 64
+    qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16().requires_grad_()
+    pad = torch.zeros(B, S, dtype=torch.bool, device="cuda")
+    pad[0, 200:] = True
+    pad[1, 17:] = True
+    out = attention_packed(qkv, B, S, H, False, pad)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    qr = qkv.detach().float().requires_grad_()
+    ref = _attn_ref(qr, B, S, H, False, pad)
+    ref.backward(dout.float())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(qkv.grad.float(), qr.grad, rtol=5e-2, atol=5e-2)
+
+
+def test_adamw_kernel_matches_torch():
+    torch.manual_seed(5)
+    C = _C()
+    n = 10007
+    p = torch.randn(n, device="cuda"); g = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda"); v = torch.zeros(n, device="cuda")
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    lr = torch.tensor(1e-3, device="cuda"); step = torch.tensor(0.0, device="cuda")
+    pr = p.clone().requires_grad_()
+    opt = torch.optim.AdamW([pr], lr=1e-3, weight_decay=0.1)
+    for _ in range(3):
+        C.add_scalar(step, 1.0)
+        C.adamw(p, g, m, v, sh, lr, step, None, 0.9, 0.999, 1e-8, 0.1, True, False)
+        pr.grad = g.clone()
+        opt.step()
+    torch.testing.assert_close(p, pr.detach(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(sh.float(), p, rtol=1e-2, atol=1e-2)
+
+
+def test_sgd_kernel_matches_torch():
+    torch.manual_seed(6)
+    C = _C()
+    n = 4099
+    p = torch.randn(n, device="cuda"); buf = torch.zeros(n, device="cuda")
+    lr = torch.tensor(0.1, device="cuda")
+    pr = p.clone().requires_grad_()
+    opt = torch.optim.SGD([pr], lr=0.1, momentum=0.9, weight_decay=5e-4)
+    for i in range(3):
+        g = torch.randn(n, device="cuda")
+        first = torch.tensor(1.0 if i == 0 else 0.0, device="cuda")
+        C.sgd(p, g, buf, None, lr, None, first, 0.9, 0.0, 5e-4, False, False)
+        pr.grad = g.clone()
+        opt.step()
+    torch.testing.assert_close(p, pr.detach(), rtol=1e-5, atol=1e-6)
+
+
+def test_linear_op_fwd_bwd_gelu_residual():
+    torch.manual_seed(7)
+    from flodl_b200.ops.linear import linear
+    x = torch.randn(300, 256, device="cuda").requires_grad_()
+    w = (torch.randn(512, 256, device="cuda") * 0.05).requires_grad_()
+    b = torch.randn(512, device="cuda").requires_grad_()
+    res = torch.randn(300, 512, device="cuda").requires_grad_()
+    y = linear(x, w, b, act="gelu", residual=res)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr, wr, br, rr = [t.detach().clone().requires_grad_() for t in (x, w, b, res)]
+    yr = rr + F.gelu(F.linear(xr.bfloat16().float(), wr.bfloat16().float(), br))
+    yr.backward(dy)
+    torch.testing.assert_close(y, yr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad, xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=3e-2, atol=1e-1)
+    torch.testing.assert_close(b.grad, br.grad, rtol=3e-2, atol=5e-2)
+    torch.testing.assert_close(res.grad, rr.grad)
