@@ -152,20 +152,19 @@ def main():
         launches_fn = cuda_ext().launch_count
 
     ids, tgt = state["ids"], state["tgt"]
-    # warm-up (eager; builds arenas, workspaces)
-    for _ in range(max(args.warmup, 3)):
-        loss = step()
+    # warm-up (eager, on a side stream so every buffer the step creates - arenas,
+    # gradients, workspaces - belongs to a non-legacy stream before capture)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
 
     graph = None
     if not args.no_graph:
         graph = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
         c0 = launches_fn() if launches_fn else 0
         with torch.cuda.graph(graph):
             static_loss = step()

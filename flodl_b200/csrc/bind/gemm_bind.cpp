@@ -87,5 +87,8 @@ void register_gemm(py::module& m) {
   m.def("num_sms", &flodl::num_sms);
   m.def("launch_count", &flodl::launch_count, "kernels launched by this library so far");
   m.def("reset_launch_count", &flodl::reset_launch_count);
+  m.def("kernel_error", &flodl::read_kernel_error,
+        "nonzero if a bounded wait in a compute kernel expired (1 = mbarrier timeout)");
+  m.def("clear_kernel_error", &flodl::clear_kernel_error);
   m.def("set_wait_limit_ns", [](int64_t ns) { flodl::set_wait_limit_ns((uint64_t)ns); });
 }

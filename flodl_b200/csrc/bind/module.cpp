@@ -9,4 +9,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_elementwise(m);
   register_optim(m);
   register_attention(m);
+  register_comm(m);
 }

@@ -335,8 +335,6 @@ struct BwdSmem {
   uint8_t dout[2][kTileBytes];
   uint8_t p[2 * kTileBytes];   // P^T: 128 keys x 128 queries
   uint8_t ds[2 * kTileBytes];  // dS^T: 128 keys x 128 queries
-  float lse[kTile];
-  float delta[kTile];
   uint64_t kv_full;
   uint64_t qdo_full[2];
   uint64_t qdo_empty[2];
@@ -507,7 +505,6 @@ __global__ void __launch_bounds__(192, 1)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const int kj = k0 + r;
-    const int tid = threadIdx.x - 64;  // 0..127
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = scale * kLog2e;
     const bool key_ok = kj < S && !(key_pad && key_pad[(size_t)b * S + kj] != 0);
@@ -515,14 +512,8 @@ __global__ void __launch_bounds__(192, 1)
     for (int it = 0; it < n_it; ++it) {
       const int qt = qt_begin + it;
       const int q0 = qt * kTile;
-      // per-query lse/delta for this tile into shared memory
-      {
-        const int qi = q0 + tid;
-        const size_t idx = ((size_t)b * H + h) * S + qi;
-        sm.lse[tid] = (qi < S) ? lse2[idx] : INFINITY;
-        sm.delta[tid] = (qi < S) ? delta[idx] : 0.f;
-      }
-      named_bar_sync(1, 128);
+      const float* lse_t = lse2 + ((size_t)b * H + h) * S + q0;
+      const float* delta_t = delta + ((size_t)b * H + h) * S + q0;
       ok = mbar_wait_bounded(&sm.sdp_full, it & 1, abort_flag, err, limit);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
@@ -537,9 +528,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int i = 0; i < 32; ++i) {
           const int qi = q0 + c + i;
           const bool valid = key_ok && qi < S && (!causal || kj <= qi);
-          const float p = valid ? exp2f(__uint_as_float(rs[i]) * sl2 - sm.lse[c + i]) : 0.f;
+          // per-query statistics: every thread reads the same words (L1 broadcast)
+          const float l2 = qi < S ? __ldg(lse_t + c + i) : 0.f;
+          const float dl = qi < S ? __ldg(delta_t + c + i) : 0.f;
+          const float p = valid ? exp2f(__uint_as_float(rs[i]) * sl2 - l2) : 0.f;
           pv[i] = p;
-          dsv[i] = p * (__uint_as_float(rdp[i]) - sm.delta[c + i]);
+          dsv[i] = p * (__uint_as_float(rdp[i]) - dl);
         }
         st_row32_sw128(sm.p, r, c, pv);
         st_row32_sw128(sm.ds, r, c, dsv);
@@ -619,6 +613,10 @@ __global__ void __launch_bounds__(192, 1)
 
 }  // namespace
 
+void set_flash_wait_limit_ns(uint64_t ns) {
+  cudaMemcpyToSymbol(g_fa_wait_limit_ns, &ns, sizeof(ns));
+}
+
 cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st) {
   if (a.D != kD || a.S <= 0 || a.B <= 0 || a.H <= 0) return cudaErrorInvalidValue;
   CUtensorMap tm;
@@ -631,7 +629,7 @@ cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st) {
   }
   dim3 grid((a.S + kTile - 1) / kTile, a.H, a.B);
   flash_fwd_kernel<<<grid, 192, smem, st>>>(tm, a.out, a.lse2, a.key_pad, a.B, a.S, a.H,
-                                            a.causal ? 1 : 0, a.scale, a.err);
+                                            a.causal ? 1 : 0, a.scale, a.err ? a.err : default_err_word());
   note_launch();
   return cudaGetLastError();
 }
@@ -654,7 +652,7 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   dim3 grid((a.S + kTile - 1) / kTile, a.H, a.B);
   flash_bwd_kernel<<<grid, 192, smem, st>>>(tm_qkv, tm_do, a.lse2, a.delta, a.dq_acc, a.dqkv,
                                             a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
-                                            a.err);
+                                            a.err ? a.err : default_err_word());
   const int64_t T = (int64_t)a.B * a.S;
   int post_blocks = (int)std::min<int64_t>((T * C / 2 + 255) / 256, (int64_t)num_sms() * 16);
   flash_bwd_post_kernel<<<post_blocks, 256, 0, st>>>(a.dq_acc, a.dqkv, T, C, a.scale);

@@ -26,5 +26,6 @@ struct FlashArgs {
 
 cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st);
 cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st);
+void set_flash_wait_limit_ns(uint64_t ns);
 
 }  // namespace flodl

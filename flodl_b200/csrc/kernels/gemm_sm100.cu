@@ -433,6 +433,30 @@ void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_re
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 void reset_launch_count() { g_launches.store(0); }
 
+static uint32_t* g_err_host = nullptr;
+static uint32_t* g_err_dev = nullptr;
+uint32_t* default_err_word() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* hp = nullptr;
+    if (cudaHostAlloc(&hp, 64, cudaHostAllocMapped) == cudaSuccess) {
+      g_err_host = static_cast<uint32_t*>(hp);
+      *g_err_host = 0;
+      void* dp = nullptr;
+      if (cudaHostGetDevicePointer(&dp, hp, 0) == cudaSuccess) g_err_dev = static_cast<uint32_t*>(dp);
+    }
+  });
+  return g_err_dev;
+}
+uint32_t read_kernel_error() {
+  default_err_word();
+  return g_err_host ? *reinterpret_cast<volatile uint32_t*>(g_err_host) : 0u;
+}
+void clear_kernel_error() {
+  default_err_word();
+  if (g_err_host) *reinterpret_cast<volatile uint32_t*>(g_err_host) = 0u;
+}
+
 void set_wait_limit_ns(uint64_t ns) {
   cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
 }
@@ -463,7 +487,7 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.k_splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, g.ep, g.M, g.N, g.K, g.k_splits,
-                                                     g.err);
+                                                     g.err ? g.err : default_err_word());
   note_launch();
   return cudaGetLastError();
 }

@@ -50,4 +50,10 @@ void note_launch(int n = 1);
 uint64_t launch_count();
 void reset_launch_count();
 
+// Host-mapped error word shared by the compute kernels (bounded waits write
+// a nonzero KernelError code here instead of hanging). Readable without a sync.
+uint32_t* default_err_word();
+uint32_t read_kernel_error();
+void clear_kernel_error();
+
 }  // namespace flodl

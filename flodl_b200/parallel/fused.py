@@ -1,0 +1,163 @@
+"""DDP with the fused peer-memory gradient all-reduce + optimizer update.
+
+``FusedDdp(model, optimizer)`` re-homes the model's parameters, gradients and
+bf16 weight shadows into symmetric peer-mapped arenas, broadcasts rank 0's
+weights with the pull kernel, and cuts the arena into buckets in reverse
+parameter order. During backward, the fused ops report each parameter's
+gradient as complete; when a bucket is complete its fused kernel is launched on
+the communication stream (overlapping the rest of backward): reduce-scatter
+over NVLink, AdamW/SGD on this rank's shard, all-gather of the updated f32
+weights and bf16 shadows into every rank, gradient clear. ``finish()`` joins
+the communication stream; there is no separate ``optimizer.step()`` or
+``zero_grad()`` in this mode.
+
+Semantics equal the reference's ``Ddp::wrap`` + ``all_reduce_gradients`` (Avg)
++ ``optimizer.step()`` (flodl/src/distributed/ddp.rs:249-260): every rank ends
+the step with identical parameters. Optimizer moments are held only for the
+shard each rank owns (the other ranks' slices of m/v stay unused).
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import torch
+import torch.distributed as dist
+
+from ..ops._common import add_grad_ready_listener, clear_grad_ready_listeners
+from ..optim.optimizer import SGD, Adam, AdamW
+from ..utils.arena import ParamArena
+from .peer import PeerComm
+
+
+class FusedDdp:
+    fuses_optimizer = True
+
+    def __init__(self, model: torch.nn.Module, optimizer, bucket_mb: float = 16.0,
+                 blocks: int = 64, group=None, timeout_s: float = 10.0):
+        self.model = model
+        self.opt = optimizer
+        if len(optimizer.groups) != 1:
+            raise ValueError("FusedDdp supports one parameter group")
+        self.group = optimizer.groups[0]
+        params = list(self.group.params)
+        self.params = params
+        self.device = params[0].device
+        numel = sum((p.numel() + 63) // 64 * 64 for p in params)
+        self.comm = PeerComm(numel, self.device, group=group, timeout_s=timeout_s)
+        self.rank, self.world = self.comm.rank, self.comm.world
+        arena = ParamArena(params, alloc=self.comm.data_alloc, grad_alloc=self.comm.grad_alloc,
+                           with_shadow=False)
+        # bf16 shadow lives in the symmetric region too
+        arena.shadow = self.comm.shadow[:arena.numel]
+        arena.rebind()
+        arena.refresh_shadow()
+        self.arena = arena
+        self.group.arena = arena
+        self.blocks = blocks
+        # optimizer state (device scalars + moments) for the whole arena
+        optimizer._device_scalars(self.group)
+        self.kind = "adamw" if isinstance(optimizer, Adam) else "sgd" if isinstance(optimizer, SGD) else None
+        if self.kind is None:
+            raise ValueError("FusedDdp supports Adam/AdamW and SGD")
+        if isinstance(optimizer, Adam) and not isinstance(optimizer, AdamW) and self.group.hyper["weight_decay"]:
+            raise ValueError("FusedDdp: Adam with L2 weight decay is not fused; use AdamW")
+        optimizer._init_fused_state(self.group)
+        if self.kind == "adamw":
+            # step_t holds the number of the update the next bucket kernels apply
+            self.comm.C.add_scalar(self.group.step_t, 1.0)
+        self.comm_stream = torch.cuda.Stream(self.device)
+        self._build_buckets(bucket_mb)
+        for p in params:
+            clear_grad_ready_listeners(p)
+            add_grad_ready_listener(p, self._on_ready)
+        # initial state: rank 0's parameters on every rank (pull broadcast)
+        torch.cuda.synchronize(self.device)
+        self.comm.broadcast_(arena.numel, root=0, slot=self._slot_bcast, blocks=blocks)
+        torch.cuda.synchronize(self.device)
+        self.comm.check()
+        if self.world > 1:
+            for b in model.buffers():
+                if b.is_floating_point():
+                    dist.broadcast(b, src=0)
+        self._launched: set = set()
+
+    def _build_buckets(self, bucket_mb: float) -> None:
+        a = self.arena
+        cap = int(bucket_mb * (1 << 20) / 4)
+        order = list(range(len(a.params)))[::-1]
+        self.buckets: List[dict] = []
+        self._bucket_of: Dict[int, dict] = {}
+        cur, size = [], 0
+        for i in order:
+            cur.append(i)
+            size += a.params[i].numel()
+            if size >= cap:
+                self._close(cur)
+                cur, size = [], 0
+        if cur:
+            self._close(cur)
+        self._slot_bcast = 2 * len(self.buckets)
+        self._slot_avg = self._slot_bcast + 2
+        if self._slot_avg + 2 >= self.comm.C.MAX_BUCKETS:
+            raise ValueError("too many buckets; raise bucket_mb")
+
+    def _close(self, idx: List[int]) -> None:
+        a = self.arena
+        start = min(a.offsets[i] for i in idx)
+        end = max(a.offsets[i] + ((a.params[i].numel() + 63) // 64) * 64 for i in idx)
+        b = {"slot": 2 * len(self.buckets), "start": start, "end": end,
+             "params": [a.params[i] for i in idx], "pending": len(idx)}
+        self.buckets.append(b)
+        for i in idx:
+            self._bucket_of[id(a.params[i])] = b
+
+    def _on_ready(self, p) -> None:
+        b = self._bucket_of.get(id(p))
+        if b is None:
+            return
+        b["pending"] -= 1
+        if b["pending"] == 0:
+            self._launch(b)
+
+    def _launch(self, b) -> None:
+        cur = torch.cuda.current_stream(self.device)
+        self.comm_stream.wait_stream(cur)
+        g = self.group
+        h = g.hyper
+        with torch.cuda.stream(self.comm_stream):
+            if self.kind == "adamw":
+                self.comm.launch(self.comm.C.FUSED_AR_ADAMW, bucket=b["slot"], start=b["start"],
+                                 end=b["end"], blocks=self.blocks, m=g.m, v=g.v, lr=g.lr_t,
+                                 step=g.step_t, gscale=self.opt.gscale_t, beta1=h["beta1"],
+                                 beta2=h["beta2"], eps=h["eps"], wd=h["weight_decay"])
+            else:
+                self.comm.launch(self.comm.C.FUSED_AR_SGD, bucket=b["slot"], start=b["start"],
+                                 end=b["end"], blocks=self.blocks, m=g.buf, lr=g.lr_t,
+                                 first=g.first_t, gscale=self.opt.gscale_t, wd=h["weight_decay"],
+                                 momentum=h["momentum"], dampening=h["dampening"],
+                                 nesterov=int(h["nesterov"]))
+        self._launched.add(b["slot"])
+
+    def finish(self) -> None:
+        """Launch buckets not yet reported ready, then join the comm stream."""
+        for b in self.buckets:
+            if b["slot"] not in self._launched:
+                self._launch(b)
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+        if self.kind == "adamw":
+            self.comm.C.add_scalar(self.group.step_t, 1.0)
+        else:
+            self.group.first_t.zero_()
+        for b in self.buckets:
+            b["pending"] = len(b["params"])
+        self._launched = set()
+
+    all_reduce_gradients = finish
+
+    def average_params(self, mass: float = 1.0, gamma: float = 1.0) -> None:
+        """Weighted parameter average across ranks (cluster averaging)."""
+        self.comm.weighted_average_(self.arena.numel, mass, gamma, slot=self._slot_avg,
+                                    blocks=self.blocks)
+
+    def close(self) -> None:
+        self.comm.close()
