@@ -60,6 +60,12 @@ void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor&
   a.rows = (int)(x.numel() / C);
   a.C = C;
   c10::cuda::CUDAGuard guard(x.device());
+  Tensor partials;
+  if (a.dgamma || a.dbeta || a.colsum) {
+    a.partial_blocks = flodl::ln_bwd_partial_blocks(a.rows);
+    partials = at::empty({3 * (int64_t)a.partial_blocks * C}, x.options().dtype(at::kFloat));
+    a.partials = partials.data_ptr<float>();
+  }
   FL_CUDA_OK(flodl::launch_ln_bwd(a, cur_stream()));
 }
 
@@ -69,9 +75,12 @@ void colsum(const Tensor& m, Tensor& out, const optional<Tensor>& scale) {
   FL_CHECK_F32(out);
   const int C = (int)m.size(-1);
   c10::cuda::CUDAGuard guard(m.device());
-  FL_CUDA_OK(flodl::launch_colsum(m.data_ptr(), m.scalar_type() == at::kBFloat16, ptr<float>(out),
-                                  (int)(m.numel() / C), C, cur_stream(),
-                                  opt_ptr<const float>(scale)));
+  const int rows = (int)(m.numel() / C);
+  const int nb = flodl::colsum_partial_blocks(rows);
+  Tensor partials = at::empty({(int64_t)nb * C}, m.options().dtype(at::kFloat));
+  FL_CUDA_OK(flodl::launch_colsum2(m.data_ptr(), m.scalar_type() == at::kBFloat16, ptr<float>(out),
+                                   rows, C, partials.data_ptr<float>(), nb, cur_stream(),
+                                   opt_ptr<const float>(scale)));
 }
 
 // Returns nothing; writes loss (scalar, overwritten) and dlogits.

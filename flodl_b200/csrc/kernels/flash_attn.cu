@@ -37,6 +37,18 @@ constexpr int kTileBytes = kTile * kD * 2;  // 16 KB: 128 rows x 128 B
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ uint64_t g_fa_wait_limit_ns = 2000000000ull;
+// Optional progress words (host-mapped, 8 per CTA: one per warp, code = stage).
+// Null unless a diagnostic run sets it; only lane 0 of a warp writes.
+__device__ uint32_t* g_fa_progress = nullptr;
+
+__device__ __forceinline__ void progress(int code) {
+  uint32_t* p = g_fa_progress;
+  if (p != nullptr && (threadIdx.x & 31) == 0) {
+    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    volatile uint32_t* w = p + cta * 8 + (threadIdx.x >> 5);
+    *w = (uint32_t)code;
+  }
+}
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -166,6 +178,7 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_3d(sm.v[st], &tm_qkv, &sm.kv_full[st], 2 * C + h * kD, j * kTile, b);
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else if (warp == 1) {
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
@@ -213,6 +226,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else {
     // --------------------------------------------------- softmax warps
     const int q4 = warp & 3;
@@ -415,10 +429,12 @@ __global__ void __launch_bounds__(192, 1)
     sm.abort = 0;
     fence_mbar_init();
   }
+  progress(1);
   if (warp == 1) {
     tmem_alloc<512>(&sm.tmem_base);
     tmem_relinquish();
   }
+  progress(2);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -441,8 +457,11 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive_expect_tx(&sm.qdo_full[st], 2 * kTileBytes);
         tma_load_3d(sm.q[st], &tm_qkv, &sm.qdo_full[st], h * kD, qt * kTile, b);
         tma_load_3d(sm.dout[st], &tm_dout, &sm.qdo_full[st], h * kD, qt * kTile, b);
+        progress(10 + it);
       }
+      progress(19);
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else if (warp == 1) {
     if (elect_one_sync()) {
       constexpr uint32_t idesc_kq = make_idesc_bf16(128, 128, 0, 0);  // M=keys, N=queries
@@ -466,7 +485,9 @@ __global__ void __launch_bounds__(192, 1)
                     make_sdesc_sw128(do_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
         }
         umma_commit(&sm.sdp_full);
+        progress(20 + 10 * it + 1);
         ok = mbar_wait_bounded(&sm.pds_ready, it & 1, abort_flag, err, limit);
+        progress(20 + 10 * it + 2);
         if (!ok) break;
         tc_fence_after();
         // dV += P^T dO ; dK += dS^T Q   (K = 128 queries)
@@ -492,7 +513,9 @@ __global__ void __launch_bounds__(192, 1)
                     make_sdesc_sw128(k_addr + kk * 2048, kTileBytes, 1024), idesc_qd, kk > 0);
         umma_commit(&sm.dq_full);
         umma_commit(&sm.qdo_empty[st]);
+        progress(20 + 10 * it + 5);
       }
+      progress(59);
       if (!ok) {
         umma_commit(&sm.drain);
         uint64_t t0 = global_timer_ns();
@@ -500,6 +523,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else {
     // --------------------------------------------------- softmax warps (thread = key row)
     const int q4 = warp & 3;
@@ -514,8 +538,10 @@ __global__ void __launch_bounds__(192, 1)
       const int q0 = qt * kTile;
       const float* lse_t = lse2 + ((size_t)b * H + h) * S + q0;
       const float* delta_t = delta + ((size_t)b * H + h) * S + q0;
+      progress(60 + 10 * it);
       ok = mbar_wait_bounded(&sm.sdp_full, it & 1, abort_flag, err, limit);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      progress(60 + 10 * it + 1);
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < kTile; c += 32) {
@@ -542,9 +568,11 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.pds_ready);
+      progress(60 + 10 * it + 2);
       // dQ tile: thread = query row (TMEM lane)
       ok = mbar_wait_bounded(&sm.dq_full, it & 1, abort_flag, err, limit);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      progress(60 + 10 * it + 3);
       tc_fence_after();
       {
         const int qi = q0 + r;
@@ -565,19 +593,22 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.dq_free);
+      progress(60 + 10 * it + 4);
     }
+    progress(90);
     // dK, dV out (thread = key row). The last dq_full wait above implies all MMAs are done.
     if (ok && n_it > 0) {
       tc_fence_after();
-      if (kj < S) {
-        __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD;
-        __nv_bfloat16* vrow = krow + C;
+      // tcgen05.ld is warp-synchronous: every lane loads, only in-range rows store
+      __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD;
+      __nv_bfloat16* vrow = krow + C;
 #pragma unroll
-        for (int c = 0; c < kD; c += 32) {
-          uint32_t rk[32], rv[32];
-          tmem_ld_32cols(t_dk + lane_off + c, rk);
-          tmem_ld_32cols(t_dv + lane_off + c, rv);
-          tmem_ld_wait();
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t rk[32], rv[32];
+        tmem_ld_32cols(t_dk + lane_off + c, rk);
+        tmem_ld_32cols(t_dv + lane_off + c, rv);
+        tmem_ld_wait();
+        if (kj < S) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 wk, wv;
@@ -603,15 +634,22 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
+  progress(95);
   tc_fence_before();
   __syncthreads();
+  progress(97);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<512>(tmem);
   }
+  progress(99);
 }
 
 }  // namespace
+
+void set_flash_progress_words(uint32_t* dev_ptr) {
+  cudaMemcpyToSymbol(g_fa_progress, &dev_ptr, sizeof(dev_ptr));
+}
 
 void set_flash_wait_limit_ns(uint64_t ns) {
   cudaMemcpyToSymbol(g_fa_wait_limit_ns, &ns, sizeof(ns));

@@ -26,6 +26,7 @@
 
 #include <cstdio>
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 namespace flodl {
@@ -34,9 +35,17 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                      // two per SM sub-partition
+constexpr int kThreads = 64 + 32 * kEpiWarps;     // producer + MMA + epilogue
 
 __device__ uint64_t g_wait_limit_ns = 2000000000ull;  // 2 s
+
+// Epilogue staging: each epilogue warp owns 4 KB of shared memory holding one
+// 32x32 output chunk (f32, 128B swizzle) or one bf16 output chunk plus one
+// bf16 pre-activation chunk (2 KB each, 64B swizzle); chunks leave through TMA
+// stores so global writes are full, coalesced lines.
+constexpr int kStageWarpBytes = 4096;
+constexpr int kStagingBytes = kEpiWarps * kStageWarpBytes;
 
 template <int BN>
 struct GemmCfg {
@@ -45,7 +54,8 @@ struct GemmCfg {
   static constexpr int kBTileBytes = BN * kBK * 2;   // 32 KB or 16 KB
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct SmemCtl {
@@ -178,18 +188,130 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, 
   }
 }
 
+// Same math as epilogue_chunk, but the warp writes its 32x32 chunk into
+// swizzled shared memory and one lane ships it with a TMA store (or a TMA
+// reduce-add for accumulation). `buf` alternates between the two staging
+// slots; the caller guarantees the slot's previous store finished reading.
+__device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, const CUtensorMap* tmOut,
+                                                   const CUtensorMap* tmAux, uint8_t* stage,
+                                                   int buf, int row0, int col0, int lane, int M,
+                                                   int N, const uint32_t (&acc)[32]) {
+  const int row = row0 + lane;
+  float v[32];
+  const float alpha = ep.alpha_ptr ? ep.alpha * __ldg(ep.alpha_ptr) : ep.alpha;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) * alpha;
+  const bool full_cols = (col0 + 32 <= N);
+  const bool row_ok = row < M;
+  if (ep.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int c = col0 + i;
+      v[i] += (c < N) ? __ldg(ep.bias + c) : 0.f;
+    }
+  }
+  const bool aux_out = (ep.flags & kEpiGelu) && ep.aux;
+  if (aux_out) {
+    // pre-activation -> bf16 staging (64B swizzle)
+    uint8_t* a = stage + 2048;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+      w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+      w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+      w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+      *reinterpret_cast<uint4*>(a + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
+    }
+  }
+  if (ep.flags & kEpiGelu) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+  }
+  if ((ep.flags & kEpiDGelu) && row_ok) {
+    const __nv_bfloat16* aux =
+        reinterpret_cast<const __nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
+    if (full_cols && ((ep.ld_aux & 7) == 0)) {
+      const uint4* src = reinterpret_cast<const uint4*>(aux + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w = src[q];
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2 f = unpack_bf16x2(ws[h]);
+          v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
+          v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] *= gelu_erf_grad(__bfloat162float(aux[col0 + i]));
+    }
+  }
+  if (ep.residual && row_ok) {
+    const float* res = ep.residual + (size_t)row * ep.ld_res;
+    if (full_cols && ((ep.ld_res & 3) == 0)) {
+      const float4* src = reinterpret_cast<const float4*>(res + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 r = src[q];
+        v[4 * q + 0] += r.x;
+        v[4 * q + 1] += r.y;
+        v[4 * q + 2] += r.z;
+        v[4 * q + 3] += r.w;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < N) v[i] += res[col0 + i];
+    }
+  }
+  if (ep.out_f32) {
+    uint8_t* o = stage;  // 32 rows x 128 B, 128B swizzle
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(o + lane * 128 + ((q ^ (lane & 7)) * 16)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    uint8_t* o = stage;  // 32 rows x 64 B, 64B swizzle
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+      w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+      w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+      w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+      *reinterpret_cast<uint4*>(o + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
+    }
+  }
+  fence_proxy_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    const uint8_t* o = stage;
+    if (ep.flags & kEpiAccumulate)
+      tma_reduce_add_2d(tmOut, o, col0, row0);
+    else
+      tma_store_2d(tmOut, o, col0, row0);
+    if (aux_out) tma_store_2d(tmAux, stage + 2048, col0, row0);
+    bulk_commit_group();
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, GemmEpilogue ep, int M, int N,
-                      int K, int k_splits, uint32_t* err) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmOut,
+                      const __grid_constant__ CUtensorMap tmAux, GemmEpilogue ep, int M, int N,
+                      int K, int k_splits, int use_tma_store, uint32_t* err) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128B-swizzled tiles need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + S * Cfg::kStageBytes);
+  uint8_t* staging = smem + S * Cfg::kStageBytes;
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(staging + kStagingBytes);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -208,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->tmem_full[a], 1);
-      mbar_init(&ctl->tmem_empty[a], 4);
+      mbar_init(&ctl->tmem_empty[a], kEpiWarps);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -217,6 +339,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (use_tma_store) {
+      tma_prefetch_desc(&tmOut);
+      tma_prefetch_desc(&tmAux);
+    }
   }
   if (warp == 1) {
     tmem_alloc<Cfg::kTmemCols>(&ctl->tmem_base);
@@ -281,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
@@ -339,9 +466,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int ew = warp - 2;              // epilogue warp 0..7
+    const int half = ew / 4;              // which half of the tile's columns
+    constexpr int kChunks = BN / 32 / 2;  // 32-column chunks per warp
+    uint8_t* stage = staging + ew * kStageWarpBytes;
     uint32_t local_tile = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local_tile) {
       int tm, tn, ks;
@@ -351,25 +483,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait_bounded(&ctl->tmem_full[acc], acc_ph, abort_flag, err, limit);
       if (!__all_sync(0xffffffffu, ok)) break;  // keep the warp converged for tcgen05.ld
       tc_fence_after();
-      const int row = tm * kBM + q * 32 + lane;
+      const int row0 = tm * kBM + q * 32;
+      const int row = row0 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const int kb0 = ks * kb_per_split;
       const bool empty_split = kb0 >= k_blocks_total;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = half * kChunks + cc;
         const int col0 = tn * BN + c * 32;
         uint32_t r[32];
         tmem_ld_32cols(t_row + c * 32, r);
         tmem_ld_wait();
-        if (c == BN / 32 - 1) {
-          // Last read of this accumulator: hand it back to the MMA warp early.
+        if (cc == kChunks - 1) {
+          // Last read of this accumulator by this warp: hand it back early.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
         }
-        if (col0 < N && !empty_split) epilogue_chunk(ep, row, col0, M, N, r);
+        if (col0 >= N || empty_split || row0 >= M) continue;
+        if (use_tma_store) {
+          // the previous chunk's store must have read the staging slot
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+          epilogue_chunk_tma(ep, &tmOut, &tmAux, stage, 0, row0, col0, lane, M, N, r);
+        } else {
+          epilogue_chunk(ep, row, col0, M, N, r);
+        }
       }
     }
+    if (use_tma_store && lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -461,6 +605,23 @@ void set_wait_limit_ns(uint64_t ns) {
   cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
 }
 
+// Output-chunk tensor map: box 32 x 32, 128B swizzle for f32 rows of 128 B,
+// 64B swizzle for bf16 rows of 64 B.
+static bool make_out_tmap(CUtensorMap* map, void* base, bool f32, uint64_t cols, uint64_t rows,
+                          uint64_t ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const uint64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base,
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
@@ -478,6 +639,20 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     ok = make_tmap_bf16_2d(&tmB, g.B, g.K, g.N, g.ldb, kBK, BN);
   if (!ok) return cudaErrorInvalidValue;
 
+  // TMA-store epilogue when the output rows are 16-byte aligned
+  CUtensorMap tmOut, tmAux;
+  std::memset(&tmOut, 0, sizeof(tmOut));
+  std::memset(&tmAux, 0, sizeof(tmAux));
+  const bool f32 = g.ep.out_f32 != 0;
+  const uint64_t out_es = f32 ? 4 : 2;
+  bool use_tma = (reinterpret_cast<uintptr_t>(g.ep.out) % 16 == 0) &&
+                 ((uint64_t)g.ep.ld_out * out_es) % 16 == 0;
+  const bool aux_out = (g.ep.flags & kEpiGelu) && g.ep.aux;
+  if (aux_out)
+    use_tma = use_tma && !f32 && (reinterpret_cast<uintptr_t>(g.ep.aux) % 16 == 0) &&
+              ((uint64_t)g.ep.ld_aux * 2) % 16 == 0;
+  if (use_tma) use_tma = make_out_tmap(&tmOut, g.ep.out, f32, g.N, g.M, g.ep.ld_out);
+  if (use_tma && aux_out) use_tma = make_out_tmap(&tmAux, g.ep.aux, false, g.N, g.M, g.ep.ld_aux);
   auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -486,7 +661,8 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   }
   const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.k_splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, g.ep, g.M, g.N, g.K, g.k_splits,
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmOut, tmAux, g.ep, g.M, g.N, g.K,
+                                                     g.k_splits, use_tma ? 1 : 0,
                                                      g.err ? g.err : default_err_word());
   note_launch();
   return cudaGetLastError();

@@ -35,11 +35,18 @@ struct LnBwdArgs {
   float* dbeta = nullptr;   // accumulated
   float* colsum = nullptr;  // accumulated sum over rows of dx
   int rows = 0, C = 0;
+  float* partials = nullptr;  // scratch [3, partial_blocks, C] for the two-stage reduction
+  int partial_blocks = 0;
 };
 cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st);
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
                           const float* scale = nullptr);
+// Two-stage (deterministic) column sum; partials is scratch [nblocks, C].
+cudaError_t launch_colsum2(const void* m, bool bf16, float* out, int rows, int C, float* partials,
+                           int nblocks, cudaStream_t st, const float* scale = nullptr);
+int colsum_partial_blocks(int rows);
+int ln_bwd_partial_blocks(int rows);
 
 // ------------------------------------------------------------- cross entropy
 struct CeArgs {

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
     const float* __restrict__ gamma, const float* __restrict__ dres, float* __restrict__ dx_f32,
     __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dgamma, float* __restrict__ dbeta,
-    float* __restrict__ colsum, int rows, int C) {
+    float* __restrict__ colsum, int rows, int C, float* __restrict__ partials) {
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int warp_global = blockIdx.x * kWarps + wib;
@@ -187,9 +187,12 @@ __global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
       }
     }
   }
-  // Block reduction of the per-column partials, then one atomic per column.
+  // Block reduction of the per-column partials. With `partials`, each block
+  // writes its three C-wide partial rows there (slot k of block b at
+  // partials[(k * gridDim.x + b) * C]) for a deterministic second pass;
+  // otherwise one atomic per column.
   __shared__ float red[kWarps][128];
-  auto flush = [&](float (&acc)[NV][4], float* out) {
+  auto flush = [&](float (&acc)[NV][4], float* out, int k) {
     if (!out) return;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -201,14 +204,85 @@ __global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) s += red[w][threadIdx.x];
         const int c = threadIdx.x + 128 * j;
-        if (c < C) atomicAdd(out + c, s);
+        if (c < C) {
+          if (partials)
+            partials[((size_t)k * gridDim.x + blockIdx.x) * C + c] = s;
+          else
+            atomicAdd(out + c, s);
+        }
       }
       __syncthreads();
     }
   };
-  flush(acc_dg, dgamma);
-  flush(acc_db, dbeta);
-  flush(acc_cs, colsum);
+  flush(acc_dg, dgamma, 0);
+  flush(acc_db, dbeta, 1);
+  flush(acc_cs, colsum, 2);
+}
+
+// Second pass of the two-stage column reductions: out[c] += sum_b partials[b][c]
+// for up to three (partials, out) pairs laid out as [k][nblocks][C].
+__global__ void reduce_partials_kernel(const float* __restrict__ partials, int nblocks, int C,
+                                       float* out0, float* out1, float* out2,
+                                       const float* __restrict__ scale) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int k = blockIdx.y;
+  float* out = k == 0 ? out0 : (k == 1 ? out1 : out2);
+  if (c >= C || out == nullptr) return;
+  const float* p = partials + (size_t)k * nblocks * C + c;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += p[(size_t)b * C];
+  if (scale) s *= *scale;
+  out[c] += s;
+}
+
+// Column sums, first pass: block b sums rows [b*R, (b+1)*R) of a [rows, C]
+// matrix; thread owns 8 consecutive columns (16-byte loads), several row
+// lanes per block when C is narrow. Writes partials[b][c].
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict__ m,
+                                                             float* __restrict__ partials,
+                                                             int rows, int C, int rows_per_block) {
+  const int groups = C / 8;                       // 8-column groups per row
+  const int tpr = groups < 256 ? groups : 256;    // threads per row slice
+  const int lanes = 256 / tpr;                    // row slices per block
+  const int g0 = blockIdx.y * 256;                // column-group offset of this block
+  const int tid = threadIdx.x;
+  const int gi = g0 + (tid % tpr);
+  const int slice = tid / tpr;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  if (slice < lanes && gi < groups) {
+    for (int r = r0 + slice; r < r1; r += lanes) {
+      const T* src = m + (size_t)r * C + gi * 8;
+      float v[8];
+      if constexpr (sizeof(T) == 2) {
+        uint4 u = *reinterpret_cast<const uint4*>(src);
+        float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c2 = unpack_bf16x2(u.z),
+               d = unpack_bf16x2(u.w);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c2.x; v[5] = c2.y; v[6] = d.x; v[7] = d.y;
+      } else {
+        float4 a = *reinterpret_cast<const float4*>(src);
+        float4 b = *reinterpret_cast<const float4*>(src + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += v[e];
+    }
+  }
+  __shared__ float red[256][9];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[tid][e] = acc[e];
+  __syncthreads();
+  if (slice == 0 && gi < groups) {
+    for (int l = 1; l < lanes; ++l)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += red[tid + l * tpr][e];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) partials[(size_t)blockIdx.x * C + gi * 8 + e] = acc[e];
+  }
 }
 
 // Column sums of a [rows, C] matrix into f32 out[C] (accumulating).
@@ -263,17 +337,47 @@ cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st) {
 
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
   if (a.C % 4 != 0) return cudaErrorInvalidValue;
-  const int grid = grid_for_rows(a.rows);
+  const int grid = a.partials ? a.partial_blocks : grid_for_rows(a.rows);
   if (a.x_bf16) {
     FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
                                a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma, a.dres,
-                               a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C)));
+                               a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C,
+                               a.partials)));
   } else {
     FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
                                a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres, a.dx_f32,
-                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C)));
+                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials)));
   }
   note_launch();
+  if (a.partials) {
+    dim3 rg((a.C + 127) / 128, 3);
+    reduce_partials_kernel<<<rg, 128, 0, st>>>(a.partials, grid, a.C, a.dgamma, a.dbeta, a.colsum,
+                                               nullptr);
+    note_launch();
+  }
+  return cudaGetLastError();
+}
+
+int ln_bwd_partial_blocks(int rows) { return grid_for_rows(rows) < num_sms() * 4 ? grid_for_rows(rows) : num_sms() * 4; }
+
+int colsum_partial_blocks(int rows) {
+  int b = num_sms() * 2;
+  return rows < b ? (rows > 0 ? rows : 1) : b;
+}
+
+cudaError_t launch_colsum2(const void* m, bool bf16, float* out, int rows, int C, float* partials,
+                           int nblocks, cudaStream_t st, const float* scale) {
+  if (C % 8 != 0) return launch_colsum(m, bf16, out, rows, C, st, scale);
+  const int rpb = (rows + nblocks - 1) / nblocks;
+  dim3 g1(nblocks, (C / 8 + 255) / 256);
+  if (bf16)
+    colsum_partial_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>((const __nv_bfloat16*)m, partials, rows,
+                                                             C, rpb);
+  else
+    colsum_partial_kernel<float><<<g1, 256, 0, st>>>((const float*)m, partials, rows, C, rpb);
+  dim3 g2((C + 127) / 128, 1);
+  reduce_partials_kernel<<<g2, 128, 0, st>>>(partials, nblocks, C, out, nullptr, nullptr, scale);
+  note_launch(2);
   return cudaGetLastError();
 }
 

@@ -6,4 +6,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   flodl::rt::register_checkpoint(m);
   flodl::rt::register_hash(m);
   flodl::rt::register_graph(m);
+  flodl::rt::register_elche(m);
+  flodl::rt::register_wire(m);
 }

@@ -209,8 +209,14 @@ class DataLoader:
     def len(self):
         return self.n
 
+    def _epoch_len(self) -> int:
+        if self.sampler_ is not None:
+            return len(self.sampler_.indices(0, self.n))
+        return self.n
+
     def num_batches(self) -> int:
-        return self.n // self.bs if self.drop_last_ else math.ceil(self.n / self.bs)
+        n = self._epoch_len()
+        return n // self.bs if self.drop_last_ else math.ceil(n / self.bs)
 
     def batch_size(self) -> int:
         return self.bs
@@ -241,7 +247,8 @@ class DataLoader:
 
     def epoch(self, epoch: int) -> Iterator[_Batch]:
         order = self._order(epoch)
-        nb = self.num_batches()
+        n = order.numel()
+        nb = n // self.bs if self.drop_last_ else math.ceil(n / self.bs)
         if self.resident:
             dev_order = order.to(self._tensors[0].device)
             for i in range(nb):

@@ -1,0 +1,205 @@
+"""Training monitor (flodl/src/monitor/mod.rs:215-1030, timeline.rs, record.rs).
+
+* ``Monitor``: per-epoch log line with ETA, metric history, resource sampling
+  (CPU/RAM from /proc, GPU utilisation/memory through NVML when present),
+  ``export_csv``, ``save_html`` (a self-contained HTML report) and a JSONL
+  record log.
+* ``Timeline``: a background sampler of resource use plus discrete events
+  (syncs, anchor changes, epoch starts), saved as JSON/CSV.
+* ``serve(port)``: a minimal live dashboard over HTTP with Server-Sent Events
+  (``/stream``) and late-join backfill (``/history``).
+"""
+from __future__ import annotations
+
+import csv
+import http.server
+import json
+import os
+import queue
+import socketserver
+import threading
+import time
+from typing import Dict, List, Optional
+
+
+def _cpu_ram():
+    try:
+        with open("/proc/meminfo") as f:
+            info = {ln.split(":")[0]: int(ln.split()[1]) for ln in f if ":" in ln}
+        used = (info.get("MemTotal", 0) - info.get("MemAvailable", 0)) / 1024
+        return {"ram_used_mb": used, "ram_total_mb": info.get("MemTotal", 0) / 1024}
+    except OSError:
+        return {}
+
+
+def _gpu_stats():
+    try:
+        import pynvml  # nvidia-ml-py
+
+        pynvml.nvmlInit()
+        out = []
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            u = pynvml.nvmlDeviceGetUtilizationRates(h)
+            m = pynvml.nvmlDeviceGetMemoryInfo(h)
+            out.append({"gpu": i, "util": u.gpu, "mem_used_mb": m.used / 2 ** 20,
+                        "mem_total_mb": m.total / 2 ** 20})
+        return out
+    except Exception:
+        return []
+
+
+class Monitor:
+    def __init__(self, total_epochs: int, record_path: Optional[str] = None, quiet: bool = False):
+        self.total = total_epochs
+        self.start = time.time()
+        self.history: List[Dict] = []
+        self.record_path = record_path
+        self.quiet = quiet
+        self._subscribers: List[queue.Queue] = []
+        self._server = None
+
+    def log(self, epoch: int, metrics: Dict[str, float], elapsed: Optional[float] = None) -> str:
+        now = time.time()
+        done = epoch + 1
+        rate = (now - self.start) / done
+        eta = rate * max(self.total - done, 0)
+        rec = {"epoch": epoch, "time": now, "elapsed": now - self.start, "eta_s": eta, **metrics,
+               **_cpu_ram()}
+        self.history.append(rec)
+        if self.record_path:
+            with open(self.record_path, "a") as f:
+                f.write(json.dumps(rec) + "\n")
+        for q in list(self._subscribers):
+            try:
+                q.put_nowait(rec)
+            except queue.Full:
+                pass
+        parts = " ".join(f"{k}={v:.4g}" if isinstance(v, float) else f"{k}={v}" for k, v in metrics.items())
+        line = f"epoch {done}/{self.total} {parts} eta {eta:.0f}s"
+        if not self.quiet:
+            print(line, flush=True)
+        return line
+
+    def export_csv(self, path: str) -> None:
+        if not self.history:
+            return
+        keys = sorted({k for r in self.history for k in r})
+        with open(path, "w", newline="") as f:
+            w = csv.DictWriter(f, fieldnames=keys)
+            w.writeheader()
+            w.writerows(self.history)
+
+    def save_html(self, path: str, title: str = "flodl_b200 training") -> None:
+        data = json.dumps(self.history)
+        html = f"""<!doctype html><html><head><meta charset="utf-8"><title>{title}</title></head>
+<body><h2>{title}</h2><div id="plots"></div><pre id="raw"></pre><script>
+const H = {data};
+const keys = [...new Set(H.flatMap(r => Object.keys(r)))].filter(k => !['epoch','time'].includes(k));
+const svgNS = 'http://www.w3.org/2000/svg';
+for (const k of keys) {{
+  const ys = H.map(r => r[k]).filter(v => typeof v === 'number'); if (!ys.length) continue;
+  const mn = Math.min(...ys), mx = Math.max(...ys) || 1, W = 480, Hh = 120;
+  const svg = document.createElementNS(svgNS, 'svg'); svg.setAttribute('width', W); svg.setAttribute('height', Hh + 20);
+  const pts = ys.map((y, i) => `${{(i / Math.max(ys.length - 1, 1)) * W}},${{Hh - (y - mn) / ((mx - mn) || 1) * Hh}}`).join(' ');
+  const pl = document.createElementNS(svgNS, 'polyline'); pl.setAttribute('points', pts);
+  pl.setAttribute('fill', 'none'); pl.setAttribute('stroke', 'steelblue'); svg.appendChild(pl);
+  const t = document.createElementNS(svgNS, 'text'); t.setAttribute('y', Hh + 15); t.textContent = k; svg.appendChild(t);
+  document.getElementById('plots').appendChild(svg);
+}}
+</script></body></html>"""
+        with open(path, "w") as f:
+            f.write(html)
+
+    # ------------------------------------------------------------ live dashboard (SSE)
+    def serve(self, port: int = 0) -> int:
+        mon = self
+
+        class H(http.server.BaseHTTPRequestHandler):
+            def log_message(self, *a):
+                pass
+
+            def do_GET(self):
+                if self.path.startswith("/history"):
+                    body = json.dumps(mon.history).encode()
+                    self.send_response(200)
+                    self.send_header("Content-Type", "application/json")
+                    self.send_header("Content-Length", str(len(body)))
+                    self.end_headers()
+                    self.wfile.write(body)
+                elif self.path.startswith("/stream"):
+                    q: queue.Queue = queue.Queue(maxsize=1024)
+                    mon._subscribers.append(q)
+                    self.send_response(200)
+                    self.send_header("Content-Type", "text/event-stream")
+                    self.end_headers()
+                    try:
+                        for rec in list(mon.history):  # late-join backfill
+                            self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
+                        self.wfile.flush()
+                        while True:
+                            rec = q.get(timeout=30)
+                            self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
+                            self.wfile.flush()
+                    except Exception:
+                        pass
+                    finally:
+                        mon._subscribers.remove(q)
+                else:
+                    body = b"<html><body>flodl_b200 monitor: /history /stream</body></html>"
+                    self.send_response(200)
+                    self.send_header("Content-Type", "text/html")
+                    self.end_headers()
+                    self.wfile.write(body)
+
+        class S(socketserver.ThreadingMixIn, http.server.HTTPServer):
+            daemon_threads = True
+
+        srv = S(("127.0.0.1", port), H)
+        self._server = srv
+        threading.Thread(target=srv.serve_forever, daemon=True).start()
+        return srv.server_address[1]
+
+    def close(self) -> None:
+        if self._server is not None:
+            self._server.shutdown()
+            self._server = None
+
+
+class Timeline:
+    """Background resource sampler with discrete events."""
+
+    def __init__(self, interval_s: float = 0.1):
+        self.interval = interval_s
+        self.samples: List[Dict] = []
+        self.events: List[Dict] = []
+        self._stop = threading.Event()
+        self._t: Optional[threading.Thread] = None
+
+    def start(self):
+        def run():
+            while not self._stop.is_set():
+                self.samples.append({"t": time.time(), **_cpu_ram(), "gpus": _gpu_stats()})
+                self._stop.wait(self.interval)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def event(self, kind: str, **fields) -> None:
+        self.events.append({"t": time.time(), "kind": kind, **fields})
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._t is not None:
+            self._t.join(timeout=2)
+
+    def save_json(self, path: str) -> None:
+        with open(path, "w") as f:
+            json.dump({"samples": self.samples, "events": self.events}, f)
+
+    def save_csv(self, path: str) -> None:
+        with open(path, "w", newline="") as f:
+            w = csv.writer(f)
+            w.writerow(["t", "kind", "detail"])
+            for e in self.events:
+                w.writerow([e["t"], e["kind"], json.dumps({k: v for k, v in e.items() if k not in ("t", "kind")})])

@@ -1,0 +1,3 @@
+"""Utilities: logging, hardware detection, flat parameter arenas, RNG."""
+from . import hw, log  # noqa: F401
+from .arena import ParamArena, arena_of  # noqa: F401
