@@ -39,7 +39,7 @@ void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor&
             const optional<Tensor>& gamma, const optional<Tensor>& dres,
             const optional<Tensor>& dx_f32, const optional<Tensor>& dx_bf16,
             const optional<Tensor>& dgamma, const optional<Tensor>& dbeta,
-            const optional<Tensor>& colsum) {
+            const optional<Tensor>& colsum, bool pre_add) {
   FL_CHECK_CUDA(dy);
   FL_CHECK_BF16(dy);
   FL_CHECK(dy.is_contiguous() && x.is_contiguous(), "ln_bwd inputs must be contiguous");
@@ -57,6 +57,7 @@ void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor&
   a.dgamma = opt_ptr<float>(dgamma);
   a.dbeta = opt_ptr<float>(dbeta);
   a.colsum = opt_ptr<float>(colsum);
+  a.pre_add = pre_add;
   a.rows = (int)(x.numel() / C);
   a.C = C;
   c10::cuda::CUDAGuard guard(x.device());
@@ -235,7 +236,7 @@ void register_norm(py::module& m) {
         py::arg("y_f32"), py::arg("mean"), py::arg("rstd"), py::arg("eps"));
   m.def("ln_bwd", &ln_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
         py::arg("gamma"), py::arg("dres"), py::arg("dx_f32"), py::arg("dx_bf16"),
-        py::arg("dgamma"), py::arg("dbeta"), py::arg("colsum"));
+        py::arg("dgamma"), py::arg("dbeta"), py::arg("colsum"), py::arg("pre_add") = false);
   m.def("colsum", &colsum, py::arg("m"), py::arg("out"), py::arg("scale") = py::none());
 }
 

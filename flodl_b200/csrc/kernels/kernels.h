@@ -37,6 +37,7 @@ struct LnBwdArgs {
   int rows = 0, C = 0;
   float* partials = nullptr;  // scratch [3, partial_blocks, C] for the two-stage reduction
   int partial_blocks = 0;
+  bool pre_add = false;  // true: normalise the gradient (dy + dres); false: dx += dres afterwards
 };
 cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st);
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);

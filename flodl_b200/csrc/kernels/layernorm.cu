@@ -118,51 +118,63 @@ __global__ void __launch_bounds__(kWarps * 32) ln_fwd_kernel(
 }
 
 template <typename TIn, int NV>
-__global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
+__global__ void __launch_bounds__(kWarps * 32, 2) ln_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const TIn* __restrict__ x,
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
     const float* __restrict__ gamma, const float* __restrict__ dres, float* __restrict__ dx_f32,
     __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dgamma, float* __restrict__ dbeta,
-    float* __restrict__ colsum, int rows, int C, float* __restrict__ partials) {
+    float* __restrict__ colsum, int rows, int C, float* __restrict__ partials, int pre_add) {
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int warp_global = blockIdx.x * kWarps + wib;
   const int nwarps = gridDim.x * kWarps;
-  float g[NV][4];
   float acc_dg[NV][4], acc_db[NV][4], acc_cs[NV][4];
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = lane * 4 + 128 * j;
+  for (int j = 0; j < NV; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      g[j][e] = (c + e < C) ? (gamma ? gamma[c + e] : 1.f) : 0.f;
-      acc_dg[j][e] = acc_db[j][e] = acc_cs[j][e] = 0.f;
-    }
-  }
+    for (int e = 0; e < 4; ++e) acc_dg[j][e] = acc_db[j][e] = acc_cs[j][e] = 0.f;
   for (int r = warp_global; r < rows; r += nwarps) {
+    // issue every load of the row up front (x, dy, skip-path gradient)
+    float xh[NV][4], dyv[NV][4], rv[NV][4];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = lane * 4 + 128 * j;
+      if (c < C) {
+        load4<TIn>(x + (size_t)r * C + c, xh[j]);
+        load4<__nv_bfloat16>(dy + (size_t)r * C + c, dyv[j]);
+        if (dres) load4<float>(dres + (size_t)r * C + c, rv[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
+      }
+    }
+    if (pre_add && dres) {
+      // post-LN blocks: the LayerNorm's output gradient is dy + dres
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dyv[j][e] += rv[j][e];
+    }
     const float mean = mean_in[r];
     const float rstd = rstd_in[r];
-    float xh[NV][4], dyv[NV][4];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = lane * 4 + 128 * j;
       if (c < C) {
-        float xv[4];
-        load4<TIn>(x + (size_t)r * C + c, xv);
-        load4<__nv_bfloat16>(dy + (size_t)r * C + c, dyv[j]);
+        const float4 g4 = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
+                                : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          xh[j][e] = (xv[e] - mean) * rstd;
-          const float gg = dyv[j][e] * g[j][e];
+          xh[j][e] = (xh[j][e] - mean) * rstd;
+          const float gg = dyv[j][e] * gv[e];
           s1 += gg;
           s2 += gg * xh[j][e];
           acc_dg[j][e] += dyv[j][e] * xh[j][e];
           acc_db[j][e] += dyv[j][e];
+          dyv[j][e] = gg;  // keep dy * gamma
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
       }
     }
     const float m1 = warp_sum(s1) / C;
@@ -173,15 +185,11 @@ __global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
       if (c < C) {
         float o[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = rstd * (dyv[j][e] * g[j][e] - m1 - xh[j][e] * m2);
-        if (dres) {
-          float rv[4];
-          load4<float>(dres + (size_t)r * C + c, rv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) o[e] += rv[e];
+        for (int e = 0; e < 4; ++e) {
+          o[e] = rstd * (dyv[j][e] - m1 - xh[j][e] * m2);
+          if (dres && !pre_add) o[e] += rv[j][e];
+          acc_cs[j][e] += o[e];
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc_cs[j][e] += o[e];
         if (dx_f32) store4_f32(dx_f32 + (size_t)r * C + c, o);
         if (dx_bf16) store4_bf16(dx_bf16 + (size_t)r * C + c, o);
       }
@@ -220,19 +228,38 @@ __global__ void __launch_bounds__(kWarps * 32) ln_bwd_kernel(
 }
 
 // Second pass of the two-stage column reductions: out[c] += sum_b partials[b][c]
-// for up to three (partials, out) pairs laid out as [k][nblocks][C].
-__global__ void reduce_partials_kernel(const float* __restrict__ partials, int nblocks, int C,
-                                       float* out0, float* out1, float* out2,
-                                       const float* __restrict__ scale) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// for up to three (partials, out) pairs laid out as [k][nblocks][C]. Block =
+// 32 columns x 8 partial lanes; each thread keeps four independent sums.
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partials,
+                                                              int nblocks, int C, float* out0,
+                                                              float* out1, float* out2,
+                                                              const float* __restrict__ scale) {
+  const int c = blockIdx.x * 32 + threadIdx.x;
   const int k = blockIdx.y;
   float* out = k == 0 ? out0 : (k == 1 ? out1 : out2);
-  if (c >= C || out == nullptr) return;
-  const float* p = partials + (size_t)k * nblocks * C + c;
-  float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += p[(size_t)b * C];
-  if (scale) s *= *scale;
-  out[c] += s;
+  if (out == nullptr) return;  // uniform across the block
+  const float* p = partials + (size_t)k * nblocks * C;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (c < C) {
+    int b = threadIdx.y;
+    for (; b + 24 < nblocks; b += 32) {
+      s0 += p[(size_t)b * C + c];
+      s1 += p[(size_t)(b + 8) * C + c];
+      s2 += p[(size_t)(b + 16) * C + c];
+      s3 += p[(size_t)(b + 24) * C + c];
+    }
+    for (; b < nblocks; b += 8) s0 += p[(size_t)b * C + c];
+  }
+  __shared__ float red[8][33];
+  red[threadIdx.y][threadIdx.x] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (threadIdx.y == 0 && c < C) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    if (scale) t *= *scale;
+    out[c] += t;
+  }
 }
 
 // Column sums, first pass: block b sums rows [b*R, (b+1)*R) of a [rows, C]
@@ -255,6 +282,7 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   if (slice < lanes && gi < groups) {
+#pragma unroll 4
     for (int r = r0 + slice; r < r1; r += lanes) {
       const T* src = m + (size_t)r * C + gi * 8;
       float v[8];
@@ -342,17 +370,18 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
     FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
                                a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma, a.dres,
                                a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C,
-                               a.partials)));
+                               a.partials, a.pre_add ? 1 : 0)));
   } else {
     FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
                                a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres, a.dx_f32,
-                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials)));
+                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials,
+                               a.pre_add ? 1 : 0)));
   }
   note_launch();
   if (a.partials) {
-    dim3 rg((a.C + 127) / 128, 3);
-    reduce_partials_kernel<<<rg, 128, 0, st>>>(a.partials, grid, a.C, a.dgamma, a.dbeta, a.colsum,
-                                               nullptr);
+    dim3 rg((a.C + 31) / 32, 3);
+    reduce_partials_kernel<<<rg, dim3(32, 8), 0, st>>>(a.partials, grid, a.C, a.dgamma, a.dbeta,
+                                                       a.colsum, nullptr);
     note_launch();
   }
   return cudaGetLastError();
@@ -375,8 +404,9 @@ cudaError_t launch_colsum2(const void* m, bool bf16, float* out, int rows, int C
                                                              C, rpb);
   else
     colsum_partial_kernel<float><<<g1, 256, 0, st>>>((const float*)m, partials, rows, C, rpb);
-  dim3 g2((C + 127) / 128, 1);
-  reduce_partials_kernel<<<g2, 128, 0, st>>>(partials, nblocks, C, out, nullptr, nullptr, scale);
+  dim3 g2((C + 31) / 32, 1);
+  reduce_partials_kernel<<<g2, dim3(32, 8), 0, st>>>(partials, nblocks, C, out, nullptr, nullptr,
+                                                     scale);
   note_launch(2);
   return cudaGetLastError();
 }

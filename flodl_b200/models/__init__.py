@@ -1,2 +1,4 @@
 """Model zoo: the benchmark models of the reference's configs."""
+from .bert import (BertConfig, BertForMaskedLM, BertForQuestionAnswering,  # noqa: F401
+                   BertForSequenceClassification, BertForTokenClassification, BertModel)
 from .transformer_lm import DecoderBlock, TransformerLM  # noqa: F401

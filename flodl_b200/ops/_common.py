@@ -15,16 +15,12 @@
 """
 from __future__ import annotations
 
-import weakref
 from typing import Callable, List
 
 import torch
 
 from .._ext import cuda_ext
 
-_GRAD_READY_LISTENERS: "weakref.WeakKeyDictionary[torch.Tensor, List[Callable]]" = (
-    weakref.WeakKeyDictionary()
-)
 
 
 def use_kernels(t: torch.Tensor) -> bool:
@@ -80,16 +76,21 @@ def grad_buffer(p: torch.Tensor) -> torch.Tensor:
 
 
 def add_grad_ready_listener(p: torch.Tensor, fn: Callable[[torch.Tensor], None]) -> None:
-    _GRAD_READY_LISTENERS.setdefault(p, []).append(fn)
+    # stored on the parameter itself (tensors cannot be dict keys: == is elementwise)
+    ls = getattr(p, "_flodl_grad_listeners", None)
+    if ls is None:
+        ls = []
+        p._flodl_grad_listeners = ls
+    ls.append(fn)
 
 
 def clear_grad_ready_listeners(p: torch.Tensor) -> None:
-    _GRAD_READY_LISTENERS.pop(p, None)
+    p._flodl_grad_listeners = []
 
 
 def grad_ready(p: torch.Tensor) -> None:
     """Called after a fused backward finished accumulating ``p.grad``."""
-    for fn in _GRAD_READY_LISTENERS.get(p, ()):
+    for fn in getattr(p, "_flodl_grad_listeners", ()):
         fn(p)
 
 
