@@ -121,6 +121,8 @@ def reference_arm(args):
 
 
 def main():
+    from flodl_b200.utils.crash import install_crash_handler
+    install_crash_handler()
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
@@ -247,8 +249,20 @@ def main():
             "gpu_launches": (per_step_launches * args.steps) if per_step_launches is not None else None,
         }
         print(json.dumps(out), flush=True)
-    if graph is not None:
-        del graph
+    # every reference to a CUDA graph that holds NCCL work must be gone before
+    # the process group is destroyed, or the exit waits on it forever
+    runner = None
+    run = None
+    static_loss = None
+    graph = None
+    ddp = state.get("ddp") if isinstance(state, dict) else None
+    state = None
+    step = None
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    if ddp is not None and hasattr(ddp, "close"):
+        ddp.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

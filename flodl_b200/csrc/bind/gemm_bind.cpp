@@ -70,7 +70,13 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t M, 
   g.ep.alpha = (float)alpha;
   if (alpha_t) { FL_CHECK_F32(*alpha_t); FL_CHECK_CUDA(*alpha_t); }
   g.ep.alpha_ptr = opt_ptr<const float>(alpha_t);
-  FL_CUDA_OK(flodl::launch_gemm(g, cur_stream()));
+  cudaStream_t st = cur_stream();
+  cudaError_t e = flodl::launch_gemm(g, st);
+  FL_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e), " ",
+           flodl::gemm_failure_detail(), " [M=", M, " N=", N, " K=", K, " a_mn=", a_mn,
+           " b_mn=", b_mn, " splits=", k_splits, "]",
+           stale_cuda_error() ? " (an earlier call in this thread had left: " : "",
+           stale_cuda_error() ? stale_cuda_error() : "", stale_cuda_error() ? ")" : "");
 }
 
 }  // namespace

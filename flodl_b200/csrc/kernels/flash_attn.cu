@@ -55,7 +55,24 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// cuTensorMapEncodeTiled is a driver call and needs a context current on the
+// calling thread. A runtime-API thread gets one lazily on its first runtime
+// call that needs it, so a fresh thread (e.g. an autograd device thread whose
+// first CUDA work is this launch) may have none yet: CUDA_ERROR_INVALID_CONTEXT.
+// cudaSetDevice makes the device's primary context current; done once per
+// thread and device.
+static void bind_current_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (bound != dev) {
+    cudaSetDevice(dev);
+    bound = dev;
+  }
+}
+
 EncodeTiledFn encode_fn() {
+  bind_current_context();
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {

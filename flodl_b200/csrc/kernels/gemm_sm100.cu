@@ -529,7 +529,24 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// cuTensorMapEncodeTiled is a driver call and needs a context current on the
+// calling thread. A runtime-API thread gets one lazily on its first runtime
+// call that needs it, so a fresh thread (e.g. an autograd device thread whose
+// first CUDA work is this launch) may have none yet: CUDA_ERROR_INVALID_CONTEXT.
+// cudaSetDevice makes the device's primary context current; done once per
+// thread and device.
+static void bind_current_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (bound != dev) {
+    cudaSetDevice(dev);
+    bound = dev;
+  }
+}
+
 EncodeTiledFn get_encode_fn() {
+  bind_current_context();
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -547,10 +564,16 @@ EncodeTiledFn get_encode_fn() {
 
 // 2D bf16 tensor map: inner dimension `inner` (contiguous), `outer` rows with
 // row pitch `ld` elements; box = box_inner x box_outer, 128-byte swizzle.
+static thread_local char g_tmap_fail[192];
+const char* tmap_failure_detail() { return g_tmap_fail; }
+
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint64_t ld, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return false;
+  if (!enc) {
+    snprintf(g_tmap_fail, sizeof(g_tmap_fail), "cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {box_inner, box_outer};
@@ -558,6 +581,11 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint6
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    snprintf(g_tmap_fail, sizeof(g_tmap_fail),
+             "CUresult %d base=%p inner=%llu outer=%llu ld=%llu box=%ux%u", (int)r, base,
+             (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld,
+             box_inner, box_outer);
   return r == CUDA_SUCCESS;
 }
 
@@ -622,6 +650,9 @@ static bool make_out_tmap(CUtensorMap* map, void* base, bool f32, uint64_t cols,
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static thread_local const char* g_gemm_fail = nullptr;
+const char* gemm_failure_detail() { return g_gemm_fail ? g_gemm_fail : ""; }
+
 template <int BN, bool A_MN, bool B_MN>
 static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
@@ -632,12 +663,18 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     ok = make_tmap_bf16_2d(&tmA, g.A, g.M, g.K, g.lda, 64, kBK);
   else
     ok = make_tmap_bf16_2d(&tmA, g.A, g.K, g.M, g.lda, kBK, kBM);
-  if (!ok) return cudaErrorInvalidValue;
+  if (!ok) {
+    g_gemm_fail = tmap_failure_detail();
+    return cudaErrorInvalidValue;
+  }
   if (B_MN)
     ok = make_tmap_bf16_2d(&tmB, g.B, g.N, g.K, g.ldb, 64, kBK);
   else
     ok = make_tmap_bf16_2d(&tmB, g.B, g.K, g.N, g.ldb, kBK, BN);
-  if (!ok) return cudaErrorInvalidValue;
+  if (!ok) {
+    g_gemm_fail = tmap_failure_detail();
+    return cudaErrorInvalidValue;
+  }
 
   // TMA-store epilogue when the output rows are 16-byte aligned
   CUtensorMap tmOut, tmAux;
@@ -669,7 +706,11 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
-  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.k_splits < 1) return cudaErrorInvalidValue;
+  g_gemm_fail = nullptr;
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.k_splits < 1) {
+    g_gemm_fail = "empty problem or bad split";
+    return cudaErrorInvalidValue;
+  }
   const bool wide = g.N >= 256 && g.bn != 128;
 #define FL_GEMM_CASE(AMN, BMN)                                                   \
   if (g.a_mn == AMN && g.b_mn == BMN)                                           \

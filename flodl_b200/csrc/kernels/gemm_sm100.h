@@ -39,6 +39,10 @@ struct GemmArgs {
   uint32_t* err = nullptr;  // device error word (nullable)
 };
 
+// Which host-side step rejected the last launch_gemm call of this thread ("" if none).
+const char* gemm_failure_detail();
+// Why the last make_tmap_bf16_2d call of this thread failed.
+const char* tmap_failure_detail();
 cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream);
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint64_t ld, uint32_t box_inner, uint32_t box_outer);

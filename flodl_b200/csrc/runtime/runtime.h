@@ -38,6 +38,8 @@ void register_elche(py::module& m);
 void register_reduce(py::module& m);
 void register_loader(py::module& m);
 void register_wire(py::module& m);
+void register_crash(py::module& m);
+void install_crash_handler();
 
 }  // namespace rt
 }  // namespace flodl

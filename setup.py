@@ -31,6 +31,33 @@ NVCC_FLAGS = [
 CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG", "-g0"]
 
 
+def _shared_libstdcxx_dir():
+    """Directory holding the SHARED libstdc++ link library.
+
+    A toolchain whose private library directory only carries ``libstdc++.a``
+    links a second, static copy of libstdc++ into each extension; that copy's
+    iostream/locale state is never initialised, so formatting a number in an
+    error message (``TORCH_CHECK(..., n)``) crashes. Putting the system
+    directory first makes both extensions use the process-wide libstdc++.so.6
+    that torch already loaded.
+    """
+    import subprocess
+
+    for cxx in ("/usr/bin/g++", "g++", "c++"):
+        try:
+            out = subprocess.run([cxx, "-print-file-name=libstdc++.so"], capture_output=True,
+                                 text=True, timeout=30).stdout.strip()
+        except Exception:
+            continue
+        if os.path.isabs(out) and os.path.exists(out):
+            return [os.path.dirname(out)]
+    return []
+
+
+LINK_DIRS = _shared_libstdcxx_dir()
+LINK_FLAGS = [f"-L{d}" for d in LINK_DIRS]
+
+
 def _sources(*patterns):
     out = []
     for p in patterns:
@@ -44,6 +71,7 @@ ext_modules = [
         sources=_sources("bind/*.cpp", "kernels/*.cu", "comm/*.cu"),
         include_dirs=[os.path.join(ROOT, CSRC)],
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+        extra_link_args=LINK_FLAGS,
     ),
     CppExtension(
         name="flodl_b200._native",
@@ -51,6 +79,7 @@ ext_modules = [
         include_dirs=[os.path.join(ROOT, CSRC)],
         extra_compile_args={"cxx": CXX_FLAGS},
         libraries=["z"],
+        extra_link_args=LINK_FLAGS,
     ),
 ]
 

@@ -27,8 +27,32 @@ def _need_gpus(n=2):
         pytest.skip(f"needs {n} GPUs (have {torch.cuda.device_count()})")
 
 
+def _collect(q, procs, world, timeout=240.0):
+    """Results from every worker; fails fast if a worker died without one."""
+    import queue
+    import time
+
+    out = []
+    deadline = time.monotonic() + timeout
+    while len(out) < world:
+        try:
+            out.append(q.get(timeout=2.0))
+            continue
+        except queue.Empty:
+            pass
+        dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+        if dead:
+            raise AssertionError(f"worker exited with code(s) {dead} before reporting")
+        if time.monotonic() > deadline:
+            raise AssertionError("workers did not report in time")
+    return out
+
+
 def _init(rank, world, port):
     import datetime
+    from flodl_b200.utils.crash import install_crash_handler
+
+    install_crash_handler()
 
     import torch.distributed as dist
 
@@ -86,7 +110,7 @@ def test_peer_collectives():
     procs = [ctx.Process(target=_collectives_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=180) for _ in range(world)]
+    res = _collect(q, procs, world)
     for p in procs:
         p.join(timeout=60)
     for rank, a, b, c, err in res:
@@ -124,7 +148,7 @@ def _fused_ddp_worker(rank, world, port, q):
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         same = all(torch.equal(gathered[0], t) for t in gathered[1:])
-        q.put((rank, same, flat.cpu(), None))
+        q.put((rank, same, flat.cpu().numpy(), None))
         ddp.close()
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover
@@ -140,7 +164,7 @@ def test_fused_ddp_matches_single_gpu_full_batch():
     procs = [ctx.Process(target=_fused_ddp_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda t: t[0])
+    res = sorted(_collect(q, procs, world), key=lambda t: t[0])
     for p in procs:
         p.join(timeout=60)
     for rank, same, _, err in res:
@@ -164,5 +188,5 @@ def test_fused_ddp_matches_single_gpu_full_batch():
         opt.step()
         opt.zero_grad()
     ref = opt.groups[0].arena.data.cpu()
-    got = res[0][2]
+    got = torch.from_numpy(res[0][2])
     torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=2e-3)
