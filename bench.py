@@ -7,6 +7,10 @@ seq 256, batch 64 per GPU, bf16 compute / f32 master weights, AdamW lr 3e-4
 wd 0.1. Weak scaling: global batch = 64 x N.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flodl|reference|torch]
+                    [--model lm|bert]
+
+``--model bert`` runs BASELINE config 4 instead (BERT-base MLM, seq 512,
+batch 32 per GPU, 15% of positions masked, AdamW).
 
 N > 1 runs under torchrun (one rank per GPU, NCCL bootstrap). The timed region
 is exactly K steps bracketed by barrier + synchronize, timed with CUDA events
@@ -39,8 +43,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "DDP samples/s & tok/s, 1/2/4/8 B200, max-over-ranks vs ref NCCL build"
-MODEL_DESC = "transformer-lm 6L d512 h8 ff2048 vocab256 pre-LN GELU"
-B_PER_GPU, SEQ, VOCAB = 64, 256, 256
 
 
 def parse():
@@ -52,6 +54,8 @@ def parse():
     ap.add_argument("--engine", default="auto", choices=["auto", "nccl", "peer"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--model", default="lm", choices=["lm", "bert"],
+                    help="lm = BASELINE config 3 (the headline); bert = config 4")
     return ap.parse_args()
 
 
@@ -139,21 +143,21 @@ def main():
     torch.manual_seed(1234)
     torch.backends.cuda.matmul.allow_tf32 = False
 
+    from flodl_b200.bench_support import MODELS
+    spec = MODELS[args.model]
+    B_PER_GPU, SEQ = spec.batch, spec.seq
     if args.impl == "torch":
-        from flodl_b200.bench_support import torch_arm_step
-        step, state = torch_arm_step(dev, world, B_PER_GPU, SEQ, VOCAB)
+        step, state = spec.torch(dev, world)
         engine = "nccl(torch DDP)"
         launches_fn = None
     else:
-        from flodl_b200.bench_support import flodl_arm_step
         engine = args.engine
         if engine == "auto":
             engine = "peer" if world > 1 else "none"
-        step, state = flodl_arm_step(dev, world, B_PER_GPU, SEQ, VOCAB, engine)
+        step, state = spec.flodl(dev, world, engine)
         from flodl_b200._ext import cuda_ext
         launches_fn = cuda_ext().launch_count
 
-    ids, tgt = state["ids"], state["tgt"]
     # warm-up (eager, on a side stream so every buffer the step creates - arenas,
     # gradients, workspaces - belongs to a non-legacy stream before capture)
     side = torch.cuda.Stream()
@@ -208,18 +212,16 @@ def main():
     e2e = None
     if args.impl == "flodl":
         from flodl_b200.train import StepRunner
-        runner = StepRunner.for_state(state, graph_step=(graph, static_loss) if graph else None,
-                                      eager_step=step)
-        ids_host = torch.randint(0, VOCAB, (B_PER_GPU, SEQ), dtype=torch.int64).pin_memory()
-        tgt_host = torch.randint(0, VOCAB, (B_PER_GPU, SEQ), dtype=torch.int64).pin_memory()
+        runner = StepRunner(step, state["inputs"], graph, static_loss if graph else None)
+        host_in = state["host_inputs"]()
         n_e2e = args.e2e_steps or args.steps
-        runner.step(ids_host, tgt_host)
+        runner.step(*host_in)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         w0 = time.perf_counter()
         for _ in range(n_e2e):
-            runner.step(ids_host, tgt_host)  # H2D inputs, replay, D2H loss
+            runner.step(*host_in)  # H2D inputs, replay, D2H loss
         torch.cuda.synchronize()
         e2e_ms = (time.perf_counter() - w0) * 1e3 / n_e2e
         te = torch.tensor([e2e_ms], device=dev)
@@ -228,7 +230,7 @@ def main():
         e2e_ms = float(te.item())
         e2e = {"value": world * B_PER_GPU * SEQ / (e2e_ms / 1e3), "unit": "tok/s",
                "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": ids_host.numel() * 8 + tgt_host.numel() * 8,
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
                "d2h_bytes_per_step": 4, "api": "flodl_b200.train.StepRunner.step"}
 
     tok_s = world * B_PER_GPU * SEQ / (ms / 1e3)
@@ -238,9 +240,9 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "samples_per_s": world * B_PER_GPU / (ms / 1e3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (uniform random byte tokens), random-init weights",
-            "config": {"model": MODEL_DESC, "global_batch": B_PER_GPU * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world}", "optimizer": "AdamW lr3e-4 wd0.1",
+            "dtype": "bf16", "data": "synthetic (uniform random tokens), random-init weights",
+            "config": {"model": spec.desc, "global_batch": B_PER_GPU * world, "seq_len": SEQ,
+                       "parallelism": f"dp{world}", "optimizer": spec.optimizer,
                        "grad_allreduce": engine, "cuda_graph": graph is not None,
                        "l2": "inputs larger than L2: ~2 GB of activations per step per GPU"},
             "impl": args.impl,

@@ -62,9 +62,6 @@ void flash_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const T
 }  // namespace
 
 void register_attention(py::module& m) {
-  m.def("set_flash_progress_words", [](int64_t dev_ptr) {
-    flodl::set_flash_progress_words(reinterpret_cast<uint32_t*>(dev_ptr));
-  });
   m.def("set_flash_wait_limit_ns", [](int64_t ns) { flodl::set_flash_wait_limit_ns((uint64_t)ns); });
   m.def("flash_attn_fwd", &flash_fwd, py::arg("qkv"), py::arg("out"), py::arg("lse2"),
         py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"), py::arg("causal"),

@@ -221,6 +221,19 @@ void gelu_bwd(const Tensor& dy, const Tensor& h, Tensor& dh) {
                                     ptr<__nv_bfloat16>(dh), h.numel(), cur_stream()));
 }
 
+void gelu_eval_f32(const Tensor& x, Tensor& y, Tensor& dydx) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK_F32(x);
+  FL_CHECK_F32(y);
+  FL_CHECK_F32(dydx);
+  FL_CHECK(x.is_contiguous() && y.is_contiguous() && dydx.is_contiguous() &&
+               x.numel() == y.numel() && x.numel() == dydx.numel(),
+           "gelu_eval_f32 layout");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_gelu_eval_f32(x.data_ptr<float>(), y.data_ptr<float>(),
+                                         dydx.data_ptr<float>(), x.numel(), cur_stream()));
+}
+
 void gelu_fwd(const Tensor& x, Tensor& y) {
   FL_CHECK_BF16(x); FL_CHECK_BF16(y);
   FL_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel(), "gelu_fwd layout");
@@ -254,6 +267,7 @@ void register_elementwise(py::module& m) {
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
+  m.def("gelu_eval_f32", &gelu_eval_f32);
 }
 
 void register_optim(py::module& m) {

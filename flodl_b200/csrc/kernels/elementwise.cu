@@ -28,7 +28,25 @@ __global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat
     y[i] = __float2bfloat16_rn(gelu_erf(__bfloat162float(x[i])));
 }
 
+// f32 GELU and GELU' exactly as the GEMM epilogues evaluate them (numerics tests).
+__global__ void gelu_eval_f32_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                     float* __restrict__ dydx, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    y[i] = gelu_erf(x[i]);
+    dydx[i] = gelu_erf_grad(x[i]);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_gelu_eval_f32(const float* x, float* y, float* dydx, int64_t n,
+                                 cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  gelu_eval_f32_kernel<<<grid_1d(n, 256), 256, 0, st>>>(x, y, dydx, n);
+  note_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gelu_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* h, __nv_bfloat16* dh,
                             int64_t n, cudaStream_t st) {

@@ -25,6 +25,7 @@
 #include "sm100_ptx.cuh"
 #include "flash_attn.h"
 
+#include <atomic>
 #include <mutex>
 
 namespace flodl {
@@ -37,19 +38,6 @@ constexpr int kTileBytes = kTile * kD * 2;  // 16 KB: 128 rows x 128 B
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ uint64_t g_fa_wait_limit_ns = 2000000000ull;
-// Optional progress words (host-mapped, 8 per CTA: one per warp, code = stage).
-// Null unless a diagnostic run sets it; only lane 0 of a warp writes.
-__device__ uint32_t* g_fa_progress = nullptr;
-
-__device__ __forceinline__ void progress(int code) {
-  uint32_t* p = g_fa_progress;
-  if (p != nullptr && (threadIdx.x & 31) == 0) {
-    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    volatile uint32_t* w = p + cta * 8 + (threadIdx.x >> 5);
-    *w = (uint32_t)code;
-  }
-}
-
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -127,20 +115,58 @@ __device__ __forceinline__ void st_row32_sw128(uint8_t* tile, int r, int c0, con
 }
 
 // ============================================================== forward
+// Persistent: each CTA walks work items (128-query tile, head, batch) with a
+// stride of gridDim.x, so Q/K/V loads and S MMAs of the next item overlap the
+// softmax and output of the current one.
+//
+// Warps: 0 = TMA producer, 1 = MMA issuer, 2..9 = softmax. Softmax warp w owns
+// TMEM lane quarter w & 3 (32 query rows) and column half (w - 2) / 4: 64 of
+// the 128 keys of S, and 32 of the 64 columns of O. The two warps sharing a
+// row set exchange partial row maxima through shared memory, synchronised by
+// a per-pair mbarrier (bounded waits, never a named barrier, so an aborting
+// warp cannot strand its partner).
+//
+// TMEM (512 columns): S double buffer at 0 / 128, O double buffer (by item
+// parity) at 256 / 320. O accumulates P V across key tiles in TMEM. The
+// running max is rescaled lazily: a row keeps its reference max until the new
+// maximum exceeds it by more than 8 (log2 units), so P stays <= 2^8 and O is
+// rescaled in TMEM only when the reference moves.
+constexpr int kFwdSoftmaxWarps = 8;
+constexpr int kFwdThreads = 64 + 32 * kFwdSoftmaxWarps;
+constexpr float kRescaleThreshold = 8.0f;
+
 struct FwdSmem {
-  uint8_t q[kTileBytes];
+  uint8_t q[2][kTileBytes];
   uint8_t k[2][kTileBytes];
   uint8_t v[2][kTileBytes];
-  uint8_t p[2 * kTileBytes];  // P tile: 128 queries x 128 keys, two 64-key blocks
-  uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
-  uint64_t s_full, s_free, p_full, o_full, drain;
+  uint8_t p[2 * kTileBytes];        // P tile: 128 queries x 128 keys, two 64-key blocks
+  float red_max[2][2][kTile];       // [tile parity][column half][row]
+  float red_sum[2][kTile];          // [column half][row] final row sums
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full, pv_done;
+  uint64_t o_full[2], o_free[2];
+  uint64_t pair[4];                 // softmax warp pairs (per lane quarter)
+  uint64_t drain;
   uint32_t tmem_base;
   uint32_t abort;
 };
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void fwd_decode(int item, int n_qt, int H, int& qt, int& h, int& b) {
+  qt = item % n_qt;
+  const int bh = item / n_qt;
+  h = bh % H;
+  b = bh / H;
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
                      float* __restrict__ lse2, const uint8_t* __restrict__ key_pad, int B, int S,
                      int H, int causal, float scale, uint32_t* err) {
@@ -148,228 +174,334 @@ __global__ void __launch_bounds__(192, 1)
   FwdSmem& sm = *reinterpret_cast<FwdSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * kTile;
   const int C = H * kD;
-  const int n_kv_total = (S + kTile - 1) / kTile;
-  const int n_kv = causal ? min(qt + 1, n_kv_total) : n_kv_total;
+  const int n_qt = (S + kTile - 1) / kTile;
+  const int n_items = n_qt * H * B;
   const uint64_t limit = g_fa_wait_limit_ns;
   volatile uint32_t* abort_flag = &sm.abort;
+  auto kv_tiles = [&](int qt) { return causal ? min(qt + 1, n_qt) : n_qt; };
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.kv_full[i], 1);
       mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.s_free[i], kFwdSoftmaxWarps);
+      mbar_init(&sm.o_full[i], 1);
+      mbar_init(&sm.o_free[i], kFwdSoftmaxWarps);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.s_free, 4);
-    mbar_init(&sm.p_full, 4);
-    mbar_init(&sm.o_full, 1);
+    mbar_init(&sm.p_full, kFwdSoftmaxWarps);
+    mbar_init(&sm.pv_done, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&sm.pair[i], 64);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc<256>(&sm.tmem_base);
+    tmem_alloc<512>(&sm.tmem_base);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t t_s = tmem;        // S: 128 columns
-  const uint32_t t_o = tmem + 128;  // O_j: 64 columns
 
   if (warp == 0) {
+    // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_qkv);
-      mbar_arrive_expect_tx(&sm.q_full, kTileBytes);
-      tma_load_3d(sm.q, &tm_qkv, &sm.q_full, h * kD, q0, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(&sm.kv_empty[st], ph ^ 1, abort_flag, err, limit)) break;
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kTileBytes);
-        tma_load_3d(sm.k[st], &tm_qkv, &sm.kv_full[st], C + h * kD, j * kTile, b);
-        tma_load_3d(sm.v[st], &tm_qkv, &sm.kv_full[st], 2 * C + h * kD, j * kTile, b);
+      uint32_t kv_it = 0;
+      bool ok = true;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int qt, h, b;
+        fwd_decode(item, n_qt, H, qt, h, b);
+        const int qb = n & 1;
+        if (!(ok = mbar_wait_bounded(&sm.q_empty[qb], ((n >> 1) & 1) ^ 1, abort_flag, err, limit)))
+          break;
+        mbar_arrive_expect_tx(&sm.q_full[qb], kTileBytes);
+        tma_load_3d(sm.q[qb], &tm_qkv, &sm.q_full[qb], h * kD, qt * kTile, b);
+        const int nkv = kv_tiles(qt);
+        for (int j = 0; j < nkv; ++j, ++kv_it) {
+          const int st = kv_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.kv_empty[st], ((kv_it >> 1) & 1) ^ 1, abort_flag, err,
+                                       limit)))
+            break;
+          mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kTileBytes);
+          tma_load_3d(sm.k[st], &tm_qkv, &sm.kv_full[st], C + h * kD, j * kTile, b);
+          tma_load_3d(sm.v[st], &tm_qkv, &sm.kv_full[st], 2 * C + h * kD, j * kTile, b);
+        }
       }
     }
-    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
+    __syncwarp();
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(128, kD, 0, 1);
-      const uint32_t q_addr = smem_u32(sm.q);
       const uint32_t p_addr = smem_u32(sm.p);
-      bool ok = mbar_wait_bounded(&sm.q_full, 0, abort_flag, err, limit);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
-        const uint32_t k_addr = smem_u32(sm.k[st]);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          umma_bf16(t_s, make_sdesc_sw128(q_addr + kk * 32, 16, 1024),
-                    make_sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
-        umma_commit(&sm.s_full);
-      };
-      if (ok) ok = mbar_wait_bounded(&sm.kv_full[0], 0, abort_flag, err, limit);
-      if (ok) issue_s(0);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv) {
-          const int st1 = (j + 1) & 1;
-          ok = mbar_wait_bounded(&sm.kv_full[st1], ((j + 1) >> 1) & 1, abort_flag, err, limit) &&
-               mbar_wait_bounded(&sm.s_free, j & 1, abort_flag, err, limit);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
-        ok = mbar_wait_bounded(&sm.p_full, j & 1, abort_flag, err, limit);
-        if (!ok) break;
+      uint32_t kv_it = 0, s_it = 0, p_it = 0;
+      bool ok = true, issued = false;
+      int n = 0;
+      auto issue_pv = [&](uint32_t kv_stage, uint32_t t_o, bool acc) -> bool {
+        if (!mbar_wait_bounded(&sm.p_full, p_it & 1, abort_flag, err, limit)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[j & 1]);
+        const uint32_t v_addr = smem_u32(sm.v[kv_stage]);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint64_t a = make_sdesc_sw128(p_addr + (kk / 4) * kTileBytes + (kk % 4) * 32, 16, 1024);
+          const uint64_t a =
+              make_sdesc_sw128(p_addr + (kk / 4) * kTileBytes + (kk % 4) * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, kTileBytes, 1024);
-          umma_bf16(t_o, a, bd, idesc_o, kk > 0);
+          umma_bf16(t_o, a, bd, idesc_o, (acc || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&sm.o_full);
-        umma_commit(&sm.kv_empty[j & 1]);
+        umma_commit(&sm.pv_done);
+        umma_commit(&sm.kv_empty[kv_stage]);
+        ++p_it;
+        return true;
+      };
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int qt, h, b;
+        fwd_decode(item, n_qt, H, qt, h, b);
+        const int qb = n & 1;
+        const uint32_t t_o = tmem + 256 + (uint32_t)qb * kD;
+        if (!(ok = mbar_wait_bounded(&sm.q_full[qb], (n >> 1) & 1, abort_flag, err, limit))) break;
+        if (!(ok = mbar_wait_bounded(&sm.o_free[qb], ((n >> 1) & 1) ^ 1, abort_flag, err, limit)))
+          break;
+        const uint32_t q_addr = smem_u32(sm.q[qb]);
+        const int nkv = kv_tiles(qt);
+        uint32_t prev_stage = 0;
+        for (int j = 0; j < nkv && ok; ++j, ++kv_it, ++s_it) {
+          const uint32_t st = kv_it & 1, sb = s_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.kv_full[st], (kv_it >> 1) & 1, abort_flag, err, limit)))
+            break;
+          if (!(ok = mbar_wait_bounded(&sm.s_free[sb], ((s_it >> 1) & 1) ^ 1, abort_flag, err,
+                                       limit)))
+            break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm.k[st]);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            umma_bf16(tmem + sb * 128, make_sdesc_sw128(q_addr + kk * 32, 16, 1024),
+                      make_sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
+          issued = true;
+          umma_commit(&sm.s_full[sb]);
+          if (j == nkv - 1) umma_commit(&sm.q_empty[qb]);  // Q no longer read
+          // P V of the previous key tile overlaps this S
+          if (j > 0 && !(ok = issue_pv(prev_stage, t_o, j > 1))) break;
+          prev_stage = st;
+        }
+        if (!ok) break;
+        if (!(ok = issue_pv(prev_stage, t_o, nkv > 1))) break;
+        umma_commit(&sm.o_full[qb]);
       }
-      if (!ok) {
+      if (!ok && issued) {
         umma_commit(&sm.drain);
-        uint64_t t0 = global_timer_ns();
+        const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&sm.drain, 0) && global_timer_ns() - t0 < 100000000ull) {
         }
       }
     }
-    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
+    __syncwarp();
   } else {
-    // --------------------------------------------------- softmax warps
+    // ------------------------------------------------------------ softmax
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // query row within the tile
-    const int qi = q0 + r;
+    const int hh = (warp - 2) >> 2;  // column half
+    const int r = q4 * 32 + lane;    // query row within the tile
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = scale * kLog2e;
-    float m_run = -INFINITY, l_run = 0.f, corr_prev = 0.f;
-    float o_acc[kD];
-#pragma unroll
-    for (int d = 0; d < kD; ++d) o_acc[d] = 0.f;
+    uint64_t* pair = &sm.pair[q4];
+    uint32_t s_it = 0, p_it = 0, pair_it = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = mbar_wait_bounded(&sm.s_full, j & 1, abort_flag, err, limit);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      float s[kTile];
-#pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld_32cols(t_s + lane_off + c * 32, raw);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_free);
-      // scale + mask
-      const int k0 = j * kTile;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kTile; ++c) {
-        const int kj = k0 + c;
-        bool valid = kj < S && (!causal || kj <= qi);
-        if (key_pad && kj < S) valid = valid && (key_pad[(size_t)b * S + kj] == 0);
-        s[c] = valid ? s[c] * sl2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float corr = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_use);
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < kTile; ++c) {
-        s[c] = exp2f(s[c] - m_use);
-        rs += s[c];
-      }
-      l_run = l_run * corr + rs;
-      m_run = m_new;
-      // fold O_{j-1} (computed with the previous max) into the accumulator
-      if (j > 0) {
-        ok = mbar_wait_bounded(&sm.o_full, (j - 1) & 1, abort_flag, err, limit);
+    int n = 0;
+    // pair exchange: every lane arrives, then waits for the partner warp
+    auto pair_sync = [&]() -> bool {
+      mbar_arrive(pair);
+      const bool w = mbar_wait_bounded(pair, pair_it & 1, abort_flag, err, limit);
+      ++pair_it;
+      return __all_sync(0xffffffffu, w);
+    };
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      int qt, h, b;
+      fwd_decode(item, n_qt, H, qt, h, b);
+      const int qb = n & 1;
+      const uint32_t t_o = tmem + 256 + (uint32_t)qb * kD;
+      const int q0 = qt * kTile;
+      const int qi = q0 + r;
+      const int nkv = kv_tiles(qt);
+      float m_ref = -INFINITY;  // reference max (scaled, log2 units)
+      float l_half = 0.f;       // this warp's partial row sum
+      for (int j = 0; j < nkv; ++j, ++s_it, ++p_it) {
+        const uint32_t sb = s_it & 1;
+        ok = mbar_wait_bounded(&sm.s_full[sb], (s_it >> 1) & 1, abort_flag, err, limit);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
+        float s[64];
 #pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t raw[32];
-          tmem_ld_32cols(t_o + lane_off + c * 32, raw);
+          tmem_ld_32cols(tmem + sb * 128 + lane_off + (uint32_t)(hh * 64 + c * 32), raw);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            o_acc[c * 32 + i] = o_acc[c * 32 + i] * corr_prev + __uint_as_float(raw[i]);
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]) * sl2;
         }
-      }
-      corr_prev = corr;
-      // P -> shared memory (bf16, SW128 K-major), then hand it to the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[sb]);
+        // masks: key range, causal diagonal, key padding
+        const int k0 = j * kTile + hh * 64;
+        const bool diag = causal && (k0 + 63 > q0);
+        const bool tail = (k0 + 64 > S);
+        if (diag || tail || key_pad) {
+          uint32_t padw[16];
+          if (key_pad) {
+            const uint8_t* kp = key_pad + (size_t)b * S + k0;
 #pragma unroll
-      for (int c = 0; c < kTile; c += 32) st_row32_sw128(sm.p, r, c, &s[c]);
-      fence_proxy_async_smem();
+            for (int w4 = 0; w4 < 16; ++w4) {
+              uint32_t word = 0;
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int kj = k0 + w4 * 4 + t;
+                const uint32_t mbyte = (kj < S) ? (uint32_t)__ldg(kp + w4 * 4 + t) : 1u;
+                word |= (mbyte ? 1u : 0u) << (8 * t);
+              }
+              padw[w4] = word;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const int kj = k0 + c;
+            bool valid = kj < S && (!causal || kj <= qi);
+            if (key_pad) valid = valid && !((padw[c >> 2] >> (8 * (c & 3))) & 0xffu);
+            if (!valid) s[c] = -INFINITY;
+          }
+        }
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        sm.red_max[j & 1][hh][r] = mx;
+        if (!pair_sync()) { ok = false; break; }
+        const float m_tile = fmaxf(mx, sm.red_max[j & 1][hh ^ 1][r]);
+        // lazy rescale: move the reference only when the max grew by > threshold
+        const bool move = m_tile > m_ref + kRescaleThreshold;
+        const float m_new = move ? m_tile : m_ref;
+        const float corr = (move && m_ref != -INFINITY) ? ex2_approx(m_ref - m_new) : 1.f;
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        m_ref = m_new;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          s[c] = ex2_approx(s[c] - m_use);
+          l4[c & 3] += s[c];
+        }
+        l_half = l_half * corr + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
+        // P is single-buffered: the previous P V must have finished reading it
+        if (p_it > 0) {
+          ok = mbar_wait_bounded(&sm.pv_done, (p_it - 1) & 1, abort_flag, err, limit);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+        }
+        // rescale this warp's 32 columns of O when any of its rows moved
+        if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+          const uint32_t taddr = t_o + lane_off + (uint32_t)(hh * 32);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[16];
+            tmem_ld_16cols(taddr + c * 16, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st_16cols(taddr + c * 16, o);
+          }
+          tmem_st_wait();
+        }
+        // P (bf16) -> this warp's 64-key block of the SW128 K-major P tile
+        uint8_t* blk = sm.p + hh * kTileBytes;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(s[8 * q + 0], s[8 * q + 1]);
+          w.y = pack_bf16x2(s[8 * q + 2], s[8 * q + 3]);
+          w.z = pack_bf16x2(s[8 * q + 4], s[8 * q + 5]);
+          w.w = pack_bf16x2(s[8 * q + 6], s[8 * q + 7]);
+          st_sw128_chunk(blk, r, q, w);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full);
+      }
+      if (!ok) break;
+      // ---- output of this item: O / l for this warp's 32 columns, and lse
+      sm.red_sum[hh][r] = l_half;
+      if (!pair_sync()) { ok = false; break; }
+      const float l = l_half + sm.red_sum[hh ^ 1][r];
+      ok = mbar_wait_bounded(&sm.o_full[qb], (n >> 1) & 1, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld_32cols(t_o + lane_off + (uint32_t)(hh * 32), o);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full);
-    }
-    if (ok) {
-      ok = mbar_wait_bounded(&sm.o_full, (n_kv - 1) & 1, abort_flag, err, limit);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kD / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld_32cols(t_o + lane_off + c * 32, raw);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o_acc[c * 32 + i] = o_acc[c * 32 + i] * corr_prev + __uint_as_float(raw[i]);
-      }
+      if (lane == 0) mbar_arrive(&sm.o_free[qb]);
       if (qi < S) {
-        const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-        __nv_bfloat16* orow = out + ((size_t)b * S + qi) * C + h * kD;
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        uint4* orow = reinterpret_cast<uint4*>(out + ((size_t)b * S + qi) * C + h * kD + hh * 32);
 #pragma unroll
-        for (int q = 0; q < kD / 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           uint4 w;
-          w.x = pack_bf16x2(o_acc[8 * q + 0] * inv_l, o_acc[8 * q + 1] * inv_l);
-          w.y = pack_bf16x2(o_acc[8 * q + 2] * inv_l, o_acc[8 * q + 3] * inv_l);
-          w.z = pack_bf16x2(o_acc[8 * q + 4] * inv_l, o_acc[8 * q + 5] * inv_l);
-          w.w = pack_bf16x2(o_acc[8 * q + 6] * inv_l, o_acc[8 * q + 7] * inv_l);
-          reinterpret_cast<uint4*>(orow)[q] = w;
+          w.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+          w.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+          w.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+          w.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
+          orow[q] = w;
         }
-        lse2[((size_t)b * H + h) * S + qi] =
-            (l_run > 0.f) ? (m_run + log2f(l_run)) : -INFINITY;
+        if (hh == 0)
+          lse2[((size_t)b * H + h) * S + qi] = (l > 0.f) ? (m_ref + log2f(l)) : -INFINITY;
       }
+      // the red_sum slot is rewritten next item only after the pair passes
+      // at least one more pair_sync (the first max exchange), so no extra sync
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<256>(tmem);
+    tmem_dealloc<512>(tmem);
   }
 }
 
 // ============================================================== backward
+// Persistent over work items (128-key tile, head, batch). Per item the CTA
+// walks the query tiles that see these keys (all, or those at/after the key
+// tile when causal):
+//   S^T = K Q_i^T, dP^T = V dO_i^T                        (TMEM, 128 x 128 each)
+//   P^T = exp2(S^T * scale * log2e - lse2_i), dS^T = P^T (dP^T - delta_i)
+//   dV += P^T dO_i, dK += dS^T Q_i                         (TMEM accumulators)
+//   dQ_i = dS K -> f32 red.add into the dQ accumulator      (TMEM, read out one tile late)
+// Warps: 0 = TMA producer, 1 = MMA issuer, 2..9 = compute. Compute warp w owns
+// key rows 32 (w & 3) .. +31 (its TMEM lane quarter) and query half (w - 2) / 4
+// of each tile (64 columns of S^T / dP^T, 32 columns of dQ / dK / dV). The
+// halves need no exchange: the softmax statistics come precomputed (lse2,
+// delta). TMEM: S^T 0, dP^T 128, dV 256, dK 320, dQ 384 (512 allocated).
+constexpr int kBwdWarps = 8;
+constexpr int kBwdThreads = 64 + 32 * kBwdWarps;
+
 struct BwdSmem {
   uint8_t k[kTileBytes];
   uint8_t v[kTileBytes];
   uint8_t q[2][kTileBytes];
   uint8_t dout[2][kTileBytes];
-  uint8_t p[2 * kTileBytes];   // P^T: 128 keys x 128 queries
-  uint8_t ds[2 * kTileBytes];  // dS^T: 128 keys x 128 queries
-  uint64_t kv_full;
-  uint64_t qdo_full[2];
-  uint64_t qdo_empty[2];
-  uint64_t sdp_full, pds_ready, dq_full, dq_free, drain;
+  uint8_t p[2 * kTileBytes];   // P^T: 128 keys x 128 queries (two 64-query SW128 blocks)
+  uint8_t ds[2 * kTileBytes];  // dS^T, same layout
+  float stat[kBwdWarps][2][64];  // per compute warp: lse2 and delta of its 64 queries
+  uint64_t kv_full, kv_empty;
+  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t s_full, s_free, p_ready, pds_free, dq_full, dq_free, dkv_full, dkv_free;
+  uint64_t drain;
   uint32_t tmem_base;
   uint32_t abort;
 };
@@ -413,7 +545,14 @@ __global__ void flash_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfl
   }
 }
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ void bwd_decode(int item, int n_kt, int H, int& kt, int& h, int& b) {
+  kt = item % n_kt;
+  const int bh = item / n_kt;
+  h = bh % H;
+  b = bh / H;
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                      const __grid_constant__ CUtensorMap tm_dout, const float* __restrict__ lse2,
                      const float* __restrict__ delta, float* __restrict__ dq_acc,
@@ -423,35 +562,36 @@ __global__ void __launch_bounds__(192, 1)
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int k0 = kt * kTile;
   const int C = H * kD;
-  const int n_q_total = (S + kTile - 1) / kTile;
-  const int qt_begin = causal ? kt : 0;
-  const int n_it = n_q_total - qt_begin;
+  const int n_t = (S + kTile - 1) / kTile;  // tiles along the sequence
+  const int n_items = n_t * H * B;
   const uint64_t limit = g_fa_wait_limit_ns;
   volatile uint32_t* abort_flag = &sm.abort;
+  auto first_q = [&](int kt) { return causal ? kt : 0; };
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.kv_full, 1);
+    mbar_init(&sm.kv_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qdo_full[i], 1);
       mbar_init(&sm.qdo_empty[i], 1);
     }
-    mbar_init(&sm.sdp_full, 1);
-    mbar_init(&sm.pds_ready, 4);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_free, kBwdWarps);
+    mbar_init(&sm.p_ready, kBwdWarps);
+    mbar_init(&sm.pds_free, 1);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_free, 4);
+    mbar_init(&sm.dq_free, kBwdWarps);
+    mbar_init(&sm.dkv_full, 1);
+    mbar_init(&sm.dkv_free, kBwdWarps);
     mbar_init(&sm.drain, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
-  progress(1);
   if (warp == 1) {
     tmem_alloc<512>(&sm.tmem_base);
     tmem_relinquish();
   }
-  progress(2);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -460,213 +600,260 @@ __global__ void __launch_bounds__(192, 1)
                  t_dq = tmem + 384;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       tma_prefetch_desc(&tm_qkv);
       tma_prefetch_desc(&tm_dout);
-      mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
-      tma_load_3d(sm.k, &tm_qkv, &sm.kv_full, C + h * kD, k0, b);
-      tma_load_3d(sm.v, &tm_qkv, &sm.kv_full, 2 * C + h * kD, k0, b);
-      for (int it = 0; it < n_it; ++it) {
-        const int st = it & 1;
-        const int qt = qt_begin + it;
-        if (!mbar_wait_bounded(&sm.qdo_empty[st], ((it >> 1) & 1) ^ 1, abort_flag, err, limit))
-          break;
-        mbar_arrive_expect_tx(&sm.qdo_full[st], 2 * kTileBytes);
-        tma_load_3d(sm.q[st], &tm_qkv, &sm.qdo_full[st], h * kD, qt * kTile, b);
-        tma_load_3d(sm.dout[st], &tm_dout, &sm.qdo_full[st], h * kD, qt * kTile, b);
-        progress(10 + it);
+      uint32_t qdo_it = 0;
+      bool ok = true;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int kt, h, b;
+        bwd_decode(item, n_t, H, kt, h, b);
+        if (!(ok = mbar_wait_bounded(&sm.kv_empty, (n & 1) ^ 1, abort_flag, err, limit))) break;
+        mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
+        tma_load_3d(sm.k, &tm_qkv, &sm.kv_full, C + h * kD, kt * kTile, b);
+        tma_load_3d(sm.v, &tm_qkv, &sm.kv_full, 2 * C + h * kD, kt * kTile, b);
+        for (int i = first_q(kt); i < n_t; ++i, ++qdo_it) {
+          const int st = qdo_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.qdo_empty[st], ((qdo_it >> 1) & 1) ^ 1, abort_flag, err,
+                                       limit)))
+            break;
+          mbar_arrive_expect_tx(&sm.qdo_full[st], 2 * kTileBytes);
+          tma_load_3d(sm.q[st], &tm_qkv, &sm.qdo_full[st], h * kD, i * kTile, b);
+          tma_load_3d(sm.dout[st], &tm_dout, &sm.qdo_full[st], h * kD, i * kTile, b);
+        }
       }
-      progress(19);
     }
-    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
+    __syncwarp();
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc_kq = make_idesc_bf16(128, 128, 0, 0);  // M=keys, N=queries
       constexpr uint32_t idesc_kd = make_idesc_bf16(128, kD, 0, 1);   // M=keys, N=D, B MN-major
       constexpr uint32_t idesc_qd = make_idesc_bf16(128, kD, 1, 1);   // M=queries, N=D, A,B MN-major
       const uint32_t k_addr = smem_u32(sm.k), v_addr = smem_u32(sm.v);
       const uint32_t p_addr = smem_u32(sm.p), ds_addr = smem_u32(sm.ds);
-      bool ok = mbar_wait_bounded(&sm.kv_full, 0, abort_flag, err, limit);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it & 1;
-        ok = mbar_wait_bounded(&sm.qdo_full[st], (it >> 1) & 1, abort_flag, err, limit);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sm.q[st]), do_addr = smem_u32(sm.dout[st]);
-        // S^T = K Q^T ; dP^T = V dO^T
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          umma_bf16(t_s, make_sdesc_sw128(k_addr + kk * 32, 16, 1024),
-                    make_sdesc_sw128(q_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
-          umma_bf16(t_dp, make_sdesc_sw128(v_addr + kk * 32, 16, 1024),
-                    make_sdesc_sw128(do_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
-        }
-        umma_commit(&sm.sdp_full);
-        progress(20 + 10 * it + 1);
-        ok = mbar_wait_bounded(&sm.pds_ready, it & 1, abort_flag, err, limit);
-        progress(20 + 10 * it + 2);
-        if (!ok) break;
-        tc_fence_after();
-        // dV += P^T dO ; dK += dS^T Q   (K = 128 queries)
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
-          umma_bf16(t_dv, make_sdesc_sw128(p_addr + aoff, 16, 1024),
-                    make_sdesc_sw128(do_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
-                    (it > 0 || kk > 0));
-          umma_bf16(t_dk, make_sdesc_sw128(ds_addr + aoff, 16, 1024),
-                    make_sdesc_sw128(q_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
-                    (it > 0 || kk > 0));
-        }
-        if (it > 0) {
-          ok = mbar_wait_bounded(&sm.dq_free, (it - 1) & 1, abort_flag, err, limit);
-          if (!ok) break;
+      uint32_t qdo_it = 0, t = 0;
+      bool ok = true, issued = false;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int kt, h, b;
+        bwd_decode(item, n_t, H, kt, h, b);
+        if (!(ok = mbar_wait_bounded(&sm.kv_full, n & 1, abort_flag, err, limit))) break;
+        if (!(ok = mbar_wait_bounded(&sm.dkv_free, (n & 1) ^ 1, abort_flag, err, limit))) break;
+        int it = 0;
+        for (int i = first_q(kt); i < n_t; ++i, ++it, ++qdo_it, ++t) {
+          const int st = qdo_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.qdo_full[st], (qdo_it >> 1) & 1, abort_flag, err,
+                                       limit)))
+            break;
+          if (!(ok = mbar_wait_bounded(&sm.s_free, (t & 1) ^ 1, abort_flag, err, limit))) break;
           tc_fence_after();
-        }
-        // dQ_i = dS K  (M = 128 queries, K = 128 keys): A = dS^T read MN-major
+          const uint32_t q_addr = smem_u32(sm.q[st]), do_addr = smem_u32(sm.dout[st]);
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16(t_dq, make_sdesc_sw128(ds_addr + kk * 2048, kTileBytes, 1024),
-                    make_sdesc_sw128(k_addr + kk * 2048, kTileBytes, 1024), idesc_qd, kk > 0);
-        umma_commit(&sm.dq_full);
-        umma_commit(&sm.qdo_empty[st]);
-        progress(20 + 10 * it + 5);
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            umma_bf16(t_s, make_sdesc_sw128(k_addr + kk * 32, 16, 1024),
+                      make_sdesc_sw128(q_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
+            umma_bf16(t_dp, make_sdesc_sw128(v_addr + kk * 32, 16, 1024),
+                      make_sdesc_sw128(do_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
+          }
+          issued = true;
+          umma_commit(&sm.s_full);
+          if (!(ok = mbar_wait_bounded(&sm.p_ready, t & 1, abort_flag, err, limit))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
+            umma_bf16(t_dv, make_sdesc_sw128(p_addr + aoff, 16, 1024),
+                      make_sdesc_sw128(do_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
+                      (it > 0 || kk > 0));
+            umma_bf16(t_dk, make_sdesc_sw128(ds_addr + aoff, 16, 1024),
+                      make_sdesc_sw128(q_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
+                      (it > 0 || kk > 0));
+          }
+          if (!(ok = mbar_wait_bounded(&sm.dq_free, (t & 1) ^ 1, abort_flag, err, limit))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_bf16(t_dq, make_sdesc_sw128(ds_addr + kk * 2048, kTileBytes, 1024),
+                      make_sdesc_sw128(k_addr + kk * 2048, kTileBytes, 1024), idesc_qd, kk > 0);
+          umma_commit(&sm.dq_full);
+          umma_commit(&sm.pds_free);
+          umma_commit(&sm.qdo_empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&sm.kv_empty);
+        umma_commit(&sm.dkv_full);
       }
-      progress(59);
-      if (!ok) {
+      if (!ok && issued) {
         umma_commit(&sm.drain);
-        uint64_t t0 = global_timer_ns();
+        const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&sm.drain, 0) && global_timer_ns() - t0 < 100000000ull) {
         }
       }
     }
-    __syncwarp();  // reconverge the warp before the CTA-wide barrier below
+    __syncwarp();
   } else {
-    // --------------------------------------------------- softmax warps (thread = key row)
+    // ------------------------------------------------------------ compute warps
+    const int wi = warp - 2;
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;
-    const int kj = k0 + r;
+    const int hh = wi >> 2;        // query half of each tile
+    const int r = q4 * 32 + lane;  // key row within the tile (and query row for dQ)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = scale * kLog2e;
-    const bool key_ok = kj < S && !(key_pad && key_pad[(size_t)b * S + kj] != 0);
+    float* st_lse = sm.stat[wi][0];
+    float* st_dl = sm.stat[wi][1];
+    uint32_t t = 0;
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int qt = qt_begin + it;
-      const int q0 = qt * kTile;
-      const float* lse_t = lse2 + ((size_t)b * H + h) * S + q0;
-      const float* delta_t = delta + ((size_t)b * H + h) * S + q0;
-      progress(60 + 10 * it);
-      ok = mbar_wait_bounded(&sm.sdp_full, it & 1, abort_flag, err, limit);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      progress(60 + 10 * it + 1);
+    int n = 0;
+    int dq_pending_q0 = -1, dq_pending_b = 0, dq_pending_h = 0;
+    // read out dQ of the previous tile (TMEM lanes = its queries) into dq_acc
+    auto flush_dq = [&]() -> bool {
+      if (dq_pending_q0 < 0) return true;
+      const bool w = mbar_wait_bounded(&sm.dq_full, (t - 1) & 1, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, w)) return false;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < kTile; c += 32) {
-        uint32_t rs[32], rdp[32];
-        tmem_ld_32cols(t_s + lane_off + c, rs);
-        tmem_ld_32cols(t_dp + lane_off + c, rdp);
-        tmem_ld_wait();
-        float pv[32], dsv[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qi = q0 + c + i;
-          const bool valid = key_ok && qi < S && (!causal || kj <= qi);
-          // per-query statistics: every thread reads the same words (L1 broadcast)
-          const float l2 = qi < S ? __ldg(lse_t + c + i) : 0.f;
-          const float dl = qi < S ? __ldg(delta_t + c + i) : 0.f;
-          const float p = valid ? exp2f(__uint_as_float(rs[i]) * sl2 - l2) : 0.f;
-          pv[i] = p;
-          dsv[i] = p * (__uint_as_float(rdp[i]) - dl);
-        }
-        st_row32_sw128(sm.p, r, c, pv);
-        st_row32_sw128(sm.ds, r, c, dsv);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.pds_ready);
-      progress(60 + 10 * it + 2);
-      // dQ tile: thread = query row (TMEM lane)
-      ok = mbar_wait_bounded(&sm.dq_full, it & 1, abort_flag, err, limit);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      progress(60 + 10 * it + 3);
-      tc_fence_after();
-      {
-        const int qi = q0 + r;
-        float* dqrow = dq_acc + ((size_t)b * S + qi) * C + h * kD;
-#pragma unroll
-        for (int c = 0; c < kD; c += 32) {
-          uint32_t raw[32];
-          tmem_ld_32cols(t_dq + lane_off + c, raw);
-          tmem_ld_wait();
-          if (qi < S) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              red_add_v4(dqrow + c + i, __uint_as_float(raw[i]), __uint_as_float(raw[i + 1]),
-                         __uint_as_float(raw[i + 2]), __uint_as_float(raw[i + 3]));
-          }
-        }
-      }
+      uint32_t raw[32];
+      tmem_ld_32cols(t_dq + lane_off + (uint32_t)(hh * 32), raw);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.dq_free);
-      progress(60 + 10 * it + 4);
-    }
-    progress(90);
-    // dK, dV out (thread = key row). The last dq_full wait above implies all MMAs are done.
-    if (ok && n_it > 0) {
-      tc_fence_after();
-      // tcgen05.ld is warp-synchronous: every lane loads, only in-range rows store
-      __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD;
-      __nv_bfloat16* vrow = krow + C;
+      const int qi = dq_pending_q0 + r;
+      if (qi < S) {
+        float* dqrow = dq_acc + ((size_t)dq_pending_b * S + qi) * C + dq_pending_h * kD + hh * 32;
 #pragma unroll
-      for (int c = 0; c < kD; c += 32) {
-        uint32_t rk[32], rv[32];
-        tmem_ld_32cols(t_dk + lane_off + c, rk);
-        tmem_ld_32cols(t_dv + lane_off + c, rv);
-        tmem_ld_wait();
-        if (kj < S) {
+        for (int i = 0; i < 32; i += 4)
+          red_add_v4(dqrow + i, __uint_as_float(raw[i]), __uint_as_float(raw[i + 1]),
+                     __uint_as_float(raw[i + 2]), __uint_as_float(raw[i + 3]));
+      }
+      dq_pending_q0 = -1;
+      return true;
+    };
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      int kt, h, b;
+      bwd_decode(item, n_t, H, kt, h, b);
+      const int kj = kt * kTile + r;
+      const bool key_ok = kj < S && !(key_pad && __ldg(key_pad + (size_t)b * S + kj) != 0);
+      for (int i = first_q(kt); i < n_t; ++i, ++t) {
+        const int q0 = i * kTile;
+        const int qc0 = q0 + hh * 64;  // first query of this warp's half
+        // this warp's 64 query statistics -> shared memory (queries >= S: p = 0)
+        {
+          const float* lrow = lse2 + ((size_t)b * H + h) * S;
+          const float* drow = delta + ((size_t)b * H + h) * S;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int qi = qc0 + u * 32 + lane;
+            st_lse[u * 32 + lane] = qi < S ? __ldg(lrow + qi) : INFINITY;
+            st_dl[u * 32 + lane] = qi < S ? __ldg(drow + qi) : 0.f;
+          }
+          __syncwarp();
+        }
+        ok = mbar_wait_bounded(&sm.s_full, t & 1, abort_flag, err, limit);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        // the previous tile's MMAs must be done reading P^T / dS^T
+        ok = mbar_wait_bounded(&sm.pds_free, (t & 1) ^ 1, abort_flag, err, limit);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        const bool diag = causal && (qc0 < kt * kTile + kTile);  // some query < some key
+        uint8_t* pb = sm.p + hh * kTileBytes;
+        uint8_t* db = sm.ds + hh * kTileBytes;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {  // two 32-query chunks of this warp's half
+          uint32_t rs[32], rdp[32];
+          tmem_ld_32cols(t_s + lane_off + (uint32_t)(hh * 64 + cc * 32), rs);
+          tmem_ld_32cols(t_dp + lane_off + (uint32_t)(hh * 64 + cc * 32), rdp);
+          tmem_ld_wait();
+          float p[32], ds[32];
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(st_lse + cc * 32 + 4 * c4);
+            const float4 d4 = *reinterpret_cast<const float4*>(st_dl + cc * 32 + 4 * c4);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+            const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int c = 4 * c4 + u;
+              bool valid = key_ok;
+              if (diag) valid = valid && (kj <= qc0 + cc * 32 + c);
+              const float pv = valid ? ex2_approx(__uint_as_float(rs[c]) * sl2 - lv[u]) : 0.f;
+              p[c] = pv;
+              ds[c] = pv * (__uint_as_float(rdp[c]) - dv[u]);
+            }
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint4 wk, wv;
-            wk.x = pack_bf16x2(__uint_as_float(rk[8 * q + 0]) * scale, __uint_as_float(rk[8 * q + 1]) * scale);
-            wk.y = pack_bf16x2(__uint_as_float(rk[8 * q + 2]) * scale, __uint_as_float(rk[8 * q + 3]) * scale);
-            wk.z = pack_bf16x2(__uint_as_float(rk[8 * q + 4]) * scale, __uint_as_float(rk[8 * q + 5]) * scale);
-            wk.w = pack_bf16x2(__uint_as_float(rk[8 * q + 6]) * scale, __uint_as_float(rk[8 * q + 7]) * scale);
-            wv.x = pack_bf16x2(__uint_as_float(rv[8 * q + 0]), __uint_as_float(rv[8 * q + 1]));
-            wv.y = pack_bf16x2(__uint_as_float(rv[8 * q + 2]), __uint_as_float(rv[8 * q + 3]));
-            wv.z = pack_bf16x2(__uint_as_float(rv[8 * q + 4]), __uint_as_float(rv[8 * q + 5]));
-            wv.w = pack_bf16x2(__uint_as_float(rv[8 * q + 6]), __uint_as_float(rv[8 * q + 7]));
-            reinterpret_cast<uint4*>(krow + c)[q] = wk;
-            reinterpret_cast<uint4*>(vrow + c)[q] = wv;
+            uint4 w, v;
+            w.x = pack_bf16x2(p[8 * q + 0], p[8 * q + 1]);
+            w.y = pack_bf16x2(p[8 * q + 2], p[8 * q + 3]);
+            w.z = pack_bf16x2(p[8 * q + 4], p[8 * q + 5]);
+            w.w = pack_bf16x2(p[8 * q + 6], p[8 * q + 7]);
+            v.x = pack_bf16x2(ds[8 * q + 0], ds[8 * q + 1]);
+            v.y = pack_bf16x2(ds[8 * q + 2], ds[8 * q + 3]);
+            v.z = pack_bf16x2(ds[8 * q + 4], ds[8 * q + 5]);
+            v.w = pack_bf16x2(ds[8 * q + 6], ds[8 * q + 7]);
+            st_sw128_chunk(pb, r, cc * 4 + q, w);
+            st_sw128_chunk(db, r, cc * 4 + q, v);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_ready);
+        // dQ of the previous tile, then remember this one
+        if (!flush_dq()) { ok = false; break; }
+        dq_pending_q0 = q0;
+        dq_pending_b = b;
+        dq_pending_h = h;
       }
-    } else if (ok && kj < S) {
-      // no query tile reaches this key tile: its gradients are zero
-      __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD;
-      for (int c = 0; c < kD; ++c) {
-        krow[c] = __float2bfloat16_rn(0.f);
-        krow[C + c] = __float2bfloat16_rn(0.f);
+      if (!ok) break;
+      ok = flush_dq();  // the last tile of this item (t was already advanced past it)
+      if (!ok) break;
+      // dK, dV of this key tile (thread = key row, 32 of the 64 columns)
+      ok = mbar_wait_bounded(&sm.dkv_full, n & 1, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t rk[32], rv[32];
+      tmem_ld_32cols(t_dk + lane_off + (uint32_t)(hh * 32), rk);
+      tmem_ld_32cols(t_dv + lane_off + (uint32_t)(hh * 32), rv);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.dkv_free);
+      if (kj < S) {
+        __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD + hh * 32;
+        __nv_bfloat16* vrow = krow + C;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 wk, wv;
+          wk.x = pack_bf16x2(__uint_as_float(rk[8 * q + 0]) * scale, __uint_as_float(rk[8 * q + 1]) * scale);
+          wk.y = pack_bf16x2(__uint_as_float(rk[8 * q + 2]) * scale, __uint_as_float(rk[8 * q + 3]) * scale);
+          wk.z = pack_bf16x2(__uint_as_float(rk[8 * q + 4]) * scale, __uint_as_float(rk[8 * q + 5]) * scale);
+          wk.w = pack_bf16x2(__uint_as_float(rk[8 * q + 6]) * scale, __uint_as_float(rk[8 * q + 7]) * scale);
+          wv.x = pack_bf16x2(__uint_as_float(rv[8 * q + 0]), __uint_as_float(rv[8 * q + 1]));
+          wv.y = pack_bf16x2(__uint_as_float(rv[8 * q + 2]), __uint_as_float(rv[8 * q + 3]));
+          wv.z = pack_bf16x2(__uint_as_float(rv[8 * q + 4]), __uint_as_float(rv[8 * q + 5]));
+          wv.w = pack_bf16x2(__uint_as_float(rv[8 * q + 6]), __uint_as_float(rv[8 * q + 7]));
+          reinterpret_cast<uint4*>(krow)[q] = wk;
+          reinterpret_cast<uint4*>(vrow)[q] = wv;
+        }
       }
     }
   }
-  progress(95);
   tc_fence_before();
   __syncthreads();
-  progress(97);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<512>(tmem);
   }
-  progress(99);
 }
 
 }  // namespace
 
-void set_flash_progress_words(uint32_t* dev_ptr) {
-  cudaMemcpyToSymbol(g_fa_progress, &dev_ptr, sizeof(dev_ptr));
-}
 
 void set_flash_wait_limit_ns(uint64_t ns) {
   cudaMemcpyToSymbol(g_fa_wait_limit_ns, &ns, sizeof(ns));
@@ -677,14 +864,23 @@ cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st) {
   CUtensorMap tm;
   if (!make_map_3d(&tm, a.qkv, a.B, a.S, 3 * a.H * kD)) return cudaErrorInvalidValue;
   const int smem = (int)sizeof(FwdSmem) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
+  {
+    // the dynamic shared-memory opt-in is a per-device function attribute
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load(std::memory_order_relaxed) & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      done.fetch_or(bit);
+    }
   }
-  dim3 grid((a.S + kTile - 1) / kTile, a.H, a.B);
-  flash_fwd_kernel<<<grid, 192, smem, st>>>(tm, a.out, a.lse2, a.key_pad, a.B, a.S, a.H,
-                                            a.causal ? 1 : 0, a.scale, a.err ? a.err : default_err_word());
+  const int64_t items = (int64_t)((a.S + kTile - 1) / kTile) * a.H * a.B;
+  const int grid = (int)std::min<int64_t>(items, (int64_t)num_sms());
+  flash_fwd_kernel<<<grid, kFwdThreads, smem, st>>>(tm, a.out, a.lse2, a.key_pad, a.B, a.S, a.H,
+                                                     a.causal ? 1 : 0, a.scale,
+                                                     a.err ? a.err : default_err_word());
   note_launch();
   return cudaGetLastError();
 }
@@ -699,13 +895,21 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   int pre_blocks = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 16);
   flash_bwd_pre_kernel<<<pre_blocks, 256, 0, st>>>(a.dout, a.out, a.delta, a.dq_acc, a.B, a.S, a.H);
   const int smem = (int)sizeof(BwdSmem) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
+  {
+    // the dynamic shared-memory opt-in is a per-device function attribute
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load(std::memory_order_relaxed) & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      done.fetch_or(bit);
+    }
   }
-  dim3 grid((a.S + kTile - 1) / kTile, a.H, a.B);
-  flash_bwd_kernel<<<grid, 192, smem, st>>>(tm_qkv, tm_do, a.lse2, a.delta, a.dq_acc, a.dqkv,
+  const int64_t items = (int64_t)((a.S + kTile - 1) / kTile) * a.H * a.B;
+  const int grid = (int)std::min<int64_t>(items, (int64_t)num_sms());
+  flash_bwd_kernel<<<grid, kBwdThreads, smem, st>>>(tm_qkv, tm_do, a.lse2, a.delta, a.dq_acc, a.dqkv,
                                             a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
                                             a.err ? a.err : default_err_word());
   const int64_t T = (int64_t)a.B * a.S;

@@ -27,7 +27,5 @@ struct FlashArgs {
 cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st);
 cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st);
 void set_flash_wait_limit_ns(uint64_t ns);
-// Diagnostics: host-mapped words (8 per CTA) that record each warp's stage.
-void set_flash_progress_words(uint32_t* dev_ptr);
 
 }  // namespace flodl

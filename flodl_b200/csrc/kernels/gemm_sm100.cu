@@ -40,22 +40,26 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;     // producer + MMA + epilogue
 
 __device__ uint64_t g_wait_limit_ns = 2000000000ull;  // 2 s
 
-// Epilogue staging: each epilogue warp owns 4 KB of shared memory holding one
-// 32x32 output chunk (f32, 128B swizzle) or one bf16 output chunk plus one
-// bf16 pre-activation chunk (2 KB each, 64B swizzle); chunks leave through TMA
-// stores so global writes are full, coalesced lines.
-constexpr int kStageWarpBytes = 4096;
+// Epilogue staging: each epilogue warp owns two 4 KB slots of shared memory.
+// A slot holds one 32x32 output chunk (f32, 128B swizzle) or one bf16 output
+// chunk plus one bf16 pre-activation chunk (2 KB each, 64B swizzle). Chunks
+// leave through TMA stores (full, coalesced lines); epilogue inputs (residual,
+// GELU' operand) arrive through TMA loads into the slot of the chunk that
+// needs them while the previous chunk is being computed. Two slots let the
+// store of chunk j drain while chunk j+1 is staged.
+constexpr int kSlotBytes = 4096;
+constexpr int kStageWarpBytes = 2 * kSlotBytes;
 constexpr int kStagingBytes = kEpiWarps * kStageWarpBytes;
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kStages = (BN == 256) ? 3 : 5;
   static constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
   static constexpr int kBTileBytes = BN * kBK * 2;   // 32 KB or 16 KB
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
   static constexpr int kSmemBytes =
-      kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
+      kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 512 /*barriers*/;
 };
 
 struct SmemCtl {
@@ -64,9 +68,11 @@ struct SmemCtl {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
+  uint64_t epi_in[kEpiWarps * 2];  // epilogue input loads, one per warp slot
   uint32_t tmem_base;
   uint32_t abort;
 };
+static_assert(sizeof(SmemCtl) <= 512, "barrier block");
 
 __device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, int col0,
                                                int M, int N, const uint32_t (&acc)[32]) {
@@ -188,92 +194,93 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, 
   }
 }
 
-// Same math as epilogue_chunk, but the warp writes its 32x32 chunk into
-// swizzled shared memory and one lane ships it with a TMA store (or a TMA
-// reduce-add for accumulation). `buf` alternates between the two staging
-// slots; the caller guarantees the slot's previous store finished reading.
-__device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, const CUtensorMap* tmOut,
-                                                   const CUtensorMap* tmAux, uint8_t* stage,
-                                                   int buf, int row0, int col0, int lane, int M,
-                                                   int N, const uint32_t (&acc)[32]) {
-  const int row = row0 + lane;
+// What the epilogue prefetches (TMA) into a staging slot before a chunk's math.
+enum EpiInput : int { kInNone = 0, kInResidual = 1, kInAux = 2 };
+
+// TMA-store epilogue of one 32x32 chunk. The warp's staging slot (4 KB) holds
+// the chunk in the layout its tensor maps use: f32 rows of 128 B with the
+// 128-byte swizzle (chunk q of row r at q ^ (r & 7)), or bf16 rows of 64 B with
+// the 64-byte swizzle (q ^ ((r >> 1) & 3)) at offset 0 plus, for a second bf16
+// tensor (pre-activation out, or the GELU' input), at offset 2048. Inputs
+// (residual f32 / pre-activation bf16) were brought in by TMA at the same
+// positions the outputs use, so each lane reads and writes its own row only.
+// Out-of-range rows/columns need no checks: TMA loads fill them with zeros and
+// TMA stores clip them; only the bias needs a bound.
+__device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float alpha,
+                                                   const CUtensorMap* tmOut,
+                                                   const CUtensorMap* tmAux, uint8_t* slot,
+                                                   int row0, int col0, int lane, int N,
+                                                   const uint32_t (&acc)[32]) {
   float v[32];
-  const float alpha = ep.alpha_ptr ? ep.alpha * __ldg(ep.alpha_ptr) : ep.alpha;
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) * alpha;
-  const bool full_cols = (col0 + 32 <= N);
-  const bool row_ok = row < M;
   if (ep.bias) {
+    if (col0 + 32 <= N && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0) {
+      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int c = col0 + i;
-      v[i] += (c < N) ? __ldg(ep.bias + c) : 0.f;
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = __ldg(b4 + q);
+        v[4 * q + 0] += b.x;
+        v[4 * q + 1] += b.y;
+        v[4 * q + 2] += b.z;
+        v[4 * q + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += (col0 + i < N) ? __ldg(ep.bias + col0 + i) : 0.f;
     }
   }
+  const int sw64 = (lane >> 1) & 3;
+  const int sw128 = lane & 7;
   const bool aux_out = (ep.flags & kEpiGelu) && ep.aux;
-  if (aux_out) {
-    // pre-activation -> bf16 staging (64B swizzle)
-    uint8_t* a = stage + 2048;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-      w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-      w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-      w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-      *reinterpret_cast<uint4*>(a + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
-    }
-  }
   if (ep.flags & kEpiGelu) {
+    if (aux_out) {  // pre-activation, kept for the backward pass
+      uint8_t* a = slot + 2048 + lane * 64;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+        *reinterpret_cast<uint4*>(a + ((q ^ sw64) * 16)) = w;
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
   }
-  if ((ep.flags & kEpiDGelu) && row_ok) {
-    const __nv_bfloat16* aux =
-        reinterpret_cast<const __nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
-    if (full_cols && ((ep.ld_aux & 7) == 0)) {
-      const uint4* src = reinterpret_cast<const uint4*>(aux + col0);
+  if (ep.flags & kEpiDGelu) {  // multiply by GELU'(pre-activation) staged at +2048
+    const uint8_t* a = slot + 2048 + lane * 64;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w = src[q];
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = *reinterpret_cast<const uint4*>(a + ((q ^ sw64) * 16));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float2 f = unpack_bf16x2(ws[h]);
-          v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
-          v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
-        }
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(ws[h]);
+        v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
+        v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
       }
-    } else {
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < N) v[i] *= gelu_erf_grad(__bfloat162float(aux[col0 + i]));
     }
   }
-  if (ep.residual && row_ok) {
-    const float* res = ep.residual + (size_t)row * ep.ld_res;
-    if (full_cols && ((ep.ld_res & 3) == 0)) {
-      const float4* src = reinterpret_cast<const float4*>(res + col0);
+  if (ep.out_f32) {
+    uint8_t* o = slot + lane * 128;
+    if (ep.residual) {  // staged f32 residual at the output positions
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float4 r = src[q];
+        const float4 r = *reinterpret_cast<const float4*>(o + ((q ^ sw128) * 16));
         v[4 * q + 0] += r.x;
         v[4 * q + 1] += r.y;
         v[4 * q + 2] += r.z;
         v[4 * q + 3] += r.w;
       }
-    } else {
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < N) v[i] += res[col0 + i];
     }
-  }
-  if (ep.out_f32) {
-    uint8_t* o = stage;  // 32 rows x 128 B, 128B swizzle
 #pragma unroll
     for (int q = 0; q < 8; ++q)
-      *reinterpret_cast<float4*>(o + lane * 128 + ((q ^ (lane & 7)) * 16)) =
+      *reinterpret_cast<float4*>(o + ((q ^ sw128) * 16)) =
           make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else {
-    uint8_t* o = stage;  // 32 rows x 64 B, 64B swizzle
+    uint8_t* o = slot + lane * 64;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint4 w;
@@ -281,18 +288,17 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, const
       w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
       w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
       w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-      *reinterpret_cast<uint4*>(o + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = w;
+      *reinterpret_cast<uint4*>(o + ((q ^ sw64) * 16)) = w;
     }
   }
   fence_proxy_async_shared();
   __syncwarp();
   if (lane == 0) {
-    const uint8_t* o = stage;
     if (ep.flags & kEpiAccumulate)
-      tma_reduce_add_2d(tmOut, o, col0, row0);
+      tma_reduce_add_2d(tmOut, slot, col0, row0);
     else
-      tma_store_2d(tmOut, o, col0, row0);
-    if (aux_out) tma_store_2d(tmAux, stage + 2048, col0, row0);
+      tma_store_2d(tmOut, slot, col0, row0);
+    if (aux_out) tma_store_2d(tmAux, slot + 2048, col0, row0);
     bulk_commit_group();
   }
 }
@@ -302,8 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmOut,
-                      const __grid_constant__ CUtensorMap tmAux, GemmEpilogue ep, int M, int N,
-                      int K, int k_splits, int use_tma_store, uint32_t* err) {
+                      const __grid_constant__ CUtensorMap tmAux,
+                      const __grid_constant__ CUtensorMap tmIn, GemmEpilogue ep, int M, int N,
+                      int K, int k_splits, int use_tma_store, int in_kind, uint32_t* err) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -333,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ctl->tmem_empty[a], kEpiWarps);
     }
     mbar_init(&ctl->drain, 1);
+    for (int i = 0; i < kEpiWarps * 2; ++i) mbar_init(&ctl->epi_in[i], 1);
     ctl->abort = 0;
     fence_mbar_init();
   }
@@ -342,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (use_tma_store) {
       tma_prefetch_desc(&tmOut);
       tma_prefetch_desc(&tmAux);
+      if (in_kind != kInNone) tma_prefetch_desc(&tmIn);
     }
   }
   if (warp == 1) {
@@ -472,43 +481,100 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;               // TMEM lane quarter this warp may access
     const int ew = warp - 2;              // epilogue warp 0..7
     const int half = ew / 4;              // which half of the tile's columns
-    constexpr int kChunks = BN / 32 / 2;  // 32-column chunks per warp
+    constexpr int kChunks = BN / 32 / 2;  // 32-column chunks per warp and tile
     uint8_t* stage = staging + ew * kStageWarpBytes;
-    uint32_t local_tile = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local_tile) {
+    uint64_t* in_bar = &ctl->epi_in[ew * 2];
+    const float alpha = ep.alpha_ptr ? ep.alpha * __ldg(ep.alpha_ptr) : ep.alpha;
+    const bool tma_in = use_tma_store && in_kind != kInNone;
+    const int my_tiles =
+        (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * kChunks;
+    // chunk j of this warp: tile blockIdx.x + (j / kChunks) * gridDim.x, column chunk j % kChunks
+    auto chunk_at = [&](int j, int& row0, int& col0) -> bool {
       int tm, tn, ks;
-      tile_coords(t, tm, tn, ks);
-      const uint32_t acc = local_tile & 1;
-      const uint32_t acc_ph = (local_tile >> 1) & 1;
-      bool ok = mbar_wait_bounded(&ctl->tmem_full[acc], acc_ph, abort_flag, err, limit);
-      if (!__all_sync(0xffffffffu, ok)) break;  // keep the warp converged for tcgen05.ld
-      tc_fence_after();
-      const int row0 = tm * kBM + q * 32;
-      const int row = row0 + lane;
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      const int kb0 = ks * kb_per_split;
-      const bool empty_split = kb0 >= k_blocks_total;
-#pragma unroll 1
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int c = half * kChunks + cc;
-        const int col0 = tn * BN + c * 32;
-        uint32_t r[32];
-        tmem_ld_32cols(t_row + c * 32, r);
-        tmem_ld_wait();
-        if (cc == kChunks - 1) {
-          // Last read of this accumulator by this warp: hand it back early.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
-        }
-        if (col0 >= N || empty_split || row0 >= M) continue;
-        if (use_tma_store) {
-          // the previous chunk's store must have read the staging slot
-          if (lane == 0) bulk_wait_group_read<0>();
-          __syncwarp();
-          epilogue_chunk_tma(ep, &tmOut, &tmAux, stage, 0, row0, col0, lane, M, N, r);
+      tile_coords((int)blockIdx.x + (j / kChunks) * (int)gridDim.x, tm, tn, ks);
+      row0 = tm * kBM + q * 32;
+      col0 = tn * BN + (half * kChunks + j % kChunks) * 32;
+      return col0 < N && row0 < M && ks * kb_per_split < k_blocks_total;
+    };
+    // TMA prefetch of chunk j's epilogue input into its slot (lane 0 issues)
+    auto issue_in = [&](int j) -> bool {
+      int row0, col0;
+      if (!chunk_at(j, row0, col0)) return false;
+      if (lane == 0) {
+        uint64_t* bar = &in_bar[j & 1];
+        uint8_t* slot = stage + (j & 1) * kSlotBytes;
+        if (in_kind == kInResidual) {
+          mbar_arrive_expect_tx(bar, 4096);
+          tma_load_2d(slot, &tmIn, bar, col0, row0);
         } else {
-          epilogue_chunk(ep, row, col0, M, N, r);
+          mbar_arrive_expect_tx(bar, 2048);
+          tma_load_2d(slot + 2048, &tmIn, bar, col0, row0);
+        }
+      }
+      return true;
+    };
+    uint32_t in_ph = 0;    // parity of the next completion of each slot's barrier
+    uint32_t pending = 0;  // slots with an input load issued but not yet consumed
+    if (tma_in && total > 0 && issue_in(0)) pending |= 1u;
+    bool aborted = false;
+    for (int j = 0; j < total; ++j) {
+      const int cc = j % kChunks;
+      const uint32_t local_tile = (uint32_t)(j / kChunks);
+      const uint32_t acc = local_tile & 1;
+      if (cc == 0) {
+        const bool ok =
+            mbar_wait_bounded(&ctl->tmem_full[acc], (local_tile >> 1) & 1, abort_flag, err, limit);
+        if (!__all_sync(0xffffffffu, ok)) {  // keep the warp converged for tcgen05.ld
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+      }
+      int row0, col0;
+      const bool live = chunk_at(j, row0, col0);
+      uint32_t r[32];
+      tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN +
+                         (uint32_t)((half * kChunks + cc) * 32),
+                     r);
+      tmem_ld_wait();
+      if (cc == kChunks - 1) {
+        // Last read of this accumulator by this warp: hand it back early.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
+      }
+      if (use_tma_store) {
+        // the other slot was last read by the store of chunk j-1
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+        if (tma_in && j + 1 < total && issue_in(j + 1)) pending |= 1u << ((j + 1) & 1);
+      }
+      if (!live) continue;
+      if (use_tma_store) {
+        uint8_t* slot = stage + (j & 1) * kSlotBytes;
+        if (tma_in) {
+          const uint32_t sb = (uint32_t)(j & 1);
+          const bool ok = mbar_wait_bounded(&in_bar[sb], (in_ph >> sb) & 1u, abort_flag, err, limit);
+          in_ph ^= 1u << sb;
+          pending &= ~(1u << sb);
+          if (!__all_sync(0xffffffffu, ok)) {
+            aborted = true;
+            break;
+          }
+        }
+        epilogue_chunk_tma(ep, alpha, &tmOut, &tmAux, slot, row0, col0, lane, N, r);
+      } else {
+        epilogue_chunk(ep, row0 + lane, col0, M, N, r);
+      }
+    }
+    if (aborted && lane == 0) {
+      // give input loads still in flight a bounded chance to land before exit
+      for (uint32_t sb = 0; sb < 2; ++sb) {
+        if (!(pending & (1u << sb))) continue;
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&in_bar[sb], (in_ph >> sb) & 1u)) {
+          if (global_timer_ns() - t0 > 100000000ull) break;
         }
       }
     }
@@ -676,30 +742,52 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   }
 
-  // TMA-store epilogue when the output rows are 16-byte aligned
-  CUtensorMap tmOut, tmAux;
+  // TMA-store epilogue when every tensor it moves is 16-byte aligned (base and
+  // row pitch) and the combination fits a 4 KB staging slot: f32 out (+ f32
+  // residual in), or bf16 out (+ bf16 pre-activation out for GELU, or bf16
+  // GELU' operand in). Anything else takes the direct-store epilogue.
+  CUtensorMap tmOut, tmAux, tmIn;
   std::memset(&tmOut, 0, sizeof(tmOut));
   std::memset(&tmAux, 0, sizeof(tmAux));
+  std::memset(&tmIn, 0, sizeof(tmIn));
+  auto aligned = [](const void* p, int ld, int es) {
+    return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((uint64_t)ld * es) % 16 == 0;
+  };
   const bool f32 = g.ep.out_f32 != 0;
-  const uint64_t out_es = f32 ? 4 : 2;
-  bool use_tma = (reinterpret_cast<uintptr_t>(g.ep.out) % 16 == 0) &&
-                 ((uint64_t)g.ep.ld_out * out_es) % 16 == 0;
   const bool aux_out = (g.ep.flags & kEpiGelu) && g.ep.aux;
-  if (aux_out)
-    use_tma = use_tma && !f32 && (reinterpret_cast<uintptr_t>(g.ep.aux) % 16 == 0) &&
-              ((uint64_t)g.ep.ld_aux * 2) % 16 == 0;
+  const bool dgelu = (g.ep.flags & kEpiDGelu) != 0;
+  const bool res = g.ep.residual != nullptr;
+  bool use_tma = aligned(g.ep.out, g.ep.ld_out, f32 ? 4 : 2);
+  if (aux_out || dgelu) use_tma = use_tma && !f32 && aligned(g.ep.aux, g.ep.ld_aux, 2);
+  if (res) use_tma = use_tma && f32 && aligned(g.ep.residual, g.ep.ld_res, 4);
+  if (aux_out && dgelu) use_tma = false;
+  int in_kind = kInNone;
   if (use_tma) use_tma = make_out_tmap(&tmOut, g.ep.out, f32, g.N, g.M, g.ep.ld_out);
   if (use_tma && aux_out) use_tma = make_out_tmap(&tmAux, g.ep.aux, false, g.N, g.M, g.ep.ld_aux);
+  if (use_tma && res) {
+    use_tma = make_out_tmap(&tmIn, const_cast<float*>(g.ep.residual), true, g.N, g.M, g.ep.ld_res);
+    in_kind = kInResidual;
+  } else if (use_tma && dgelu) {
+    use_tma = make_out_tmap(&tmIn, g.ep.aux, false, g.N, g.M, g.ep.ld_aux);
+    in_kind = kInAux;
+  }
+  if (!use_tma) in_kind = kInNone;
   auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    attr_set = true;
+  // the dynamic shared-memory opt-in is a per-device function attribute
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit);
   }
   const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.k_splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmOut, tmAux, g.ep, g.M, g.N, g.K,
-                                                     g.k_splits, use_tma ? 1 : 0,
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N,
+                                                     g.K, g.k_splits, use_tma ? 1 : 0, in_kind,
                                                      g.err ? g.err : default_err_word());
   note_launch();
   return cudaGetLastError();

@@ -124,6 +124,9 @@ namespace flodl {
 // dh = dy * gelu'(h), all bf16 [n]
 cudaError_t launch_gelu_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* h, __nv_bfloat16* dh,
                             int64_t n, cudaStream_t st);
+// y = gelu(x), dydx = gelu'(x), f32 (the epilogue math, for numerics tests)
+cudaError_t launch_gelu_eval_f32(const float* x, float* y, float* dydx, int64_t n,
+                                 cudaStream_t st);
 // y = gelu(x) bf16 -> bf16
 cudaError_t launch_gelu_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n, cudaStream_t st);
 }  // namespace flodl

@@ -312,12 +312,39 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 }
 
 // ---------------------------------------------------------------- math helpers
+// erf for the GEMM epilogues: Abramowitz & Stegun, Handbook of Mathematical
+// Functions, eq. 7.1.28 (after Hastings):
+//   erf(x) = 1 - 1 / (1 + a1 x + a2 x^2 + ... + a6 x^6)^16,  x >= 0,
+//   |error| <= 3e-7,
+// extended to x < 0 by oddness. One reciprocal and eleven multiply-adds; the
+// outputs it feeds are rounded to bf16 (relative step 2^-8), far coarser than
+// the approximation error. The polynomial is evaluated at min(|x|, 8), where
+// the result is already 1 to single precision. The reciprocal is the hardware
+// approximation (rel. error ~2^-23), negligible after the subtraction from 1.
+__device__ __forceinline__ float erf_as7128(float x) {
+  const float ax = fminf(fabsf(x), 8.0f);
+  float p = 0.0000430638f;
+  p = fmaf(p, ax, 0.0002765672f);
+  p = fmaf(p, ax, 0.0001520143f);
+  p = fmaf(p, ax, 0.0092705272f);
+  p = fmaf(p, ax, 0.0422820123f);
+  p = fmaf(p, ax, 0.0705230784f);
+  p = fmaf(p, ax, 1.0f);
+  p = p * p;  // ^2
+  p = p * p;  // ^4
+  p = p * p;  // ^8
+  p = p * p;  // ^16
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(p));
+  return copysignf(1.0f - r, x);
+}
+
 __device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+  return 0.5f * x * (1.0f + erf_as7128(x * 0.70710678118654752f));
 }
 // d/dx of the erf GELU.
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+  const float cdf = 0.5f * (1.0f + erf_as7128(x * 0.70710678118654752f));
   const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
   return cdf + x * pdf;
 }

@@ -203,13 +203,21 @@ class BertForMaskedLM(Module):
         dev = torch.device(device) if device is not None else torch.device("cpu")
         self._grad_anchor = torch.zeros((), device=dev, requires_grad=True)
 
+    def move_to_device(self, device):
+        super().move_to_device(device)
+        self._grad_anchor = torch.zeros((), device=torch.device(device), requires_grad=True)
+        return self
+
     def forward(self, ids, token_type_ids=None, attention_mask=None):
         return self.cls(self.bert(ids, token_type_ids, attention_mask))
 
-    def loss(self, ids, labels, token_type_ids=None, attention_mask=None):
-        """Masked-LM loss: mean cross-entropy over positions whose label != -100."""
+    def loss(self, ids, labels, token_type_ids=None, attention_mask=None, masked_rows=None):
+        """Masked-LM loss: mean cross-entropy over positions whose label != -100.
+        ``masked_rows`` (CUDA training path) fixes how many positions the head
+        processes, which avoids a host sync (needed for CUDA-graph capture)."""
         if ids.is_cuda and self.training and torch.is_grad_enabled():
-            return ops.bert_mlm_train_loss(self, ids, labels, token_type_ids, attention_mask)
+            return ops.bert_mlm_train_loss(self, ids, labels, token_type_ids, attention_mask,
+                                           masked_rows)
         h = self.bert(ids, token_type_ids, attention_mask)
         sel = labels.reshape(-1) != -100
         hm = h.reshape(-1, h.shape[-1])[sel]

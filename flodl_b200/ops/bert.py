@@ -25,7 +25,7 @@ from .transformer import _empty, _wgrad
 
 
 class PostBlockParams:
-    __slots__ = ("wqkv", "bqkv", "wo", "bo", "ln1_w", "ln1_b", "w1", "b1", "w2", "b2", "eps")
+    __slots__ = ("wqkv", "bqkv", "wo", "bo", "ln1_w", "ln1_b", "w1", "b1", "w2", "b2", "eps", "_ln2")
 
     def __init__(self, layer):
         a = layer.attention
@@ -117,7 +117,7 @@ def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, 
 
 class _BertMLMTrainFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, anchor, model, ids, labels, token_type_ids, attention_mask):
+    def forward(ctx, anchor, model, ids, labels, token_type_ids, attention_mask, masked_rows):
         K = C()
         cfg = model.config
         B, S = ids.shape
@@ -142,8 +142,20 @@ class _BertMLMTrainFn(torch.autograd.Function):
             saved.append(sv)
         # MLM head on the masked rows
         lab = labels.reshape(-1)
-        sel = (lab != -100).nonzero(as_tuple=True)[0]
-        Tm = int(sel.numel())
+        if masked_rows is None:
+            sel = (lab != -100).nonzero(as_tuple=True)[0]  # host sync for the count
+            Tm = int(sel.numel())
+            lab_sel = lab.index_select(0, sel).contiguous()
+        else:
+            # fixed row budget: no host sync, so the step can be graph-captured.
+            # Padding rows point at row 0 and carry label -100 (ignored); masked
+            # rows beyond the budget are dropped.
+            Tm = int(masked_rows)
+            keep = lab != -100
+            sel = torch.nonzero_static(keep, size=Tm, fill_value=0).reshape(-1)
+            valid = torch.arange(Tm, device=dev) < keep.sum()
+            lab_sel = torch.where(valid, lab.index_select(0, sel),
+                                  torch.full_like(sel, -100)).contiguous()
         head = model.cls
         hm16 = x16.index_select(0, sel)
         t = _empty((Tm, Cd), torch.bfloat16, dev)
@@ -161,7 +173,7 @@ class _BertMLMTrainFn(torch.autograd.Function):
         loss = torch.zeros((), device=dev, dtype=torch.float32)
         inv = _empty((), torch.float32, dev)
         dlogits = torch.empty_like(logits)
-        K.softmax_ce(logits, lab.index_select(0, sel).contiguous(), loss, inv, dlogits, -100, 0.0)
+        K.softmax_ce(logits, lab_sel, loss, inv, dlogits, -100, 0.0)
         ctx.model = model
         ctx.blocks = blocks
         ctx.saved_blocks = saved
@@ -225,9 +237,12 @@ class _BertMLMTrainFn(torch.autograd.Function):
                   emb.LayerNorm.weight, emb.LayerNorm.bias):
             grad_ready(q)
         ctx.saved_blocks = None
-        return None, None, None, None, None, None
+        return None, None, None, None, None, None, None
 
 
-def bert_mlm_train_loss(model, ids, labels, token_type_ids=None, attention_mask=None):
+def bert_mlm_train_loss(model, ids, labels, token_type_ids=None, attention_mask=None,
+                        masked_rows=None):
+    """Mean MLM loss over positions whose label is not -100. ``masked_rows``
+    (optional) fixes the number of head rows so no host sync is needed."""
     return _BertMLMTrainFn.apply(model._grad_anchor, model, ids, labels, token_type_ids,
-                                 attention_mask)
+                                 attention_mask, masked_rows)

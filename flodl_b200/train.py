@@ -26,7 +26,8 @@ class StepRunner:
     @classmethod
     def for_state(cls, state, graph_step=None, eager_step=None) -> "StepRunner":
         g, l = graph_step if graph_step is not None else (None, None)
-        return cls(eager_step, [state["ids"], state["tgt"]], g, l)
+        inputs = state["inputs"] if "inputs" in state else [state["ids"], state["tgt"]]
+        return cls(eager_step, inputs, g, l)
 
     @classmethod
     def capture(cls, step_fn: Callable[[], torch.Tensor], inputs: Sequence[torch.Tensor],

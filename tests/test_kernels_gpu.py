@@ -182,3 +182,21 @@ def test_linear_op_fwd_bwd_gelu_residual():
         rel = ((got - ref).norm() / ref.norm()).item()
         assert rel < 1e-2, rel
     torch.testing.assert_close(res.grad, rr.grad)
+
+
+def test_gelu_epilogue_math_matches_erf_gelu():
+    """The epilogue GELU (erf after Abramowitz & Stegun 7.1.28) against
+    PyTorch's erf GELU and its derivative, on a dense grid."""
+    from flodl_b200._ext import cuda_ext
+    x = torch.linspace(-12, 12, 1 << 20, device="cuda", dtype=torch.float64)
+    xf = x.float().contiguous()
+    y = torch.empty_like(xf)
+    d = torch.empty_like(xf)
+    cuda_ext().gelu_eval_f32(xf, y, d)
+    ref = F.gelu(xf.double())
+    cdf = 0.5 * (1 + torch.erf(xf.double() / 2 ** 0.5))
+    dref = cdf + xf.double() * torch.exp(-0.5 * xf.double() ** 2) / (2 * torch.pi) ** 0.5
+    err = (y.double() - ref).abs() / (1 + xf.double().abs())
+    assert err.max().item() < 2e-6, err.max().item()
+    derr = (d.double() - dref).abs()
+    assert derr.max().item() < 2e-6, derr.max().item()
