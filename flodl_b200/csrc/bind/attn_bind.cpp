@@ -35,7 +35,7 @@ void flash_fwd(const Tensor& qkv, Tensor& out, Tensor& lse2, int64_t B, int64_t 
 
 void flash_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse2,
                Tensor& dqkv, int64_t B, int64_t S, int64_t H, int64_t D, bool causal,
-               double scale, const optional<Tensor>& key_pad) {
+               double scale, const optional<Tensor>& key_pad, const optional<Tensor>& dbias) {
   FL_CHECK_BF16(dout); FL_CHECK_BF16(qkv); FL_CHECK_BF16(out); FL_CHECK_BF16(dqkv);
   FL_CHECK(dout.is_contiguous() && qkv.is_contiguous() && out.is_contiguous() &&
                dqkv.is_contiguous(), "layout");
@@ -52,6 +52,11 @@ void flash_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const T
   a.delta = delta.data_ptr<float>();
   a.dq_acc = dq_acc.data_ptr<float>();
   if (key_pad) a.key_pad = reinterpret_cast<const uint8_t*>(key_pad->data_ptr());
+  if (dbias) {
+    FL_CHECK_F32(*dbias);
+    FL_CHECK(dbias->is_contiguous() && dbias->numel() == 3 * H * D, "dbias must be f32 [3*H*D]");
+    a.dbias = dbias->data_ptr<float>();
+  }
   a.B = (int)B; a.S = (int)S; a.H = (int)H; a.D = (int)D;
   a.causal = causal;
   a.scale = (float)scale;
@@ -68,5 +73,6 @@ void register_attention(py::module& m) {
         py::arg("scale"), py::arg("key_pad") = py::none());
   m.def("flash_attn_bwd", &flash_bwd, py::arg("dout"), py::arg("qkv"), py::arg("out"),
         py::arg("lse2"), py::arg("dqkv"), py::arg("B"), py::arg("S"), py::arg("H"), py::arg("D"),
-        py::arg("causal"), py::arg("scale"), py::arg("key_pad") = py::none());
+        py::arg("causal"), py::arg("scale"), py::arg("key_pad") = py::none(),
+        py::arg("dbias") = py::none());
 }

@@ -61,12 +61,8 @@ void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor&
   a.rows = (int)(x.numel() / C);
   a.C = C;
   c10::cuda::CUDAGuard guard(x.device());
-  Tensor partials;
-  if (a.dgamma || a.dbeta || a.colsum) {
-    a.partial_blocks = flodl::ln_bwd_partial_blocks(a.rows);
-    partials = at::empty({3 * (int64_t)a.partial_blocks * C}, x.options().dtype(at::kFloat));
-    a.partials = partials.data_ptr<float>();
-  }
+  // column reductions (dgamma, dbeta, bias gradient) accumulate with one
+  // atomic per column and block: no scratch, no second pass
   FL_CUDA_OK(flodl::launch_ln_bwd(a, cur_stream()));
 }
 
@@ -78,10 +74,9 @@ void colsum(const Tensor& m, Tensor& out, const optional<Tensor>& scale) {
   c10::cuda::CUDAGuard guard(m.device());
   const int rows = (int)(m.numel() / C);
   const int nb = flodl::colsum_partial_blocks(rows);
-  Tensor partials = at::empty({(int64_t)nb * C}, m.options().dtype(at::kFloat));
-  FL_CUDA_OK(flodl::launch_colsum2(m.data_ptr(), m.scalar_type() == at::kBFloat16, ptr<float>(out),
-                                   rows, C, partials.data_ptr<float>(), nb, cur_stream(),
-                                   opt_ptr<const float>(scale)));
+  FL_CUDA_OK(flodl::launch_colsum_atomic(m.data_ptr(), m.scalar_type() == at::kBFloat16,
+                                         ptr<float>(out), rows, C, nb, cur_stream(),
+                                         opt_ptr<const float>(scale)));
 }
 
 // Returns nothing; writes loss (scalar, overwritten) and dlogits.
@@ -221,6 +216,19 @@ void gelu_bwd(const Tensor& dy, const Tensor& h, Tensor& dh) {
                                     ptr<__nv_bfloat16>(dh), h.numel(), cur_stream()));
 }
 
+void mul_bf16(const Tensor& a, const Tensor& b, Tensor& y) {
+  FL_CHECK_CUDA(a);
+  FL_CHECK_BF16(a);
+  FL_CHECK_BF16(b);
+  FL_CHECK_BF16(y);
+  FL_CHECK(a.is_contiguous() && b.is_contiguous() && y.is_contiguous() &&
+               a.numel() == b.numel() && a.numel() == y.numel(),
+           "mul_bf16 layout");
+  c10::cuda::CUDAGuard guard(a.device());
+  FL_CUDA_OK(flodl::launch_mul_bf16(ptr<__nv_bfloat16>(a), ptr<__nv_bfloat16>(b),
+                                    ptr<__nv_bfloat16>(y), a.numel(), cur_stream()));
+}
+
 void gelu_eval_f32(const Tensor& x, Tensor& y, Tensor& dydx) {
   FL_CHECK_CUDA(x);
   FL_CHECK_F32(x);
@@ -268,6 +276,7 @@ void register_elementwise(py::module& m) {
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_eval_f32", &gelu_eval_f32);
+  m.def("mul_bf16", &mul_bf16);
 }
 
 void register_optim(py::module& m) {

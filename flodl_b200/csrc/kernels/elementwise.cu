@@ -38,7 +38,23 @@ __global__ void gelu_eval_f32_kernel(const float* __restrict__ x, float* __restr
   }
 }
 
+__global__ void mul_bf16_kernel(const __nv_bfloat16* __restrict__ a,
+                                const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = __float2bfloat16_rn(__bfloat162float(a[i]) * __bfloat162float(b[i]));
+}
+
 }  // namespace
+
+cudaError_t launch_mul_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* y,
+                            int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  mul_bf16_kernel<<<grid_1d(n, 256), 256, 0, st>>>(a, b, y, n);
+  note_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gelu_eval_f32(const float* x, float* y, float* dydx, int64_t n,
                                  cudaStream_t st) {

@@ -507,41 +507,104 @@ struct BwdSmem {
 };
 
 // delta[b,h,s] = sum_d dO * O ; also zeroes the f32 dQ accumulator rows.
+// A warp handles four (token, head) rows per step: eight lanes per row, each
+// with 16-byte loads of dO and O (8 values) and a 3-step shuffle reduction.
 __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
                                      const __nv_bfloat16* __restrict__ out, float* __restrict__ delta,
                                      float* __restrict__ dq_acc, int B, int S, int H) {
   const int C = H * kD;
   const int64_t rows = (int64_t)B * S * H;
-  const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int64_t warp_g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
-  const int nw = gridDim.x * blockDim.x / 32;
-  for (int64_t rw = warp_g; rw < rows; rw += nw) {
-    const int64_t tok = rw / H;
-    const int h = (int)(rw % H);
-    const __nv_bfloat16* a = dout + tok * C + h * kD;
-    const __nv_bfloat16* o = out + tok * C + h * kD;
-    float2 x = unpack_bf16x2(reinterpret_cast<const uint32_t*>(a)[lane]);
-    float2 y = unpack_bf16x2(reinterpret_cast<const uint32_t*>(o)[lane]);
-    float s = x.x * y.x + x.y * y.y;
+  const int sub = lane >> 3, part = lane & 7;
+  const int64_t nw = (int64_t)gridDim.x * blockDim.x / 32;
+#pragma unroll 2
+  for (int64_t base = warp_g * 4; base < rows; base += nw * 4) {
+    const int64_t rw = base + sub;
+    float s = 0.f;
+    int64_t tok = 0;
+    int h = 0;
+    if (rw < rows) {
+      tok = rw / H;
+      h = (int)(rw % H);
+      const uint4 x = *reinterpret_cast<const uint4*>(dout + tok * C + h * kD + part * 8);
+      const uint4 y = *reinterpret_cast<const uint4*>(out + tok * C + h * kD + part * 8);
+      const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    const int b = (int)(tok / S), si = (int)(tok % S);
-    if (lane == 0) delta[((int64_t)b * H + h) * S + si] = s;
-    float2* dq = reinterpret_cast<float2*>(dq_acc + tok * C + h * kD);
-    dq[lane] = make_float2(0.f, 0.f);
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = unpack_bf16x2(xs[k]), c = unpack_bf16x2(ys[k]);
+        s = fmaf(a.x, c.x, fmaf(a.y, c.y, s));
+      }
+      float4* dq = reinterpret_cast<float4*>(dq_acc + tok * C + h * kD + part * 8);
+      dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (rw < rows && part == 0) {
+      const int bb = (int)(tok / S), si = (int)(tok % S);
+      delta[((int64_t)bb * H + h) * S + si] = s;
+    }
   }
 }
 
-// dqkv[:, q cols] = bf16(dq_acc * scale)
-__global__ void flash_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv,
-                                      int64_t T, int C, float scale) {
-  const int64_t n = T * C / 2;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
-    const int64_t t = (2 * i) / C;
-    const int c = (int)((2 * i) % C);
-    float2 v = reinterpret_cast<const float2*>(dq_acc)[i];
-    *reinterpret_cast<uint32_t*>(dqkv + t * 3 * C + c) = pack_bf16x2(v.x * scale, v.y * scale);
+// dqkv[:, q cols] = bf16(dq_acc * scale). With dbias, also the bias gradient
+// of the packed projection: dbias[c] += sum over rows of dqkv[:, c] for all
+// 3C columns (the dK/dV columns were written by the main kernel), one atomic
+// per column and row slice. Thread = 8 consecutive columns of a row.
+constexpr int kPostLanes = 4;  // row lanes per block of the finalize kernel
+__global__ void __launch_bounds__(256 * kPostLanes) flash_bwd_post_kernel(
+    const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int T, int C, float scale,
+    float* __restrict__ dbias, int rows_per_block) {
+  const int groups = 3 * C / 8;
+  const int g = blockIdx.y * 256 + (threadIdx.x & 255);
+  const int rl = threadIdx.x >> 8;  // row lane
+  const int c0 = g * 8;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(T, r0 + rows_per_block);
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  if (g < groups) {
+#pragma unroll 4
+    for (int r = r0 + rl; r < r1; r += kPostLanes) {
+      uint4* dst = reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * C + c0);
+      uint4 w;
+      if (c0 < C) {
+        const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * C + c0);
+        const float4 a = src[0], b = src[1];
+        w.x = pack_bf16x2(a.x * scale, a.y * scale);
+        w.y = pack_bf16x2(a.z * scale, a.w * scale);
+        w.z = pack_bf16x2(b.x * scale, b.y * scale);
+        w.w = pack_bf16x2(b.z * scale, b.w * scale);
+        *dst = w;
+      } else if (dbias) {
+        w = *dst;
+      } else {
+        continue;
+      }
+      if (dbias) {
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = unpack_bf16x2(ws[h]);
+          acc[2 * h] += f.x;
+          acc[2 * h + 1] += f.y;
+        }
+      }
+    }
+  }
+  if (dbias == nullptr) return;  // uniform across the block
+  __shared__ float red[256 * kPostLanes][9];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[threadIdx.x][e] = acc[e];
+  __syncthreads();
+  if (rl == 0 && g < groups) {
+    for (int l = 1; l < kPostLanes; ++l)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += red[threadIdx.x + 256 * l][e];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) atomicAdd(dbias + c0 + e, acc[e]);
   }
 }
 
@@ -892,7 +955,7 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   if (!make_map_3d(&tm_qkv, a.qkv, a.B, a.S, 3 * C)) return cudaErrorInvalidValue;
   if (!make_map_3d(&tm_do, a.dout, a.B, a.S, C)) return cudaErrorInvalidValue;
   const int64_t rows = (int64_t)a.B * a.S * a.H;
-  int pre_blocks = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms() * 16);
+  int pre_blocks = (int)std::min<int64_t>((rows + 31) / 32, (int64_t)num_sms() * 16);
   flash_bwd_pre_kernel<<<pre_blocks, 256, 0, st>>>(a.dout, a.out, a.delta, a.dq_acc, a.B, a.S, a.H);
   const int smem = (int)sizeof(BwdSmem) + 1024;
   {
@@ -912,9 +975,12 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   flash_bwd_kernel<<<grid, kBwdThreads, smem, st>>>(tm_qkv, tm_do, a.lse2, a.delta, a.dq_acc, a.dqkv,
                                             a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
                                             a.err ? a.err : default_err_word());
-  const int64_t T = (int64_t)a.B * a.S;
-  int post_blocks = (int)std::min<int64_t>((T * C / 2 + 255) / 256, (int64_t)num_sms() * 16);
-  flash_bwd_post_kernel<<<post_blocks, 256, 0, st>>>(a.dq_acc, a.dqkv, T, C, a.scale);
+  const int T = a.B * a.S;
+  const int gy = (3 * C / 8 + 255) / 256;
+  const int gx = std::max(1, std::min(T, num_sms() / gy));
+  const int rpb = (T + gx - 1) / gx;
+  flash_bwd_post_kernel<<<dim3(gx, gy), 256 * kPostLanes, 0, st>>>(a.dq_acc, a.dqkv, T, C,
+                                                                    a.scale, a.dbias, rpb);
   note_launch(3);
   return cudaGetLastError();
 }

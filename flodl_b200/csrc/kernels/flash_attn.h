@@ -18,6 +18,7 @@ struct FlashArgs {
   __nv_bfloat16* dqkv = nullptr;       // [B*S, 3*H*D]
   float* delta = nullptr;              // [B, H, S] scratch
   float* dq_acc = nullptr;             // [B*S, H*D] f32 scratch
+  float* dbias = nullptr;              // [3*H*D] f32: += column sums of dqkv (nullable)
   int B = 0, S = 0, H = 0, D = 0;
   bool causal = false;
   float scale = 1.f;

@@ -42,7 +42,7 @@ __device__ uint64_t g_wait_limit_ns = 2000000000ull;  // 2 s
 
 // Epilogue staging: each epilogue warp owns two 4 KB slots of shared memory.
 // A slot holds one 32x32 output chunk (f32, 128B swizzle) or one bf16 output
-// chunk plus one bf16 pre-activation chunk (2 KB each, 64B swizzle). Chunks
+// chunk plus one bf16 GELU' chunk (2 KB each, 64B swizzle). Chunks
 // leave through TMA stores (full, coalesced lines); epilogue inputs (residual,
 // GELU' operand) arrive through TMA loads into the slot of the chunk that
 // needs them while the previous chunk is being computed. Two slots let the
@@ -91,28 +91,29 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, 
     }
   }
   if (ep.flags & kEpiGelu) {
-    if (ep.aux) {  // keep the pre-activation for the backward pass
+    float dg[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) gelu_and_grad(v[i], v[i], dg[i]);
+    if (ep.aux) {  // keep GELU' for the backward pass
       __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
       if (full_cols && ((ep.ld_aux & 7) == 0)) {
         uint4* dst = reinterpret_cast<uint4*>(aux + col0);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
-          w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-          w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-          w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-          w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+          w.x = pack_bf16x2(dg[8 * q + 0], dg[8 * q + 1]);
+          w.y = pack_bf16x2(dg[8 * q + 2], dg[8 * q + 3]);
+          w.z = pack_bf16x2(dg[8 * q + 4], dg[8 * q + 5]);
+          w.w = pack_bf16x2(dg[8 * q + 6], dg[8 * q + 7]);
           dst[q] = w;
         }
       } else {
         for (int i = 0; i < 32; ++i)
-          if (col0 + i < N) aux[col0 + i] = __float2bfloat16_rn(v[i]);
+          if (col0 + i < N) aux[col0 + i] = __float2bfloat16_rn(dg[i]);
       }
     }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
   }
-  if (ep.flags & kEpiDGelu) {  // multiply by GELU'(pre-activation)
+  if (ep.flags & kEpiDGelu) {  // multiply by the stored GELU'
     const __nv_bfloat16* aux =
         reinterpret_cast<const __nv_bfloat16*>(ep.aux) + (size_t)row * ep.ld_aux;
     if (full_cols && ((ep.ld_aux & 7) == 0)) {
@@ -124,13 +125,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& ep, int row, 
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           float2 f = unpack_bf16x2(ws[h]);
-          v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
-          v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+          v[8 * q + 2 * h + 0] *= f.x;
+          v[8 * q + 2 * h + 1] *= f.y;
         }
       }
     } else {
       for (int i = 0; i < 32; ++i)
-        if (col0 + i < N) v[i] *= gelu_erf_grad(__bfloat162float(aux[col0 + i]));
+        if (col0 + i < N) v[i] *= __bfloat162float(aux[col0 + i]);
     }
   }
   if (ep.residual) {
@@ -201,8 +202,8 @@ enum EpiInput : int { kInNone = 0, kInResidual = 1, kInAux = 2 };
 // the chunk in the layout its tensor maps use: f32 rows of 128 B with the
 // 128-byte swizzle (chunk q of row r at q ^ (r & 7)), or bf16 rows of 64 B with
 // the 64-byte swizzle (q ^ ((r >> 1) & 3)) at offset 0 plus, for a second bf16
-// tensor (pre-activation out, or the GELU' input), at offset 2048. Inputs
-// (residual f32 / pre-activation bf16) were brought in by TMA at the same
+// tensor (GELU' out, or the GELU' input), at offset 2048. Inputs
+// (residual f32 / GELU' bf16) were brought in by TMA at the same
 // positions the outputs use, so each lane reads and writes its own row only.
 // Out-of-range rows/columns need no checks: TMA loads fill them with zeros and
 // TMA stores clip them; only the bias needs a bound.
@@ -234,22 +235,23 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
   const int sw128 = lane & 7;
   const bool aux_out = (ep.flags & kEpiGelu) && ep.aux;
   if (ep.flags & kEpiGelu) {
-    if (aux_out) {  // pre-activation, kept for the backward pass
+    float dg[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) gelu_and_grad(v[i], v[i], dg[i]);
+    if (aux_out) {  // GELU', kept for the backward pass
       uint8_t* a = slot + 2048 + lane * 64;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 w;
-        w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-        w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-        w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-        w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+        w.x = pack_bf16x2(dg[8 * q + 0], dg[8 * q + 1]);
+        w.y = pack_bf16x2(dg[8 * q + 2], dg[8 * q + 3]);
+        w.z = pack_bf16x2(dg[8 * q + 4], dg[8 * q + 5]);
+        w.w = pack_bf16x2(dg[8 * q + 6], dg[8 * q + 7]);
         *reinterpret_cast<uint4*>(a + ((q ^ sw64) * 16)) = w;
       }
     }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
   }
-  if (ep.flags & kEpiDGelu) {  // multiply by GELU'(pre-activation) staged at +2048
+  if (ep.flags & kEpiDGelu) {  // multiply by the stored GELU' (staged at +2048)
     const uint8_t* a = slot + 2048 + lane * 64;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -258,8 +260,8 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const float2 f = unpack_bf16x2(ws[h]);
-        v[8 * q + 2 * h + 0] *= gelu_erf_grad(f.x);
-        v[8 * q + 2 * h + 1] *= gelu_erf_grad(f.y);
+        v[8 * q + 2 * h + 0] *= f.x;
+        v[8 * q + 2 * h + 1] *= f.y;
       }
     }
   }
@@ -744,7 +746,7 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
 
   // TMA-store epilogue when every tensor it moves is 16-byte aligned (base and
   // row pitch) and the combination fits a 4 KB staging slot: f32 out (+ f32
-  // residual in), or bf16 out (+ bf16 pre-activation out for GELU, or bf16
+  // residual in), or bf16 out (+ bf16 GELU' out for GELU, or bf16
   // GELU' operand in). Anything else takes the direct-store epilogue.
   CUtensorMap tmOut, tmAux, tmIn;
   std::memset(&tmOut, 0, sizeof(tmOut));

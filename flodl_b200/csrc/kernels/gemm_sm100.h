@@ -7,8 +7,8 @@
 namespace flodl {
 
 enum GemmEpiFlags : int {
-  kEpiGelu = 1,        // out = gelu(acc + bias); pre-activation -> aux (if aux != null)
-  kEpiDGelu = 2,       // out = (acc) * gelu'(aux)
+  kEpiGelu = 1,        // out = gelu(acc + bias); GELU'(acc + bias) -> aux (if aux != null)
+  kEpiDGelu = 2,       // out = acc * aux   (aux = GELU' kept by the forward epilogue)
   kEpiAccumulate = 4,  // out(f32) += result (atomic, also used for split-K)
 };
 
@@ -19,7 +19,7 @@ struct GemmEpilogue {
   const float* bias = nullptr;      // f32 [N] or null
   const float* residual = nullptr;  // f32 [M, ld_res] or null (added last)
   int ld_res = 0;
-  void* aux = nullptr;  // bf16 [M, ld_aux]: pre-activation out (gelu) / in (dgelu)
+  void* aux = nullptr;  // bf16 [M, ld_aux]: GELU' out (gelu) / in (dgelu)
   int ld_aux = 0;
   int flags = 0;
   float alpha = 1.f;

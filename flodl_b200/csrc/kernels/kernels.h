@@ -44,6 +44,10 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
                           const float* scale = nullptr);
 // Two-stage (deterministic) column sum; partials is scratch [nblocks, C].
+// Single-pass column sums: nblocks row slices, one atomic per column and
+// slice into out (accumulating; optionally scaled by *scale).
+cudaError_t launch_colsum_atomic(const void* m, bool bf16, float* out, int rows, int C,
+                                 int nblocks, cudaStream_t st, const float* scale = nullptr);
 cudaError_t launch_colsum2(const void* m, bool bf16, float* out, int rows, int C, float* partials,
                            int nblocks, cudaStream_t st, const float* scale = nullptr);
 int colsum_partial_blocks(int rows);
@@ -123,6 +127,9 @@ cudaError_t launch_cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cu
 namespace flodl {
 // dh = dy * gelu'(h), all bf16 [n]
 cudaError_t launch_gelu_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* h, __nv_bfloat16* dh,
+                            int64_t n, cudaStream_t st);
+// y = a * b elementwise, bf16 (e.g. dy * GELU' kept by a GELU epilogue)
+cudaError_t launch_mul_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* y,
                             int64_t n, cudaStream_t st);
 // y = gelu(x), dydx = gelu'(x), f32 (the epilogue math, for numerics tests)
 cudaError_t launch_gelu_eval_f32(const float* x, float* y, float* dydx, int64_t n,

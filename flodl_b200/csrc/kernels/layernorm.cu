@@ -15,6 +15,8 @@
 #include "sm100_ptx.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace flodl {
 
 namespace {
@@ -265,13 +267,15 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
 // Column sums, first pass: block b sums rows [b*R, (b+1)*R) of a [rows, C]
 // matrix; thread owns 8 consecutive columns (16-byte loads), several row
 // lanes per block when C is narrow. Writes partials[b][c].
-template <typename T>
-__global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict__ m,
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT) colsum_partial_kernel(const T* __restrict__ m,
                                                              float* __restrict__ partials,
-                                                             int rows, int C, int rows_per_block) {
+                                                             int rows, int C, int rows_per_block,
+                                                             float* __restrict__ out,
+                                                             const float* __restrict__ scale) {
   const int groups = C / 8;                       // 8-column groups per row
   const int tpr = groups < 256 ? groups : 256;    // threads per row slice
-  const int lanes = 256 / tpr;                    // row slices per block
+  const int lanes = NT / tpr;                     // row slices per block
   const int g0 = blockIdx.y * 256;                // column-group offset of this block
   const int tid = threadIdx.x;
   const int gi = g0 + (tid % tpr);
@@ -282,7 +286,7 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   if (slice < lanes && gi < groups) {
-#pragma unroll 4
+#pragma unroll 8
     for (int r = r0 + slice; r < r1; r += lanes) {
       const T* src = m + (size_t)r * C + gi * 8;
       float v[8];
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict
       for (int e = 0; e < 8; ++e) acc[e] += v[e];
     }
   }
-  __shared__ float red[256][9];
+  __shared__ float red[NT][9];
 #pragma unroll
   for (int e = 0; e < 8; ++e) red[tid][e] = acc[e];
   __syncthreads();
@@ -308,8 +312,15 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const T* __restrict
     for (int l = 1; l < lanes; ++l)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] += red[tid + l * tpr][e];
+    if (partials) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) partials[(size_t)blockIdx.x * C + gi * 8 + e] = acc[e];
+      for (int e = 0; e < 8; ++e) partials[(size_t)blockIdx.x * C + gi * 8 + e] = acc[e];
+    } else {
+      // single pass: one atomic per column and block
+      const float sc = scale ? __ldg(scale) : 1.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(out + gi * 8 + e, acc[e] * sc);
+    }
   }
 }
 
@@ -365,7 +376,9 @@ cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st) {
 
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
   if (a.C % 4 != 0) return cudaErrorInvalidValue;
-  const int grid = a.partials ? a.partial_blocks : grid_for_rows(a.rows);
+  // with partials: two deterministic passes; without: one pass, one atomic
+  // per column and block (grid capped at two blocks per SM)
+  const int grid = a.partials ? a.partial_blocks : std::min(grid_for_rows(a.rows), num_sms() * 2);
   if (a.x_bf16) {
     FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
                                a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma, a.dres,
@@ -390,7 +403,9 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
 int ln_bwd_partial_blocks(int rows) { return grid_for_rows(rows) < num_sms() * 4 ? grid_for_rows(rows) : num_sms() * 4; }
 
 int colsum_partial_blocks(int rows) {
-  int b = num_sms() * 2;
+  // one row slice per SM: enough loads in flight (8-deep unrolled) to stream
+  // at HBM speed, and only num_sms atomics per column in the single-pass mode
+  int b = num_sms();
   return rows < b ? (rows > 0 ? rows : 1) : b;
 }
 
@@ -400,14 +415,30 @@ cudaError_t launch_colsum2(const void* m, bool bf16, float* out, int rows, int C
   const int rpb = (rows + nblocks - 1) / nblocks;
   dim3 g1(nblocks, (C / 8 + 255) / 256);
   if (bf16)
-    colsum_partial_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>((const __nv_bfloat16*)m, partials, rows,
-                                                             C, rpb);
+    colsum_partial_kernel<__nv_bfloat16, 256><<<g1, 256, 0, st>>>(
+        (const __nv_bfloat16*)m, partials, rows, C, rpb, nullptr, nullptr);
   else
-    colsum_partial_kernel<float><<<g1, 256, 0, st>>>((const float*)m, partials, rows, C, rpb);
+    colsum_partial_kernel<float, 256><<<g1, 256, 0, st>>>((const float*)m, partials, rows, C, rpb,
+                                                          nullptr, nullptr);
   dim3 g2((C + 31) / 32, 1);
   reduce_partials_kernel<<<g2, dim3(32, 8), 0, st>>>(partials, nblocks, C, out, nullptr, nullptr,
                                                      scale);
   note_launch(2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_colsum_atomic(const void* m, bool bf16, float* out, int rows, int C,
+                                 int nblocks, cudaStream_t st, const float* scale) {
+  if (C % 8 != 0) return launch_colsum(m, bf16, out, rows, C, st, scale);
+  const int rpb = (rows + nblocks - 1) / nblocks;
+  dim3 g1(nblocks, (C / 8 + 255) / 256);
+  if (bf16)
+    colsum_partial_kernel<__nv_bfloat16, 1024><<<g1, 1024, 0, st>>>(
+        (const __nv_bfloat16*)m, nullptr, rows, C, rpb, out, scale);
+  else
+    colsum_partial_kernel<float, 1024><<<g1, 1024, 0, st>>>((const float*)m, nullptr, rows, C, rpb,
+                                                            out, scale);
+  note_launch();
   return cudaGetLastError();
 }
 

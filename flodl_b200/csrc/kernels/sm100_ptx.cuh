@@ -342,6 +342,13 @@ __device__ __forceinline__ float erf_as7128(float x) {
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erf_as7128(x * 0.70710678118654752f));
 }
+// GELU and its derivative together (the forward epilogue keeps GELU'(x) for
+// the backward): g = x Phi(x), dg = Phi(x) + x phi(x), phi the normal density.
+__device__ __forceinline__ void gelu_and_grad(float x, float& g, float& dg) {
+  const float cdf = 0.5f * (1.0f + erf_as7128(x * 0.70710678118654752f));
+  g = x * cdf;
+  dg = cdf + x * (0.39894228040143268f * __expf(-0.5f * x * x));
+}
 // d/dx of the erf GELU.
 __device__ __forceinline__ float gelu_erf_grad(float x) {
   const float cdf = 0.5f * (1.0f + erf_as7128(x * 0.70710678118654752f));

@@ -31,12 +31,15 @@ def attn_fwd_packed(qkv: torch.Tensor, B: int, S: int, H: int, causal: bool,
 
 def attn_bwd_packed(dout: torch.Tensor, qkv: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
                     B: int, S: int, H: int, causal: bool,
-                    key_padding: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Gradient of the packed QKV: dqkv [B*S, 3*H*D] bf16."""
+                    key_padding: Optional[torch.Tensor] = None,
+                    bias_grad: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gradient of the packed QKV: dqkv [B*S, 3*H*D] bf16. With ``bias_grad``
+    (f32 [3*H*D]) the column sums of dqkv - the gradient of the packed
+    projection's bias - are accumulated into it in the same pass."""
     D = qkv.shape[1] // (3 * H)
     dqkv = torch.empty_like(qkv)
     C().flash_attn_bwd(dout.contiguous(), qkv, out, lse, dqkv, B, S, H, D, bool(causal),
-                       1.0 / math.sqrt(D), key_padding)
+                       1.0 / math.sqrt(D), key_padding, bias_grad)
     return dqkv
 
 

@@ -57,7 +57,7 @@ def post_block_forward(x, x16, p: PostBlockParams, B, S, H, key_pad):
     K.ln_fwd(y1, p.ln1_w.detach(), p.ln1_b.detach(), x1_16, x1, m1, r1, p.eps)
     F4 = p.w1.shape[0]
     a = _empty((T, F4), torch.bfloat16, dev)
-    pre = _empty((T, F4), torch.bfloat16, dev)
+    pre = _empty((T, F4), torch.bfloat16, dev)  # GELU'(fc1 pre-activation), kept for backward
     K.gemm(x1_16, bf16_shadow(p.w1), a, T, F4, Cd, False, False, bias=p.b1.detach(), aux=pre,
            flags=K.EPI_GELU)
     y2 = _empty((T, Cd), torch.float32, dev)
@@ -107,8 +107,8 @@ def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, 
     _wgrad(dy1_16, attn, p.wo)
     dattn = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dy1_16, bf16_shadow(p.wo), dattn, T, Cd, Cd, False, True)
-    dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, False, key_pad)
-    K.colsum(dqkv, grad_buffer(p.bqkv))
+    dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, False, key_pad,
+                           bias_grad=grad_buffer(p.bqkv))
     _wgrad(dqkv, x16, p.wqkv)
     dxq = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dqkv, bf16_shadow(p.wqkv), dxq, T, Cd, 3 * Cd, False, True)
@@ -204,7 +204,7 @@ class _BertMLMTrainFn(torch.autograd.Function):
                  grad_buffer(head.transform_LayerNorm.weight), grad_buffer(head.transform_LayerNorm.bias),
                  None)
         dtp = _empty((Tm, Cd), torch.bfloat16, dev)
-        K.gelu_bwd(dt, tpre, dtp)
+        K.mul_bf16(dt, tpre, dtp)  # tpre holds GELU' of the transform
         K.colsum(dtp, grad_buffer(head.transform_dense.bias))
         _wgrad(dtp, hm16, head.transform_dense.weight)
         dhm = _empty((Tm, Cd), torch.bfloat16, dev)

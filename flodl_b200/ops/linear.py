@@ -66,9 +66,9 @@ class _LinearFn(torch.autograd.Function):
         dy2 = as_bf16_2d(dy)
         T = dy2.shape[0]
         if ctx.act == "gelu":
-            # dy of the pre-activation: dy * gelu'(h), materialised once (bf16).
+            # dy of the pre-activation: dy * GELU' (kept by the forward epilogue)
             dh = torch.empty((T, N), device=dy.device, dtype=torch.bfloat16)
-            C().gelu_bwd(dy2, aux, dh)
+            C().mul_bf16(dy2.contiguous(), aux, dh)
             dy2 = dh
         dx = None
         if ctx.needs_input_grad[0]:

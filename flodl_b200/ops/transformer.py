@@ -9,10 +9,11 @@ LayerNorm + GELU, flodl/src/nn/attention.rs, benchmarks/src/tier1/transformer.rs
 
 What is fused on sm_100a (per block, forward 7 kernels, backward 13):
 * LayerNorm writes its output in bf16 straight into the next GEMM's operand.
-* qkv/proj/fc1/fc2 GEMM epilogues add the bias, apply GELU (keeping the
-  pre-activation), and add the f32 residual stream.
+* qkv/proj/fc1/fc2 GEMM epilogues add the bias, apply GELU (keeping GELU'
+  of the pre-activation in bf16 for the backward), and add the f32 residual
+  stream.
 * Flash attention reads Q/K/V from the packed qkv buffer and writes [T, C].
-* Backward: the fc2 dgrad epilogue applies GELU'; LayerNorm backward adds the
+* Backward: the fc2 dgrad epilogue multiplies by the stored GELU'; LayerNorm backward adds the
   skip-path gradient, writes the f32 residual gradient AND its bf16 copy, and
   accumulates dgamma/dbeta plus the bias gradient (column sum) of the Linear
   whose output fed that residual stream; weight gradients accumulate in f32
@@ -85,7 +86,7 @@ def block_forward(x, p: BlockParams, B, S, H, causal, key_pad=None):
     K.ln_fwd(x2, p.ln2_w.detach(), p.ln2_b.detach(), h2, None, mean2, rstd2, p.eps)
     F4 = p.w1.shape[0]
     a = _empty((T, F4), torch.bfloat16, dev)
-    pre = _empty((T, F4), torch.bfloat16, dev)
+    pre = _empty((T, F4), torch.bfloat16, dev)  # GELU'(fc1 pre-activation), kept for backward
     K.gemm(h2, bf16_shadow(p.w1), a, T, F4, Cd, False, False, bias=p.b1.detach(), aux=pre,
            flags=K.EPI_GELU)
     x3 = _empty((T, Cd), torch.float32, dev)
@@ -122,8 +123,8 @@ def block_backward(dx3, dx3_16, p: BlockParams, saved, B, S, H, causal, prev_bia
     _wgrad(dx2_16, attn, p.wo)
     dattn = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dx2_16, bf16_shadow(p.wo), dattn, T, Cd, Cd, False, True)
-    dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, causal, key_pad)
-    K.colsum(dqkv, grad_buffer(p.bqkv))
+    dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, causal, key_pad,
+                           bias_grad=grad_buffer(p.bqkv))
     _wgrad(dqkv, h1, p.wqkv)
     dh1 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dqkv, bf16_shadow(p.wqkv), dh1, T, Cd, 3 * Cd, False, True)

@@ -45,9 +45,12 @@ def test_gemm_bias_gelu_aux_bf16():
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     aux = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     C.gemm(A, B, out, M, N, K, False, False, bias=bias, aux=aux, flags=C.EPI_GELU)
-    pre = A.float() @ B.float().t() + bias
-    torch.testing.assert_close(aux.float(), pre, rtol=2e-2, atol=2e-2)
-    torch.testing.assert_close(out.float(), torch.nn.functional.gelu(pre), rtol=2e-2, atol=2e-2)
+    pre = (A.float() @ B.float().t() + bias).requires_grad_()
+    g = torch.nn.functional.gelu(pre)
+    g.backward(torch.ones_like(g))
+    torch.testing.assert_close(out.float(), g.detach(), rtol=2e-2, atol=2e-2)
+    # aux keeps GELU'(pre) for the backward pass
+    torch.testing.assert_close(aux.float(), pre.grad, rtol=2e-2, atol=2e-2)
 
 
 def test_gemm_residual_and_dgelu():
@@ -60,12 +63,14 @@ def test_gemm_residual_and_dgelu():
     out = torch.empty(M, N, device="cuda")
     C.gemm(A, B, out, M, N, K, False, False, residual=res)
     torch.testing.assert_close(out, A.float() @ B.float().t() + res, rtol=1e-3, atol=1e-3)
-    h = torch.randn(M, N, device="cuda").bfloat16()
+    g = torch.rand(M, N, device="cuda").bfloat16()  # stored GELU' values
     out2 = torch.empty(M, N, device="cuda")
-    C.gemm(A, B, out2, M, N, K, False, False, aux=h, flags=C.EPI_DGELU)
-    x = h.float().requires_grad_()
-    torch.nn.functional.gelu(x).backward(torch.ones_like(x))
-    torch.testing.assert_close(out2, (A.float() @ B.float().t()) * x.grad, rtol=1e-3, atol=1e-3)
+    C.gemm(A, B, out2, M, N, K, False, False, aux=g, flags=C.EPI_DGELU)
+    torch.testing.assert_close(out2, (A.float() @ B.float().t()) * g.float(), rtol=1e-3, atol=1e-3)
+    out3 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)  # TMA epilogue path
+    C.gemm(A, B, out3, M, N, K, False, False, aux=g, flags=C.EPI_DGELU)
+    torch.testing.assert_close(out3.float(), (A.float() @ B.float().t()) * g.float(), rtol=2e-2,
+                               atol=2e-2)
 
 
 def test_gemm_splitk_accumulate():
