@@ -1,0 +1,199 @@
+"""Kernel micro-benchmarks at the headline model's shapes.
+
+    python -m flodl_b200.bench_kernels [--case NAME|all] [--iters N] [--warmup W]
+                                       [--launches K]
+
+Each case builds its inputs once on ``cuda:0`` and times ``iters`` launches
+with CUDA events after ``warmup`` launches (inputs larger than L2 where the
+case is memory-bound), then prints one JSON line per case: microseconds per
+launch, the algorithmic FLOPs or bytes, the achieved rate, and its fraction
+of the measured peaks in ``MEASURED_PEAKS.json`` (cuBLAS bf16 GEMM burst and
+STREAM-style copy bandwidth, measured on this hardware). ``--launches K``
+instead runs exactly K launches untimed - the small, bounded workload used
+for profiler captures.
+
+Shapes are those of the transformer LM benchmark (64 x 256 tokens, d=512,
+8 heads, FFN 2048); the reference's own kernel benchmarks live in
+``benchmarks/`` of fab2s/floDl and time libtorch's kernels the same way.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+T, D, H, FF, S, B = 16384, 512, 8, 2048, 256, 64
+
+
+def _peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def _bf(*s):
+    return torch.randn(*s, device="cuda").bfloat16()
+
+
+def case_gemm(kind):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    if kind == "gemm_qkv":  # x @ Wqkv^T + b  (bf16 out)
+        M, N, K = T, 3 * D, D
+        A, Bm = _bf(M, K), _bf(N, K)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        bias = torch.randn(N, device="cuda")
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False, bias=bias)
+        nbytes = (M * K + N * K + M * N) * 2
+    elif kind == "gemm_fc1_gelu":  # gelu(x W1^T + b1), GELU' kept (two bf16 outputs)
+        M, N, K = T, FF, D
+        A, Bm = _bf(M, K), _bf(N, K)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        aux = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        bias = torch.randn(N, device="cuda")
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False, bias=bias, aux=aux,
+                            flags=C.EPI_GELU)
+        nbytes = (M * K + N * K + 2 * M * N) * 2
+    elif kind == "gemm_fc2_residual":  # x + h W2^T + b2 (f32 residual stream)
+        M, N, K = T, D, FF
+        A, Bm = _bf(M, K), _bf(N, K)
+        out = torch.empty(M, N, device="cuda")
+        res = torch.randn(M, N, device="cuda")
+        bias = torch.randn(N, device="cuda")
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False, bias=bias, residual=res)
+        nbytes = (M * K + N * K) * 2 + 2 * M * N * 4
+    elif kind == "gemm_dgrad_dgelu":  # (dy W2) * GELU'
+        M, N, K = T, FF, D
+        A, Bm = _bf(M, K), _bf(K, N)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        g = _bf(M, N)
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, True, aux=g, flags=C.EPI_DGELU)
+        nbytes = (M * K + N * K + 2 * M * N) * 2
+    elif kind == "gemm_wgrad":  # dW1 += da^T h (f32, split-K)
+        from .ops._common import splitk_for
+        M, N, K = FF, D, T
+        A, Bm = _bf(K, M), _bf(K, N)
+        out = torch.zeros(M, N, device="cuda")
+        ks = splitk_for(M, N, K)
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, True, True, flags=C.EPI_ACCUMULATE, k_splits=ks)
+        nbytes = (M * K + N * K) * 2 + 2 * M * N * 4
+    else:
+        raise KeyError(kind)
+    return fn, 2.0 * M * N * K, nbytes
+
+
+def case_flash(kind):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    qkv = _bf(B * S, 3 * D)
+    out = torch.empty(B * S, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, H, S, device="cuda")
+    sc = 1.0 / math.sqrt(D // H)
+    C.flash_attn_fwd(qkv, out, lse, B, S, H, D // H, True, sc)
+    # causal attention FLOPs: 4 B H S^2 d / 2 forward, 2.5x that backward
+    f_fwd = 4.0 * B * H * S * S * (D // H) / 2
+    if kind == "flash_fwd":
+        fn = lambda: C.flash_attn_fwd(qkv, out, lse, B, S, H, D // H, True, sc)
+        return fn, f_fwd, (B * S * 3 * D + B * S * D) * 2
+    dout = _bf(B * S, D)
+    dqkv = torch.empty_like(qkv)
+    fn = lambda: C.flash_attn_bwd(dout, qkv, out, lse, dqkv, B, S, H, D // H, True, sc)
+    return fn, 2.5 * f_fwd, (B * S * 3 * D * 2 + 2 * B * S * D) * 2
+
+
+def case_ln(kind):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    x = torch.randn(T, D, device="cuda")
+    w = torch.randn(D, device="cuda")
+    b = torch.randn(D, device="cuda")
+    y16 = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    mean = torch.empty(T, device="cuda")
+    rstd = torch.empty(T, device="cuda")
+    C.ln_fwd(x, w, b, y16, None, mean, rstd, 1e-5)
+    if kind == "ln_fwd":
+        fn = lambda: C.ln_fwd(x, w, b, y16, None, mean, rstd, 1e-5)
+        return fn, 0.0, T * D * (4 + 2) + T * 8
+    dy = _bf(T, D)
+    dres = torch.randn(T, D, device="cuda")
+    dx = torch.empty(T, D, device="cuda")
+    dx16 = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(D, device="cuda")
+    db = torch.zeros(D, device="cuda")
+    dbias = torch.zeros(D, device="cuda")
+    fn = lambda: C.ln_bwd(dy, x, mean, rstd, w, dres, dx, dx16, dw, db, dbias)
+    return fn, 0.0, T * D * (2 + 4 + 4 + 4 + 2)
+
+
+def case_adamw(_):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    n = 19 * (1 << 20)
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    lr = torch.full((), 3e-4, device="cuda")
+    step = torch.ones((), device="cuda")
+    fn = lambda: C.adamw(p, g, m, v, sh, lr, step, None, 0.9, 0.999, 1e-8, 0.1, True, False)
+    return fn, 0.0, n * (4 * 4 + 3 * 4 + 2)
+
+
+CASES = {
+    "gemm_qkv": case_gemm, "gemm_fc1_gelu": case_gemm, "gemm_fc2_residual": case_gemm,
+    "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm,
+    "flash_fwd": case_flash, "flash_bwd": case_flash,
+    "ln_fwd": case_ln, "ln_bwd": case_ln, "adamw": case_adamw,
+}
+
+
+def run(name, iters, warmup, launches):
+    fn, flops, nbytes = CASES[name](name)
+    if launches:
+        for _ in range(launches):
+            fn()
+        torch.cuda.synchronize()
+        return {"case": name, "launches": launches}
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    tf_peak, bw_peak, src = _peaks()
+    rec = {"case": name, "us": round(us, 2)}
+    if flops:
+        tf = flops / us / 1e6
+        rec.update(tflops=round(tf, 1), frac_of_bf16_peak=round(tf / tf_peak, 3))
+    gbs = nbytes / us / 1e3
+    rec.update(gbs=round(gbs, 1), frac_of_hbm=round(gbs / bw_peak, 3), peaks=src)
+    return rec
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--launches", type=int, default=0)
+    a = ap.parse_args()
+    names = list(CASES) if a.case == "all" else a.case.split(",")
+    for n in names:
+        print(json.dumps(run(n, a.iters, a.warmup, a.launches)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
