@@ -54,8 +54,8 @@ def parse():
     ap.add_argument("--engine", default="auto", choices=["auto", "nccl", "peer"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
-    ap.add_argument("--model", default="lm", choices=["lm", "bert"],
-                    help="lm = BASELINE config 3 (the headline); bert = config 4")
+    ap.add_argument("--model", default="lm", choices=["lm", "bert", "resnet20"],
+                    help="lm = BASELINE config 3 (the headline); bert = config 4; resnet20 = config 2")
     return ap.parse_args()
 
 
@@ -146,6 +146,7 @@ def main():
     from flodl_b200.bench_support import MODELS
     spec = MODELS[args.model]
     B_PER_GPU, SEQ = spec.batch, spec.seq
+    UNIT = "samples/s" if SEQ == 1 else "tok/s"  # image models: one sample per "token"
     if args.impl == "torch":
         step, state = spec.torch(dev, world)
         engine = "nccl(torch DDP)"
@@ -228,7 +229,7 @@ def main():
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te.item())
-        e2e = {"value": world * B_PER_GPU * SEQ / (e2e_ms / 1e3), "unit": "tok/s",
+        e2e = {"value": world * B_PER_GPU * SEQ / (e2e_ms / 1e3), "unit": UNIT,
                "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
                "d2h_bytes_per_step": 4, "api": "flodl_b200.train.StepRunner.step"}
@@ -236,7 +237,7 @@ def main():
     tok_s = world * B_PER_GPU * SEQ / (ms / 1e3)
     if rank == 0:
         out = {
-            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "samples_per_s": world * B_PER_GPU / (ms / 1e3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -184,6 +184,95 @@ def _bert_torch(dev, world):
     return step, {"inputs": [ids, labels], "host_inputs": host, "model": model, "opt": opt}
 
 
+# --------------------------------------------------------------------------- ResNet-20 (config 2)
+RN_B = 128
+
+
+def _rn_batch(dev, gen=None):
+    kw = {"generator": gen} if gen is not None else {}
+    d = dev if gen is not None else "cpu"
+    x = torch.randn(RN_B, 3, 32, 32, device=d, **kw)
+    y = torch.randint(0, 10, (RN_B,), device=d, **kw)
+    return x, y
+
+
+def _rn_flodl(dev, world, engine):
+    from .models import ResNet20
+    from .optim import SGD
+    from .parallel.ddp import Ddp
+
+    model = ResNet20(device=dev)
+    ddp = None
+    mk = lambda: SGD(model.parameters(), lr=0.1, momentum=0.9, weight_decay=1e-4)
+    if world > 1 and engine == "peer":
+        from .parallel.fused import FusedDdp
+        opt = mk()
+        ddp = FusedDdp(model, opt)
+    elif world > 1:
+        ddp = Ddp(model, engine="nccl")
+        opt = mk()
+    else:
+        opt = mk()
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    x, y = _rn_batch(dev, g)
+    step = _make_step(lambda: model.loss(x, y), ddp, opt)
+
+    def host():
+        a, b = _rn_batch("cpu")
+        return [a.pin_memory(), b.pin_memory()]
+
+    return step, {"inputs": [x, y], "host_inputs": host, "model": model, "opt": opt, "ddp": ddp}
+
+
+class _TorchBlock2(torch.nn.Module):
+    def __init__(self, cin, cout, stride):
+        super().__init__()
+        nn = torch.nn
+        self.c1 = nn.Conv2d(cin, cout, 3, stride, 1, bias=False)
+        self.b1 = nn.BatchNorm2d(cout)
+        self.c2 = nn.Conv2d(cout, cout, 3, 1, 1, bias=False)
+        self.b2 = nn.BatchNorm2d(cout)
+        self.ds = (nn.Sequential(nn.Conv2d(cin, cout, 1, stride, bias=False), nn.BatchNorm2d(cout))
+                   if stride != 1 or cin != cout else None)
+
+    def forward(self, x):
+        idn = self.ds(x) if self.ds is not None else x
+        return F.relu(self.b2(self.c2(F.relu(self.b1(self.c1(x))))) + idn)
+
+
+class _TorchResNet20(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        nn = torch.nn
+        self.c = nn.Conv2d(3, 16, 3, 1, 1, bias=False)
+        self.b = nn.BatchNorm2d(16)
+        blocks = []
+        for cin, cout, s in ((16, 16, 1), (16, 32, 2), (32, 64, 2)):
+            blocks += [_TorchBlock2(cin, cout, s), _TorchBlock2(cout, cout, 1),
+                       _TorchBlock2(cout, cout, 1)]
+        self.blocks = nn.Sequential(*blocks)
+        self.fc = nn.Linear(64, 10)
+
+    def forward(self, x, y):
+        h = self.blocks(F.relu(self.b(self.c(x))))
+        return F.cross_entropy(self.fc(F.adaptive_avg_pool2d(h, 1).flatten(1)).float(), y)
+
+
+def _rn_torch(dev, world):
+    model = _TorchResNet20().to(dev).to(memory_format=torch.channels_last)
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    x, y = _rn_batch(dev, g)
+    step, model, opt = _torch_step(model, dev, world, lambda m: m(x, y), "sgd", lr=0.1, wd=1e-4)
+
+    def host():
+        a, b = _rn_batch("cpu")
+        return [a.pin_memory(), b.pin_memory()]
+
+    return step, {"inputs": [x, y], "host_inputs": host, "model": model, "opt": opt}
+
+
 # --------------------------------------------------------------------------- shared
 def _make_step(loss_fn, ddp, opt):
     if ddp is not None and getattr(ddp, "fuses_optimizer", False):
@@ -230,4 +319,6 @@ MODELS: Dict[str, BenchModel] = {
                      "AdamW lr3e-4 wd0.1", _lm_flodl, _lm_torch),
     "bert": BenchModel("bert", "bert-base MLM 12L d768 h12 ff3072 vocab30522 (15% masked)",
                        BERT_B, BERT_S, "AdamW lr1e-4 wd0.01", _bert_flodl, _bert_torch),
+    "resnet20": BenchModel("resnet20", "resnet-20 CIFAR (3x3 basic blocks 16/32/64, BN, ReLU), 3x32x32",
+                           RN_B, 1, "SGD lr0.1 momentum0.9 wd1e-4", _rn_flodl, _rn_torch),
 }

@@ -68,10 +68,17 @@ void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor&
 
 void colsum(const Tensor& m, Tensor& out, const optional<Tensor>& scale) {
   FL_CHECK_CUDA(m);
-  FL_CHECK(m.is_contiguous(), "colsum input must be contiguous");
   FL_CHECK_F32(out);
   const int C = (int)m.size(-1);
   c10::cuda::CUDAGuard guard(m.device());
+  if (!m.is_contiguous()) {
+    // row-strided 2-D view (e.g. the first V columns of a padded buffer)
+    FL_CHECK(m.dim() == 2 && m.stride(1) == 1, "colsum input must be contiguous or a row-strided 2-D view");
+    FL_CUDA_OK(flodl::launch_colsum(m.data_ptr(), m.scalar_type() == at::kBFloat16, ptr<float>(out),
+                                    (int)m.size(0), C, cur_stream(), opt_ptr<const float>(scale),
+                                    (int)m.stride(0)));
+    return;
+  }
   const int rows = (int)(m.numel() / C);
   const int nb = flodl::colsum_partial_blocks(rows);
   FL_CUDA_OK(flodl::launch_colsum_atomic(m.data_ptr(), m.scalar_type() == at::kBFloat16,
@@ -102,8 +109,11 @@ void softmax_ce(const Tensor& logits, const Tensor& targets, Tensor& loss, Tenso
   a.inv_count = ptr<float>(inv_count);
   a.loss = ptr<float>(loss);
   if (dlogits) {
-    FL_CHECK(dlogits->is_contiguous() && dlogits->size(0) == T && dlogits->size(1) == V, "dlogits");
+    FL_CHECK(dlogits->dim() == 2 && dlogits->stride(1) == 1 && dlogits->size(0) == T &&
+                 dlogits->size(1) == V,
+             "dlogits must be [T, V] row-major (any row pitch)");
     a.dlogits = ptr<__nv_bfloat16>(*dlogits);
+    a.ld_d = (int)dlogits->stride(0);
   }
   FL_CUDA_OK(flodl::launch_softmax_ce(a, st));
 }

@@ -10,4 +10,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_optim(m);
   register_attention(m);
   register_comm(m);
+  register_conv(m);
 }

@@ -42,7 +42,7 @@ struct LnBwdArgs {
 cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st);
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
-                          const float* scale = nullptr);
+                          const float* scale = nullptr, int ld = 0);
 // Two-stage (deterministic) column sum; partials is scratch [nblocks, C].
 // Single-pass column sums: nblocks row slices, one atomic per column and
 // slice into out (accumulating; optionally scaled by *scale).
@@ -64,6 +64,7 @@ struct CeArgs {
   const float* inv_count = nullptr;       // device scalar: 1 / #valid rows
   float* loss = nullptr;                  // device scalar, accumulated mean loss
   __nv_bfloat16* dlogits = nullptr;       // [T, V] gradient of the mean loss (nullable)
+  int ld_d = 0;                           // row pitch of dlogits (0: V)
 };
 cudaError_t launch_ce_count(const int64_t* targets, int T, int64_t ignore_index, float* inv_count,
                             float* loss_zero, cudaStream_t st);
@@ -136,4 +137,47 @@ cudaError_t launch_gelu_eval_f32(const float* x, float* y, float* dydx, int64_t 
                                  cudaStream_t st);
 // y = gelu(x) bf16 -> bf16
 cudaError_t launch_gelu_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n, cudaStream_t st);
+// ------------------------------------------------------------- conv / batch norm (conv.cu)
+// Activations are NHWC bf16; a convolution is im2col -> tcgen05 GEMM (-> col2im).
+// cols [N*Ho*Wo, k*k*C], column (kh*k + kw)*C + ci; C a multiple of 8
+cudaError_t launch_im2col(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W, int C,
+                          int k, int s, int p, cudaStream_t st);
+cudaError_t launch_col2im(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx, const void* add,
+                          bool add_f32, const __nv_bfloat16* mask, int N, int H, int W, int C,
+                          int k, int s, int p, cudaStream_t st);
+// ws: 2C f32 zeros, ticket: one zero word; both are left zeroed for the next call.
+cudaError_t launch_bn_stats(const __nv_bfloat16* x, int64_t M, int C, float eps, float momentum,
+                            float* mean, float* rstd, float* run_mean, float* run_var, float* ws,
+                            unsigned* ticket, cudaStream_t st);
+cudaError_t launch_bn_apply(const __nv_bfloat16* x, int64_t M, int C, const float* mean,
+                            const float* rstd, const float* gamma, const float* beta,
+                            const __nv_bfloat16* identity, bool relu, __nv_bfloat16* y,
+                            cudaStream_t st);
+// sums: 2C f32 scratch (sum dz, sum dz*xhat); dz_out (nullable) receives the masked dy.
+cudaError_t launch_bn_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
+                          const __nv_bfloat16* x, int64_t M, int C, const float* mean,
+                          const float* rstd, const float* gamma, float* dgamma, float* dbeta,
+                          float* sums, float* ws, unsigned* ticket, __nv_bfloat16* dx,
+                          __nv_bfloat16* dz_out, cudaStream_t st);
+cudaError_t launch_avgpool_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int N, int HW, int C,
+                               cudaStream_t st);
+cudaError_t launch_avgpool_bwd(const __nv_bfloat16* dy, int ld, __nv_bfloat16* dx, int N, int HW,
+                               int C, cudaStream_t st);
+cudaError_t launch_nchw_to_nhwc(const float* x, __nv_bfloat16* y, int N, int C, int HW, int Cp,
+                                cudaStream_t st);
+// One convolution of a network-wide weight pack / gradient unpack table.
+struct ConvPackEntry {
+  const float* w;          // f32 OIHW parameter [cout, cin, k, k]
+  __nv_bfloat16* packed;   // bf16 [cout, k*k*cin_pad], column (kh*k + kw)*cin_pad + ci
+  float* gacc;             // f32 [cout, k*k*cin_pad] gradient in packed order (zeroed on unpack)
+  float* grad;             // f32 OIHW gradient (+=)
+  int cout, cin, cin_pad, k;
+};
+cudaError_t launch_pack_conv_weights(const ConvPackEntry* table, int n, int max_elems,
+                                     cudaStream_t st);
+cudaError_t launch_unpack_conv_grads(const ConvPackEntry* table, int n, int max_elems,
+                                     cudaStream_t st);
+cudaError_t launch_cast_pad(const float* x, __nv_bfloat16* y, int rows, int cols, int ld,
+                            cudaStream_t st);
+
 }  // namespace flodl

@@ -327,13 +327,13 @@ __global__ void __launch_bounds__(NT) colsum_partial_kernel(const T* __restrict_
 // Column sums of a [rows, C] matrix into f32 out[C] (accumulating).
 template <typename T>
 __global__ void colsum_kernel(const T* __restrict__ m, float* __restrict__ out, int rows, int C,
-                              int rows_per_block, const float* __restrict__ scale) {
+                              int rows_per_block, const float* __restrict__ scale, int ld) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   float s = 0.f;
-  for (int r = r0; r < r1; ++r) s += to_f32(m[(size_t)r * C + c]);
+  for (int r = r0; r < r1; ++r) s += to_f32(m[(size_t)r * ld + c]);
   if (scale) s *= *scale;
   atomicAdd(out + c, s);
 }
@@ -443,16 +443,17 @@ cudaError_t launch_colsum_atomic(const void* m, bool bf16, float* out, int rows,
 }
 
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
-                          const float* scale) {
+                          const float* scale, int ld) {
+  if (ld <= 0) ld = C;
   const int threads = 128;
   const int rows_per_block = 256;
   dim3 grid((C + threads - 1) / threads, (rows + rows_per_block - 1) / rows_per_block);
   if (bf16)
     colsum_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>((const __nv_bfloat16*)m, out, rows, C,
-                                                           rows_per_block, scale);
+                                                           rows_per_block, scale, ld);
   else
     colsum_kernel<float><<<grid, threads, 0, st>>>((const float*)m, out, rows, C, rows_per_block,
-                                                   scale);
+                                                   scale, ld);
   note_launch();
   return cudaGetLastError();
 }

@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
       loss_acc += (lse - (1.f - eps) * zt - eps / a.V * sz) * inv_n;
     }
     if (a.dlogits) {
-      __nv_bfloat16* dz = a.dlogits + (size_t)t * a.V;
+      __nv_bfloat16* dz = a.dlogits + (size_t)t * (a.ld_d > 0 ? a.ld_d : a.V);
       const float off = eps / a.V;
       for (int j = threadIdx.x; j < a.V; j += kThreads) {
         float g = 0.f;

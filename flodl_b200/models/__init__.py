@@ -2,3 +2,4 @@
 from .bert import (BertConfig, BertForMaskedLM, BertForQuestionAnswering,  # noqa: F401
                    BertForSequenceClassification, BertForTokenClassification, BertModel)
 from .transformer_lm import DecoderBlock, TransformerLM  # noqa: F401
+from .resnet import BasicBlock, ResNet20  # noqa: F401

@@ -6,3 +6,4 @@ from .misc import batch_norm2d, conv2d, embedding, gelu  # noqa: F401
 from .norm import layer_norm  # noqa: F401
 from .transformer import lm_train_loss  # noqa: F401,E402
 from .bert import bert_mlm_train_loss  # noqa: F401,E402
+from .resnet import resnet_train_loss  # noqa: F401,E402

@@ -167,12 +167,13 @@ class _BertMLMTrainFn(torch.autograd.Function):
         K.ln_fwd(t, head.transform_LayerNorm.weight.detach(), head.transform_LayerNorm.bias.detach(),
                  tl16, None, mt, rt, head.transform_LayerNorm.eps)
         V = cfg.vocab_size
-        logits = _empty((Tm, V), torch.bfloat16, dev)
+        Vp = (V + 7) // 8 * 8  # 16-byte row pitch for the TMA-fed GEMMs
+        logits = _empty((Tm, Vp), torch.bfloat16, dev)[:, :V]
         K.gemm(tl16, bf16_shadow(head.decoder_weight), logits, Tm, V, Cd, False, False,
                bias=head.bias.detach())
         loss = torch.zeros((), device=dev, dtype=torch.float32)
         inv = _empty((), torch.float32, dev)
-        dlogits = torch.empty_like(logits)
+        dlogits = _empty((Tm, Vp), torch.bfloat16, dev)[:, :V]
         K.softmax_ce(logits, lab_sel, loss, inv, dlogits, -100, 0.0)
         ctx.model = model
         ctx.blocks = blocks

@@ -18,6 +18,11 @@ from ._common import (C, as_bf16_2d, bf16_shadow, grad_buffer, grad_ready, split
                       use_kernels, wants_grad)
 
 
+def gelu_op(y):
+    from .misc import gelu
+    return gelu(y)
+
+
 def wgrad_accumulate(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor,
                      alpha_t: Optional[torch.Tensor] = None) -> None:
     """weight.grad += dy2^T @ x2  (dy2 [T, N] bf16, x2 [T, K] bf16)."""
@@ -87,6 +92,54 @@ class _LinearFn(torch.autograd.Function):
         return dx, None, None, None, dres
 
 
+def _ceil8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+class _PaddedLinearFn(torch.autograd.Function):
+    """Linear whose in/out features are not multiples of 8: the TMA-fed GEMMs
+    need 16-byte row pitches, so operands are zero-padded to the next multiple
+    of 8 (a copy of x, of the bf16 weight and of dy) and the results sliced."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        N, K = weight.shape
+        Np, Kp = _ceil8(N), _ceil8(K)
+        x2 = F.pad(as_bf16_2d(x), (0, Kp - K))
+        w16 = F.pad(bf16_shadow(weight), (0, Kp - K, 0, Np - N))
+        T = x2.shape[0]
+        bias_p = F.pad(bias.detach().float(), (0, Np - N)) if bias is not None else None
+        out = torch.empty((T, Np), device=x.device, dtype=torch.bfloat16)
+        C().gemm(x2, w16, out, T, Np, Kp, False, False, bias=bias_p)
+        ctx.save_for_backward(x2, w16, weight, bias)
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        return out[:, :N].reshape(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w16, weight, bias = ctx.saved_tensors
+        N, K = weight.shape
+        Np, Kp = w16.shape
+        dyp = F.pad(as_bf16_2d(dy), (0, Np - N)).contiguous()
+        T = dyp.shape[0]
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx2 = torch.empty((T, Kp), device=dy.device, dtype=torch.bfloat16)
+            C().gemm(dyp, w16, dx2, T, Kp, Np, False, True)
+            dx = dx2[:, :K].to(ctx.x_dtype if ctx.x_dtype == torch.float32 else torch.bfloat16)
+            dx = dx.reshape(ctx.x_shape)
+        if wants_grad(weight):
+            gp = torch.zeros((Np, Kp), device=dy.device, dtype=torch.float32)
+            C().gemm(dyp, x2, gp, Np, Kp, T, True, True, flags=C().EPI_ACCUMULATE,
+                     k_splits=splitk_for(Np, Kp, T))
+            grad_buffer(weight).add_(gp[:N, :K])
+            grad_ready(weight)
+        if bias is not None and wants_grad(bias):
+            C().colsum(dyp[:, :N], grad_buffer(bias))
+            grad_ready(bias)
+        return dx, None, None
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            act: Optional[str] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``act(x @ weight.T + bias) + residual``.
@@ -106,6 +159,15 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         if residual is not None:
             y = residual + y
         return y
+    if weight.shape[0] % 8 or weight.shape[1] % 8:
+        y = _PaddedLinearFn.apply(x, weight, bias)
+        if act == "gelu":
+            y = gelu_op(y)
+        elif act == "relu":
+            y = F.relu(y)
+        elif act is not None:
+            raise ValueError(f"unsupported fused activation {act!r}")
+        return y if residual is None else residual + y
     if act not in (None, "gelu"):
         y = _LinearFn.apply(x, weight, bias, None, None)
         y = F.relu(y) if act == "relu" else y

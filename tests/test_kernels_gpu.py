@@ -200,3 +200,20 @@ def test_gelu_epilogue_math_matches_erf_gelu():
     assert err.max().item() < 2e-6, err.max().item()
     derr = (d.double() - dref).abs()
     assert derr.max().item() < 2e-6, derr.max().item()
+
+
+def test_linear_odd_features_padded_path():
+    torch.manual_seed(11)
+    from flodl_b200.ops.linear import linear
+    x = torch.randn(37, 20, device="cuda").requires_grad_()
+    w = (torch.randn(10, 20, device="cuda") * 0.2).requires_grad_()
+    b = torch.randn(10, device="cuda").requires_grad_()
+    y = linear(x, w, b)
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    xr, wr, br = [t.detach().clone().requires_grad_() for t in (x, w, b)]
+    yr = F.linear(xr.bfloat16().float(), wr.bfloat16().float(), br)
+    yr.backward(dy)
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    for got, ref in ((x.grad, xr.grad), (w.grad, wr.grad), (b.grad, br.grad)):
+        assert ((got - ref).norm() / ref.norm()).item() < 2e-2

@@ -1,0 +1,155 @@
+"""Convolution / batch-norm kernels and the fused ResNet-20 training op
+against PyTorch fp32 references (NHWC bf16 activations on the device)."""
+import copy
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from flodl_b200._ext import cuda_ext
+    return cuda_ext()
+
+
+@pytest.mark.parametrize("Cin,k,s,p,H", [(8, 3, 1, 1, 32), (16, 3, 2, 1, 32), (32, 1, 2, 0, 16),
+                                         (64, 3, 1, 1, 8)])
+def test_im2col_col2im_match_unfold_fold(Cin, k, s, p, H):
+    C = _C()
+    torch.manual_seed(0)
+    N = 3
+    x = torch.randn(N, Cin, H, H, device="cuda").bfloat16()
+    xh = x.permute(0, 2, 3, 1).contiguous()
+    Ho = (H + 2 * p - k) // s + 1
+    K = Cin * k * k
+    L = Ho * Ho
+    cols = torch.full((N * L, K), 7.0, device="cuda", dtype=torch.bfloat16)
+    C.im2col(xh, cols, k, s, p)
+    # unfold gives columns ordered (c, kh, kw); the kernel orders them (kh, kw, c)
+    ref = F.unfold(x.float(), k, padding=p, stride=s).reshape(N, Cin, k * k, L)
+    ref = ref.permute(0, 3, 2, 1).reshape(N * L, K)
+    torch.testing.assert_close(cols.float(), ref)
+    # col2im = adjoint of im2col (sum over taps), with add and ReLU mask
+    dcols = torch.randn(N * L, K, device="cuda").bfloat16()
+    add = torch.randn(N, H, H, Cin, device="cuda").bfloat16()
+    mask = torch.randn(N, H, H, Cin, device="cuda").bfloat16()
+    dx = torch.empty(N, H, H, Cin, device="cuda", dtype=torch.bfloat16)
+    C.col2im(dcols, dx, k, s, p, add, mask)
+    dc = dcols.float().reshape(N, L, k * k, Cin).permute(0, 3, 2, 1).reshape(N, K, L)
+    fold = F.fold(dc, (H, H), k, padding=p, stride=s).permute(0, 2, 3, 1)
+    exp = (fold + add.float()) * (mask.float() > 0)
+    torch.testing.assert_close(dx.float(), exp, rtol=2e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("Cc", [16, 32, 64])
+def test_batch_norm_kernels_match_torch(Cc):
+    C = _C()
+    torch.manual_seed(1)
+    M = 4096 + 37
+    y = (torch.randn(M, Cc, device="cuda") * 2 + 0.5).bfloat16()
+    ident = torch.randn(M, Cc, device="cuda").bfloat16()
+    gamma = torch.rand(Cc, device="cuda") + 0.5
+    beta = torch.randn(Cc, device="cuda")
+    rm, rv = torch.zeros(Cc, device="cuda"), torch.ones(Cc, device="cuda")
+    ws = torch.zeros(2 * Cc + 1, device="cuda")
+    mean, rstd = torch.empty(Cc, device="cuda"), torch.empty(Cc, device="cuda")
+    out = torch.empty_like(y)
+    for _ in range(2):  # the workspace must come back zeroed
+        C.bn_stats(y, mean, rstd, rm, rv, ws, 1e-5, 0.1)
+    C.bn_apply(y, mean, rstd, gamma, beta, ident, True, out)
+    yf = y.float().requires_grad_()
+    g_, b_ = gamma.clone().requires_grad_(), beta.clone().requires_grad_()
+    rm2, rv2 = torch.zeros(Cc, device="cuda"), torch.ones(Cc, device="cuda")
+    z = F.batch_norm(yf, rm2, rv2, g_, b_, True, 0.1, 1e-5)
+    F.batch_norm(y.float(), rm2, rv2, None, None, True, 0.1, 1e-5)
+    ref = torch.relu(z + ident.float())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2)
+    torch.testing.assert_close(rm, rm2, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(rv, rv2, rtol=1e-3, atol=1e-3)
+    assert ws.abs().max().item() == 0.0
+    # backward with the ReLU mask of the output and the masked gradient
+    dy = torch.randn(M, Cc, device="cuda").bfloat16()
+    ref.backward(dy.float())
+    dg, db = torch.zeros(Cc, device="cuda"), torch.zeros(Cc, device="cuda")
+    sums = torch.empty(2 * Cc, device="cuda")
+    dx, dz = torch.empty_like(y), torch.empty_like(y)
+    C.bn_bwd(dy, out, y, mean, rstd, gamma, dg, db, sums, ws, dx, dz)
+    torch.testing.assert_close(dz.float(), dy.float() * (out.float() > 0))
+    torch.testing.assert_close(dx.float(), yf.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(dg, g_.grad, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(db, b_.grad, rtol=2e-2, atol=2e-2)
+
+
+def test_resnet20_fused_matches_bf16_autocast_reference():
+    """bf16 training of ResNet-20 deviates from fp32 by tens of percent per
+    gradient (BatchNorm backward cancels most of each gradient); the fused op
+    must deviate from fp32 no more than PyTorch's own bf16 autocast run of the
+    same network does."""
+    from flodl_b200.bench_support import _TorchResNet20
+    from flodl_b200.models import ResNet20
+
+    torch.manual_seed(0)
+    cpu = ResNet20()
+    gpu = copy.deepcopy(cpu)
+    gpu.move_to_device(torch.device("cuda"))
+    ref = _TorchResNet20()
+    with torch.no_grad():
+        for (n1, p1), (n2, p2) in zip(cpu.named_parameters(), ref.named_parameters()):
+            assert p1.shape == p2.shape, (n1, n2)
+            p2.copy_(p1)
+    ref = ref.cuda().to(memory_format=torch.channels_last)
+    x = torch.randn(32, 3, 32, 32)
+    t = torch.randint(0, 10, (32,))
+    lc = cpu.loss(x, t)
+    lc.backward()
+    lg = gpu.loss(x.cuda(), t.cuda())
+    lg.backward()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        la = ref(x.cuda(), t.cuda())
+    la.backward()
+    torch.cuda.synchronize()
+    assert abs(lg.item() - lc.item()) < 5e-2, (lg.item(), lc.item())
+    tot_f, tot_a = 0.0, 0.0
+    for (name, pc), (_, pg), (_, pa) in zip(cpu.named_parameters(), gpu.named_parameters(),
+                                            ref.named_parameters()):
+        assert pg.grad is not None, name
+        rf = ((pg.grad.cpu() - pc.grad).norm() / pc.grad.norm()).item()
+        ra = ((pa.grad.cpu() - pc.grad).norm() / pc.grad.norm()).item()
+        assert rf < 2.0 * ra + 0.05, f"{name}: fused {rf:.3f} vs autocast {ra:.3f}"
+        tot_f += rf
+        tot_a += ra
+    assert tot_f < 1.2 * tot_a, (tot_f, tot_a)
+    gb = dict(gpu.named_buffers())
+    for name, bc in cpu.named_buffers():
+        torch.testing.assert_close(gb[name].cpu(), bc, rtol=2e-2, atol=2e-2)
+
+
+def test_generic_conv2d_and_batchnorm_ops():
+    from flodl_b200 import ops
+    torch.manual_seed(3)
+    x = torch.randn(4, 16, 16, 16, device="cuda", requires_grad=True)
+    w = torch.randn(32, 16, 3, 3, device="cuda", requires_grad=True)
+    b = torch.randn(32, device="cuda", requires_grad=True)
+    y = ops.conv2d(x, w, b, 2, 1)
+    y.float().sum().backward()
+    x2, w2, b2 = [t.detach().clone().requires_grad_() for t in (x, w, b)]
+    y2 = F.conv2d(x2.bfloat16().float(), w2.bfloat16().float(), b2, 2, 1)
+    y2.sum().backward()
+    for u, v in ((y.float(), y2), (x.grad, x2.grad), (w.grad, w2.grad), (b.grad, b2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 1e-2
+    z = torch.randn(8, 32, 8, 8, device="cuda", requires_grad=True)
+    g = torch.rand(32, device="cuda", requires_grad=True)
+    be = torch.randn(32, device="cuda", requires_grad=True)
+    rm, rv = torch.zeros(32, device="cuda"), torch.ones(32, device="cuda")
+    o = ops.batch_norm2d(z, rm, rv, g, be, True, 0.1, 1e-5)
+    dy = torch.randn_like(z)
+    o.float().backward(dy)
+    z2, g2, be2 = [t.detach().clone().requires_grad_() for t in (z, g, be)]
+    rm2, rv2 = torch.zeros(32, device="cuda"), torch.ones(32, device="cuda")
+    o2 = F.batch_norm(z2.bfloat16().float(), rm2, rv2, g2, be2, True, 0.1, 1e-5)
+    o2.backward(dy.bfloat16().float())
+    for u, v in ((o.float(), o2), (z.grad, z2.grad), (g.grad, g2.grad), (be.grad, be2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 2e-2
+    torch.testing.assert_close(rm, rm2, rtol=1e-3, atol=1e-3)
