@@ -31,12 +31,16 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "../kernels/sm100_ptx.cuh"
 #include "peer_comm.h"
 
 namespace flodl {
 
 namespace {
+
+constexpr int kIlp = 2;  // float4 elements per thread and loop iteration
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -75,13 +79,20 @@ __device__ __forceinline__ bool wait_ge(const uint32_t* p, uint32_t target, uint
 //   [done   + k]                 : completion counter of bucket k (peers add)
 //   [epoch  + k]                 : local: completed launches of bucket k
 //   [finish + k]                 : local: blocks finished in the current launch
+//   [base + k]                   : local: value of done[k] when the previous launch ended
+// The completion target of a launch is base + world * gridDim, so launches of
+// one slot may use different grid sizes.
 struct SigLayout {
   static constexpr int kReady = 0;
   static constexpr int kDone = kReady + kMaxBuckets * kMaxRanks;
   static constexpr int kEpoch = kDone + kMaxBuckets;
   static constexpr int kFinish = kEpoch + kMaxBuckets;
   static constexpr int kCount = kFinish + kMaxBuckets;  // count/mass exchange (f32 bits)
-  static constexpr int kWords = kCount + kMaxBuckets * kMaxRanks * 2;
+  static constexpr int kBase = kCount + kMaxBuckets * kMaxRanks * 2;
+  static constexpr int kGo = kBase + kMaxBuckets;       // local: all peers ready (epoch)
+  static constexpr int kFinCnt = kGo + kMaxBuckets;     // local: blocks done with a phase
+  static constexpr int kFinGo = kFinCnt + kMaxBuckets;  // local: phase complete everywhere
+  static constexpr int kWords = kFinGo + kMaxBuckets;
 };
 
 struct Handles {
@@ -91,16 +102,21 @@ struct Handles {
   uint32_t* sig[kMaxRanks];
 };
 
-// Phase 1+5 helpers shared by all fused kernels. Returns the launch epoch.
+// Start-of-launch handshake. Only block 0 of each rank talks to the peers: it
+// publishes "rank r reached this launch of slot k" on every peer and waits
+// until every peer did the same, then opens a local gate that the other
+// blocks of the launch wait on. Returns the launch epoch (1, 2, ... per slot).
 __device__ __forceinline__ uint32_t announce(const Handles& h, int rank, int world, int bucket,
                                              uint32_t* sig_local) {
   __shared__ uint32_t epoch_sh;
   if (threadIdx.x == 0) {
     const uint32_t e = *(volatile uint32_t*)(sig_local + SigLayout::kEpoch + bucket) + 1;
     epoch_sh = e;
-    __threadfence_system();
-    for (int p = 0; p < world; ++p)
-      st_release_sys(h.sig[p] + SigLayout::kReady + bucket * kMaxRanks + rank, e);
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < world; ++p)
+        st_release_sys(h.sig[p] + SigLayout::kReady + bucket * kMaxRanks + rank, e);
+    }
   }
   __syncthreads();
   return epoch_sh;
@@ -112,39 +128,69 @@ __device__ __forceinline__ bool wait_all_ready(const Handles& h, int world, int 
   __shared__ int ok_sh;
   if (threadIdx.x == 0) {
     bool ok = true;
-    for (int p = 0; p < world && ok; ++p)
-      ok = wait_ge(sig_local + SigLayout::kReady + bucket * kMaxRanks + p, epoch, limit, err,
-                   kErrPeerTimeout);
+    if (blockIdx.x == 0) {
+      for (int p = 0; p < world && ok; ++p)
+        ok = wait_ge(sig_local + SigLayout::kReady + bucket * kMaxRanks + p, epoch, limit, err,
+                     kErrPeerTimeout);
+      if (ok) st_release_sys(sig_local + SigLayout::kGo + bucket, epoch);
+    } else {
+      ok = wait_ge(sig_local + SigLayout::kGo + bucket, epoch, limit, err, kErrPeerTimeout);
+    }
     ok_sh = ok;
   }
   __syncthreads();
   return ok_sh != 0;
 }
 
-// Signal "this block's shard writes are done" on every peer, then wait until
-// every peer's blocks did the same for this rank; the last local block to get
-// here advances the bucket epoch.
-__device__ __forceinline__ bool finish_bucket(const Handles& h, int world, int bucket,
-                                              uint32_t epoch, uint32_t* sig_local, uint64_t limit,
-                                              uint32_t* err) {
+// End-of-phase handshake on completion slot `slot` (the bucket, or bucket + 1
+// for a second phase). Every block makes its peer-memory writes visible and
+// counts itself; the last block of this rank signals each peer once and waits
+// until all peers did, then opens a local gate for the other blocks. The
+// completion target is base + world, base = the slot's count when the
+// previous launch ended (recorded by end_launch).
+__device__ __forceinline__ bool phase_done(const Handles& h, int world, int slot, uint32_t epoch,
+                                           uint32_t* sig_local, uint64_t limit, uint32_t* err) {
   __shared__ int ok_sh;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    for (int p = 0; p < world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + bucket, 1u);
-    const uint32_t target = epoch * (uint32_t)(world * gridDim.x);
-    ok_sh = wait_ge(sig_local + SigLayout::kDone + bucket, target, limit, err, kErrPeerTimeout);
+    const uint32_t prev = atomicAdd(sig_local + SigLayout::kFinCnt + slot, 1u);
+    bool ok;
+    if (prev == gridDim.x - 1) {
+      sig_local[SigLayout::kFinCnt + slot] = 0;
+      __threadfence_system();
+      for (int p = 0; p < world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + slot, 1u);
+      const uint32_t target =
+          *(volatile uint32_t*)(sig_local + SigLayout::kBase + slot) + (uint32_t)world;
+      ok = wait_ge(sig_local + SigLayout::kDone + slot, target, limit, err, kErrPeerTimeout);
+      if (ok) st_release_sys(sig_local + SigLayout::kFinGo + slot, epoch);
+    } else {
+      ok = wait_ge(sig_local + SigLayout::kFinGo + slot, epoch, limit, err, kErrPeerTimeout);
+    }
+    ok_sh = ok;
   }
   __syncthreads();
   return ok_sh != 0;
 }
 
+__device__ __forceinline__ bool finish_bucket(const Handles& h, int world, int bucket,
+                                              uint32_t epoch, uint32_t* sig_local, uint64_t limit,
+                                              uint32_t* err) {
+  return phase_done(h, world, bucket, epoch, sig_local, limit, err);
+}
+
+// The last local block of a launch records the done counters (slot and
+// slot + 1, which the all-reduce uses for its second round) as the base of
+// the next launch, then advances the epoch. No peer can add to them before
+// this rank announces its next launch.
 __device__ __forceinline__ void end_launch(int bucket, uint32_t* sig_local) {
   if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t prev = atomicAdd(sig_local + SigLayout::kFinish + bucket, 1u);
     if (prev == gridDim.x - 1) {
       sig_local[SigLayout::kFinish + bucket] = 0;
+      for (int k = bucket; k < bucket + 2 && k < kMaxBuckets; ++k)
+        sig_local[SigLayout::kBase + k] = *(volatile uint32_t*)(sig_local + SigLayout::kDone + k);
       __threadfence();
       atomicAdd(sig_local + SigLayout::kEpoch + bucket, 1u);
     }
@@ -187,27 +233,44 @@ __global__ void __launch_bounds__(512) fused_ar_adamw_kernel(FusedArgs a, Handle
   const float bc2s = sqrtf(1.f - powf(a.beta2, t));
   const float gs = (a.gscale ? *a.gscale : 1.f) / (float)a.world;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+  // two float4 per thread and iteration: all peer loads of both are issued
+  // before any use, doubling the bytes in flight over NVLink
+  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
+       i0 += kIlp * stride) {
+    float4 g[kIlp];
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
     for (int p = 0; p < a.world; ++p) {
-      const float4 x = ld_cg4(h.grad[p] + 4 * i);
-      g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+#pragma unroll
+      for (int j = 0; j < kIlp; ++j) {
+        const int64_t i = i0 + j * stride;
+        if (i < s1) {
+          const float4 x = ld_cg4(h.grad[p] + 4 * i);
+          g[j].x += x.x; g[j].y += x.y; g[j].z += x.z; g[j].w += x.w;
+        }
+      }
     }
-    g.x *= gs; g.y *= gs; g.z *= gs; g.w *= gs;
-    float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
-    float4 m = reinterpret_cast<float4*>(a.m)[i];
-    float4 v = reinterpret_cast<float4*>(a.v)[i];
-    adamw4(pv, g, m, v, lr, a.beta1, a.beta2, a.eps, a.wd, bc1, bc2s);
-    reinterpret_cast<float4*>(a.m)[i] = m;
-    reinterpret_cast<float4*>(a.v)[i] = v;
-    uint2 sh;
-    sh.x = pack_bf16x2(pv.x, pv.y);
-    sh.y = pack_bf16x2(pv.z, pv.w);
-    for (int p = 0; p < a.world; ++p) {
-      const int q = (a.rank + p) % a.world;  // stagger destinations across ranks
-      reinterpret_cast<float4*>(h.data[q])[i] = pv;
-      reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) {
+      const int64_t i = i0 + j * stride;
+      if (i >= s1) break;
+      float4 gj = g[j];
+      gj.x *= gs; gj.y *= gs; gj.z *= gs; gj.w *= gs;
+      float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
+      float4 m = reinterpret_cast<float4*>(a.m)[i];
+      float4 v = reinterpret_cast<float4*>(a.v)[i];
+      adamw4(pv, gj, m, v, lr, a.beta1, a.beta2, a.eps, a.wd, bc1, bc2s);
+      reinterpret_cast<float4*>(a.m)[i] = m;
+      reinterpret_cast<float4*>(a.v)[i] = v;
+      uint2 sh;
+      sh.x = pack_bf16x2(pv.x, pv.y);
+      sh.y = pack_bf16x2(pv.z, pv.w);
+      for (int p = 0; p < a.world; ++p) {
+        const int q = (a.rank + p) % a.world;  // stagger destinations across ranks
+        reinterpret_cast<float4*>(h.data[q])[i] = pv;
+        reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
+      }
     }
   }
   if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
@@ -239,35 +302,50 @@ __global__ void __launch_bounds__(512) fused_ar_sgd_kernel(FusedArgs a, Handles 
   const bool first = a.first ? (*a.first != 0.f) : false;
   const float gs = (a.gscale ? *a.gscale : 1.f) / (float)a.world;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
+       i0 += kIlp * stride) {
+    float4 gv[kIlp];
+#pragma unroll
+    for (int jj = 0; jj < kIlp; ++jj) gv[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
     for (int p = 0; p < a.world; ++p) {
-      const float4 x = ld_cg4(h.grad[p] + 4 * i);
-      g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
-    }
-    float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
-    float* pp = &pv.x;
-    float* gg = &g.x;
-    float4 bv = a.m ? reinterpret_cast<float4*>(a.m)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    float* bb = &bv.x;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float d = gg[e] * gs + a.wd * pp[e];
-      if (a.m) {
-        bb[e] = first ? d : a.momentum * bb[e] + (1.f - a.dampening) * d;
-        d = a.nesterov ? d + a.momentum * bb[e] : bb[e];
+      for (int jj = 0; jj < kIlp; ++jj) {
+        const int64_t i = i0 + jj * stride;
+        if (i < s1) {
+          const float4 x = ld_cg4(h.grad[p] + 4 * i);
+          gv[jj].x += x.x; gv[jj].y += x.y; gv[jj].z += x.z; gv[jj].w += x.w;
+        }
       }
-      pp[e] -= lr * d;
     }
-    if (a.m) reinterpret_cast<float4*>(a.m)[i] = bv;
-    uint2 sh;
-    sh.x = pack_bf16x2(pv.x, pv.y);
-    sh.y = pack_bf16x2(pv.z, pv.w);
-    for (int p = 0; p < a.world; ++p) {
-      const int q = (a.rank + p) % a.world;
-      reinterpret_cast<float4*>(h.data[q])[i] = pv;
-      if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
+#pragma unroll
+    for (int jj = 0; jj < kIlp; ++jj) {
+      const int64_t i = i0 + jj * stride;
+      if (i >= s1) break;
+      float4 g = gv[jj];
+      float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
+      float* pp = &pv.x;
+      float* gg = &g.x;
+      float4 bv = a.m ? reinterpret_cast<float4*>(a.m)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float* bb = &bv.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float d = gg[e] * gs + a.wd * pp[e];
+        if (a.m) {
+          bb[e] = first ? d : a.momentum * bb[e] + (1.f - a.dampening) * d;
+          d = a.nesterov ? d + a.momentum * bb[e] : bb[e];
+        }
+        pp[e] -= lr * d;
+      }
+      if (a.m) reinterpret_cast<float4*>(a.m)[i] = bv;
+      uint2 sh;
+      sh.x = pack_bf16x2(pv.x, pv.y);
+      sh.y = pack_bf16x2(pv.z, pv.w);
+      for (int p = 0; p < a.world; ++p) {
+        const int q = (a.rank + p) % a.world;
+        reinterpret_cast<float4*>(h.data[q])[i] = pv;
+        if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
+      }
     }
   }
   if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
@@ -299,15 +377,31 @@ __global__ void __launch_bounds__(512) all_reduce_kernel(FusedArgs a, Handles h)
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   // reduce into registers first, then a second barrier before writing so no
   // rank overwrites a shard another rank is still reading
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
+       i0 += kIlp * stride) {
+    float4 g[kIlp];
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
     for (int p = 0; p < a.world; ++p) {
-      const float4 x = ld_cg4(h.grad[p] + 4 * i);
-      g.x += x.x; g.y += x.y; g.z += x.z; g.w += x.w;
+#pragma unroll
+      for (int j = 0; j < kIlp; ++j) {
+        const int64_t i = i0 + j * stride;
+        if (i < s1) {
+          const float4 x = ld_cg4(h.grad[p] + 4 * i);
+          g[j].x += x.x; g[j].y += x.y; g[j].z += x.z; g[j].w += x.w;
+        }
+      }
     }
-    g.x *= sc; g.y *= sc; g.z *= sc; g.w *= sc;
-    reinterpret_cast<float4*>(h.data[a.rank])[i] = g;  // staging (data region)
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) {
+      const int64_t i = i0 + j * stride;
+      if (i < s1) {
+        float4 gj = g[j];
+        gj.x *= sc; gj.y *= sc; gj.z *= sc; gj.w *= sc;
+        reinterpret_cast<float4*>(h.data[a.rank])[i] = gj;  // staging (data region)
+      }
+    }
   }
   if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
     end_launch(a.bucket, sig);
@@ -321,16 +415,9 @@ __global__ void __launch_bounds__(512) all_reduce_kernel(FusedArgs a, Handles h)
       reinterpret_cast<float4*>(h.grad[q])[i] = g;
     }
   }
-  // second completion round on a separate bucket slot (bucket + 1)
-  const int b2 = a.bucket + 1;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < a.world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + b2, 1u);
-    wait_ge(sig + SigLayout::kDone + b2, epoch * (uint32_t)(a.world * gridDim.x), limit, a.err,
-            kErrPeerTimeout);
-  }
-  __syncthreads();
+  // second completion round on a separate slot (bucket + 1): every rank's
+  // result is in every buffer before anyone reuses them
+  phase_done(h, a.world, a.bucket + 1, epoch, sig, limit, a.err);
   end_launch(a.bucket, sig);
 }
 
@@ -414,8 +501,9 @@ __global__ void __launch_bounds__(512) weighted_average_kernel(FusedArgs a, Hand
   if (threadIdx.x == 0) {
     __threadfence_system();
     for (int p = 0; p < a.world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + b2, 1u);
-    wait_ge(sig + SigLayout::kDone + b2, epoch * (uint32_t)(a.world * gridDim.x), limit, a.err,
-            kErrPeerTimeout);
+    wait_ge(sig + SigLayout::kDone + b2,
+            *(volatile uint32_t*)(sig + SigLayout::kBase + b2) + (uint32_t)(a.world * gridDim.x),
+            limit, a.err, kErrPeerTimeout);
   }
   __syncthreads();
   // the gradient arena served as staging for this rank's shard: clear it
@@ -469,24 +557,32 @@ cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, c
     h.sig[p] = p < a.world ? ptrs.sig[p] : nullptr;
   }
   const int threads = 512;
-  int blocks = a.blocks > 0 ? a.blocks : 32;
+  const void* fn = nullptr;
   switch (op) {
-    case FusedOp::kArAdamW:
-      fused_ar_adamw_kernel<<<blocks, threads, 0, st>>>(a, h);
-      break;
-    case FusedOp::kArSgd:
-      fused_ar_sgd_kernel<<<blocks, threads, 0, st>>>(a, h);
-      break;
-    case FusedOp::kAllReduce:
-      all_reduce_kernel<<<blocks, threads, 0, st>>>(a, h);
-      break;
-    case FusedOp::kWeightedAverage:
-      weighted_average_kernel<<<blocks, threads, 0, st>>>(a, h);
-      break;
-    case FusedOp::kBroadcast:
-      broadcast_pull_kernel<<<blocks, threads, 0, st>>>(a, h);
-      break;
+    case FusedOp::kArAdamW: fn = (const void*)fused_ar_adamw_kernel; break;
+    case FusedOp::kArSgd: fn = (const void*)fused_ar_sgd_kernel; break;
+    case FusedOp::kAllReduce: fn = (const void*)all_reduce_kernel; break;
+    case FusedOp::kWeightedAverage: fn = (const void*)weighted_average_kernel; break;
+    case FusedOp::kBroadcast: fn = (const void*)broadcast_pull_kernel; break;
   }
+  if (fn == nullptr) return cudaErrorInvalidValue;
+  // Every block waits (bounded) for all blocks of all ranks, so the grid must
+  // be co-resident: cap it by the occupancy of this kernel (0 = the cap).
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int cap = per_sm * num_sms();
+  // default: enough blocks for about two float4 pairs per thread of this
+  // rank's shard (small messages: few blocks, less start/finish overhead)
+  const int64_t shard4 = ((a.end - a.start) / 4 + a.world - 1) / a.world;
+  const int64_t want = std::max<int64_t>(1, (shard4 + threads * kIlp * 2 - 1) / (threads * kIlp * 2));
+  int blocks = a.blocks > 0 ? std::min(a.blocks, cap) : (int)std::min<int64_t>(want, cap);
+  FusedArgs al = a;
+  al.blocks = blocks;
+  void* args[] = {(void*)&al, (void*)&h};
+  cudaError_t e = cudaLaunchKernel(fn, dim3(blocks), dim3(threads), args, 0, st);
+  if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
 }

@@ -1,0 +1,218 @@
+"""Collective benchmarks on one NVLink/NVSwitch node.
+
+Launch one rank per GPU (``torchrun --nproc-per-node N --master-addr 127.0.0.1
+-m flodl_b200.parallel.bench_collectives --mode ...``); rank 0 prints JSON
+lines. All times are CUDA-event device times, max over ranks.
+
+Modes:
+
+* ``sweep``     all-reduce (sum) of fp32 and bf16 buffers from 1 KiB to 1 GiB:
+                the peer-memory kernel (fp32) and NCCL (fp32, bf16); algorithmic
+                and bus bandwidth (2 (n-1)/n x bytes / time).
+* ``fused``     the fused gradient all-reduce + AdamW kernel on a parameter
+                arena the size of the LM benchmark (or ``--numel``), reported
+                against its NVLink roofline: each rank reads (n-1)/n of the f32
+                gradients from its peers and writes (n-1)/n of the updated f32
+                weights and bf16 shadows to them; the target time is the larger
+                direction over the measured 770 GB/s per-direction peer copy
+                bandwidth.
+* ``averaging`` cluster parameter averaging with uneven work: ResNet-20,
+                rank r runs 4 + r local SGD steps per round on its own batch,
+                then the parameters are averaged weighted by the steps each
+                rank did (the reference's realized-work mass), through the fused
+                weighted-average kernel (``--engine peer``) or NCCL
+                (``--engine nccl``: scale, all-reduce, divide).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+LINK_GBS = 770.0  # measured peer copy bandwidth per direction (B200 NVLink 5)
+
+
+def _init():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return rank, world, dev
+
+
+def _time(fn, iters, warmup, world):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())  # ms
+
+
+def sweep(rank, world, dev, args):
+    from .peer import PeerComm
+    max_bytes = 1 << args.max_log2
+    comm = PeerComm(max_bytes // 4, dev, with_shadow=False, timeout_s=10.0)
+    buf = torch.empty(max_bytes // 4, device=dev)
+    buf16 = torch.empty(max_bytes // 2, device=dev, dtype=torch.bfloat16)
+    nb = 10
+    while nb <= args.max_log2:
+        nbytes = 1 << nb
+        iters = 50 if nbytes <= (64 << 20) else 10
+        n32 = max(nbytes // 4, 4)
+        comm.grad[:n32].fill_(1.0)
+        t_peer = _time(lambda: comm.all_reduce_(n32, average=False, slot=0), iters, 3, world)
+        comm.check()
+        t_nccl = _time(lambda: dist.all_reduce(buf[:n32]), iters, 3, world)
+        n16 = max(nbytes // 2, 8)
+        t_nccl16 = _time(lambda: dist.all_reduce(buf16[:n16]), iters, 3, world)
+        if rank == 0:
+            f = 2.0 * (world - 1) / world
+            rec = {"mode": "sweep", "n_gpus": world, "bytes": nbytes}
+            for name, t in (("peer_f32", t_peer), ("nccl_f32", t_nccl), ("nccl_bf16", t_nccl16)):
+                rec[name] = {"us": round(t * 1e3, 2), "algbw_gbs": round(nbytes / t / 1e6, 2),
+                             "busbw_gbs": round(f * nbytes / t / 1e6, 2)}
+            print(json.dumps(rec), flush=True)
+        nb += 2
+    comm.close()
+
+
+def fused(rank, world, dev, args):
+    from .peer import PeerComm
+    n = (args.numel + 63) // 64 * 64
+    comm = PeerComm(n, dev, timeout_s=10.0)
+    C = comm.C
+    comm.data[:n].normal_()
+    comm.grad[:n].normal_()
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    lr = torch.full((), 1e-4, device=dev)
+    step = torch.ones((), device=dev)
+    buckets = max(1, args.buckets)
+    per = (n // buckets + 63) // 64 * 64
+
+    def run():
+        for i in range(buckets):
+            s0 = i * per
+            s1 = min(n, s0 + per)
+            if s0 >= s1:
+                break
+            comm.launch(C.FUSED_AR_ADAMW, bucket=2 * i, start=s0, end=s1, blocks=args.blocks,
+                        m=m, v=v, lr=lr, step=step, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.1)
+
+    t = _time(run, 20, 3, world)
+    comm.check()
+    frac = (world - 1) / world
+    in_bytes = frac * 4 * n            # f32 gradient shards read from peers
+    out_bytes = frac * (4 + 2) * n     # f32 weights + bf16 shadows written to peers
+    target_ms = max(in_bytes, out_bytes) / (LINK_GBS * 1e9) * 1e3
+    if rank == 0:
+        print(json.dumps({"mode": "fused_allreduce_adamw", "n_gpus": world, "numel": n,
+                          "buckets": buckets, "us": round(t * 1e3, 2),
+                          "nvlink_roofline_us": round(target_ms * 1e3, 2),
+                          "frac_of_roofline": round(target_ms / t, 3) if world > 1 else None,
+                          "link_gbs_assumed": LINK_GBS}), flush=True)
+    comm.close()
+
+
+def averaging(rank, world, dev, args):
+    from ..models import ResNet20
+    from ..optim import SGD
+    from ..utils.arena import ParamArena
+    torch.manual_seed(0)
+    model = ResNet20(device=dev)
+    params = list(model.parameters())
+    comm = None
+    if args.engine == "peer" and world > 1:
+        from .peer import PeerComm
+        numel = sum((p.numel() + 63) // 64 * 64 for p in params)
+        comm = PeerComm(numel, dev, timeout_s=10.0)
+        arena = ParamArena(params, alloc=comm.data_alloc, grad_alloc=comm.grad_alloc,
+                           with_shadow=False)
+        arena.shadow = comm.shadow[:arena.numel]
+        arena.rebind()
+        arena.refresh_shadow()
+    else:
+        arena = ParamArena(params)
+    opt = SGD(params, lr=0.1, momentum=0.9, weight_decay=1e-4)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(128, 3, 32, 32, device=dev, generator=g)
+    y = torch.randint(0, 10, (128,), device=dev, generator=g)
+    local_steps = 4 + rank
+    steps = [local_steps]
+    if world > 1:
+        all_steps = [None] * world
+        dist.all_gather_object(all_steps, local_steps)
+        steps = all_steps
+    bufs = [b for b in model.buffers() if b.is_floating_point()]
+
+    def round_():
+        for _ in range(local_steps):
+            loss = model.loss(x, y)
+            loss.backward()
+            opt.step()
+            opt.zero_grad()
+        if world == 1:
+            return
+        mass = float(local_steps)
+        if comm is not None:
+            comm.weighted_average_(arena.numel, mass, 1.0, slot=0)
+        else:
+            arena.data.mul_(mass)
+            dist.all_reduce(arena.data)
+            arena.data.div_(float(sum(steps)))
+            arena.refresh_shadow()
+        for b in bufs:  # batch-norm running statistics, same weighting
+            b.mul_(mass / float(sum(steps)))
+            dist.all_reduce(b)
+
+    t = _time(round_, args.rounds, 2, world)
+    if comm is not None:
+        comm.check()
+    samples = 128 * sum(steps)
+    if rank == 0:
+        print(json.dumps({"mode": "averaging", "engine": args.engine if world > 1 else "none",
+                          "n_gpus": world, "model": "resnet20", "batch_per_step": 128,
+                          "local_steps_per_rank": steps, "round_ms": round(t, 3),
+                          "samples_per_s": round(samples / (t / 1e3), 1),
+                          "note": "device time per round (local steps + weighted average), max over ranks"}),
+              flush=True)
+    if comm is not None:
+        comm.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", default="sweep", choices=["sweep", "fused", "averaging"])
+    ap.add_argument("--max-log2", type=int, default=30)
+    ap.add_argument("--numel", type=int, default=19_000_000)
+    ap.add_argument("--buckets", type=int, default=4)
+    ap.add_argument("--blocks", type=int, default=0)
+    ap.add_argument("--engine", default="peer", choices=["peer", "nccl"])
+    ap.add_argument("--rounds", type=int, default=10)
+    args = ap.parse_args()
+    rank, world, dev = _init()
+    {"sweep": sweep, "fused": fused, "averaging": averaging}[args.mode](rank, world, dev, args)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -33,7 +33,7 @@ class FusedDdp:
     fuses_optimizer = True
 
     def __init__(self, model: torch.nn.Module, optimizer, bucket_mb: float = 16.0,
-                 blocks: int = 64, group=None, timeout_s: float = 10.0):
+                 blocks: int = 0, group=None, timeout_s: float = 10.0):
         self.model = model
         self.opt = optimizer
         if len(optimizer.groups) != 1:

@@ -31,6 +31,10 @@ class PeerTimeout(RuntimeError):
 
 
 class PeerComm:
+    """Symmetric peer-mapped buffers of one rank plus the fused collective
+    launches over them. ``blocks`` arguments: CTAs per launch, 0 = as many as
+    can be co-resident (the kernels wait on all of their own blocks)."""
+
     def __init__(self, numel: int, device: torch.device, group=None, with_shadow: bool = True,
                  timeout_s: float = 10.0):
         C = cuda_ext()
@@ -109,18 +113,18 @@ class PeerComm:
         if code:
             raise PeerTimeout(f"peer communicator: {ERR_NAMES.get(code, code)} on rank {self.rank}")
 
-    def all_reduce_(self, n: int, average: bool = True, slot: int = 0, blocks: int = 32) -> None:
+    def all_reduce_(self, n: int, average: bool = True, slot: int = 0, blocks: int = 0) -> None:
         """In-place all-reduce of grad[:n] (uses data[:n] as scratch)."""
         self.launch(self.C.FUSED_ALL_REDUCE, bucket=slot, start=0, end=(n + 3) // 4 * 4,
                     average=int(average), blocks=blocks)
 
-    def broadcast_(self, n: int, root: int = 0, slot: int = 0, blocks: int = 32) -> None:
+    def broadcast_(self, n: int, root: int = 0, slot: int = 0, blocks: int = 0) -> None:
         """Every rank pulls data[:n] (and refreshes its bf16 shadow) from ``root``."""
         self.launch(self.C.FUSED_BROADCAST, bucket=slot, start=0, end=(n + 3) // 4 * 4, root=root,
                     blocks=blocks)
 
     def weighted_average_(self, n: int, mass: float, gamma: float = 1.0, slot: int = 0,
-                          divergence: Optional[torch.Tensor] = None, blocks: int = 32) -> None:
+                          divergence: Optional[torch.Tensor] = None, blocks: int = 0) -> None:
         """data[:n] <- sum_i (mass_i^gamma / sum mass^gamma) data_i[:n]."""
         self.launch(self.C.FUSED_WEIGHTED_AVG, bucket=slot, start=0, end=(n + 3) // 4 * 4,
                     mass=float(mass), gamma=float(gamma), m=divergence, blocks=blocks)

@@ -153,3 +153,10 @@ def test_dot_export():
     g = FlowBuilder.from_(Linear(2, 2)).tag("a").also(Linear(2, 2)).build()
     d = g.dot()
     assert d.startswith("digraph") and '"linear_1" -> "linear_2"' in d
+
+
+def test_quickstart_mlp_flowbuilder_learns():
+    """BASELINE config 1 (CPU FlowBuilder MLP regression), shortened."""
+    from flodl_b200.examples.mlp_flowbuilder import run
+    r = run(steps=300)
+    assert r["final_loss"] < 0.3 * r["first_loss"], r
