@@ -170,7 +170,9 @@ def main():
     torch.cuda.synchronize()
 
     graph = None
-    if not args.no_graph:
+    # stock torch DDP cannot be captured into a CUDA graph (its reducer
+    # issues host-side work during backward): the torch arm runs eager at N > 1
+    if not args.no_graph and not (args.impl == "torch" and world > 1):
         graph = torch.cuda.CUDAGraph()
         c0 = launches_fn() if launches_fn else 0
         with torch.cuda.graph(graph):

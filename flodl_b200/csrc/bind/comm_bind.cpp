@@ -82,7 +82,9 @@ void fused_launch(int64_t op, py::dict cfg, const std::vector<int64_t>& data,
   a.bucket = (int)geti("bucket", 0);
   a.start = geti("start", 0);
   a.end = geti("end", 0);
-  a.blocks = (int)geti("blocks", 32);
+  a.blocks = (int)geti("blocks", 0);
+  a.threads = (int)geti("threads", 512);
+  FL_CHECK(a.threads == 128 || a.threads == 256 || a.threads == 512, "threads must be 128, 256 or 512");
   a.m = reinterpret_cast<float*>(getp("m"));
   a.v = reinterpret_cast<float*>(getp("v"));
   a.lr = reinterpret_cast<const float*>(getp("lr"));

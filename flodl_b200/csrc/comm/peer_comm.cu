@@ -556,7 +556,7 @@ cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, c
     h.shadow[p] = p < a.world ? ptrs.shadow[p] : nullptr;
     h.sig[p] = p < a.world ? ptrs.sig[p] : nullptr;
   }
-  const int threads = 512;
+  const int threads = a.threads;
   const void* fn = nullptr;
   switch (op) {
     case FusedOp::kArAdamW: fn = (const void*)fused_ar_adamw_kernel; break;

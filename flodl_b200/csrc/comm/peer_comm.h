@@ -30,7 +30,8 @@ struct FusedArgs {
   int rank = 0, world = 1, root = 0;
   int bucket = 0;          // signal slot (uses slots bucket and bucket+1)
   int64_t start = 0, end = 0;  // element range in the arenas (multiples of 4)
-  int blocks = 32;
+  int blocks = 0;           // CTAs (0: sized to the message, capped by co-residency)
+  int threads = 512;        // threads per CTA: 128 lets a launch share SMs with compute kernels
   // optimizer state (local, full arena size) and hyper-parameters
   float* m = nullptr;
   float* v = nullptr;
