@@ -3,3 +3,4 @@ from .bert import (BertConfig, BertForMaskedLM, BertForQuestionAnswering,  # noq
                    BertForSequenceClassification, BertForTokenClassification, BertModel)
 from .transformer_lm import DecoderBlock, TransformerLM  # noqa: F401
 from .resnet import BasicBlock, ResNet20  # noqa: F401
+from .zoo import ZOO, CharRNN, ModelDef, OLMo  # noqa: F401
