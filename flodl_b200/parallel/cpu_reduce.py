@@ -47,8 +47,9 @@ def _recv_exact(sock: socket.socket, n: int) -> bytes:
     return bytes(buf)
 
 
-def send_frame(sock, key: bytes, kind: int, seq: int, payload: bytes, lock=None) -> None:
-    f = native().encode_frame(MAGIC, kind, seq, payload, key)
+def send_frame(sock, key: bytes, kind: int, seq: int, payload: bytes, lock=None,
+               magic: int = MAGIC) -> None:
+    f = native().encode_frame(magic, kind, seq, payload, key)
     if lock:
         with lock:
             sock.sendall(f)
@@ -56,16 +57,22 @@ def send_frame(sock, key: bytes, kind: int, seq: int, payload: bytes, lock=None)
         sock.sendall(f)
 
 
-def recv_frame(sock, key: bytes) -> Tuple[int, int, bytes]:
+def recv_frame(sock, key: bytes, magic: int = MAGIC,
+               max_frame: int = MAX_FRAME) -> Tuple[int, int, bytes]:
+    """Read one signed frame; raises ConnectionError on a wrong channel magic,
+    an oversized frame or a bad signature."""
     N = native()
     hdr = _recv_exact(sock, N.WIRE_HEADER_BYTES)
-    magic, kind, flags, seq, ln = N.peek_header(hdr)
-    if magic != MAGIC:
+    got, kind, flags, seq, ln = N.peek_header(hdr)
+    if got != magic:
         raise ConnectionError("bad frame magic")
-    if ln > MAX_FRAME:
+    if ln > max_frame:
         raise ConnectionError("frame exceeds ceiling")
     rest = _recv_exact(sock, ln + 8)
-    _m, kind, _f, seq, payload = N.decode_frame(hdr + rest, key, MAX_FRAME)
+    try:
+        _m, kind, _f, seq, payload = N.decode_frame(hdr + rest, key, max_frame)
+    except Exception as e:  # signature or format failure
+        raise ConnectionError(f"rejected frame: {e}") from e
     return kind, seq, payload
 
 
