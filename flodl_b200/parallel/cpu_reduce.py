@@ -12,6 +12,13 @@ rank):
     CONSENSUS(round, bytes)           controller -> rank: sum(payloads) / sum(mass)
     HEARTBEAT(rank)                   rank -> controller, every ``heartbeat_s``
     DEAD(rank)                        controller -> ranks when a heartbeat is stale
+    HOSTFRAME(round, mass, dtype, ranks, bytes)
+                                      relay -> controller: the folded sum of a
+                                      host's ranks (flodl_b200.parallel.relay)
+
+One connection may carry several ranks (a per-host relay): every HELLO on it
+registers one more rank, a HEARTBEAT or BYE with a rank payload speaks for
+that rank only, and a DEAD from a relay reports a local rank that exited.
 
 A round completes when every live rank contributed; a rank whose heartbeat is
 older than ``heartbeat_timeout`` is declared dead, dropped from membership
@@ -32,7 +39,7 @@ import torch
 from .._ext import native
 
 MAGIC = 0x464C4443  # "FLDC"
-K_HELLO, K_ROUND, K_CONSENSUS, K_HEARTBEAT, K_DEAD, K_BYE = 1, 2, 3, 4, 5, 6
+K_HELLO, K_ROUND, K_CONSENSUS, K_HEARTBEAT, K_DEAD, K_BYE, K_HOSTFRAME = 1, 2, 3, 4, 5, 6, 7
 DT_F32, DT_BF16 = 0, 1
 MAX_FRAME = 1 << 34
 
@@ -93,28 +100,37 @@ def decode_tensor(dt: int, raw: bytes) -> torch.Tensor:
 class CpuReduceController:
     """Accepts rank connections, runs reduce rounds, tracks heartbeats."""
 
-    def __init__(self, world: int, key: bytes, host: str = "127.0.0.1", port: int = 0,
+    def __init__(self, world: int, key: bytes, host: str = "127.0.0.1", port: Optional[int] = 0,
                  heartbeat_timeout: float = 30.0):
+        """``port=None`` binds nothing: connections arrive through :meth:`adopt`
+        (the single-port mux of :mod:`flodl_b200.parallel.portmux`)."""
         self.world = world
         self.key = key
         self.hb_timeout = heartbeat_timeout
-        self.srv = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
-        self.srv.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
-        self.srv.bind((host, port))
-        self.srv.listen(world + 8)
-        self.port = self.srv.getsockname()[1]
+        self.srv = None
+        self.port = None
+        if port is not None:
+            self.srv = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+            self.srv.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+            self.srv.bind((host, port))
+            self.srv.listen(world + 8)
+            self.port = self.srv.getsockname()[1]
         self.conns: Dict[int, socket.socket] = {}
         self.send_locks: Dict[int, threading.Lock] = {}
         self.alive = set(range(world))
         self.dead: List[int] = []
         self.last_hb: Dict[int, float] = {}
-        self.pending: Dict[int, Dict[int, Tuple[torch.Tensor, float]]] = {}
+        self.pending: Dict[int, Dict[int, Tuple[Optional[torch.Tensor], float]]] = {}
+        self.host_parts: Dict[int, List[Tuple[torch.Tensor, float]]] = {}
         self.lock = threading.Lock()
         self.cv = threading.Condition(self.lock)
         self.rejected = 0
+        self.frames_in = 0        # data frames received (ROUND + HOSTFRAME)
+        self.bytes_in = 0         # their payload bytes
         self._stop = threading.Event()
         self.rounds_done = 0
-        threading.Thread(target=self._accept_loop, daemon=True).start()
+        if self.srv is not None:
+            threading.Thread(target=self._accept_loop, daemon=True).start()
         threading.Thread(target=self._watchdog, daemon=True).start()
 
     # ------------------------------------------------------------ plumbing
@@ -124,32 +140,83 @@ class CpuReduceController:
                 c, _ = self.srv.accept()
             except OSError:
                 return
-            threading.Thread(target=self._serve, args=(c,), daemon=True).start()
+            self.adopt(c)
+
+    def adopt(self, c: socket.socket) -> None:
+        """Serve a connection accepted elsewhere (its first bytes unread)."""
+        threading.Thread(target=self._serve, args=(c,), daemon=True).start()
+
+    def _register(self, c: socket.socket, rank: int, lock: threading.Lock) -> None:
+        with self.lock:
+            self.conns[rank] = c
+            self.send_locks[rank] = lock
+            self.last_hb[rank] = time.time()
+
+    def _declare_dead(self, rank: int) -> None:
+        with self.cv:
+            if rank not in self.alive:
+                return
+            self.alive.discard(rank)
+            self.dead.append(rank)
+            for rnd in list(self.pending):
+                self._maybe_finish(rnd)
+        self._broadcast(K_DEAD, 0, struct.pack("<i", rank))
 
     def _serve(self, c: socket.socket):
-        rank = None
+        mine: List[int] = []
+        lock = threading.Lock()
         try:
             kind, _, payload = recv_frame(c, self.key)
             if kind != K_HELLO:
                 raise ConnectionError("expected HELLO")
             (rank,) = struct.unpack("<i", payload)
-            with self.lock:
-                self.conns[rank] = c
-                self.send_locks[rank] = threading.Lock()
-                self.last_hb[rank] = time.time()
+            mine.append(rank)
+            self._register(c, rank, lock)
             while not self._stop.is_set():
                 kind, seq, payload = recv_frame(c, self.key)
                 if kind == K_HEARTBEAT:
+                    now = time.time()
+                    who = struct.unpack("<i", payload) if len(payload) == 4 else mine
                     with self.lock:
-                        self.last_hb[rank] = time.time()
+                        for r in who:
+                            self.last_hb[r] = now
                 elif kind == K_ROUND:
                     rnd, mass, dt = struct.unpack("<qdi", payload[:20])
                     t = decode_tensor(dt, payload[20:])
                     with self.cv:
-                        self.last_hb[rank] = time.time()
-                        self.pending.setdefault(rnd, {})[rank] = (t, mass)
+                        self.frames_in += 1
+                        self.bytes_in += len(payload)
+                        self.last_hb[mine[0]] = time.time()
+                        self.pending.setdefault(rnd, {})[mine[0]] = (t, mass)
                         self._maybe_finish(rnd)
+                elif kind == K_HOSTFRAME:
+                    rnd, mass, dt, nr = struct.unpack("<qdii", payload[:24])
+                    ranks = struct.unpack(f"<{nr}i", payload[24:24 + 4 * nr])
+                    t = decode_tensor(dt, payload[24 + 4 * nr:])
+                    with self.cv:
+                        self.frames_in += 1
+                        self.bytes_in += len(payload)
+                        now = time.time()
+                        got = self.pending.setdefault(rnd, {})
+                        for r in ranks:
+                            got[r] = (None, 0.0)
+                            self.last_hb[r] = now
+                        self.host_parts.setdefault(rnd, []).append((t, mass))
+                        self._maybe_finish(rnd)
+                elif kind == K_HELLO:  # relay: one more local rank on this connection
+                    (r,) = struct.unpack("<i", payload)
+                    mine.append(r)
+                    self._register(c, r, lock)
+                elif kind == K_DEAD:  # relay: a local rank exited
+                    (r,) = struct.unpack("<i", payload)
+                    self._declare_dead(r)
                 elif kind == K_BYE:
+                    if len(payload) == 4:
+                        (r,) = struct.unpack("<i", payload)
+                        if r in mine:
+                            mine.remove(r)
+                        if mine:
+                            continue
                     break
         except Exception:
             with self.lock:
@@ -178,10 +245,12 @@ class CpuReduceController:
                 self._broadcast(K_DEAD, 0, struct.pack("<i", r))
 
     def _broadcast(self, kind, seq, payload, ranks=None):
+        sent = set()  # a relay's connection carries several ranks: send once
         for r in list(ranks if ranks is not None else self.alive):
             c = self.conns.get(r)
-            if c is None:
+            if c is None or id(c) in sent:
                 continue
+            sent.add(id(c))
             try:
                 send_frame(c, self.key, kind, seq, payload, self.send_locks[r])
             except OSError:
@@ -191,7 +260,8 @@ class CpuReduceController:
         got = self.pending.get(rnd, {})
         if not self.alive or not self.alive.issubset(got.keys()):
             return
-        contribs = [got[r] for r in sorted(self.alive)]
+        contribs = [got[r] for r in sorted(self.alive) if got[r][0] is not None]
+        contribs += self.host_parts.pop(rnd, [])
         out = native().reduce_scaled([t for t, _ in contribs], [m for _, m in contribs])
         dt, raw = DT_F32, out.numpy().tobytes()
         payload = struct.pack("<qi", rnd, dt) + raw
@@ -203,7 +273,8 @@ class CpuReduceController:
     def close(self):
         self._stop.set()
         try:
-            self.srv.close()
+            if self.srv is not None:
+                self.srv.close()
         except OSError:
             pass
         for c in list(self.conns.values()):

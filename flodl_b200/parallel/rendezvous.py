@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import json
 import os
+import queue
 import socket
 import threading
 import time
@@ -46,20 +47,26 @@ class RendezvousServer:
     """Collects ``world`` HELLOs, assigns ranks (requested ranks are kept,
     the rest fill the gaps in arrival order), then relays rank 0's UID."""
 
-    def __init__(self, world: int, key: bytes, host: str = "127.0.0.1", port: int = 0,
+    def __init__(self, world: int, key: bytes, host: str = "127.0.0.1", port: Optional[int] = 0,
                  idle_timeout: float = IDLE_TIMEOUT_S, reject_cap: int = REJECT_CAP):
+        """``port=None`` binds nothing: connections arrive through :meth:`adopt`
+        (the single-port mux of :mod:`flodl_b200.parallel.portmux`)."""
         self.world, self.key = world, key
         self.idle_timeout, self.reject_cap = idle_timeout, reject_cap
         self.rejected = 0
         self.error: Optional[str] = None
         self.members: List[dict] = []
         self._conns: List[socket.socket] = []
-        self._sock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
-        self._sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
-        self._sock.bind((host, port))
-        self._sock.listen(128)
-        self._sock.settimeout(0.2)
-        self.host, self.port = self._sock.getsockname()
+        self._adopted: "queue.Queue[socket.socket]" = queue.Queue()
+        self._sock = None
+        self.host, self.port = host, None
+        if port is not None:
+            self._sock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+            self._sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+            self._sock.bind((host, port))
+            self._sock.listen(128)
+            self._sock.settimeout(0.2)
+            self.host, self.port = self._sock.getsockname()
         self._done = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
 
@@ -69,6 +76,18 @@ class RendezvousServer:
 
     def wait(self, timeout: Optional[float] = None) -> bool:
         return self._done.wait(timeout)
+
+    def adopt(self, c: socket.socket) -> None:
+        """Take a connection accepted elsewhere (its first bytes unread)."""
+        self._adopted.put(c)
+
+    def _accept(self) -> socket.socket:
+        if self._sock is None:
+            try:
+                return self._adopted.get(timeout=0.2)
+            except queue.Empty:
+                raise socket.timeout() from None
+        return self._sock.accept()[0]
 
     def _reject(self, c: socket.socket, reason: str) -> None:
         self.rejected += 1
@@ -91,7 +110,7 @@ class RendezvousServer:
                     self.error = f"rendezvous stopped after {self.rejected} rejected connections"
                     break
                 try:
-                    c, _ = self._sock.accept()
+                    c = self._accept()
                 except socket.timeout:
                     continue
                 c.settimeout(10.0)
@@ -143,7 +162,8 @@ class RendezvousServer:
                     c.close()
                 except OSError:
                     pass
-            self._sock.close()
+            if self._sock is not None:
+                self._sock.close()
             self._done.set()
 
 
