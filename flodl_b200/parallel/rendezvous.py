@@ -24,7 +24,7 @@ import socket
 import threading
 import time
 from dataclasses import dataclass
-from typing import Callable, Dict, List, Optional
+from typing import Callable, Dict, List, Optional, Sequence
 
 from .cpu_reduce import recv_frame, send_frame
 
@@ -48,10 +48,16 @@ class RendezvousServer:
     the rest fill the gaps in arrival order), then relays rank 0's UID."""
 
     def __init__(self, world: int, key: bytes, host: str = "127.0.0.1", port: Optional[int] = 0,
-                 idle_timeout: float = IDLE_TIMEOUT_S, reject_cap: int = REJECT_CAP):
+                 idle_timeout: float = IDLE_TIMEOUT_S, reject_cap: int = REJECT_CAP,
+                 agree_on: Sequence[str] = ("model_sig",)):
         """``port=None`` binds nothing: connections arrive through :meth:`adopt`
-        (the single-port mux of :mod:`flodl_b200.parallel.portmux`)."""
+        (the single-port mux of :mod:`flodl_b200.parallel.portmux`).
+        ``agree_on`` names HELLO ``info`` keys every rank must report equal
+        (the model signature by default): a mismatch refuses the formation,
+        since ranks training different models would corrupt each other at
+        the first collective."""
         self.world, self.key = world, key
+        self.agree_on = tuple(agree_on)
         self.idle_timeout, self.reject_cap = idle_timeout, reject_cap
         self.rejected = 0
         self.error: Optional[str] = None
@@ -128,6 +134,10 @@ class RendezvousServer:
                     continue
                 hellos.append((want, hello, c))
                 last = time.monotonic()
+            for k in self.agree_on:
+                vals = {json.dumps(h.get("info", {}).get(k)) for _, h, _ in hellos}
+                if len(vals) > 1:
+                    self.error = f"ranks disagree on {k}: formation refused"
             if self.error:
                 for _, _, c in hellos:
                     self._reject(c, self.error)
