@@ -1,0 +1,233 @@
+"""Command line: ``python -m flodl_b200 <command>``.
+
+Reference role: flodl-cli (``fdl``) - probe, diagnose, status, start, launch,
+scaffold and shell completions (flodl-cli/src/{probe,diagnose.rs,status.rs,
+init.rs,completions}). Build and download commands of the reference (libtorch,
+NCCL) have no counterpart: this framework builds against the installed
+PyTorch with ``python setup.py build_ext --inplace``.
+
+Commands:
+
+    probe [--json]                     GPUs, findings, driver, host memory
+    diagnose [--json]                  import/extension/device/NCCL/peer checks
+    status HOST:PORT [--json]          the controller's state.json
+    start HOST:PORT [--token HEX]      arm a manual/hybrid start
+    launch --devices D0,D1 [--policy abort|shrink] -- CMD ...
+    init NAME                          scaffold a training script
+    completions bash                   bash completion script
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import urllib.error
+import urllib.request
+from typing import List, Tuple
+
+COMMANDS = ("probe", "diagnose", "status", "start", "launch", "init", "completions")
+
+
+def _probe(a) -> int:
+    from .utils import hw
+    r = hw.report()
+    if a.json:
+        print(json.dumps(r, indent=2))
+        return 0
+    print(f"driver {r['driver'] or 'n/a'}; host RAM {r['host_memory_mb'] / 1024:.0f} GiB "
+          f"({r['host_available_mb'] / 1024:.0f} available); {r['cpus']} CPUs")
+    if not r["gpus"]:
+        print("no visible GPU")
+    for g in r["gpus"]:
+        print(f"  [{g['index']}] {g['name']}  {g['arch']}  {g['vram_mb'] / 1024:.0f} GiB")
+    for n in r["notes"]:
+        print(f"  note ({n['vendor']}, {n['kind']}): {n['message']}")
+    return 0
+
+
+def diagnose_checks() -> List[Tuple[str, str, str]]:
+    """(check, OK|WARN|FAIL, detail) rows; read-only, changes no device setting."""
+    rows = []
+    try:
+        import torch
+        rows.append(("torch", "OK", f"{torch.__version__} (CUDA {torch.version.cuda})"))
+    except Exception as e:
+        return [("torch", "FAIL", repr(e))]
+    from . import _ext
+    rows.append(("native runtime (_native)", "OK" if _ext._native else "FAIL",
+                 "loaded" if _ext._native else repr(_ext._NATIVE_ERR)))
+    have_cuda = torch.cuda.is_available()
+    c_state = "OK" if _ext._C else ("FAIL" if have_cuda else "WARN")
+    rows.append(("sm_100a kernels (_C)", c_state, "loaded" if _ext._C else repr(_ext._C_ERR)))
+    from .utils import hw
+    gpus = hw.detect_gpus()
+    if not gpus:
+        rows.append(("GPUs", "WARN", "none visible: CPU paths only"))
+    for g in gpus:
+        ok = g.covered_by("10.0")
+        rows.append((f"GPU {g.index} arch", "OK" if ok else "FAIL",
+                     f"{g.name} {g.arch}" + ("" if ok else ": kernels are built for sm_100a only")))
+    if have_cuda:
+        try:
+            v = torch.cuda.nccl.version()
+            rows.append(("NCCL", "OK", ".".join(map(str, v)) if isinstance(v, tuple) else str(v)))
+        except Exception as e:
+            rows.append(("NCCL", "WARN", repr(e)))
+        n = torch.cuda.device_count()
+        missing = [(i, j) for i in range(n) for j in range(n)
+                   if i != j and not torch.cuda.can_device_access_peer(i, j)]
+        if n > 1:
+            rows.append(("peer access", "OK" if not missing else "WARN",
+                         f"all {n * (n - 1)} pairs" if not missing else f"no access for {missing[:4]}"))
+    for k in ("NCCL_P2P_DISABLE", "NCCL_SHM_DISABLE", "NCCL_NVLS_ENABLE"):
+        if k in os.environ:
+            rows.append((k, "WARN", f"set to {os.environ[k]!r}"))
+    return rows
+
+
+def _diagnose(a) -> int:
+    rows = diagnose_checks()
+    if a.json:
+        print(json.dumps([{"check": c, "state": s, "detail": d} for c, s, d in rows], indent=2))
+    else:
+        for c, s, d in rows:
+            print(f"{s:5s} {c}: {d}")
+    return 1 if any(s == "FAIL" for _, s, _ in rows) else 0
+
+
+def _url(hostport: str, path: str) -> str:
+    return f"http://{hostport}{path}"
+
+
+def _status(a) -> int:
+    try:
+        body = urllib.request.urlopen(_url(a.controller, "/state.json"), timeout=10).read()
+    except urllib.error.HTTPError as e:
+        print(f"controller answered {e.code}: {e.read().decode(errors='replace')}", file=sys.stderr)
+        return 1
+    except OSError as e:
+        print(f"controller unreachable: {e}", file=sys.stderr)
+        return 1
+    st = json.loads(body)
+    if a.json:
+        print(json.dumps(st, indent=2))
+    else:
+        for k, v in st.items():
+            print(f"{k}: {v}")
+    return 0
+
+
+def _start(a) -> int:
+    q = f"?token={a.token}" if a.token else ""
+    req = urllib.request.Request(_url(a.controller, "/start" + q), method="POST", data=b"")
+    try:
+        print(urllib.request.urlopen(req, timeout=10).read().decode())
+        return 0
+    except urllib.error.HTTPError as e:
+        print(f"refused ({e.code}): {e.read().decode(errors='replace')}", file=sys.stderr)
+        return 1
+
+
+def _launch(a) -> int:
+    from .parallel.launcher import LocalLauncher
+    cmd = a.command[1:] if a.command and a.command[0] == "--" else a.command
+    if not cmd:
+        print("launch: missing command after --", file=sys.stderr)
+        return 2
+    r = LocalLauncher(cmd, a.devices.split(","), a.policy, a.max_restarts).run()
+    print(json.dumps(r.__dict__))
+    return 0 if r.ok else 1
+
+
+_SCAFFOLD = '''"""{name}: a flodl_b200 training script (generated by `python -m flodl_b200 init`)."""
+import torch
+
+from flodl_b200 import FlowBuilder
+from flodl_b200.nn import GELU, Linear, mse_loss
+from flodl_b200.optim import Adam
+
+
+def main(steps: int = 200):
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    model = (FlowBuilder.from_(Linear(2, 16, device=dev)).through(GELU())
+             .through(Linear(16, 2, device=dev)).build())
+    opt = Adam(list(model.parameters()), lr=1e-2)
+    x = torch.randn(256, 2, device=dev)
+    y = torch.stack([x[:, 0] + x[:, 1], x[:, 0] - x[:, 1]], 1)
+    for step in range(steps):
+        loss = mse_loss(model(x), y)
+        loss.backward()
+        opt.step()
+        opt.zero_grad()
+        if step % 50 == 0:
+            print(f"step {{step}} loss {{loss.item():.4f}}")
+
+
+if __name__ == "__main__":
+    main()
+'''
+
+
+def _init(a) -> int:
+    d = a.name
+    if os.path.exists(d):
+        print(f"init: {d} already exists", file=sys.stderr)
+        return 1
+    os.makedirs(d)
+    with open(os.path.join(d, "train.py"), "w") as f:
+        f.write(_SCAFFOLD.format(name=os.path.basename(d)))
+    print(f"created {d}/train.py - run it with `python {d}/train.py`")
+    return 0
+
+
+_BASH = """_flodl_b200() {
+  local cur=${COMP_WORDS[COMP_CWORD]}
+  if [ $COMP_CWORD -eq 1 ]; then
+    COMPREPLY=( $(compgen -W "%s" -- "$cur") )
+  else
+    COMPREPLY=( $(compgen -W "--json --devices --policy --token --max-restarts" -- "$cur") )
+  fi
+}
+complete -F _flodl_b200 flodl_b200
+"""
+
+
+def _completions(a) -> int:
+    if a.shell != "bash":
+        print("completions: only bash is generated", file=sys.stderr)
+        return 2
+    print(_BASH % " ".join(COMMANDS))
+    return 0
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="python -m flodl_b200",
+                                 description="flodl_b200 command line")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("probe", help="hardware survey")
+    p.add_argument("--json", action="store_true")
+    p = sub.add_parser("diagnose", help="environment checks")
+    p.add_argument("--json", action="store_true")
+    p = sub.add_parser("status", help="controller state.json")
+    p.add_argument("controller")
+    p.add_argument("--json", action="store_true")
+    p = sub.add_parser("start", help="arm a manual start")
+    p.add_argument("controller")
+    p.add_argument("--token", default="")
+    p = sub.add_parser("launch", help="one process per device")
+    p.add_argument("--devices", required=True)
+    p.add_argument("--policy", default="abort", choices=["abort", "shrink"])
+    p.add_argument("--max-restarts", type=int, default=1)
+    p.add_argument("command", nargs=argparse.REMAINDER)
+    p = sub.add_parser("init", help="scaffold a training script")
+    p.add_argument("name")
+    p = sub.add_parser("completions", help="shell completion script")
+    p.add_argument("shell")
+    return ap
+
+
+def main(argv=None) -> int:
+    a = build_parser().parse_args(argv)
+    return {"probe": _probe, "diagnose": _diagnose, "status": _status, "start": _start,
+            "launch": _launch, "init": _init, "completions": _completions}[a.cmd](a)

@@ -1,0 +1,57 @@
+"""Command line: probe, diagnose, status/start against a live status board,
+init scaffold, completions (reference: flodl-cli/src/cli_tests.rs)."""
+import json
+import subprocess
+import sys
+
+from flodl_b200.cli import diagnose_checks, main
+from flodl_b200.parallel.membership import StartMode
+from flodl_b200.parallel.portmux import PortMux, StatusBoard
+
+
+def test_probe_json_with_spoofed_hardware(monkeypatch, capsys):
+    monkeypatch.setenv("FLODL_TESTING_GPU_JSON", json.dumps([{"arch": "10.0", "name": "NVIDIA B200"}] * 2))
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    assert main(["probe", "--json"]) == 0
+    r = json.loads(capsys.readouterr().out)
+    assert [g["arch"] for g in r["gpus"]] == ["sm_100", "sm_100"] and r["cpus"] > 0
+
+
+def test_diagnose_flags_uncovered_arch(monkeypatch):
+    monkeypatch.setenv("FLODL_TESTING_GPU_JSON", json.dumps([{"arch": "9.0"}]))
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    rows = {c: s for c, s, _ in diagnose_checks()}
+    assert rows["native runtime (_native)"] == "OK" and rows["GPU 0 arch"] == "FAIL"
+    assert main(["diagnose"]) == 1
+
+
+def test_status_and_start(capsys):
+    mux = PortMux()
+    board = StatusBoard()
+    mux.serve_status(board)
+    hp = f"127.0.0.1:{mux.port}"
+    assert main(["status", hp]) == 1  # nothing published yet
+    capsys.readouterr()
+    board.publish({"phase": "joining", "members": 1})
+    assert main(["status", hp, "--json"]) == 0
+    st = json.loads(capsys.readouterr().out)
+    assert st["phase"] == "joining" and st["members"] == 1
+    board.configure_start(StartMode.Manual, "ff" * 16)
+    assert main(["start", hp]) == 0 and board.start_requested()
+    mux.close()
+
+
+def test_init_scaffold_runs(tmp_path):
+    d = tmp_path / "proj"
+    assert main(["init", str(d)]) == 0
+    assert main(["init", str(d)]) == 1  # refuses to overwrite
+    r = subprocess.run([sys.executable, "-c",
+                        f"import runpy; m = runpy.run_path({str(d / 'train.py')!r}); m['main'](51)"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "step 50 loss" in r.stdout
+
+
+def test_completions(capsys):
+    assert main(["completions", "bash"]) == 0
+    assert "complete -F _flodl_b200" in capsys.readouterr().out
