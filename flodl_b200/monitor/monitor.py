@@ -6,8 +6,12 @@
   record log.
 * ``Timeline``: a background sampler of resource use plus discrete events
   (syncs, anchor changes, epoch starts), saved as JSON/CSV.
-* ``serve(port)``: a minimal live dashboard over HTTP with Server-Sent Events
-  (``/stream``) and late-join backfill (``/history``).
+* ``serve(port)``: a live dashboard over HTTP. ``/events`` is the whole-run
+  epoch feed (Server-Sent Events, late-join backfill) and ``/history`` its
+  JSON; with ``?path=`` the path-scoped record plane answers instead:
+  ``/paths`` (known nodes), ``/node?path=p`` (latest record of ``p`` and its
+  direct children), ``/history?path=p&n=N`` and ``/stream?path=p`` (SSE),
+  backed by :class:`~flodl_b200.monitor.records.RecordStore`.
 """
 from __future__ import annotations
 
@@ -20,6 +24,9 @@ import socketserver
 import threading
 import time
 from typing import Dict, List, Optional
+from urllib.parse import parse_qs, urlparse
+
+from .records import Leaf, RecordLog, RecordStore, build_tree, event_record
 
 
 def _cpu_ram():
@@ -50,7 +57,9 @@ def _gpu_stats():
 
 
 class Monitor:
-    def __init__(self, total_epochs: int, record_path: Optional[str] = None, quiet: bool = False):
+    def __init__(self, total_epochs: int, record_path: Optional[str] = None, quiet: bool = False,
+                 record_dir: Optional[str] = None, records: Optional[RecordStore] = None):
+        self.records = records or RecordStore(log=RecordLog(record_dir) if record_dir else None)
         self.total = total_epochs
         self.start = time.time()
         self.history: List[Dict] = []
@@ -75,11 +84,18 @@ class Monitor:
                 q.put_nowait(rec)
             except queue.Full:
                 pass
+        num = {k: float(v) for k, v in metrics.items() if isinstance(v, (int, float))}
+        self.records.publish_tree(build_tree([Leaf([], 1.0, num)], epoch_complete=True), epoch=epoch)
         parts = " ".join(f"{k}={v:.4g}" if isinstance(v, float) else f"{k}={v}" for k, v in metrics.items())
         line = f"epoch {done}/{self.total} {parts} eta {eta:.0f}s"
         if not self.quiet:
             print(line, flush=True)
         return line
+
+    def alert(self, message: str, sev: str = "warn", path: str = "root", **fields) -> None:
+        """Alert lane: a ``log`` record delivered to every viewer at or above ``path``."""
+        from .records import Severity
+        self.records.publish(event_record(path, "log", message, Severity(sev), **fields))
 
     def export_csv(self, path: str) -> None:
         if not self.history:
@@ -119,36 +135,61 @@ for (const k of keys) {{
             def log_message(self, *a):
                 pass
 
+            def _json(self, obj, code=200):
+                body = json.dumps(obj).encode()
+                self.send_response(code)
+                self.send_header("Content-Type", "application/json")
+                self.send_header("Content-Length", str(len(body)))
+                self.end_headers()
+                self.wfile.write(body)
+
+            def _sse(self, backfill, q, unsubscribe):
+                self.send_response(200)
+                self.send_header("Content-Type", "text/event-stream")
+                self.send_header("Cache-Control", "no-cache")
+                self.end_headers()
+                try:
+                    for rec in backfill:  # late-join backfill
+                        self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
+                    self.wfile.flush()
+                    while True:
+                        try:
+                            rec = q.get(timeout=15)
+                        except queue.Empty:
+                            self.wfile.write(b": keep-alive\n\n")
+                            self.wfile.flush()
+                            continue
+                        self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
+                        self.wfile.flush()
+                except Exception:
+                    pass
+                finally:
+                    unsubscribe()
+
             def do_GET(self):
-                if self.path.startswith("/history"):
-                    body = json.dumps(mon.history).encode()
-                    self.send_response(200)
-                    self.send_header("Content-Type", "application/json")
-                    self.send_header("Content-Length", str(len(body)))
-                    self.end_headers()
-                    self.wfile.write(body)
-                elif self.path.startswith("/stream"):
+                url = urlparse(self.path)
+                qs = parse_qs(url.query)
+                p = qs.get("path", [None])[0]
+                n = int(qs.get("n", ["256"])[0])
+                if url.path == "/paths":
+                    self._json(mon.records.paths())
+                elif url.path == "/node":
+                    self._json(mon.records.node(p or "root"))
+                elif url.path == "/history":
+                    self._json(mon.records.history(p, n) if p else mon.history)
+                elif url.path == "/stream" and p:
+                    q = mon.records.subscribe(p)
+                    self._sse(mon.records.history(p, n), q, lambda: mon.records.unsubscribe(q))
+                elif url.path in ("/stream", "/events"):
                     q: queue.Queue = queue.Queue(maxsize=1024)
                     mon._subscribers.append(q)
-                    self.send_response(200)
-                    self.send_header("Content-Type", "text/event-stream")
-                    self.end_headers()
-                    try:
-                        for rec in list(mon.history):  # late-join backfill
-                            self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
-                        self.wfile.flush()
-                        while True:
-                            rec = q.get(timeout=30)
-                            self.wfile.write(f"data: {json.dumps(rec)}\n\n".encode())
-                            self.wfile.flush()
-                    except Exception:
-                        pass
-                    finally:
-                        mon._subscribers.remove(q)
+                    self._sse(list(mon.history), q, lambda: mon._subscribers.remove(q))
                 else:
-                    body = b"<html><body>flodl_b200 monitor: /history /stream</body></html>"
+                    body = (b"<html><body>flodl_b200 monitor: /events /history /paths "
+                            b"/node?path= /history?path= /stream?path=</body></html>")
                     self.send_response(200)
                     self.send_header("Content-Type", "text/html")
+                    self.send_header("Content-Length", str(len(body)))
                     self.end_headers()
                     self.wfile.write(body)
 
