@@ -71,7 +71,9 @@ class Graph(Module):
         self._step_count = 0
         self._epoch_count = 0
         self._profiling = False
+        self._profiler = None
         self._timings: Dict[str, float] = {}
+        self._level_of = {ni: li for li, lvl in enumerate(self.levels) for ni in lvl}
         self._hash: Optional[str] = None
         self._optimizer = None
         self._scheduler = None
@@ -90,7 +92,9 @@ class Graph(Module):
         tag_of = {}
         for t, ref in self.tag_names.items():
             tag_of.setdefault(self._index[ref.node_id], []).append(t)
-        prof = self._profiling and torch.cuda.is_available()
+        prof = self.profiler if self._profiling else None
+        if prof is not None:
+            prof.begin()
         for ni in self.order:
             node = self._node_list[ni]
             args: List[Optional[torch.Tensor]] = [None] * len(node.input_ports)
@@ -101,11 +105,10 @@ class Graph(Module):
                 remaining[si] -= 1
             for pi, name in self._fwd_ref_readers.get(ni, ()):
                 args[pi] = self._fwd_ref_state.get(name)
-            t0 = time.perf_counter() if prof else 0.0
+            mark = prof.node_start() if prof is not None else None
             out = self._run_node(node, args)
-            if prof:
-                torch.cuda.synchronize()
-                self._timings[node.id] = self._timings.get(node.id, 0.0) + time.perf_counter() - t0
+            if prof is not None:
+                prof.node_end(ni, mark, self._level_of[ni])
             slots[ni] = out
             for t in tag_of.get(ni, ()):
                 self._tag_values[t] = out
@@ -115,6 +118,10 @@ class Graph(Module):
         for name, wi in self._fwd_ref_writers.items():
             v = self._tag_values.get(name)
             self._fwd_ref_state[name] = v
+        if prof is not None:
+            p = prof.end()
+            for n in p.nodes:
+                self._timings[n.id] = self._timings.get(n.id, 0.0) + n.duration
         return slots[self._index[self.output.node_id]]
 
     def forward_multi(self, inputs: Sequence[torch.Tensor]):
@@ -496,10 +503,78 @@ class Graph(Module):
 
     # ------------------------------------------------------------ profiling / viz
     def enable_profiling(self, on: bool = True) -> None:
+        """Time every node of every forward with reusable device events (host
+        clock on CPU); durations resolve once per forward."""
         self._profiling = on
 
-    def timing(self) -> Dict[str, float]:
-        return dict(self._timings)
+    def disable_profiling(self) -> None:
+        self._profiling = False
+
+    def profiling(self) -> bool:
+        return self._profiling
+
+    @property
+    def profiler(self):
+        if self._profiler is None:
+            from .profile import GraphProfiler
+            self._profiler = GraphProfiler(self)
+        return self._profiler
+
+    def profile(self):
+        """The last forward's :class:`~flodl_b200.graph.profile.Profile`, or None."""
+        s = self.profiler.samples
+        return s[-1] if s else None
+
+    def profile_stats(self):
+        return self.profiler.stats()
+
+    def timing(self, tag: Optional[str] = None):
+        """Accumulated seconds per node id, or the last forward's time of one tag."""
+        if tag is None:
+            return dict(self._timings)
+        p = self.profile()
+        return p.timing(tag) if p else 0.0
+
+    def collect_timings(self, tags: Sequence[str]) -> None:
+        self.profiler.collect_timings(tags)
+
+    def flush_timings(self, tags: Sequence[str] = ()) -> None:
+        self.profiler.flush_timings(tags)
+
+    def timing_trend(self, tag: str) -> Trend:
+        return self.profiler.timing_trend(tag)
+
+    def reset_timing_trend(self, tags: Sequence[str]) -> None:
+        self.profiler.reset_timing_trend(tags)
+
+    def heatmap_svg(self, path: Optional[str] = None) -> str:
+        from .profile import heatmap_svg
+        return heatmap_svg(self, self.profile(), path)
+
+    def plot_html(self, path: str, tags: Sequence[str] = ()) -> None:
+        from .profile import plot_html
+        plot_html(self, path, tags)
+
+    def plot_timings_html(self, path: str, tags: Sequence[str] = ()) -> None:
+        from .profile import plot_timings_html
+        plot_timings_html(self, path, tags)
+
+    def export_trends(self, path: str, tags: Sequence[str] = ()) -> None:
+        from .profile import export_trends
+        export_trends(self, path, tags)
+
+    def export_timing_trends(self, path: str, tags: Sequence[str] = ()) -> None:
+        from .profile import export_timing_trends
+        export_timing_trends(self, path, tags)
+
+    def write_log(self, path: str, total_epochs: int, tags: Sequence[str] = ()) -> None:
+        from .profile import write_log
+        write_log(self, path, total_epochs, tags)
+
+    def snapshot_cpu(self):
+        """A :class:`~flodl_b200.graph.profile.ModelSnapshot` for a background save."""
+        from .profile import ModelSnapshot
+        return ModelSnapshot.take(self, self.structural_hash())
 
     def describe(self) -> str:
         lines = [f"Graph {self._label or ''} [{self.short_hash()}] "

@@ -160,3 +160,58 @@ def test_quickstart_mlp_flowbuilder_learns():
     from flodl_b200.examples.mlp_flowbuilder import run
     r = run(steps=300)
     assert r["final_loss"] < 0.3 * r["first_loss"], r
+
+
+def test_profiling_levels_stats_trends_and_viz(tmp_path):
+    """Per-node timing, levels and parallelism, statistics, timing trends,
+    heatmap, HTML plots, CSV/log export (reference: graph/profile.rs,
+    heatmap.rs, plot.rs tests)."""
+    a, b = Linear(16, 16), Linear(16, 16)
+    g = (FlowBuilder.from_(Linear(8, 16)).tag("enc").split([a, b]).merge(MergeOp.ADD)
+         .through(Linear(16, 4)).tag("head").build())
+    g.enable_profiling()
+    x = torch.randn(32, 8)
+    for i in range(3):
+        g(x)
+        g.collect_timings(["enc", "head"])
+        g.flush_timings()
+        g.record_scalar("loss", 1.0 / (i + 1))
+        g.flush(["loss"])
+    p = g.profile()
+    assert p.source == "host_clock" and len(p.nodes) == len(g.order)
+    assert p.timing("enc") > 0 and p.total >= max(n.duration for n in p.nodes)
+    split_level = [l for l in p.levels if l.num_nodes == 2]
+    assert split_level and split_level[0].parallelism() > 0
+    st = g.profile_stats()
+    assert st.samples == 3 and st.total_min <= st.total_mean
+    assert len(g.timing_trend("enc")) == 3
+    assert set(g.timing()) == {n.id for n in p.nodes}
+    svg = g.heatmap_svg(str(tmp_path / "h.svg"))
+    assert svg.startswith("<svg") and svg.count("<rect") == len(g.order)
+    g.plot_html(str(tmp_path / "p.html"))
+    g.plot_timings_html(str(tmp_path / "t.html"))
+    g.export_trends(str(tmp_path / "tr.csv"))
+    g.export_timing_trends(str(tmp_path / "tt.csv"))
+    g.write_log(str(tmp_path / "log.txt"), 3)
+    assert (tmp_path / "tr.csv").read_text().splitlines()[0] == "flush,loss"
+    assert (tmp_path / "log.txt").read_text().splitlines()[2].startswith("epoch 3/3 loss=0.3333")
+    assert "enc" in (tmp_path / "t.html").read_text()
+    g.disable_profiling()
+    n = len(g.profiler.samples)
+    g(x)
+    assert len(g.profiler.samples) == n
+
+
+def test_snapshot_cpu_background_save(tmp_path):
+    from flodl_b200.nn.checkpoint import load_checkpoint
+    g = FlowBuilder.from_(Linear(4, 4)).through(LayerNorm(4)).build()
+    snap = g.snapshot_cpu()
+    before = [t.clone() for _, t in snap.named]
+    with torch.no_grad():
+        for p in g.parameters():
+            p.add_(1.0)  # training continues; the snapshot is unaffected
+    snap.save_background(str(tmp_path / "m.fdl")).join()
+    g2 = FlowBuilder.from_(Linear(4, 4)).through(LayerNorm(4)).build()
+    rep = load_checkpoint(str(tmp_path / "m.fdl"), g2.graph_named_parameters(), (), g2.structural_hash())
+    for (_, t), ref in zip(g2.graph_named_parameters(), before):
+        torch.testing.assert_close(t.detach(), ref)
