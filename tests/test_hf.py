@@ -42,3 +42,38 @@ def test_matches_hf_transformers_bert(tmp_path):
     with torch.no_grad():
         ref2 = hf2(input_ids=ids, attention_mask=mask).logits
     torch.testing.assert_close(ref2[valid], ref[valid], rtol=1e-4, atol=1e-4)
+
+
+def _wordpiece_tokenizer(path):
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers import Tokenizer, models, normalizers, pre_tokenizers, processors
+    vocab = ["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]", "hello", "world", "the", "cat", "sat",
+             "on", "mat", "##s", "what", "where", "is", "?", "."]
+    tok = Tokenizer(models.WordPiece({w: i for i, w in enumerate(vocab)}, unk_token="[UNK]"))
+    tok.add_special_tokens(["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]"])
+    tok.normalizer = normalizers.BertNormalizer(lowercase=True)
+    tok.pre_tokenizer = pre_tokenizers.BertPreTokenizer()
+    tok.post_processor = processors.TemplateProcessing(
+        single="[CLS] $A [SEP]", pair="[CLS] $A [SEP] $B:1 [SEP]:1",
+        special_tokens=[("[CLS]", 2), ("[SEP]", 3)])
+    tok.save(path)
+
+
+def test_tokenizer_batch_pairs_and_masks(tmp_path):
+    from flodl_b200.hf.tokenizer import HfTokenizer, build_extended_attention_mask
+    p = str(tmp_path / "tokenizer.json")
+    _wordpiece_tokenizer(p)
+    tok = HfTokenizer.from_file(p)
+    b = tok.encode(["Hello world", "the cats sat on the mat."])
+    assert b.input_ids.shape == (2, 10) and b.input_ids.dtype == torch.int64
+    assert b.input_ids[0].tolist()[:4] == [2, 5, 6, 3] and b.attention_mask[0].tolist() == [1] * 4 + [0] * 6
+    assert b.input_ids[1].tolist()[2:4] == [8, 12]  # "cats" -> cat ##s
+    assert b.sequence_ids[0].tolist()[:4] == [-1, 0, 0, -1] and b.position_ids[1, -1] == 9
+    pr = tok.encode_pairs([("what is the cat", "the cat sat")])
+    assert pr.token_type_ids[0].tolist() == [0] * 6 + [1] * 4
+    assert pr.sequence_ids[0].tolist() == [-1, 0, 0, 0, 0, -1, 1, 1, 1, -1]
+    assert tok.decode(pr.input_ids[0].tolist()) == "what is the cat the cat sat"
+    ext = build_extended_attention_mask(b.attention_mask)
+    assert ext.shape == (2, 1, 1, 10) and ext[0, 0, 0, 0] == 0 and ext[0, 0, 0, 9] < -1e30
+    on = tok.encode_on_device(["hello"], "cpu")
+    assert on.input_ids.tolist() == [[2, 5, 3]]
