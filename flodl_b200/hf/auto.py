@@ -4,12 +4,12 @@ Reference: flodl-hf/src/models/auto.rs:225 (dispatch on ``config.json``'s
 ``model_type``) and export.rs. A directory holds ``config.json`` and
 ``model.safetensors``; no network access is used.
 
-Families: ``bert``, ``roberta``, ``xlm-roberta``, ``distilbert``, ``albert``.
-Each loads into this package's modules (same names as HuggingFace except the
+Families: ``bert``, ``roberta``, ``xlm-roberta``, ``distilbert``, ``albert``,
+``deberta-v2`` (also DeBERTa-v3 checkpoints, which use that model type). Each
+loads into this package's modules (same names as HuggingFace except the
 packed ``qkv`` projection). Keys are translated per family: query/key/value
 packing, head renames, tied decoder weights dropped on load and written back
-on export. ``deberta-v2`` is recognised and refused with a clear error: its
-disentangled relative-position attention has no module here yet.
+on export.
 """
 from __future__ import annotations
 
@@ -20,6 +20,7 @@ from typing import Callable, Dict, List, Optional, Tuple
 
 import torch
 
+from ..models import deberta as D
 from ..models import encoders as E
 from ..models.bert import (BertConfig, BertForMaskedLM, BertForQuestionAnswering,
                            BertForSequenceClassification, BertForTokenClassification, BertModel)
@@ -104,6 +105,16 @@ def _albert_to_hf(model, sd):
                  [("predictions.decoder.weight", "predictions.bias", "predictions.decoder.bias")])
 
 
+def _deberta_to_ours(sd):
+    return E.pack_qkv(_drop(sd, ("cls.predictions.decoder.", "mask_predictions.")), "deberta")
+
+
+def _deberta_to_hf(model, sd):
+    sd = E.unpack_qkv(sd, "deberta")
+    return _tied(model, sd, "deberta.embeddings.word_embeddings.weight",
+                 [("cls.predictions.decoder.weight", "cls.predictions.bias", "cls.predictions.decoder.bias")])
+
+
 _ROBERTA = Family(E.RobertaConfig.from_dict,
                   {"base": E.RobertaModel, "mlm": E.RobertaForMaskedLM,
                    "seq": E.RobertaForSequenceClassification, "tok": E.RobertaForTokenClassification,
@@ -128,8 +139,14 @@ FAMILIES: Dict[str, Family] = {
                       "seq": E.AlbertForSequenceClassification, "tok": E.AlbertForTokenClassification,
                       "qa": E.AlbertForQuestionAnswering},
                      "albert", "albert.", _albert_to_ours, _albert_to_hf),
+    "deberta-v2": Family(D.DebertaV2Config.from_dict,
+                         {"base": D.DebertaV2Model, "mlm": D.DebertaV2ForMaskedLM,
+                          "seq": D.DebertaV2ForSequenceClassification,
+                          "tok": D.DebertaV2ForTokenClassification,
+                          "qa": D.DebertaV2ForQuestionAnswering},
+                         "deberta", "deberta.", _deberta_to_ours, _deberta_to_hf),
 }
-RECOGNISED = set(FAMILIES) | {"deberta-v2"}
+RECOGNISED = set(FAMILIES)
 BERT_LIKE = {"bert", "roberta", "xlm-roberta"}
 
 
@@ -211,7 +228,7 @@ class AutoModelForQuestionAnswering(_Auto):
 _ARCH = {"base": "Model", "mlm": "ForMaskedLM", "seq": "ForSequenceClassification",
          "tok": "ForTokenClassification", "qa": "ForQuestionAnswering"}
 _HF_NAME = {"bert": "Bert", "roberta": "Roberta", "xlm-roberta": "XLMRoberta",
-            "distilbert": "DistilBert", "albert": "Albert"}
+            "distilbert": "DistilBert", "albert": "Albert", "deberta-v2": "DebertaV2"}
 
 
 def export_hf(model, path: str, model_type: Optional[str] = None) -> None:

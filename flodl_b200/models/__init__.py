@@ -4,3 +4,13 @@ from .bert import (BertConfig, BertForMaskedLM, BertForQuestionAnswering,  # noq
 from .transformer_lm import DecoderBlock, TransformerLM  # noqa: F401
 from .resnet import BasicBlock, ResNet20  # noqa: F401
 from .zoo import ZOO, CharRNN, ModelDef, OLMo  # noqa: F401
+from .encoders import (AlbertConfig, AlbertForMaskedLM, AlbertForQuestionAnswering,  # noqa: F401
+                       AlbertForSequenceClassification, AlbertForTokenClassification, AlbertModel,
+                       DistilBertConfig, DistilBertForMaskedLM, DistilBertForQuestionAnswering,
+                       DistilBertForSequenceClassification, DistilBertForTokenClassification,
+                       DistilBertModel, RobertaConfig, RobertaForMaskedLM,
+                       RobertaForQuestionAnswering, RobertaForSequenceClassification,
+                       RobertaForTokenClassification, RobertaModel)
+from .deberta import (DebertaV2Config, DebertaV2ForMaskedLM, DebertaV2ForQuestionAnswering,  # noqa: F401
+                      DebertaV2ForSequenceClassification, DebertaV2ForTokenClassification,
+                      DebertaV2Model)

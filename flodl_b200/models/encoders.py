@@ -53,6 +53,8 @@ QKV_PATTERNS = {
              ".attention.self.qkv."),
     "distilbert": (".attention.q_lin.", ".attention.k_lin.", ".attention.v_lin.", ".attention.qkv."),
     "albert": (".attention.query.", ".attention.key.", ".attention.value.", ".attention.qkv."),
+    "deberta": (".attention.self.query_proj.", ".attention.self.key_proj.",
+                ".attention.self.value_proj.", ".attention.self.qkv."),
 }
 
 

@@ -95,10 +95,43 @@ def test_family_head_parity_and_export(tmp_path, family, head):
     _cmp(_hf_out(hf2, ids, mask), ref, mask, seq_level)
 
 
-def test_deberta_v2_is_refused_clearly(tmp_path):
-    cfg = T.DebertaV2Config(vocab_size=V, hidden_size=32, num_hidden_layers=1, num_attention_heads=2,
-                            intermediate_size=64)
-    d = str(tmp_path / "deb")
-    T.DebertaV2Model(cfg).save_pretrained(d, safe_serialization=True)
-    with pytest.raises(NotImplementedError, match="deberta-v2"):
-        AutoModel.from_pretrained(d)
+_DEBERTA_VARIANTS = {
+    # DeBERTa-v3 layout: relative attention, log buckets, shared keys, LN on rel embeddings
+    "v3": dict(relative_attention=True, position_buckets=16, max_relative_positions=40,
+               pos_att_type="p2c|c2p", share_att_key=True, norm_rel_ebd="layer_norm",
+               position_biased_input=False, type_vocab_size=0, embedding_size=24, legacy=True),
+    # DeBERTa-v2 xlarge layout: separate position projections, conv after layer 0, no buckets
+    "v2conv": dict(relative_attention=True, max_relative_positions=16, pos_att_type=["c2p", "p2c"],
+                   share_att_key=False, conv_kernel_size=3, position_biased_input=True,
+                   type_vocab_size=2, legacy=False),
+}
+
+
+@pytest.mark.parametrize("variant", list(_DEBERTA_VARIANTS))
+@pytest.mark.parametrize("head", [h for h, _ in _HEADS])
+def test_deberta_v2_parity_and_export(tmp_path, variant, head):
+    torch.manual_seed(0)
+    cfg = T.DebertaV2Config(vocab_size=V, hidden_size=32, num_hidden_layers=2, num_attention_heads=2,
+                            intermediate_size=64, max_position_embeddings=40,
+                            num_labels=2 if head == "ForQuestionAnswering" else 3,
+                            **_DEBERTA_VARIANTS[variant])
+    hf_cls = getattr(T, "DebertaV2" + head)
+    hf = hf_cls(cfg).eval()
+    d = str(tmp_path / "hf")
+    hf.save_pretrained(d, safe_serialization=True)
+    ours = dict(_HEADS)[head].from_pretrained(d).eval()
+    assert not ours.load_report, ours.load_report
+    ids, mask = _inputs("deberta")
+    ref = _hf_out(hf, ids, mask)
+    got = _ours_out(ours, ids, mask)
+    seq_level = head == "ForSequenceClassification"
+    _cmp(got, ref, mask, seq_level)
+    out = str(tmp_path / "export")
+    export_hf(ours, out)
+    if head == "ForMaskedLM" and not cfg.legacy:
+        # transformers cannot reload its own non-legacy DeBERTa MLM checkpoints
+        # (tied-weight bookkeeping fails); check the export through this loader
+        back = dict(_HEADS)[head].from_pretrained(out).eval()
+        _cmp(_ours_out(back, ids, mask), ref, mask, seq_level)
+        return
+    _cmp(_hf_out(hf_cls.from_pretrained(out).eval(), ids, mask), ref, mask, seq_level)
