@@ -52,3 +52,28 @@ def test_hf_ddp_tiers(tier):
     from flodl_b200.examples.hf_ddp import run
     r = run(tier, epochs=3)
     assert r["last"] < r["first"]
+
+
+def test_dnaseq_conv1d():
+    from flodl_b200.examples.dnaseq_conv1d import run
+    r = run(epochs=8, n_train=2000, n_val=300, L=64)  # shorter sequences than the default 200
+    assert r["val_accuracy"] > 0.9
+
+
+def test_dna_autoencoder():
+    from flodl_b200.examples.dna_autoencoder import run
+    r = run(epochs=25, n=256)
+    assert r["per_base_accuracy"] > 0.5 and r["reload_matches"] and r["latent_shape"] == [2, 32]
+
+
+def test_regression():
+    from flodl_b200.examples.regression import run
+    r = run()
+    assert abs(r["slope"] - 2) < 0.05 and abs(r["intercept"] - 1) < 0.05
+    assert r["logistic_accuracy"] > 0.95
+
+
+def test_schedulers():
+    from flodl_b200.examples.schedulers import run
+    r = run()
+    assert r["lr_peak"] <= 1e-3 + 1e-12 and r["lr_final"] < r["lr_peak"] and r["final_loss"] < r["first_loss"]
