@@ -16,9 +16,14 @@ import torch
 
 
 class Prefetcher:
-    def __init__(self, host: List[torch.Tensor], order: torch.Tensor, bs: int, nb: int, device,
-                 depth: int = 2):
-        self.host = host
+    """``fetch(idx) -> host rows``; with a device sample ``pool`` only the
+    pool's misses are uploaded, hits are gathered on the device and the
+    uploaded rows are admitted to the pool while it has room."""
+
+    def __init__(self, fetch, order: torch.Tensor, bs: int, nb: int, device,
+                 depth: int = 2, pool=None):
+        self.fetch = fetch
+        self.pool = pool
         self.order = order
         self.bs, self.nb = bs, nb
         self.device = torch.device(device)
@@ -35,19 +40,49 @@ class Prefetcher:
                 if self._stop.is_set():
                     break
                 idx = self.order[i * self.bs:(i + 1) * self.bs]
-                rows = [t.index_select(0, idx) for t in self.host]
                 if self.cuda:
-                    pinned = [r.pin_memory() for r in rows]
-                    with torch.cuda.stream(self.stream):
-                        dev = [p.to(self.device, non_blocking=True) for p in pinned]
-                        ev = torch.cuda.Event()
-                        ev.record(self.stream)
-                    self.q.put((dev, ev, pinned))
+                    self.q.put(self._upload(idx))
                 else:
-                    self.q.put((rows, None, None))
+                    self.q.put((self.fetch(idx), None, None))
         except BaseException as e:  # surfaced to the consumer
             self.q.put(e)
         self.q.put(None)
+
+    def _upload(self, idx: torch.Tensor):
+        pool = self.pool
+        if pool is None:
+            pinned = [r.pin_memory() for r in self.fetch(idx)]
+            with torch.cuda.stream(self.stream):
+                dev = [p.to(self.device, non_blocking=True) for p in pinned]
+                ev = torch.cuda.Event()
+                ev.record(self.stream)
+            return dev, ev, pinned
+        slots = pool.lookup(idx)
+        hit = slots >= 0
+        miss_pos = (~hit).nonzero().flatten()
+        hit_pos = hit.nonzero().flatten()
+        pinned = [r.pin_memory() for r in self.fetch(idx[miss_pos])] if miss_pos.numel() else None
+        with torch.cuda.stream(self.stream):
+            out = None
+            if pinned is not None:
+                up = [p.to(self.device, non_blocking=True) for p in pinned]
+                out = [torch.empty((idx.numel(), *u.shape[1:]), dtype=u.dtype, device=self.device)
+                       for u in up]
+                mp = miss_pos.to(self.device, non_blocking=True)
+                for o, u in zip(out, up):
+                    o.index_copy_(0, mp, u)
+                pool.admit(idx[miss_pos], up)
+            if hit_pos.numel():
+                rows = pool.gather(slots[hit_pos])
+                if out is None:
+                    out = rows
+                else:
+                    hp = hit_pos.to(self.device, non_blocking=True)
+                    for o, r in zip(out, rows):
+                        o.index_copy_(0, hp, r)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        return out, ev, pinned
 
     def __iter__(self):
         while True:
