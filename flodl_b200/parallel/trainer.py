@@ -57,6 +57,7 @@ class TrainedState:
     syncs: int = 0
     batch_counts: List[List[int]] = field(default_factory=list)
     divergence: List[float] = field(default_factory=list)
+    start_epoch: int = 0
 
 
 def _free_port() -> int:
@@ -182,7 +183,15 @@ def _rank_main(rank: int, world: int, port: int, key: bytes, spec: dict, out_q) 
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
-    except Exception:
+    except Exception as e:
+        cfg = spec.get("config")
+        if cfg is not None and getattr(cfg, "save_path_", None):
+            try:  # forensic record next to the bundle, one file per rank
+                from .bundle import CheckpointBundle, RankDeathRecord
+                RankDeathRecord(rank, world, repr(e)).write_to_file(
+                    CheckpointBundle.death_record_path(cfg.save_path_, rank))
+            except OSError:
+                pass
         out_q.put(("err", f"rank {rank}: " + traceback.format_exc()))
 
 
@@ -204,6 +213,12 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
             port_t[0] = cpu_ctl.port
         dist.broadcast(port_t, src=0)
         cpu_client = CpuReduceClient(rank, "127.0.0.1", int(port_t.item()), key)
+    start_epoch, global_step = 0, 0
+    if cfg.resume_from_:
+        # every rank loads the same bundle; the initial broadcast then agrees anyway
+        from .bundle import load_bundle
+        meta = load_bundle(cfg.resume_from_, model, opt)
+        start_epoch, global_step = meta.epoch + 1, meta.global_step
     avg = _Averager(model, opt, backend, rank, world, device, cpu_client, ec.gamma_)
     avg.broadcast_initial()
     sampler = DistributedSampler(rank, world, seed=spec.get("seed", 0))
@@ -225,7 +240,8 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
     outer = OuterStepper(spec.get("outer") or OuterAvg())
     st = TrainedState(world=world, mode=ec.mode_.value)
     counts = [1] * world if policy != ApplyPolicy.CADENCE else [ec.anchor_] * world
-    for epoch in range(cfg.num_epochs_):
+    st.start_epoch = start_epoch
+    for epoch in range(start_epoch, cfg.num_epochs_):
         model.train()
         losses = []
         it = iter(loader.epoch(epoch))
@@ -252,6 +268,7 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
                 opt.zero_grad()
                 losses.append(float(loss.detach().float().item()))
                 done += 1
+                global_step += 1
             if device.type == "cuda":
                 torch.cuda.synchronize(device)
             wall_ms = (time.perf_counter() - t0) * 1e3
@@ -304,8 +321,17 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
         if cfg.save_path_ and cfg.checkpoint_every_ and (epoch + 1) % cfg.checkpoint_every_ == 0 and rank == 0:
             from .bundle import save_bundle
 
-            save_bundle(cfg.save_path_, model, opt, {"epoch": epoch, "syncs": st.syncs,
-                                                      "mode": ec.mode_.value})
+            from .bundle import CheckpointMeta, ElCheState, SaveReason
+            es = None
+            if native is not None:
+                ph = native.phase()
+                es = ElCheState(int(native.anchor()), int(native.anchor_rank()),
+                                [float(x) for x in native.ms_per_batch()],
+                                ph.lower() if isinstance(ph, str) else
+                                ("probe", "warmup", "stable", "mature")[int(ph)],
+                                int(native.calibrations()))
+            save_bundle(cfg.save_path_, model, opt,
+                        CheckpointMeta(epoch, global_step, st.syncs, world, SaveReason.Checkpoint, es))
     st.params = [(n, p.detach().cpu().clone()) for n, p in model.named_parameters()]
     st.buffers = [(n, b.detach().cpu().clone()) for n, b in model.named_buffers()]
     avg.close()
