@@ -2,6 +2,7 @@
 live store over HTTP/SSE, dashboard sink (reference: monitor/record.rs,
 record_log.rs, record_store.rs, server.rs tests)."""
 import json
+import os
 import threading
 import time
 import urllib.request
@@ -110,3 +111,29 @@ def test_dashboard_sink_receives_signed_rank_records():
         time.sleep(0.02)
     assert sink.rejected == 1 and "root/evil" not in store.paths()
     em.close(), bad.close(), sink.close()
+
+
+def test_timeline_spill_and_shipper_mirror_with_rotation(tmp_path):
+    from flodl_b200.monitor.telemetry import TelemetryShipper, TimelineSpill, telemetry_dir
+    d = telemetry_dir("job", str(tmp_path / "local"))
+    assert os.path.basename(d).startswith("job-")
+    spill = TimelineSpill(d, segment_bytes=600, flush_s=0.05)
+    ship = TelemetryShipper(d, str(tmp_path / "shared"), interval_s=0.05)
+    for i in range(60):
+        spill.event("step", i=i)
+        if i % 7 == 0:
+            time.sleep(0.06)
+    spill.close()
+    assert ship.finish(10)
+    lines = (tmp_path / "shared" / "timeline.log").read_text().splitlines()
+    got = [json.loads(l)["i"] for l in lines]
+    assert got == list(range(60)), "the mirror keeps the full history across local rotation"
+    assert json.loads((tmp_path / "shared" / "meta.json").read_text())["pid"] == os.getpid()
+    assert os.path.getsize(os.path.join(d, "timeline.log")) < 1500  # local copy stays bounded
+
+
+def test_scalar_drain():
+    from flodl_b200.monitor.telemetry import drain_scalars, record_scalar
+    record_scalar("acc", 0.5)
+    record_scalar("acc", 1.0)
+    assert drain_scalars() == {"acc": 0.75} and drain_scalars() == {}
