@@ -15,6 +15,8 @@ Commands:
     launch --devices D0,D1 [--policy abort|shrink] -- CMD ...
     init NAME                          scaffold a training script
     completions bash                   bash completion script
+    commands [@env]                    commands of ./fdl.yml (with an overlay)
+    run CMD [@env] [-- ARGS]           run a manifest command
 """
 from __future__ import annotations
 
@@ -26,7 +28,7 @@ import urllib.error
 import urllib.request
 from typing import List, Tuple
 
-COMMANDS = ("probe", "diagnose", "status", "start", "launch", "init", "completions")
+COMMANDS = ("probe", "diagnose", "status", "start", "launch", "init", "completions", "commands", "run")
 
 
 def _probe(a) -> int:
@@ -201,6 +203,21 @@ def _completions(a) -> int:
     return 0
 
 
+def _commands(a) -> int:
+    from .manifest import list_commands, split_env
+    env, _ = split_env(a.rest)
+    for k, v in list_commands(".", env).items():
+        print(f"{k:16s} {v}")
+    return 0
+
+
+def _run(a) -> int:
+    from .manifest import run, split_env
+    env, rest = split_env(a.rest)
+    extra = rest[1:] if rest and rest[0] == "--" else rest
+    return run(a.name, extra, ".", env, a.dry_run)
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m flodl_b200",
                                  description="flodl_b200 command line")
@@ -224,10 +241,17 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("name")
     p = sub.add_parser("completions", help="shell completion script")
     p.add_argument("shell")
+    p = sub.add_parser("commands", help="list fdl.yml commands")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
+    p = sub.add_parser("run", help="run an fdl.yml command")
+    p.add_argument("name")
+    p.add_argument("--dry-run", action="store_true")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
     return ap
 
 
 def main(argv=None) -> int:
     a = build_parser().parse_args(argv)
     return {"probe": _probe, "diagnose": _diagnose, "status": _status, "start": _start,
-            "launch": _launch, "init": _init, "completions": _completions}[a.cmd](a)
+            "launch": _launch, "init": _init, "completions": _completions,
+            "commands": _commands, "run": _run}[a.cmd](a)

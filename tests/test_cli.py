@@ -55,3 +55,32 @@ def test_init_scaffold_runs(tmp_path):
 def test_completions(capsys):
     assert main(["completions", "bash"]) == 0
     assert "complete -F _flodl_b200" in capsys.readouterr().out
+
+
+def test_manifest_overlays_and_run(tmp_path, monkeypatch, capsys):
+    from flodl_b200.manifest import deep_merge, load_manifest, resolve
+    (tmp_path / "fdl.yml").write_text(
+        "env: {A: '1'}\ncommands:\n  hello: {run: 'echo hello', append: '--x'}\n  gone: {run: 'true'}\n  sub:\n")
+    (tmp_path / "fdl.ci.yml").write_text("commands:\n  hello: {append: '--ci'}\n  gone:\n")
+    (tmp_path / "sub").mkdir()
+    (tmp_path / "sub" / "fdl.yml").write_text("commands:\n  inner: {run: 'echo inner'}\n")
+    assert deep_merge({"a": {"b": 1, "c": 2}}, {"a": {"c": None, "d": 3}}) == {"a": {"b": 1, "d": 3}}
+    m = load_manifest(str(tmp_path), "ci")
+    assert m["commands"]["hello"]["append"] == "--ci" and "gone" not in m["commands"]
+    spec, d = resolve(m, "sub:inner", str(tmp_path))
+    assert spec["run"] == "echo inner" and d.endswith("sub")
+    monkeypatch.chdir(tmp_path)
+    assert main(["run", "--dry-run", "hello", "@ci", "--", "extra"]) == 0
+    assert capsys.readouterr().out.strip() == "echo hello --ci extra"
+    assert main(["run", "sub:inner"]) == 0
+    assert main(["commands", "@ci"]) == 0
+    out = capsys.readouterr().out
+    assert "hello" in out and "sub-manifest" in out and "gone" not in out
+
+
+def test_repo_manifest_parses():
+    import os
+    from flodl_b200.manifest import list_commands
+    root = os.path.dirname(os.path.dirname(__file__))
+    cmds = list_commands(root, "quick")
+    assert {"build", "test", "test-gpu", "bench"} <= set(cmds)
