@@ -205,6 +205,11 @@ class MapBuilder:
 
 
 # ---------------------------------------------------------------- routers
+def _wide(t: torch.Tensor) -> torch.Tensor:
+    """At least f32 for the routing math (bf16/f16 widen; f32/f64 stay)."""
+    return t.float() if t.dtype in (torch.float16, torch.bfloat16) else t
+
+
 class SoftmaxRouter(Module):
     NAME = "softmax_router"
 
@@ -213,14 +218,14 @@ class SoftmaxRouter(Module):
         self.proj = Linear(input_dim, num_experts, device=device)
 
     def forward(self, x):
-        return torch.softmax(self.proj(x).float(), dim=-1).to(x.dtype)
+        return torch.softmax(_wide(self.proj(x)), dim=-1).to(x.dtype)
 
 
 class SigmoidRouter(SoftmaxRouter):
     NAME = "sigmoid_router"
 
     def forward(self, x):
-        return torch.sigmoid(self.proj(x).float()).to(x.dtype)
+        return torch.sigmoid(_wide(self.proj(x))).to(x.dtype)
 
 
 class FixedSelector(Module):
@@ -269,4 +274,4 @@ class LearnedHalt(Module):
         self.proj = Linear(input_dim, 1, device=device)
 
     def forward(self, x):
-        return torch.sigmoid(self.proj(x).float()).mean() - 0.5
+        return torch.sigmoid(_wide(self.proj(x))).mean() - 0.5

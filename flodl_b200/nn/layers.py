@@ -365,7 +365,7 @@ class RMSNorm(Module):
         self.weight = torch.nn.Parameter(torch.ones(size, device=_dev(device)))
 
     def forward(self, x):
-        xf = x.float()
+        xf = x.float() if x.dtype in (torch.float16, torch.bfloat16) else x  # at least f32
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
         return (y * self.weight).to(x.dtype)
 

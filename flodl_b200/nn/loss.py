@@ -45,7 +45,15 @@ def ctc_loss(log_probs, targets, input_lengths, target_lengths, blank: int = 0):
 
 
 def focal_loss(logits, target, alpha: float = 0.25, gamma: float = 2.0):
-    """Binary focal loss on logits (Lin et al. 2017)."""
+    """Focal loss (Lin et al. 2017). Class-index targets ``[N]`` with logits
+    ``[N, C]`` (reference nn/loss.rs:174): mean of ``-alpha (1 - p_t)^gamma
+    log p_t``; reduces to ``alpha`` x cross-entropy at ``gamma = 0``.
+    Floating targets of the logits' shape select the binary form."""
+    if not target.is_floating_point():
+        log_p = torch.log_softmax(logits, dim=-1)
+        log_pt = log_p.gather(-1, target.unsqueeze(-1)).squeeze(-1)
+        pt = log_pt.exp()
+        return (-alpha * (1 - pt) ** gamma * log_pt).mean()
     p = torch.sigmoid(logits)
     ce = F.binary_cross_entropy_with_logits(logits, target, reduction="none")
     p_t = p * target + (1 - p) * (1 - target)

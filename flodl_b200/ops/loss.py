@@ -41,7 +41,10 @@ def cross_entropy(logits: torch.Tensor, targets: torch.Tensor, ignore_index: int
                   label_smoothing: float = 0.0) -> torch.Tensor:
     """Mean cross-entropy of ``logits [..., V]`` against integer ``targets``."""
     if not use_kernels(logits) or targets.dtype.is_floating_point:
-        return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(),
+        lg = logits.reshape(-1, logits.shape[-1])
+        if lg.dtype in (torch.float16, torch.bfloat16):
+            lg = lg.float()  # at least f32; f64 stays f64
+        return F.cross_entropy(lg,
                                targets.reshape(-1) if not targets.dtype.is_floating_point
                                else targets.reshape(-1, targets.shape[-1]),
                                ignore_index=ignore_index, label_smoothing=label_smoothing)
