@@ -150,6 +150,29 @@ RECOGNISED = set(FAMILIES)
 BERT_LIKE = {"bert", "roberta", "xlm-roberta"}
 
 
+HUB_FILES = ["config.json", "model.safetensors", "tokenizer.json"]
+
+
+def resolve_model_dir(name_or_path: str) -> str:
+    """A local directory as is; otherwise a Hub repo id resolved through the
+    HuggingFace cache (``huggingface_hub.snapshot_download``; with
+    ``HF_HUB_OFFLINE=1`` only the cache is consulted)."""
+    if os.path.isdir(name_or_path):
+        return name_or_path
+    try:
+        from huggingface_hub import snapshot_download
+    except ImportError as e:
+        raise FileNotFoundError(f"{name_or_path!r} is not a directory and huggingface_hub is "
+                                f"not installed") from e
+    offline = os.environ.get("HF_HUB_OFFLINE", "0") not in ("0", "", "false", "False")
+    try:
+        return snapshot_download(repo_id=name_or_path, allow_patterns=HUB_FILES,
+                                 local_files_only=offline)
+    except Exception as e:
+        raise FileNotFoundError(f"{name_or_path!r}: not a local directory and not resolvable "
+                                f"from the HuggingFace Hub{' cache' if offline else ''}: {e}") from e
+
+
 def _read_config(path: str) -> dict:
     with open(os.path.join(path, "config.json")) as f:
         return json.load(f)
@@ -176,6 +199,7 @@ def _align_prefix(sd: Dict[str, torch.Tensor], own: List[str], prefix: str) -> D
 
 
 def _load(kind: str, path: str, device=None, strict: bool = False):
+    path = resolve_model_dir(path)
     cfgd = _read_config(path)
     mt = cfgd.get("model_type", "bert")
     if mt not in RECOGNISED:

@@ -49,10 +49,12 @@ class HfTokenizer:
         return HfTokenizer(Tokenizer.from_file(path))
 
     @staticmethod
-    def from_pretrained(directory: str) -> "HfTokenizer":
-        """A local model directory holding ``tokenizer.json`` (no network)."""
+    def from_pretrained(name_or_path: str) -> "HfTokenizer":
+        """``tokenizer.json`` of a local model directory or of a Hub repo id
+        (through the HuggingFace cache)."""
         import os
-        return HfTokenizer.from_file(os.path.join(directory, "tokenizer.json"))
+        from .auto import resolve_model_dir
+        return HfTokenizer.from_file(os.path.join(resolve_model_dir(name_or_path), "tokenizer.json"))
 
     def save(self, path: str) -> None:
         self.inner.save(path)

@@ -77,3 +77,26 @@ def test_tokenizer_batch_pairs_and_masks(tmp_path):
     assert ext.shape == (2, 1, 1, 10) and ext[0, 0, 0, 0] == 0 and ext[0, 0, 0, 9] < -1e30
     on = tok.encode_on_device(["hello"], "cpu")
     assert on.input_ids.tolist() == [[2, 5, 3]]
+
+
+def test_hub_repo_id_resolves_from_cache_offline(tmp_path, monkeypatch):
+    transformers = pytest.importorskip("transformers")
+    pytest.importorskip("huggingface_hub")
+    cfg = transformers.BertConfig(vocab_size=64, hidden_size=32, num_hidden_layers=1, num_attention_heads=2,
+                                  intermediate_size=64, max_position_embeddings=32)
+    snap = tmp_path / "hub" / "models--acme--tiny-bert" / "snapshots" / "abc123"
+    snap.mkdir(parents=True)
+    transformers.BertForMaskedLM(cfg).save_pretrained(str(snap), safe_serialization=True)
+    refs = tmp_path / "hub" / "models--acme--tiny-bert" / "refs"
+    refs.mkdir()
+    (refs / "main").write_text("abc123")
+    monkeypatch.setenv("HF_HUB_CACHE", str(tmp_path / "hub"))
+    monkeypatch.setenv("HF_HUB_OFFLINE", "1")
+
+    import huggingface_hub.constants as hc
+    monkeypatch.setattr(hc, "HF_HUB_CACHE", str(tmp_path / "hub"))
+    monkeypatch.setattr(hc, "HF_HUB_OFFLINE", True)
+    m = AutoModelForMaskedLM.from_pretrained("acme/tiny-bert")
+    assert m.config.hidden_size == 32
+    with pytest.raises(FileNotFoundError, match="acme/missing"):
+        AutoModelForMaskedLM.from_pretrained("acme/missing")
