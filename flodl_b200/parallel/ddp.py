@@ -24,6 +24,8 @@ from typing import Dict, List, Optional, Sequence
 import torch
 import torch.distributed as dist
 
+from ..utils import log
+
 from ..ops._common import add_grad_ready_listener, clear_grad_ready_listeners
 from ..utils.arena import ParamArena, arena_of
 
@@ -119,7 +121,8 @@ class Ddp:
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):
             sl = self.arena.grad[b.start:b.end]
-            dist.all_reduce(sl, op=dist.ReduceOp.AVG, group=self.group)
+            with log.collective("ddp.bucket_all_reduce", numel=sl.numel()):
+                dist.all_reduce(sl, op=dist.ReduceOp.AVG, group=self.group)
         self._launched.append(b)
 
     # ------------------------------------------------------------ public API
@@ -131,7 +134,8 @@ class Ddp:
             self.reset_pending()
             return
         if not self.overlap:
-            dist.all_reduce(self.arena.grad, op=dist.ReduceOp.AVG, group=self.group)
+            with log.collective("ddp.all_reduce_gradients", numel=self.arena.grad.numel()):
+                dist.all_reduce(self.arena.grad, op=dist.ReduceOp.AVG, group=self.group)
             self.reset_pending()
             return
         for b in self.buckets:
@@ -153,7 +157,8 @@ class Ddp:
     @torch.no_grad()
     def sync_params(self) -> None:
         """Broadcast rank 0's parameters and buffers to every rank."""
-        dist.broadcast(self.arena.data, src=0, group=self.group)
+        with log.collective("ddp.sync_params", numel=self.arena.data.numel()):
+            dist.broadcast(self.arena.data, src=0, group=self.group)
         self.arena.refresh_shadow()
         self.sync_buffers()
 
@@ -165,7 +170,8 @@ class Ddp:
 
     @torch.no_grad()
     def average_params(self) -> None:
-        dist.all_reduce(self.arena.data, op=dist.ReduceOp.AVG, group=self.group)
+        with log.collective("ddp.average_params", numel=self.arena.data.numel()):
+            dist.all_reduce(self.arena.data, op=dist.ReduceOp.AVG, group=self.group)
         self.arena.refresh_shadow()
 
     @torch.no_grad()

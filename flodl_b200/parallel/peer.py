@@ -19,6 +19,8 @@ from __future__ import annotations
 from typing import List, Optional
 
 import torch
+
+from ..utils import log
 import torch.distributed as dist
 
 from .._ext import cuda_ext
@@ -104,8 +106,10 @@ class PeerComm:
         cfg.setdefault("world", self.world)
         cfg.setdefault("timeout_ns", self.timeout_ns)
         cfg.setdefault("err", self.err_dev)
-        self.C.fused_launch(op, cfg, self.ptrs["data"], self.ptrs["grad"], self.ptrs["shadow"],
-                            self.ptrs["sig"])
+        with log.collective("peer.fused_launch", op=op, bucket=cfg.get("bucket", 0),
+                            start=cfg.get("start", 0), end=cfg.get("end", 0)):
+            self.C.fused_launch(op, cfg, self.ptrs["data"], self.ptrs["grad"], self.ptrs["shadow"],
+                                self.ptrs["sig"])
 
     def check(self) -> None:
         """Raise if a kernel recorded a timeout (no device synchronisation)."""

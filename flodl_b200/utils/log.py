@@ -69,3 +69,37 @@ def debug(text: str) -> None:
 
 def trace(text: str) -> None:
     _emit(Verbosity.TRACE, text)
+
+
+_seq = {"n": 0}
+_seq_lock = threading.Lock()
+
+
+class collective:
+    """``with log.collective("all_reduce", bytes=n):`` - at Trace level,
+    ENTER/EXIT lines with a per-process sequence number around a collective,
+    so the first rank whose sequence diverges pins a desynchronised rank
+    (reference role: the ENTER/EXIT trace around every collective,
+    distributed/ddp_run/worker/sync.rs:141-227). Costs one comparison when
+    Trace is off."""
+
+    def __init__(self, name: str, **meta):
+        self.name, self.meta = name, meta
+        self.on = _level >= Verbosity.TRACE
+
+    def __enter__(self):
+        if self.on:
+            with _seq_lock:
+                _seq["n"] += 1
+                self.k = _seq["n"]
+            extra = " ".join(f"{k}={v}" for k, v in self.meta.items())
+            _emit(Verbosity.TRACE, f"ENTER {self.name} #{self.k} {extra}".rstrip())
+            self.t0 = time.perf_counter()
+        return self
+
+    def __exit__(self, et, ev, tb):
+        if self.on:
+            ms = (time.perf_counter() - self.t0) * 1e3
+            state = "EXIT" if et is None else f"FAIL({et.__name__})"
+            _emit(Verbosity.TRACE, f"{state} {self.name} #{self.k} {ms:.2f} ms")
+        return False

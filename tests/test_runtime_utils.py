@@ -65,3 +65,23 @@ def test_rng_deterministic_unbiased_shuffle():
     xs = Rng(3).shuffle(list(range(20)))
     assert sorted(xs) == list(range(20)) and xs != list(range(20))
     assert 0.0 <= Rng(5).uniform() < 1.0
+
+
+def test_collective_trace_enter_exit(capsys):
+    from flodl_b200.utils import log
+    old = log.verbosity()
+    log.set_verbosity(log.Verbosity.TRACE)
+    try:
+        with log.collective("all_reduce", numel=8):
+            pass
+        with pytest.raises(ValueError):
+            with log.collective("broadcast"):
+                raise ValueError("x")
+    finally:
+        log.set_verbosity(old)
+    err = capsys.readouterr().err
+    assert "ENTER all_reduce #" in err and "numel=8" in err and "EXIT all_reduce" in err
+    assert "FAIL(ValueError) broadcast" in err
+    with log.collective("quiet"):
+        pass
+    assert "quiet" not in capsys.readouterr().err
