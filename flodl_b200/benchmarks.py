@@ -317,7 +317,8 @@ class _TorchLoopModel(tnn.Module):
         x = self.enc(x)
         for _ in range(self.iters):
             x = self.body(x)
-            if self.halt is not None and float(self.halt(x).mean()) > 0:
+            # the same learned halting rule as the graph arm: mean sigmoid(Wx) - 0.5 > 0
+            if self.halt is not None and float(torch.sigmoid(self.halt(x)).mean()) - 0.5 > 0:
                 break
         return self.dec(x)
 

@@ -27,6 +27,9 @@ from .flow import DEFAULT_INPUT, DEFAULT_OUTPUT, FlowBuilder, MergeOp, Node
 from .trend import Trend, TrendGroup
 
 
+_ADD = object()  # plan marker: a two-input add node
+
+
 class Graph(Module):
     NAME = "graph"
 
@@ -74,6 +77,7 @@ class Graph(Module):
         self._profiler = None
         self._timings: Dict[str, float] = {}
         self._level_of = {ni: li for li, lvl in enumerate(self.levels) for ni in lvl}
+        self._plan_cache = None
         self._hash: Optional[str] = None
         self._optimizer = None
         self._scheduler = None
@@ -81,48 +85,76 @@ class Graph(Module):
         self._frozen: set = set()
 
     # ------------------------------------------------------------ execution
+    def _plan(self):
+        """Per-node execution records, built once: (node index, node, in-edge
+        (port, src) pairs, forward-ref reader ports, input slot or -1, tags,
+        direct module or None, level)."""
+        tag_of: Dict[int, List[str]] = {}
+        for t, ref in self.tag_names.items():
+            tag_of.setdefault(self._index[ref.node_id], []).append(t)
+        plan = []
+        for ni in self.order:
+            node = self._node_list[ni]
+            direct = None
+            if (node.kind in ("module", "loop", "gate", "switch", "map") and len(node.input_ports) == 1
+                    and ni not in self._fwd_ref_readers):
+                direct = node.module
+            elif (node.kind == "add" and len(node.input_ports) == 2 and ni not in self._fwd_ref_readers
+                  and len(self._in_edges[ni]) == 2 and ni not in self._input_node):
+                direct = _ADD
+            plan.append((ni, node, [(pi, si) for pi, si, _ in self._in_edges[ni]],
+                         self._fwd_ref_readers.get(ni, ()), self._input_node.get(ni, -1),
+                         tag_of.get(ni, ()), direct, self._level_of[ni]))
+        self._plan_cache = plan
+        self._out_idx = self._index[self.output.node_id]
+        self._keep = set(self._fwd_ref_writers.values()) | {self._out_idx}
+        return plan
+
     def forward(self, *inputs):
         if len(inputs) == 1 and isinstance(inputs[0], (list, tuple)):
             inputs = tuple(inputs[0])
         if len(inputs) != len(self.inputs):
             raise ValueError(f"graph expects {len(self.inputs)} inputs, got {len(inputs)}")
-        n = len(self._node_list)
-        slots: List[Optional[torch.Tensor]] = [None] * n
+        plan = self._plan_cache if self._plan_cache is not None else self._plan()
+        slots: List[Optional[torch.Tensor]] = [None] * len(self._node_list)
         remaining = list(self._consumers)
-        tag_of = {}
-        for t, ref in self.tag_names.items():
-            tag_of.setdefault(self._index[ref.node_id], []).append(t)
+        keep = self._keep
+        tag_values = self._tag_values
         prof = self.profiler if self._profiling else None
         if prof is not None:
             prof.begin()
-        for ni in self.order:
-            node = self._node_list[ni]
-            args: List[Optional[torch.Tensor]] = [None] * len(node.input_ports)
-            if ni in self._input_node:
-                args[0] = inputs[self._input_node[ni]]
-            for pi, si, _port in self._in_edges[ni]:
-                args[pi] = slots[si]
-                remaining[si] -= 1
-            for pi, name in self._fwd_ref_readers.get(ni, ()):
-                args[pi] = self._fwd_ref_state.get(name)
+        for ni, node, ins, ref_ports, in_slot, tags, direct, level in plan:
             mark = prof.node_start() if prof is not None else None
-            out = self._run_node(node, args)
+            if direct is _ADD:  # residual join of two slots
+                out = slots[ins[0][1]] + slots[ins[1][1]]
+            elif direct is not None:  # one input, no forward refs: call the module
+                x = inputs[in_slot] if in_slot >= 0 else slots[ins[0][1]]
+                out = direct(x)
+            else:
+                args: List[Optional[torch.Tensor]] = [None] * len(node.input_ports)
+                if in_slot >= 0:
+                    args[0] = inputs[in_slot]
+                for pi, si in ins:
+                    args[pi] = slots[si]
+                for pi, name in ref_ports:
+                    args[pi] = self._fwd_ref_state.get(name)
+                out = self._run_node(node, args)
             if prof is not None:
-                prof.node_end(ni, mark, self._level_of[ni])
+                prof.node_end(ni, mark, level)
             slots[ni] = out
-            for t in tag_of.get(ni, ()):
-                self._tag_values[t] = out
-            for pi, si, _ in self._in_edges[ni]:
-                if remaining[si] == 0 and si != self._index[self.output.node_id] and si not in self._fwd_ref_writers.values():
+            for t in tags:
+                tag_values[t] = out
+            for _pi, si in ins:  # free intermediates whose consumers all ran
+                remaining[si] -= 1
+                if remaining[si] == 0 and si not in keep:
                     slots[si] = None
         for name, wi in self._fwd_ref_writers.items():
-            v = self._tag_values.get(name)
-            self._fwd_ref_state[name] = v
+            self._fwd_ref_state[name] = tag_values.get(name)
         if prof is not None:
             p = prof.end()
             for n in p.nodes:
                 self._timings[n.id] = self._timings.get(n.id, 0.0) + n.duration
-        return slots[self._index[self.output.node_id]]
+        return slots[self._out_idx]
 
     def forward_multi(self, inputs: Sequence[torch.Tensor]):
         return self.forward(*inputs)

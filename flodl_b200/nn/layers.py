@@ -99,16 +99,30 @@ class _ConvNd(Module):
         self.weight = torch.nn.Parameter(_init.kaiming_uniform(wshape, fan_in, math.sqrt(5.0), dev))
         self.bias = torch.nn.Parameter(_init.uniform_bias(fan_in, (out_ch,), dev)) if bias else None
 
+    def _lib_operands(self, x):
+        """Library-path convolutions follow the activation's precision: a bf16
+        activation (from a tcgen05 layer) meets a bf16 cast of the f32 master
+        weight, as under autocast; f32 activations use the weight as is."""
+        w, b = self.weight, self.bias
+        if x.dtype != w.dtype and x.dtype in (torch.bfloat16, torch.float16):
+            w = w.to(x.dtype)
+            b = b.to(x.dtype) if b is not None else None
+        elif x.dtype != w.dtype:
+            x = x.to(w.dtype)
+        return x, w, b
+
     def forward(self, x):
         if self.transposed:
             fn = {1: F.conv_transpose1d, 2: F.conv_transpose2d, 3: F.conv_transpose3d}[self.nd]
-            return fn(x, self.weight, self.bias, self.stride, self.padding, self.output_padding,
-                      self.groups, self.dilation)
+            x, w, b = self._lib_operands(x)
+            return fn(x, w, b, self.stride, self.padding, self.output_padding, self.groups,
+                      self.dilation)
         if self.nd == 2:
             return ops.conv2d(x, self.weight, self.bias, self.stride, self.padding, self.dilation,
                               self.groups)
         fn = {1: F.conv1d, 3: F.conv3d}[self.nd]
-        return fn(x, self.weight, self.bias, self.stride, self.padding, self.dilation, self.groups)
+        x, w, b = self._lib_operands(x)
+        return fn(x, w, b, self.stride, self.padding, self.dilation, self.groups)
 
 
 class Conv1d(_ConvNd):

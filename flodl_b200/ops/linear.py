@@ -92,6 +92,40 @@ class _LinearFn(torch.autograd.Function):
         return dx, None, None, None, dres
 
 
+class _SmallLinearFn(torch.autograd.Function):
+    """Forward and input gradient on the library GEMM (bf16 operands from the
+    cached weight shadow, f32 accumulation); the weight and bias gradients
+    accumulate into ``.grad`` through the split-K tcgen05 GEMM and fire the
+    gradient-ready listeners, exactly as the fused path does."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        x2 = as_bf16_2d(x)
+        w16 = bf16_shadow(weight)
+        b16 = bf16_shadow(bias) if bias is not None else None
+        out = F.linear(x2, w16, b16)
+        ctx.save_for_backward(x2, weight, bias)
+        ctx.x_shape, ctx.x_dtype = x.shape, x.dtype
+        return out.reshape(*x.shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight, bias = ctx.saved_tensors
+        dy2 = as_bf16_2d(dy)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.mm(dy2, bf16_shadow(weight)).reshape(ctx.x_shape)
+            if ctx.x_dtype == torch.float32:
+                dx = dx.float()
+        if wants_grad(weight):
+            wgrad_accumulate(dy2, x2, weight)
+            grad_ready(weight)
+        if bias is not None and wants_grad(bias):
+            bias_grad_accumulate(dy2, bias)
+            grad_ready(bias)
+        return dx, None, None
+
+
 def _ceil8(n: int) -> int:
     return (n + 7) // 8 * 8
 
@@ -140,6 +174,22 @@ class _PaddedLinearFn(torch.autograd.Function):
         return dx, None, None
 
 
+_SMALL = {"tiles": None}
+
+
+def set_small_gemm_tiles(n: Optional[int]) -> None:
+    """Problems with fewer output tiles than ``n`` use the library GEMM
+    (``None``: a quarter of the SMs; ``0``: always the tcgen05 kernels)."""
+    _SMALL["tiles"] = n
+
+
+def _few_tiles(M: int, N: int) -> bool:
+    """Fewer 128x256 output tiles than the threshold (default: SMs / 4)."""
+    if _SMALL["tiles"] is None:
+        _SMALL["tiles"] = max(1, C().num_sms() // 4)
+    return ((M + 127) // 128) * ((N + 255) // 256) < _SMALL["tiles"]
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            act: Optional[str] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``act(x @ weight.T + bias) + residual``.
@@ -159,6 +209,20 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         if residual is not None:
             y = residual + y
         return y
+    if (weight.shape[0] % 8 == 0 and weight.shape[1] % 8 == 0
+            and _few_tiles(x.numel() // x.shape[-1], weight.shape[0])):
+        # A handful of output tiles would occupy a handful of SMs: the library
+        # GEMM's split-K / small-tile kernels spread such problems over the
+        # whole GPU. Same precision as the fused path (bf16 operands, f32
+        # accumulation, bf16 output).
+        y = _SmallLinearFn.apply(x, weight, bias)
+        if act == "gelu":
+            y = gelu_op(y)
+        elif act == "relu":
+            y = F.relu(y)
+        elif act is not None:
+            raise ValueError(f"unsupported fused activation {act!r}")
+        return y if residual is None else residual + y
     if weight.shape[0] % 8 or weight.shape[1] % 8:
         y = _PaddedLinearFn.apply(x, weight, bias)
         if act == "gelu":

@@ -160,7 +160,32 @@ def test_sgd_kernel_matches_torch():
     torch.testing.assert_close(p, pr.detach(), rtol=1e-5, atol=1e-6)
 
 
-def test_linear_op_fwd_bwd_gelu_residual():
+@pytest.fixture
+def fused_linear_only():
+    """Route even small problems through the tcgen05 kernels."""
+    from flodl_b200.ops import linear as L
+    L.set_small_gemm_tiles(0)
+    yield
+    L.set_small_gemm_tiles(None)
+
+
+def test_linear_small_problem_library_path_matches():
+    torch.manual_seed(5)
+    from flodl_b200.ops.linear import linear
+    x = torch.randn(256, 1024, device="cuda").requires_grad_()
+    w = (torch.randn(1024, 1024, device="cuda") * 0.03).requires_grad_()
+    b = torch.randn(1024, device="cuda").requires_grad_()
+    y = linear(x, w, b, act="gelu")
+    y.float().sum().backward()
+    xr, wr, br = [t.detach().clone().requires_grad_() for t in (x, w, b)]
+    yr = F.gelu(F.linear(xr.bfloat16().float(), wr.bfloat16().float(), br))
+    yr.sum().backward()
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    for got, ref in ((x.grad, xr.grad), (w.grad, wr.grad), (b.grad, br.grad)):
+        assert ((got - ref).norm() / ref.norm()).item() < 2e-2
+
+
+def test_linear_op_fwd_bwd_gelu_residual(fused_linear_only):
     torch.manual_seed(7)
     from flodl_b200.ops.linear import linear
     x = torch.randn(300, 256, device="cuda").requires_grad_()
@@ -202,7 +227,7 @@ def test_gelu_epilogue_math_matches_erf_gelu():
     assert derr.max().item() < 2e-6, derr.max().item()
 
 
-def test_linear_odd_features_padded_path():
+def test_linear_odd_features_padded_path(fused_linear_only):
     torch.manual_seed(11)
     from flodl_b200.ops.linear import linear
     x = torch.randn(37, 20, device="cuda").requires_grad_()
