@@ -516,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
+    bool prev_stored = false;  // chunk j-1 committed a store group (its slot may be in flight)
     uint32_t in_ph = 0;    // parity of the next completion of each slot's barrier
     uint32_t pending = 0;  // slots with an input load issued but not yet consumed
     if (tma_in && total > 0 && issue_in(0)) pending |= 1u;
@@ -547,11 +548,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
       }
       if (use_tma_store) {
-        // the other slot was last read by the store of chunk j-1
-        if (lane == 0) bulk_wait_group_read<0>();
+        // Slot j&1 was last read by the store of chunk j-2. With epilogue
+        // inputs, the other slot (last read by chunk j-1's store) is about to
+        // receive chunk j+1's input, so every store must have read its slot.
+        // Without inputs only chunk j-2's store must have: chunk j-1's store
+        // (the newest group) may still be reading while chunk j is computed.
+        if (lane == 0) {
+          if (tma_in || !prev_stored)
+            bulk_wait_group_read<0>();
+          else
+            bulk_wait_group_read<1>();
+        }
         __syncwarp();
         if (tma_in && j + 1 < total && issue_in(j + 1)) pending |= 1u << ((j + 1) & 1);
       }
+      prev_stored = live && use_tma_store;
       if (!live) continue;
       if (use_tma_store) {
         uint8_t* slot = stage + (j & 1) * kSlotBytes;
