@@ -16,7 +16,10 @@ with one rank less (membership only shrinks), up to ``max_restarts`` times -
 the job is expected to resume from its last checkpoint bundle.
 
 Remote hosts: :meth:`LocalLauncher.remote_command` builds the ``ssh`` command
-line that starts the same role envelope on another host (fan-out over SSH).
+line that starts the same role envelope on another host (fan-out over SSH);
+with dial-in membership the host runs ``python -m flodl_b200.parallel.agent``
+instead (:mod:`flodl_b200.parallel.agent`), which joins the controller's window
+and spawns the host's ranks itself.
 """
 from __future__ import annotations
 
