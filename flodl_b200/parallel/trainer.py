@@ -58,6 +58,7 @@ class TrainedState:
     batch_counts: List[List[int]] = field(default_factory=list)
     divergence: List[float] = field(default_factory=list)
     start_epoch: int = 0
+    meta_nudges: List[float] = field(default_factory=list)
 
 
 def _free_port() -> int:
@@ -237,6 +238,8 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
             native.set_max_batch_diff(ec.max_batch_diff_)
         native.set_max_total(max(1, loader.num_batches() * world))
     guard = (NoGuard() if not ec.divergence_guard_ else LevelGuard(ec.divergence_threshold_))
+    from .meta import LrEventMeta
+    meta = LrEventMeta()
     outer = OuterStepper(spec.get("outer") or OuterAvg())
     st = TrainedState(world=world, mode=ec.mode_.value)
     counts = [1] * world if policy != ApplyPolicy.CADENCE else [ec.anchor_] * world
@@ -306,8 +309,14 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
                                  device=device if device.type == "cuda" else "cpu")
                 gathered = [torch.zeros_like(t) for _ in range(world)]
                 dist.all_gather(gathered, t)
-                if guard.observe(div) == Verdict.SHRINK and ec.meta_controller_:
-                    native.nudge_anchor_down(0.5)
+                verdict = guard.observe(div)
+                if ec.meta_controller_:
+                    lr_now = opt.lr() if hasattr(opt, "lr") else 0.0
+                    f = meta.observe(lr_now, int(native.anchor()),
+                                     "shrink" if verdict == Verdict.SHRINK else "ok", native.phase())
+                    if f is not None:
+                        native.nudge_anchor_down(f)
+                        st.meta_nudges.append(f)
                 native.report_timing([float(g[0]) for g in gathered],
                                      [int(g[1]) for g in gathered], sync_ms)
                 counts = list(native.batch_counts())
