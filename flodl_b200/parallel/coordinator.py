@@ -284,3 +284,24 @@ class AlertLane:
         if self.store is not None:
             self.store.publish(dict(rec))
         return rec
+
+
+# ----------------------------------------------------------------- failure threshold
+@dataclass
+class MaxFailureThreshold:
+    """When ``dead >= limit_for(world)`` the run is unrecoverable: survivors
+    save (``SaveReason.MaxFailureExceeded``) and stop instead of waiting for a
+    re-formation that cannot complete. ``absolute`` counts ranks; ``percent``
+    is a fraction of the world, clamped to [0, 1] and rounded up."""
+
+    absolute: Optional[int] = None
+    percent: Optional[float] = None
+
+    def limit_for(self, world: int) -> int:
+        if self.absolute is not None:
+            return self.absolute
+        p = min(max(self.percent or 0.0, 0.0), 1.0)
+        return int(-(-p * world // 1))  # ceil
+
+    def breached(self, dead: int, world: int) -> bool:
+        return dead >= self.limit_for(world)

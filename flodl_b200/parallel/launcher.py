@@ -125,7 +125,10 @@ class LocalLauncher:
 
     def __init__(self, command: Sequence[str], devices: Sequence[str], policy: str = "abort",
                  max_restarts: int = 1, env: Optional[Dict[str, str]] = None,
-                 timeout_s: float = 3600.0, death_log: Optional[str] = None):
+                 timeout_s: float = 3600.0, death_log: Optional[str] = None,
+                 max_failure=None):
+        """``max_failure``: a :class:`~flodl_b200.parallel.coordinator.MaxFailureThreshold`
+        over the initial world; once breached, ``shrink`` stops relaunching."""
         if policy not in ("abort", "shrink"):
             raise ValueError("policy must be 'abort' or 'shrink'")
         self.command = list(command)
@@ -134,6 +137,7 @@ class LocalLauncher:
         self.env = dict(env or {})
         self.timeout_s = timeout_s
         self.death_log = death_log
+        self.max_failure = max_failure
         self.key = secrets.token_bytes(32)
 
     def _spawn(self, devices: List[str], rdv: RendezvousServer, attempt: int):
@@ -189,8 +193,10 @@ class LocalLauncher:
             if self.death_log:
                 with open(self.death_log, "a") as f:
                     f.write(json.dumps(rec) + "\n")
+            breached = (self.max_failure is not None and
+                        self.max_failure.breached(len(deaths), len(self.devices)))
             if (self.policy == "abort" or attempt >= self.max_restarts or idx < 0
-                    or len(devices) <= 1):
+                    or len(devices) <= 1 or breached):
                 return LaunchResult(False, len(devices), attempt + 1,
                                     [p.returncode for p in procs], deaths)
             devices.pop(idx)  # elastic shrink: relaunch without the failed device

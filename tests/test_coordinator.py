@@ -116,3 +116,13 @@ def test_alert_lane_collapses_and_publishes():
     assert any(r.get("class") == "rank_lost" for r in store.history("root", 10))
     with pytest.raises(ValueError):
         lane.raise_("info", "root", "x")
+
+
+def test_max_failure_threshold():
+    from flodl_b200.parallel.coordinator import MaxFailureThreshold
+    assert MaxFailureThreshold(absolute=3).limit_for(100) == 3
+    assert MaxFailureThreshold(percent=0.2).limit_for(10) == 2
+    assert MaxFailureThreshold(percent=0.2).limit_for(5) == 1
+    assert MaxFailureThreshold(percent=1.5).limit_for(4) == 4
+    assert MaxFailureThreshold(percent=0.0).breached(0, 8)
+    assert not MaxFailureThreshold(absolute=2).breached(1, 4)
