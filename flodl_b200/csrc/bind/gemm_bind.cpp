@@ -10,7 +10,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t M, 
           int64_t K, bool a_mn, bool b_mn, const c10::optional<at::Tensor>& bias,
           const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& aux,
           int64_t flags, double alpha, int64_t k_splits, int64_t bn,
-          const c10::optional<at::Tensor>& alpha_t) {
+          const c10::optional<at::Tensor>& alpha_t, const c10::optional<at::Tensor>& colsum) {
   FL_CHECK_CUDA(A);
   FL_CHECK_CUDA(B);
   FL_CHECK_CUDA(out);
@@ -70,6 +70,13 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t M, 
   g.ep.alpha = (float)alpha;
   if (alpha_t) { FL_CHECK_F32(*alpha_t); FL_CHECK_CUDA(*alpha_t); }
   g.ep.alpha_ptr = opt_ptr<const float>(alpha_t);
+  if (colsum) {
+    FL_CHECK_F32(*colsum);
+    FL_CHECK_CUDA(*colsum);
+    FL_CHECK(colsum->numel() == N && colsum->is_contiguous(), "colsum must be f32 [N]");
+    FL_CHECK(k_splits == 1 && !(flags & flodl::kEpiAccumulate), "colsum needs a full-K epilogue");
+  }
+  g.ep.colsum = opt_ptr<float>(colsum);
   cudaStream_t st = cur_stream();
   cudaError_t e = flodl::launch_gemm(g, st);
   FL_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e), " ",
@@ -86,7 +93,8 @@ void register_gemm(py::module& m) {
         py::arg("out"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("aux") = py::none(), py::arg("flags") = 0, py::arg("alpha") = 1.0,
-        py::arg("k_splits") = 1, py::arg("bn") = 0, py::arg("alpha_t") = py::none());
+        py::arg("k_splits") = 1, py::arg("bn") = 0, py::arg("alpha_t") = py::none(),
+        py::arg("colsum") = py::none());
   m.attr("EPI_GELU") = (int)flodl::kEpiGelu;
   m.attr("EPI_DGELU") = (int)flodl::kEpiDGelu;
   m.attr("EPI_ACCUMULATE") = (int)flodl::kEpiAccumulate;

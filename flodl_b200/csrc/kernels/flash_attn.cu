@@ -551,14 +551,17 @@ __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
 // dqkv[:, q cols] = bf16(dq_acc * scale). With dbias, also the bias gradient
 // of the packed projection: dbias[c] += sum over rows of dqkv[:, c] for all
 // 3C columns (the dK/dV columns were written by the main kernel), one atomic
-// per column and row slice. Thread = 8 consecutive columns of a row.
-constexpr int kPostLanes = 4;  // row lanes per block of the finalize kernel
-__global__ void __launch_bounds__(256 * kPostLanes) flash_bwd_post_kernel(
+// per column and row slice. Thread = 8 consecutive columns of a row; a block
+// is `lanes` row lanes of `gw` threads each (gw = the 3C/8 column groups
+// rounded up to a warp), so (almost) every thread has a column group.
+constexpr int kPostMaxThreads = 1024;
+__global__ void __launch_bounds__(kPostMaxThreads) flash_bwd_post_kernel(
     const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int T, int C, float scale,
-    float* __restrict__ dbias, int rows_per_block) {
+    float* __restrict__ dbias, int rows_per_block, int gw) {
   const int groups = 3 * C / 8;
-  const int g = blockIdx.y * 256 + (threadIdx.x & 255);
-  const int rl = threadIdx.x >> 8;  // row lane
+  const int lanes = blockDim.x / gw;
+  const int g = blockIdx.y * gw + (int)(threadIdx.x % gw);
+  const int rl = (int)(threadIdx.x / gw);  // row lane
   const int c0 = g * 8;
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(T, r0 + rows_per_block);
@@ -567,7 +570,7 @@ __global__ void __launch_bounds__(256 * kPostLanes) flash_bwd_post_kernel(
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
   if (g < groups) {
 #pragma unroll 4
-    for (int r = r0 + rl; r < r1; r += kPostLanes) {
+    for (int r = r0 + rl; r < r1; r += lanes) {
       uint4* dst = reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * C + c0);
       uint4 w;
       if (c0 < C) {
@@ -595,14 +598,14 @@ __global__ void __launch_bounds__(256 * kPostLanes) flash_bwd_post_kernel(
     }
   }
   if (dbias == nullptr) return;  // uniform across the block
-  __shared__ float red[256 * kPostLanes][9];
+  __shared__ float red[kPostMaxThreads][9];
 #pragma unroll
   for (int e = 0; e < 8; ++e) red[threadIdx.x][e] = acc[e];
   __syncthreads();
   if (rl == 0 && g < groups) {
-    for (int l = 1; l < kPostLanes; ++l)
+    for (int l = 1; l < lanes; ++l)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += red[threadIdx.x + 256 * l][e];
+      for (int e = 0; e < 8; ++e) acc[e] += red[threadIdx.x + gw * l][e];
 #pragma unroll
     for (int e = 0; e < 8; ++e) atomicAdd(dbias + c0 + e, acc[e]);
   }
@@ -976,11 +979,14 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
                                             a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
                                             a.err ? a.err : default_err_word());
   const int T = a.B * a.S;
-  const int gy = (3 * C / 8 + 255) / 256;
+  const int groups = 3 * C / 8;
+  const int gw = std::min(kPostMaxThreads, (groups + 31) / 32 * 32);  // threads per row lane
+  const int gy = (groups + gw - 1) / gw;
+  const int lanes = kPostMaxThreads / gw;
   const int gx = std::max(1, std::min(T, num_sms() / gy));
   const int rpb = (T + gx - 1) / gx;
-  flash_bwd_post_kernel<<<dim3(gx, gy), 256 * kPostLanes, 0, st>>>(a.dq_acc, a.dqkv, T, C,
-                                                                    a.scale, a.dbias, rpb);
+  flash_bwd_post_kernel<<<dim3(gx, gy), gw * lanes, 0, st>>>(a.dq_acc, a.dqkv, T, C, a.scale,
+                                                            a.dbias, rpb, gw);
   note_launch(3);
   return cudaGetLastError();
 }

@@ -24,6 +24,7 @@ struct GemmEpilogue {
   int flags = 0;
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;  // optional device scalar multiplied into alpha
+  float* colsum = nullptr;  // f32 [N] or null: += column sums of the output (TMA-store path)
 };
 
 struct GemmArgs {

@@ -93,8 +93,9 @@ def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, 
     # FFN
     _wgrad(dy2_16, a, p.w2)
     da = _empty((T, F4), torch.bfloat16, dev)
-    K.gemm(dy2_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU)
-    K.colsum(da, grad_buffer(p.b1))
+    # da = (dy W2) * GELU'; the epilogue also adds column sums of da to fc1's bias gradient
+    K.gemm(dy2_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU,
+           colsum=grad_buffer(p.b1))
     _wgrad(da, x1_16, p.w1)
     dx1 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(da, bf16_shadow(p.w1), dx1, T, Cd, F4, False, True)

@@ -108,9 +108,10 @@ def block_backward(dx3, dx3_16, p: BlockParams, saved, B, S, H, causal, prev_bia
     # fc2
     _wgrad(dx3_16, a, p.w2)
     da = _empty((T, F4), torch.bfloat16, dev)
-    K.gemm(dx3_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU)
+    # da = (dy W2) * GELU'; the epilogue also adds column sums of da to fc1's bias gradient
+    K.gemm(dx3_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU,
+           colsum=grad_buffer(p.b1))
     # fc1
-    K.colsum(da, grad_buffer(p.b1))
     _wgrad(da, h2, p.w1)
     dh2 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(da, bf16_shadow(p.w1), dh2, T, Cd, F4, False, True)

@@ -83,3 +83,27 @@ def test_gemm_splitk_accumulate():
     C.gemm(A, B, out, M, N, K, True, True, flags=C.EPI_ACCUMULATE, k_splits=8)
     ref = A.float().t() @ B.float() + 1.0
     torch.testing.assert_close(out, ref, rtol=1e-3, atol=5e-2)
+
+
+@pytest.mark.parametrize("M,N,K,b_mn", [(300, 512, 384, True), (16384 // 8, 2048, 512, True),
+                                        (256, 200, 128, False)])
+def test_gemm_fused_column_sums(M, N, K, b_mn):
+    """colsum += column sums of the epilogue output (DGELU and plain), added to
+    what the buffer already holds; partial row tiles contribute zeros."""
+    torch.manual_seed(3)
+    C = _C()
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    Bm = (torch.randn(K, N, device="cuda") * 0.1).bfloat16() if b_mn else \
+        (torch.randn(N, K, device="cuda") * 0.1).bfloat16()
+    ref = _ref(A, Bm, False, b_mn)
+    g = torch.rand(M, N, device="cuda").bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cs = torch.full((N,), 0.5, device="cuda")
+    C.gemm(A, Bm, out, M, N, K, False, b_mn, aux=g, flags=C.EPI_DGELU, colsum=cs)
+    want = ref * g.float()
+    torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(cs, 0.5 + want.sum(0), rtol=1e-3, atol=1e-2 * (M ** 0.5))
+    cs2 = torch.zeros(N, device="cuda")
+    out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, Bm, out2, M, N, K, False, b_mn, colsum=cs2)
+    torch.testing.assert_close(cs2, ref.sum(0), rtol=1e-3, atol=1e-2 * (M ** 0.5))
