@@ -17,6 +17,10 @@ Commands:
     completions bash                   bash completion script
     commands [@env]                    commands of ./fdl.yml (with an overlay)
     run CMD [@env] [-- ARGS]           run a manifest command
+    join HOST:PORT [--key-hex K]       dial a controller as this host's agent
+    api-ref [MODULE] [--json]          public API surface with one-line docs
+    add hf [--dir D]                   scaffold a HuggingFace playground + fdl.yml entry
+    publish SRC DEST                   validate a run directory and publish its manifest
 """
 from __future__ import annotations
 
@@ -28,7 +32,8 @@ import urllib.error
 import urllib.request
 from typing import List, Tuple
 
-COMMANDS = ("probe", "diagnose", "status", "start", "launch", "init", "completions", "commands", "run")
+COMMANDS = ("probe", "diagnose", "status", "start", "launch", "init", "completions", "commands", "run",
+            "join", "api-ref", "add", "publish")
 
 
 def _probe(a) -> int:
@@ -218,6 +223,143 @@ def _run(a) -> int:
     return run(a.name, extra, ".", env, a.dry_run)
 
 
+def _join(a) -> int:
+    from .parallel.agent import run_agent
+    key = bytes.fromhex(a.key_hex or os.environ.get("FLODL_INTERNAL_KEY", ""))
+    return run_agent(a.controller, key, a.devices)
+
+
+def api_reference(module: str = "flodl_b200") -> dict:
+    """{module: {public name: first docstring line}} for a package tree."""
+    import importlib
+    import inspect
+    import pkgutil
+    root = importlib.import_module(module)
+    mods = [root]
+    if hasattr(root, "__path__"):
+        for info in pkgutil.walk_packages(root.__path__, module + "."):
+            if info.name.split(".")[-1].startswith("_") or ".csrc" in info.name:
+                continue
+            try:
+                mods.append(importlib.import_module(info.name))
+            except Exception:
+                continue
+    out = {}
+    for m in mods:
+        names = {}
+        for n, obj in vars(m).items():
+            if n.startswith("_") or getattr(obj, "__module__", None) != m.__name__:
+                continue
+            if inspect.isclass(obj) or inspect.isfunction(obj):
+                doc = (inspect.getdoc(obj) or "").strip().splitlines()
+                names[n] = doc[0] if doc else ""
+        if names:
+            out[m.__name__] = dict(sorted(names.items()))
+    return out
+
+
+def _api_ref(a) -> int:
+    ref = api_reference(a.module)
+    if a.json:
+        print(json.dumps(ref, indent=2))
+    else:
+        for mod, names in ref.items():
+            print(f"## {mod}")
+            for n, d in names.items():
+                print(f"  {n}: {d}")
+    return 0
+
+
+_HF_PLAYGROUND = """\"\"\"HuggingFace playground: load a local model directory or a cached Hub id
+and run it (generated by `python -m flodl_b200 add hf`).\"\"\"
+import sys
+
+import torch
+
+from flodl_b200.hf import AutoModelForSequenceClassification, HfTokenizer
+
+name = sys.argv[1] if len(sys.argv) > 1 else "distilbert-base-uncased"
+model = AutoModelForSequenceClassification.from_pretrained(name).eval()
+tok = HfTokenizer.from_pretrained(name)
+batch = tok.encode(["flodl_b200 runs this on a B200", "and on the CPU"])
+with torch.no_grad():
+    print(model(batch.input_ids, attention_mask=batch.attention_mask))
+"""
+
+
+def _add(a) -> int:
+    if a.target not in ("hf", "flodl-hf"):
+        print(f"add: unknown target {a.target!r} (supported: hf)", file=sys.stderr)
+        return 2
+    d = os.path.join(a.dir, "flodl-hf")
+    if os.path.exists(d):
+        print(f"add: {d} already exists", file=sys.stderr)
+        return 1
+    os.makedirs(d)
+    with open(os.path.join(d, "main.py"), "w") as f:
+        f.write(_HF_PLAYGROUND)
+    with open(os.path.join(d, "fdl.yml"), "w") as f:
+        f.write("commands:\n  run:\n    description: run the HF playground\n    run: python main.py\n")
+    manifest = os.path.join(a.dir, "fdl.yml")
+    entry = "  flodl-hf:                     # sub-manifest ./flodl-hf/fdl.yml\n"
+    if os.path.exists(manifest):
+        text = open(manifest).read()
+        if "flodl-hf:" not in text:
+            if "commands:" not in text:
+                text += "\ncommands:\n"
+            text = text.replace("commands:\n", "commands:\n" + entry, 1)
+            open(manifest, "w").write(text)
+    else:
+        open(manifest, "w").write("commands:\n" + entry)
+    print(f"created {d}/ (run it with `python -m flodl_b200 run flodl-hf:run`)")
+    return 0
+
+
+def publish(src: str, dest: str) -> dict:
+    """Validate a run directory (its Python files compile, its fdl.yml parses)
+    and publish it into ``dest`` with a ``run.json`` manifest agents read."""
+    import hashlib
+    import py_compile
+    import shutil
+    import time
+    files = []
+    for root, _, fs in os.walk(src):
+        for f in fs:
+            p = os.path.join(root, f)
+            if f.endswith(".py"):
+                py_compile.compile(p, doraise=True)
+            files.append(os.path.relpath(p, src))
+    if os.path.exists(os.path.join(src, "fdl.yml")):
+        from .manifest import load_manifest
+        load_manifest(src)
+    h = hashlib.sha256()
+    for f in sorted(files):
+        h.update(f.encode())
+        h.update(open(os.path.join(src, f), "rb").read())
+    digest = h.hexdigest()[:16]
+    target = os.path.join(dest, f"run-{digest}")
+    if not os.path.exists(target):
+        shutil.copytree(src, target + ".tmp")
+        os.replace(target + ".tmp", target)
+    man = {"run": os.path.basename(target), "digest": digest, "files": sorted(files),
+           "published_at": time.time()}
+    tmp = os.path.join(dest, "run.json.tmp")
+    with open(tmp, "w") as f:
+        json.dump(man, f, indent=2)
+    os.replace(tmp, os.path.join(dest, "run.json"))
+    return man
+
+
+def _publish(a) -> int:
+    try:
+        man = publish(a.src, a.dest)
+    except Exception as e:
+        print(f"publish: refused: {e}", file=sys.stderr)
+        return 1
+    print(json.dumps(man))
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m flodl_b200",
                                  description="flodl_b200 command line")
@@ -247,6 +389,19 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("name")
     p.add_argument("--dry-run", action="store_true")
     p.add_argument("rest", nargs=argparse.REMAINDER)
+    p = sub.add_parser("join", help="join a controller as this host's agent")
+    p.add_argument("controller")
+    p.add_argument("--key-hex", default="")
+    p.add_argument("--devices", type=int, default=None)
+    p = sub.add_parser("api-ref", help="public API surface")
+    p.add_argument("module", nargs="?", default="flodl_b200")
+    p.add_argument("--json", action="store_true")
+    p = sub.add_parser("add", help="scaffold an add-on playground")
+    p.add_argument("target")
+    p.add_argument("--dir", default=".")
+    p = sub.add_parser("publish", help="validate and publish a run directory")
+    p.add_argument("src")
+    p.add_argument("dest")
     return ap
 
 
@@ -254,4 +409,5 @@ def main(argv=None) -> int:
     a = build_parser().parse_args(argv)
     return {"probe": _probe, "diagnose": _diagnose, "status": _status, "start": _start,
             "launch": _launch, "init": _init, "completions": _completions,
-            "commands": _commands, "run": _run}[a.cmd](a)
+            "commands": _commands, "run": _run, "join": _join, "api-ref": _api_ref, "add": _add,
+            "publish": _publish}[a.cmd](a)

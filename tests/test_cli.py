@@ -84,3 +84,20 @@ def test_repo_manifest_parses():
     root = os.path.dirname(os.path.dirname(__file__))
     cmds = list_commands(root, "quick")
     assert {"build", "test", "test-gpu", "bench"} <= set(cmds)
+
+
+def test_api_ref_add_hf_and_publish(tmp_path, capsys):
+    from flodl_b200.cli import api_reference, publish
+    ref = api_reference("flodl_b200.parallel")
+    assert "ChunkPool" in ref["flodl_b200.parallel.coordinator"]
+    assert main(["add", "hf", "--dir", str(tmp_path)]) == 0
+    assert (tmp_path / "flodl-hf" / "main.py").exists()
+    assert "flodl-hf:" in (tmp_path / "fdl.yml").read_text()
+    compile((tmp_path / "flodl-hf" / "main.py").read_text(), "main.py", "exec")
+    src = tmp_path / "job"
+    src.mkdir()
+    (src / "train.py").write_text("print('hi')\n")
+    man = publish(str(src), str(tmp_path / "pub"))
+    assert man["files"] == ["train.py"] and (tmp_path / "pub" / man["run"] / "train.py").exists()
+    (src / "bad.py").write_text("def x(:\n")
+    assert main(["publish", str(src), str(tmp_path / "pub")]) == 1
