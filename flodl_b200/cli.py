@@ -251,7 +251,7 @@ def api_reference(module: str = "flodl_b200") -> dict:
             if n.startswith("_") or getattr(obj, "__module__", None) != m.__name__:
                 continue
             if inspect.isclass(obj) or inspect.isfunction(obj):
-                doc = (inspect.getdoc(obj) or "").strip().splitlines()
+                doc = inspect.cleandoc(obj.__doc__ or "").strip().splitlines()  # own docstring only
                 names[n] = doc[0] if doc else ""
         if names:
             out[m.__name__] = dict(sorted(names.items()))
