@@ -127,3 +127,38 @@ def test_resolve_cached_prefers_source_then_acquires_once(tmp_path):
     assert resolve_cached(str(src), "ds", "a.bin", lambda p: True, fetch, str(cache)) == p and len(calls) == 1
     (src / "ds" / "b.bin").write_text("x")
     assert resolve_cached(str(src), "ds", "b.bin", lambda p: True, fetch, str(cache)) == str(src / "ds" / "b.bin")
+
+
+def test_fixed_stride_records_and_cifar_mnist_readers(tmp_path):
+    import struct
+
+    import numpy as np
+
+    from flodl_b200.data.datasets import cifar10, mnist
+    from flodl_b200.data.records import FixedStrideRecords, cifar10_records, mnist_records
+    rng = np.random.default_rng(0)
+    for name in [f"data_batch_{i}.bin" for i in range(1, 6)]:
+        recs = np.concatenate([rng.integers(0, 10, (7, 1)), rng.integers(0, 256, (7, 3072))], 1)
+        recs.astype(np.uint8).tofile(str(tmp_path / name))
+    full, streamed = cifar10(str(tmp_path)), cifar10_records(str(tmp_path))
+    assert len(streamed) == 35
+    for i in (0, 6, 7, 34):
+        x, y = streamed.get(i)
+        torch.testing.assert_close(x, full.tensors[0][i])
+        assert int(y) == int(full.tensors[1][i])
+    imgs = rng.integers(0, 256, (5, 28, 28)).astype(np.uint8)
+    labs = rng.integers(0, 10, 5).astype(np.uint8)
+    (tmp_path / "train-images-idx3-ubyte").write_bytes(struct.pack(">IIII", 0x803, 5, 28, 28) + imgs.tobytes())
+    (tmp_path / "train-labels-idx1-ubyte").write_bytes(struct.pack(">II", 0x801, 5) + labs.tobytes())
+    m, ms = mnist(str(tmp_path)), mnist_records(str(tmp_path))
+    for i in range(5):
+        x, y = ms.get(i)
+        torch.testing.assert_close(x, m.tensors[0][i])
+        assert int(y) == int(m.tensors[1][i])
+    import pytest
+    bad = tmp_path / "bad.bin"
+    bad.write_bytes(b"x" * 10)
+    with pytest.raises(ValueError, match="whole number"):
+        FixedStrideRecords(str(bad), 3)
+    dl = DataLoader.from_dataset(streamed).batch_size(8).streaming().build()
+    assert sum(b[0].shape[0] for b in dl.epoch(0)) == 35
