@@ -352,6 +352,7 @@ class FlowBuilder:
         if self.pending:
             raise ValueError(f"unresolved forward references: {sorted(self.pending)}")
         g = Graph(self)
-        if self._verbose:
-            print(g.describe())
+        from ..utils import log
+        if self._verbose or log.verbosity() >= log.Verbosity.VERBOSE:
+            log.msg(g.describe()) if self._verbose else log.verbose(g.describe())
         return g

@@ -238,6 +238,28 @@ class Timeline:
         with open(path, "w") as f:
             json.dump({"samples": self.samples, "events": self.events}, f)
 
+    def save_html(self, path: str, title: str = "timeline") -> None:
+        """Self-contained page: GPU utilisation and host RAM over time, with the
+        discrete events (syncs, anchor changes, epochs) listed beneath."""
+        import html as _html
+        from ..ddp_report import line_chart_svg
+        series = {}
+        for smp in self.samples:
+            for g in smp.get("gpus", []):
+                series.setdefault(f"gpu{g['gpu']} util %", []).append(float(g.get("util", 0)))
+            if "ram_used_mb" in smp:
+                series.setdefault("host RAM used (GB)", []).append(smp["ram_used_mb"] / 1024)
+        t0 = self.samples[0]["t"] if self.samples else (self.events[0]["t"] if self.events else 0.0)
+        rows = "".join(f"<tr><td>{e['t'] - t0:.3f}</td><td>{_html.escape(e['kind'])}</td>"
+                       f"<td>{_html.escape(json.dumps({k: v for k, v in e.items() if k not in ('t', 'kind')}))}</td></tr>"
+                       for e in self.events)
+        charts = "".join(line_chart_svg({k: v}, k) for k, v in series.items()) or "<p>no samples</p>"
+        with open(path, "w") as f:
+            f.write(f"<!doctype html><html><head><meta charset='utf-8'><title>{_html.escape(title)}</title>"
+                    f"</head><body><h2>{_html.escape(title)}</h2>{charts}<h3>events</h3>"
+                    f"<table border=1><tr><th>t (s)</th><th>kind</th><th>detail</th></tr>{rows}</table>"
+                    f"</body></html>")
+
     def save_csv(self, path: str) -> None:
         with open(path, "w", newline="") as f:
             w = csv.writer(f)

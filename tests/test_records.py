@@ -137,3 +137,25 @@ def test_scalar_drain():
     record_scalar("acc", 0.5)
     record_scalar("acc", 1.0)
     assert drain_scalars() == {"acc": 0.75} and drain_scalars() == {}
+
+
+def test_timeline_html_and_verbose_build(tmp_path, capsys):
+    from flodl_b200.monitor.monitor import Timeline
+    tl = Timeline(0.01).start()
+    tl.event("sync", round=1)
+    time.sleep(0.05)
+    tl.event("anchor", value=4)
+    tl.stop()
+    tl.save_html(str(tmp_path / "t.html"))
+    text = (tmp_path / "t.html").read_text()
+    assert "<svg" in text and "anchor" in text
+    from flodl_b200.graph import FlowBuilder
+    from flodl_b200.nn import Linear
+    from flodl_b200.utils import log
+    old = log.verbosity()
+    log.set_verbosity(log.Verbosity.VERBOSE)
+    try:
+        FlowBuilder.from_(Linear(2, 2)).build()
+    finally:
+        log.set_verbosity(old)
+    assert "Graph" in capsys.readouterr().err
