@@ -305,12 +305,24 @@ class _TorchResBody(tnn.Module):
         return x + self.f(x)
 
 
+def _halt_init(lin) -> None:
+    """Both arms start from the same halting head (zero weights, bias -2:
+    sigmoid < 0.5, so every forward runs all iterations; the halting decision
+    is not differentiable, so it stays that way). Random heads would make the
+    two arms run different iteration counts and time different work."""
+    with torch.no_grad():
+        lin.weight.zero_()
+        lin.bias.fill_(-2.0)
+
+
 class _TorchLoopModel(tnn.Module):
     def __init__(self, D, iters, halt):
         super().__init__()
         self.enc = tnn.Sequential(tnn.Linear(D, D), tnn.GELU(), tnn.LayerNorm(D))
         self.body, self.iters = _TorchResBody(D), iters
         self.halt = tnn.Linear(D, 1) if halt else None
+        if self.halt is not None:
+            _halt_init(self.halt)
         self.dec = tnn.Linear(D, D)
 
     def forward(self, x):
@@ -331,7 +343,12 @@ def _loop_model(arm, dev, s, D0, iters, halt):
         body = FlowBuilder.new().also(_residual_block_flodl(D, dev)).build()
         b = (FlowBuilder.from_(Linear(D, D, device=dev)).through(GELU()).through(LayerNorm(D, device=dev))
              .loop_body(body))
-        b = b.until_cond(LearnedHalt(D, device=dev), iters) if halt else b.for_n(iters)
+        if halt:
+            lh = LearnedHalt(D, device=dev)
+            _halt_init(lh.proj)
+            b = b.until_cond(lh, iters)
+        else:
+            b = b.for_n(iters)
         m = b.through(Linear(D, D, device=dev)).build()
     else:
         m = _TorchLoopModel(D, iters, halt).to(dev)

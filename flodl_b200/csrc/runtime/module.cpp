@@ -9,4 +9,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   flodl::rt::register_elche(m);
   flodl::rt::register_wire(m);
   flodl::rt::register_crash(m);
+  flodl::rt::register_chunk_pool(m);
 }

@@ -39,6 +39,7 @@ void register_reduce(py::module& m);
 void register_loader(py::module& m);
 void register_wire(py::module& m);
 void register_crash(py::module& m);
+void register_chunk_pool(py::module& m);
 void install_crash_handler();
 
 }  // namespace rt

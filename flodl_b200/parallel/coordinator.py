@@ -2,8 +2,8 @@
 callback-role election and the alert lane.
 
 Reference roles: flodl/src/distributed/chunk_pool.rs (spans, cursors,
-stealing, forfeit, coverage), cluster_coordinator/window_ledger.rs,
-callback_roles.rs and alerts.rs.
+stealing, forfeit, coverage - native, csrc/runtime/chunk_pool.cpp),
+cluster_coordinator/window_ledger.rs, callback_roles.rs and alerts.rs.
 
 Progressive dispatch: an epoch's permutation (offsets ``0..total``) is split
 into contiguous per-rank spans sized by measured throughput. A rank's chunks
@@ -38,134 +38,27 @@ def spans_from_throughput(total: int, rates: Sequence[float]) -> List[int]:
 
 
 class ChunkPool:
-    def __init__(self, epoch: int, total: int, spans: Sequence[int]):
-        if sum(spans) != total:
-            raise ValueError("spans must cover the epoch exactly")
-        self.epoch, self.total = epoch, total
-        self.start: List[int] = []
-        acc = 0
-        for s in spans:
-            self.start.append(acc)
-            acc += s
-        self.cursor = list(self.start)                       # owner's front
-        self.end = [a + s for a, s in zip(self.start, spans)]  # thieves move this down
-        self.reclaimed: Deque[Tuple[int, int]] = collections.deque()
-        self.outstanding: Dict[int, List[Tuple[int, int]]] = {r: [] for r in range(len(spans))}
-        self.completed = 0
-        self.done_samples: Dict[int, int] = {r: 0 for r in range(len(spans))}
-        self.t0 = time.monotonic()
+    """Progressive dispatch pool. The state machine lives in the native
+    runtime (``flodl_b200._native.ChunkPool``); constructing this class
+    returns that object, whose methods are ``take_chunk(size, rank)``,
+    ``rollback_take``, ``mark_completed``, ``forfeit``, ``residue``,
+    ``reservation``, ``remaining``, ``in_flight``, ``is_epoch_done``,
+    ``uncovered_ranges`` and the ``completed`` counter."""
+
+    def __new__(cls, epoch: int, total: int, spans: Sequence[int]):
+        from .._ext import native
+        return native().ChunkPool(int(epoch), int(total), [int(s) for s in spans])
 
     @staticmethod
-    def equal(epoch: int, total: int, world: int) -> "ChunkPool":
+    def equal(epoch: int, total: int, world: int):
         return ChunkPool(epoch, total, spans_from_throughput(total, [1.0] * world))
 
-    # ------------------------------------------------------------ views
-    def residue(self, rank: int) -> int:
-        return self.end[rank] - self.cursor[rank]
-
-    def reservation(self, rank: int) -> Tuple[int, int]:
-        return self.cursor[rank], self.residue(rank)
-
-    def remaining(self) -> int:
-        return sum(self.residue(r) for r in range(len(self.cursor))) + sum(n for _, n in self.reclaimed)
-
-    def in_flight(self, rank: int) -> int:
-        return sum(n for _, n in self.outstanding[rank])
-
-    def is_epoch_done(self) -> bool:
-        return self.remaining() == 0 and all(not v for v in self.outstanding.values())
-
-    def epoch_elapsed_ms(self) -> float:
-        return (time.monotonic() - self.t0) * 1e3
-
-    # ------------------------------------------------------------ dispatch
-    def take_chunk(self, size: int, rank: int) -> Optional[Tuple[int, int]]:
-        if size <= 0:
-            return None
-        if self.reclaimed:                       # close coverage holes first
-            off, n = self.reclaimed.popleft()
-            k = min(n, size)
-            if k < n:
-                self.reclaimed.appendleft((off + k, n - k))
-            chunk = (off, k)
-        elif self.residue(rank) > 0:             # own span, front to back
-            off = self.cursor[rank]
-            k = min(size, self.residue(rank))
-            self.cursor[rank] += k
-            chunk = (off, k)
-        else:                                    # steal the tail of the largest residue
-            donor = max(range(len(self.cursor)), key=self.residue)
-            if self.residue(donor) <= 0:
-                return None
-            k = min(size, self.residue(donor))
-            self.end[donor] -= k
-            chunk = (self.end[donor], k)
-        self.outstanding[rank].append(chunk)
-        return chunk
-
-    def rollback_take(self, rank: int, offset: int, size: int) -> None:
-        """Undo the rank's newest take (a dispatch whose send failed)."""
-        out = self.outstanding[rank]
-        if not out or out[-1] != (offset, size):
-            raise ValueError("rollback must name the rank's newest outstanding chunk")
-        out.pop()
-        if self.cursor[rank] == offset + size and self.start[rank] <= offset:
-            self.cursor[rank] = offset
-        else:
-            self.reclaimed.appendleft((offset, size))
-
-    def mark_completed(self, rank: int, samples: int) -> None:
-        out = self.outstanding[rank]
-        left = samples
-        while left > 0 and out:
-            off, n = out[0]
-            if n <= left:
-                out.pop(0)
-                left -= n
-            else:
-                out[0] = (off + left, n - left)
-                left = 0
-        done = samples - left  # a falsely-dead rank reporting late is clamped
-        self.completed += done
-        self.done_samples[rank] += done
-
-    def forfeit(self, rank: int) -> int:
-        """A dead rank: its outstanding chunks and unassigned span return to
-        the pool for the survivors. Returns the reclaimed sample count."""
-        n = 0
-        for off, k in self.outstanding[rank]:
-            self.reclaimed.append((off, k))
-            n += k
-        self.outstanding[rank] = []
-        if self.residue(rank) > 0:
-            self.reclaimed.append((self.cursor[rank], self.residue(rank)))
-            n += self.residue(rank)
-            self.cursor[rank] = self.end[rank]
-        return n
-
-    # ------------------------------------------------------------ coverage (resume)
-    def uncovered_ranges(self) -> List[Tuple[int, int]]:
-        """(offset, length) ranges not yet dispatched-and-completed."""
-        rs = [(self.cursor[r], self.residue(r)) for r in range(len(self.cursor)) if self.residue(r)]
-        rs += [c for v in self.outstanding.values() for c in v] + list(self.reclaimed)
-        rs.sort()
-        merged: List[Tuple[int, int]] = []
-        for off, n in rs:
-            if merged and merged[-1][0] + merged[-1][1] >= off:
-                o, m = merged[-1]
-                merged[-1] = (o, max(o + m, off + n) - o)
-            else:
-                merged.append((off, n))
-        return merged
-
     @staticmethod
-    def from_coverage(epoch: int, total: int, world: int,
-                      uncovered: Sequence[Tuple[int, int]]) -> "ChunkPool":
-        p = ChunkPool(epoch, total, [0] * (world - 1) + [total])
-        p.cursor = list(p.end)  # every span consumed; only the holes remain
-        p.reclaimed = collections.deque(sorted(uncovered))
-        p.completed = total - sum(n for _, n in uncovered)
-        return p
+    def from_coverage(epoch: int, total: int, world: int, uncovered: Sequence[Tuple[int, int]]):
+        """A pool whose only work is the ``uncovered`` (offset, size) ranges."""
+        from .._ext import native
+        return native().ChunkPool.from_coverage(int(epoch), int(total), int(world),
+                                                [(int(o), int(n)) for o, n in uncovered])
 
 
 # ----------------------------------------------------------------- window ledger

@@ -163,7 +163,8 @@ def test_sgd_kernel_matches_torch():
 @pytest.fixture
 def fused_linear_only():
     """Route even small problems through the tcgen05 kernels."""
-    from flodl_b200.ops import linear as L
+    import importlib
+    L = importlib.import_module("flodl_b200.ops.linear")  # the module, not the function
     L.set_small_gemm_tiles(0)
     yield
     L.set_small_gemm_tiles(None)
