@@ -23,9 +23,12 @@ the device (host clock on CPU).
 
 Arms: ``flodl`` builds the model from this package (FlowBuilder graphs, its
 layers, its sm_100a kernels on CUDA - bf16 tensor-core GEMMs with f32
-accumulation and f32 master weights); ``torch`` builds the same model from
-``torch.nn`` in f32; ``torch-bf16`` runs that under bf16 autocast, the
-precision-matched baseline.
+accumulation and f32 master weights); ``flodl-graph`` is the same model with
+the whole training step (forward, loss, backward, optimizer) captured once as
+a CUDA graph and replayed (``StepRunner.capture_training``; models with
+host-side control flow cannot be captured and report so); ``torch`` builds the
+same model from ``torch.nn`` in f32; ``torch-bf16`` runs that under bf16
+autocast, the precision-matched baseline.
 
     python -m flodl_b200.benchmarks [--models mlp,transformer] [--arms flodl,torch]
                                     [--runs 4] [--warmup 3] [--epochs 20] [--scale 1.0]
@@ -436,7 +439,7 @@ SUITE: Dict[str, Tuple[BenchConfig, Callable]] = {
 # ----------------------------------------------------------------- harness
 def _optimizer(arm, params):
     params = list(params)
-    if arm == "flodl":
+    if arm.startswith("flodl"):
         from .optim import Adam
         return Adam(params, lr=1e-3)
     return torch.optim.Adam(params, lr=1e-3)
@@ -449,7 +452,7 @@ def run_benchmark(name: str, arm: str = "flodl", device: Optional[str] = None, r
     cfg, build = SUITE[name]
     dev = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
     torch.manual_seed(seed)
-    model, data, loss_fn = build("flodl" if arm == "flodl" else "torch", dev, scale)
+    model, data, loss_fn = build("flodl" if arm.startswith("flodl") else "torch", dev, scale)
     model.train()
     opt = _optimizer(arm, model.parameters())
     B = max(1, int(cfg.batch_size * batch_scale))
@@ -459,8 +462,26 @@ def run_benchmark(name: str, arm: str = "flodl", device: Optional[str] = None, r
            else contextlib.nullcontext())
     cuda = dev.type == "cuda"
 
+    runner = None
+    if arm == "flodl-graph":
+        if not cuda:
+            raise RuntimeError("flodl-graph needs CUDA")
+        from .train import StepRunner
+
+        def lf(out, y):
+            return loss_fn(out.float(), y) if y.is_floating_point() else loss_fn(out, y)
+        runner = StepRunner.capture_training(model, opt, lf, list(batches[0]))
+
     def epoch() -> Tuple[float, float]:
         total = torch.zeros((), device=dev)
+        if runner is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for x, y in batches:
+                total += runner.replay(x, y)
+            e1.record()
+            e1.synchronize()
+            return e0.elapsed_time(e1), float(total) / nb
         if cuda:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
@@ -511,7 +532,7 @@ def run_benchmark(name: str, arm: str = "flodl", device: Optional[str] = None, r
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--models", default=",".join(SUITE))
-    ap.add_argument("--arms", default="flodl,torch,torch-bf16")
+    ap.add_argument("--arms", default="flodl,torch,torch-bf16,flodl-graph")
     ap.add_argument("--runs", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--epochs", type=int, default=20)
@@ -523,15 +544,23 @@ def main(argv=None):
     for name in a.models.split(","):
         rows = {}
         for arm in a.arms.split(","):
-            r = run_benchmark(name, arm, a.device, a.runs, a.warmup, a.epochs, a.batches or None,
-                              a.scale, a.batch_scale)
+            try:
+                r = run_benchmark(name, arm, a.device, a.runs, a.warmup, a.epochs, a.batches or None,
+                                  a.scale, a.batch_scale)
+            except Exception as e:  # e.g. a model with host-side control flow under capture
+                print(json.dumps({"name": name, "arm": arm, "unavailable": repr(e)[:300]}), flush=True)
+                continue
             rows[arm] = r
             print(json.dumps(asdict(r)), flush=True)
         if "flodl" in rows and "torch" in rows:
             f, t = rows["flodl"].median_epoch_ms, rows["torch"].median_epoch_ms
-            print(json.dumps({"name": name, "speedup_vs_torch_f32": round(t / f, 3),
-                              **({"speedup_vs_torch_bf16": round(rows["torch-bf16"].median_epoch_ms / f, 3)}
-                                 if "torch-bf16" in rows else {})}), flush=True)
+            extra = {}
+            if "torch-bf16" in rows:
+                extra["speedup_vs_torch_bf16"] = round(rows["torch-bf16"].median_epoch_ms / f, 3)
+            if "flodl-graph" in rows:
+                extra["graph_speedup_vs_torch_f32"] = round(t / rows["flodl-graph"].median_epoch_ms, 3)
+            print(json.dumps({"name": name, "speedup_vs_torch_f32": round(t / f, 3), **extra}),
+                  flush=True)
 
 
 if __name__ == "__main__":

@@ -44,6 +44,38 @@ class StepRunner:
             loss = step_fn()
         return cls(step_fn, inputs, g, loss)
 
+    @classmethod
+    def capture_training(cls, model, optimizer, loss_fn, example_inputs: Sequence[torch.Tensor],
+                         warmup: int = 3) -> "StepRunner":
+        """Capture ``loss_fn(model(x), y)`` + backward + ``optimizer.step()`` +
+        ``zero_grad`` as one CUDA graph over static input buffers (copies of
+        ``example_inputs``). The warm-up steps (on a side stream) create the
+        optimizer's flat arena and device scalars, so the captured step
+        allocates nothing and syncs with the host nowhere. Models whose
+        forward makes host-side decisions (``while``/``until`` loops, hard
+        switches) cannot be captured; the capture then raises."""
+        static = [t.detach().clone() for t in example_inputs]
+
+        def step():
+            out = model(*static[:-1])
+            loss = loss_fn(out, static[-1])
+            loss.backward()
+            optimizer.step()
+            optimizer.zero_grad()
+            return loss.detach()
+
+        return cls.capture(step, static, warmup)
+
+    def replay(self, *device_inputs: torch.Tensor) -> torch.Tensor:
+        """Device-side step: copy inputs into the static buffers, replay,
+        return the loss tensor (no host sync)."""
+        for dst, src in zip(self.inputs, device_inputs):
+            dst.copy_(src, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            return self.graph_loss
+        return self.step_fn()
+
     def step(self, *host_inputs: torch.Tensor) -> float:
         if len(host_inputs) != len(self.inputs):
             raise ValueError(f"expected {len(self.inputs)} inputs, got {len(host_inputs)}")
