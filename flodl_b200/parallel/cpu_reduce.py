@@ -12,6 +12,10 @@ rank):
     CONSENSUS(round, bytes)           controller -> rank: sum(payloads) / sum(mass)
     HEARTBEAT(rank)                   rank -> controller, every ``heartbeat_s``
     DEAD(rank)                        controller -> ranks when a heartbeat is stale
+    BCAST(round, rank, root flag, dtype, bytes)
+                                      rank -> controller: initial-state broadcast;
+                                      the root's bytes go to every rank once all
+                                      alive ranks asked (the others send none)
     HOSTFRAME(round, mass, dtype, ranks, bytes)
                                       relay -> controller: the folded sum of a
                                       host's ranks (flodl_b200.parallel.relay)
@@ -40,6 +44,7 @@ from .._ext import native
 
 MAGIC = 0x464C4443  # "FLDC"
 K_HELLO, K_ROUND, K_CONSENSUS, K_HEARTBEAT, K_DEAD, K_BYE, K_HOSTFRAME = 1, 2, 3, 4, 5, 6, 7
+K_BCAST = 8
 DT_F32, DT_BF16 = 0, 1
 MAX_FRAME = 1 << 34
 
@@ -122,6 +127,7 @@ class CpuReduceController:
         self.last_hb: Dict[int, float] = {}
         self.pending: Dict[int, Dict[int, Tuple[Optional[torch.Tensor], float]]] = {}
         self.host_parts: Dict[int, List[Tuple[torch.Tensor, float]]] = {}
+        self.bcasts: Dict[int, dict] = {}  # rnd -> {"ranks": set, "payload": bytes | None}
         self.lock = threading.Lock()
         self.cv = threading.Condition(self.lock)
         self.rejected = 0
@@ -203,6 +209,14 @@ class CpuReduceController:
                             self.last_hb[r] = now
                         self.host_parts.setdefault(rnd, []).append((t, mass))
                         self._maybe_finish(rnd)
+                elif kind == K_BCAST:  # the sender's rank rides in the payload (relays)
+                    rnd, who, is_root, dt = struct.unpack("<qiii", payload[:20])
+                    with self.cv:
+                        b = self.bcasts.setdefault(rnd, {"ranks": set(), "payload": None})
+                        b["ranks"].add(who)
+                        if is_root:
+                            b["payload"] = struct.pack("<qi", rnd, dt) + payload[20:]
+                        self._maybe_bcast(rnd)
                 elif kind == K_HELLO:  # relay: one more local rank on this connection
                     (r,) = struct.unpack("<i", payload)
                     mine.append(r)
@@ -256,6 +270,13 @@ class CpuReduceController:
             except OSError:
                 pass
 
+    def _maybe_bcast(self, rnd: int):
+        b = self.bcasts.get(rnd)
+        if b is None or b["payload"] is None or not self.alive.issubset(b["ranks"]):
+            return
+        del self.bcasts[rnd]
+        self._broadcast(K_CONSENSUS, rnd % (1 << 64), b["payload"], sorted(self.alive))
+
     def _maybe_finish(self, rnd: int):
         got = self.pending.get(rnd, {})
         if not self.alive or not self.alive.issubset(got.keys()):
@@ -268,7 +289,7 @@ class CpuReduceController:
         ranks = sorted(got.keys() & self.alive)
         del self.pending[rnd]
         self.rounds_done += 1
-        self._broadcast(K_CONSENSUS, rnd, payload, ranks)
+        self._broadcast(K_CONSENSUS, rnd % (1 << 64), payload, ranks)
 
     def close(self):
         self._stop.set()
@@ -340,13 +361,31 @@ class CpuReduceClient:
                           timeout: float = 120.0) -> torch.Tensor:
         dt, raw = encode_tensor(t.detach().float() * mass, self.bf16)
         payload = struct.pack("<qdi", rnd, float(mass), dt) + raw
-        send_frame(self.sock, self.key, K_ROUND, rnd, payload, self.lock)
+        send_frame(self.sock, self.key, K_ROUND, rnd % (1 << 64), payload, self.lock)
         deadline = time.time() + timeout
         with self._cv:
             while rnd not in self._inbox:
                 left = deadline - time.time()
                 if left <= 0:
                     raise TimeoutError(f"rank {self.rank}: reduce round {rnd} timed out")
+                self._cv.wait(left)
+            out = self._inbox.pop(rnd)
+        return out.reshape(t.shape).to(t.device, t.dtype)
+
+    def broadcast_from_root(self, t: torch.Tensor, root: int, rnd: int,
+                            timeout: float = 120.0) -> torch.Tensor:
+        """Every rank receives the root's tensor (the initial parameter state);
+        non-root ranks send no payload."""
+        is_root = self.rank == root
+        dt, raw = encode_tensor(t, self.bf16) if is_root else (DT_F32, b"")
+        send_frame(self.sock, self.key, K_BCAST, rnd % (1 << 64),
+                   struct.pack("<qiii", rnd, self.rank, int(is_root), dt) + raw, self.lock)
+        deadline = time.time() + timeout
+        with self._cv:
+            while rnd not in self._inbox:
+                left = deadline - time.time()
+                if left <= 0:
+                    raise TimeoutError(f"rank {self.rank}: broadcast {rnd} timed out")
                 self._cv.wait(left)
             out = self._inbox.pop(rnd)
         return out.reshape(t.shape).to(t.device, t.dtype)

@@ -13,6 +13,7 @@ the relay holds ONE upstream connection to the controller for the whole host:
   never a division (the controller divides exactly once); the deposit that
   completes the round (every locally alive rank merged) ships one HOSTFRAME
   upstream, so uplink bytes scale with hosts, not ranks;
+* BCAST (initial-state broadcast) frames are forwarded as they are;
 * the controller's CONSENSUS arrives once and is fanned out to the local
   ranks of that round; a DEAD from the controller is forwarded to every local
   rank and drops the rank from the local fold;
@@ -29,8 +30,8 @@ from typing import Dict, List, Optional, Set, Tuple
 
 import torch
 
-from .cpu_reduce import (DT_F32, K_BYE, K_CONSENSUS, K_DEAD, K_HEARTBEAT, K_HELLO, K_HOSTFRAME,
-                         K_ROUND, decode_tensor, recv_frame, send_frame)
+from .cpu_reduce import (DT_F32, K_BCAST, K_BYE, K_CONSENSUS, K_DEAD, K_HEARTBEAT, K_HELLO,
+                         K_HOSTFRAME, K_ROUND, decode_tensor, recv_frame, send_frame)
 
 RELAY_DATA_LOOPBACK_OFFSET = 4  # loopback port = controller port + 4
 
@@ -129,6 +130,8 @@ class RelayAgent:
                     self._send_up(K_HEARTBEAT, 0, struct.pack("<i", rank))
                 elif kind == K_ROUND:
                     self._deposit(rank, payload)
+                elif kind == K_BCAST:  # initial-state broadcast: forwarded (it carries its rank)
+                    self._send_up(K_BCAST, seq, payload)
                 elif kind == K_BYE:
                     break
         except Exception:
@@ -168,7 +171,7 @@ class RelayAgent:
         body = total.contiguous().numpy().tobytes()
         payload = (struct.pack("<qdii", rnd, mass, DT_F32, len(ranks))
                    + struct.pack(f"<{len(ranks)}i", *ranks) + body)
-        self._send_up(K_HOSTFRAME, rnd, payload)
+        self._send_up(K_HOSTFRAME, rnd % (1 << 64), payload)
         with self.lock:
             self.frames_up += 1
             self.bytes_up += len(payload)

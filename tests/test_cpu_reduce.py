@@ -76,3 +76,22 @@ def test_reduce_scaled_native_matches_python():
     ms = [1.0, 2.0, 3.0, 4.0]
     out = native().reduce_scaled(ts, ms)
     torch.testing.assert_close(out, sum(ts) / sum(ms))
+
+
+def test_broadcast_from_root():
+    ctl = CpuReduceController(3, KEY)
+    clients = [CpuReduceClient(r, "127.0.0.1", ctl.port, KEY, heartbeat_s=0.2) for r in range(3)]
+    src = torch.randn(257)
+    out = [None] * 3
+
+    def run(r):
+        t = src.clone() if r == 1 else torch.zeros(257)
+        out[r] = clients[r].broadcast_from_root(t, root=1, rnd=-5, timeout=20)
+
+    ts = [threading.Thread(target=run, args=(r,)) for r in range(3)]
+    [t.start() for t in ts]
+    [t.join() for t in ts]
+    for o in out:
+        torch.testing.assert_close(o, src)
+    [c.close() for c in clients]
+    ctl.close()

@@ -155,3 +155,25 @@ def test_bind_diagnosis_message_from_port_mux():
     with pytest.raises(OSError, match="busy"):
         PortMux("127.0.0.1", port)
     s.close()
+
+
+def test_broadcast_through_a_relay():
+    ctl = CpuReduceController(3, KEY)
+    ra = RelayAgent(("127.0.0.1", ctl.port), KEY)
+    clients = [CpuReduceClient(r, "127.0.0.1", ra.port if r < 2 else ctl.port, KEY, heartbeat_s=0.2)
+               for r in range(3)]
+    assert _wait(lambda: len(ctl.conns) == 3)
+    src = torch.randn(33)
+    out = [None] * 3
+
+    def run(r):
+        out[r] = clients[r].broadcast_from_root(src.clone() if r == 2 else torch.zeros(33), root=2,
+                                                rnd=0, timeout=20)
+
+    ts = [threading.Thread(target=run, args=(r,)) for r in range(3)]
+    [t.start() for t in ts]
+    [t.join() for t in ts]
+    for o in out:
+        torch.testing.assert_close(o, src)
+    [c.close() for c in clients]
+    ra.close(), ctl.close()
