@@ -523,6 +523,20 @@ class Graph(Module):
     def set_lr_scale(self, s: float) -> None:
         self._lr_scale = s
 
+    def set_data_loader(self, loader) -> None:
+        """Bind a streaming DataLoader: its prefetch sizing keeps ~3x the
+        parameter bytes free for gradients and optimizer state (the step
+        memory a VRAM probe cannot see before the first step)."""
+        self._data_loader = loader
+        if getattr(loader, "step_reserve_", None) is None:
+            loader.step_reserve_ = 3 * sum(p.numel() * p.element_size() for p in self.parameters())
+
+    def epoch_batches(self, epoch: int):
+        """Batches of the bound loader for ``epoch``."""
+        if getattr(self, "_data_loader", None) is None:
+            raise RuntimeError("Graph.epoch_batches(): no data loader set")
+        return self._data_loader.epoch(epoch)
+
     def step(self) -> None:
         """Optimizer step + scheduler update + zero_grad (graph/distributed.rs)."""
         if self._optimizer is None:

@@ -215,3 +215,23 @@ def test_snapshot_cpu_background_save(tmp_path):
     rep = load_checkpoint(str(tmp_path / "m.fdl"), g2.graph_named_parameters(), (), g2.structural_hash())
     for (_, t), ref in zip(g2.graph_named_parameters(), before):
         torch.testing.assert_close(t.detach(), ref)
+
+
+def test_training_glue_with_data_loader():
+    from flodl_b200.data import DataLoader, TensorDataSet
+    from flodl_b200.optim import SGD, StepDecay
+    g = FlowBuilder.from_(Linear(3, 1)).build()
+    x = torch.randn(64, 3)
+    dl = DataLoader.from_dataset(TensorDataSet(x, x.sum(1, keepdim=True))).batch_size(16).build()
+    g.set_data_loader(dl)
+    g.set_optimizer(SGD(g.parameters(), lr=0.1))
+    g.set_scheduler(StepDecay(0.1, 2, 0.5))
+    first = last = None
+    for ep in range(6):
+        for xb, yb in g.epoch_batches(ep):
+            loss = torch.nn.functional.mse_loss(g(xb), yb)
+            loss.backward()
+            g.step()
+            first = first if first is not None else loss.item()
+            last = loss.item()
+    assert last < first and g.step_count() == 24
