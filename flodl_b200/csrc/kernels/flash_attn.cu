@@ -159,9 +159,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ void fwd_decode(int item, int n_qt, int H, int& qt, int& h, int& b) {
-  qt = item % n_qt;
-  const int bh = item / n_qt;
+// Work order: the tile index is the slowest-varying coordinate and, under a
+// causal mask, the heaviest tiles (most key tiles) come first. CTA c takes
+// items c, c + grid, ...; with the tile index fastest, an even grid would hand
+// every CTA of one parity the same tile (all-heavy vs all-light CTAs), while
+// heaviest-first striding gives each CTA a near-equal mix (longest-processing-
+// time-first list scheduling).
+__device__ __forceinline__ void fwd_decode(int item, int n_qt, int H, int n_bh, bool causal,
+                                           int& qt, int& h, int& b) {
+  const int t = item / n_bh;
+  const int bh = item - t * n_bh;
+  qt = causal ? n_qt - 1 - t : t;
   h = bh % H;
   b = bh / H;
 }
@@ -217,7 +225,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       int n = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int qt, h, b;
-        fwd_decode(item, n_qt, H, qt, h, b);
+        fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
         const int qb = n & 1;
         if (!(ok = mbar_wait_bounded(&sm.q_empty[qb], ((n >> 1) & 1) ^ 1, abort_flag, err, limit)))
           break;
@@ -263,7 +271,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       };
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int qt, h, b;
-        fwd_decode(item, n_qt, H, qt, h, b);
+        fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
         const int qb = n & 1;
         const uint32_t t_o = tmem + 256 + (uint32_t)qb * kD;
         if (!(ok = mbar_wait_bounded(&sm.q_full[qb], (n >> 1) & 1, abort_flag, err, limit))) break;
@@ -324,7 +332,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     };
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
       int qt, h, b;
-      fwd_decode(item, n_qt, H, qt, h, b);
+      fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
       const int qb = n & 1;
       const uint32_t t_o = tmem + 256 + (uint32_t)qb * kD;
       const int q0 = qt * kTile;
@@ -611,9 +619,11 @@ __global__ void __launch_bounds__(kPostMaxThreads) flash_bwd_post_kernel(
   }
 }
 
-__device__ __forceinline__ void bwd_decode(int item, int n_kt, int H, int& kt, int& h, int& b) {
-  kt = item % n_kt;
-  const int bh = item / n_kt;
+// Same order as the forward: tile slowest; under a causal mask key tile 0
+// sees every query tile, so ascending key tiles are heaviest-first.
+__device__ __forceinline__ void bwd_decode(int item, int n_bh, int H, int& kt, int& h, int& b) {
+  kt = item / n_bh;
+  const int bh = item - kt * n_bh;
   h = bh % H;
   b = bh / H;
 }
@@ -675,7 +685,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int n = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int kt, h, b;
-        bwd_decode(item, n_t, H, kt, h, b);
+        bwd_decode(item, H * B, H, kt, h, b);
         if (!(ok = mbar_wait_bounded(&sm.kv_empty, (n & 1) ^ 1, abort_flag, err, limit))) break;
         mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
         tma_load_3d(sm.k, &tm_qkv, &sm.kv_full, C + h * kD, kt * kTile, b);
@@ -705,7 +715,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int n = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int kt, h, b;
-        bwd_decode(item, n_t, H, kt, h, b);
+        bwd_decode(item, H * B, H, kt, h, b);
         if (!(ok = mbar_wait_bounded(&sm.kv_full, n & 1, abort_flag, err, limit))) break;
         if (!(ok = mbar_wait_bounded(&sm.dkv_free, (n & 1) ^ 1, abort_flag, err, limit))) break;
         int it = 0;
@@ -799,7 +809,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     };
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
       int kt, h, b;
-      bwd_decode(item, n_t, H, kt, h, b);
+      bwd_decode(item, H * B, H, kt, h, b);
       const int kj = kt * kTile + r;
       const bool key_ok = kj < S && !(key_pad && __ldg(key_pad + (size_t)b * S + kj) != 0);
       for (int i = first_q(kt); i < n_t; ++i, ++t) {

@@ -41,7 +41,12 @@ class GpuGraph:
             for _ in range(warmup):
                 fn()
         torch.cuda.current_stream().wait_stream(s)
-        with torch.cuda.graph(self.graph, pool=self.pool, capture_error_mode=self.mode.value):
+        # capture on the warm-up stream: autograd nodes that outlive a warm-up
+        # step (e.g. loop traces kept for inspection) carry that stream, and a
+        # backward that touches them from another stream would wait on work
+        # outside the capture
+        with torch.cuda.graph(self.graph, pool=self.pool, stream=s,
+                              capture_error_mode=self.mode.value):
             self.output = fn()
         self.captured = True
         return self.output

@@ -40,7 +40,11 @@ class StepRunner:
                 step_fn()
         torch.cuda.current_stream().wait_stream(s)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # captured on the warm-up stream: autograd nodes that outlive a warm-up
+        # step (loop traces, cached gradient accumulators) record the stream
+        # they were created on, and a captured backward that syncs with a
+        # stream outside the capture is invalid
+        with torch.cuda.graph(g, stream=s):
             loss = step_fn()
         return cls(step_fn, inputs, g, loss)
 
