@@ -352,7 +352,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_ld_32cols(tmem + sb * 128 + lane_off + (uint32_t)(hh * 64 + c * 32), raw);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]) * sl2;
+          for (int i = 0; i < 32; i += 2)
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1])),
+                             f2_splat(sl2)),
+                      s[c * 32 + i], s[c * 32 + i + 1]);
         }
         tc_fence_before();
         __syncwarp();
@@ -398,13 +401,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float corr = (move && m_ref != -INFINITY) ? ex2_approx(m_ref - m_new) : 1.f;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         m_ref = m_new;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint64_t l2a = f2_splat(0.f), l2b = f2_splat(0.f);
+        const uint64_t neg_m = f2_splat(-m_use);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          s[c] = ex2_approx(s[c] - m_use);
-          l4[c & 3] += s[c];
+        for (int c = 0; c < 64; c += 2) {
+          float a0, a1;
+          f2_unpack(f2_add(f2_pack(s[c], s[c + 1]), neg_m), a0, a1);
+          s[c] = ex2_approx(a0);
+          s[c + 1] = ex2_approx(a1);
+          if (c & 2)
+            l2b = f2_add(l2b, f2_pack(s[c], s[c + 1]));
+          else
+            l2a = f2_add(l2a, f2_pack(s[c], s[c + 1]));
         }
-        l_half = l_half * corr + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
+        float la0, la1, lb0, lb1;
+        f2_unpack(l2a, la0, la1);
+        f2_unpack(l2b, lb0, lb1);
+        l_half = l_half * corr + ((la0 + la1) + (lb0 + lb1));
         // P is single-buffered: the previous P V must have finished reading it
         if (p_it > 0) {
           ok = mbar_wait_bounded(&sm.pv_done, (p_it - 1) & 1, abort_flag, err, limit);
@@ -778,6 +791,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = q4 * 32 + lane;  // key row within the tile (and query row for dQ)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = scale * kLog2e;
+    const uint64_t sl2x2 = f2_splat(sl2);
     float* st_lse = sm.stat[wi][0];
     float* st_dl = sm.stat[wi][1];
     uint32_t t = 0;
@@ -822,8 +836,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int qi = qc0 + u * 32 + lane;
-            st_lse[u * 32 + lane] = qi < S ? __ldg(lrow + qi) : INFINITY;
-            st_dl[u * 32 + lane] = qi < S ? __ldg(drow + qi) : 0.f;
+            // stored negated, so that P^T and dS^T take packed FMAs/adds
+            st_lse[u * 32 + lane] = qi < S ? -__ldg(lrow + qi) : -INFINITY;
+            st_dl[u * 32 + lane] = qi < S ? -__ldg(drow + qi) : 0.f;
           }
           __syncwarp();
         }
@@ -850,13 +865,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
             const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 4; u += 2) {
               const int c = 4 * c4 + u;
-              bool valid = key_ok;
-              if (diag) valid = valid && (kj <= qc0 + cc * 32 + c);
-              const float pv = valid ? ex2_approx(__uint_as_float(rs[c]) * sl2 - lv[u]) : 0.f;
-              p[c] = pv;
-              ds[c] = pv * (__uint_as_float(rdp[c]) - dv[u]);
+              float a0, a1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sl2x2,
+                               f2_pack(lv[u], lv[u + 1])),
+                        a0, a1);
+              const bool v0 = key_ok && (!diag || kj <= qc0 + cc * 32 + c);
+              const bool v1 = key_ok && (!diag || kj <= qc0 + cc * 32 + c + 1);
+              p[c] = v0 ? ex2_approx(a0) : 0.f;
+              p[c + 1] = v1 ? ex2_approx(a1) : 0.f;
+              const uint64_t dd = f2_add(
+                  f2_pack(__uint_as_float(rdp[c]), __uint_as_float(rdp[c + 1])),
+                  f2_pack(dv[u], dv[u + 1]));
+              f2_unpack(f2_mul(f2_pack(p[c], p[c + 1]), dd), ds[c], ds[c + 1]);
             }
           }
 #pragma unroll

@@ -264,20 +264,24 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
                                                    int row0, int col0, int lane, int N,
                                                    const uint32_t (&acc)[32]) {
   float v[32];
+  if (ep.bias && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0) {
+    // v = acc * alpha + bias, two columns per packed FMA
+    const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+    const uint64_t al = f2_splat(alpha);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) * alpha;
-  if (ep.bias) {
-    if (col0 + 32 <= N && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0) {
-      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = __ldg(b4 + q);
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(acc[4 * q]), __uint_as_float(acc[4 * q + 1])), al,
+                       f2_pack(b.x, b.y)),
+                v[4 * q], v[4 * q + 1]);
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(acc[4 * q + 2]), __uint_as_float(acc[4 * q + 3])),
+                       al, f2_pack(b.z, b.w)),
+                v[4 * q + 2], v[4 * q + 3]);
+    }
+  } else {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 b = __ldg(b4 + q);
-        v[4 * q + 0] += b.x;
-        v[4 * q + 1] += b.y;
-        v[4 * q + 2] += b.z;
-        v[4 * q + 3] += b.w;
-      }
-    } else {
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]) * alpha;
+    if (ep.bias) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += (col0 + i < N) ? __ldg(ep.bias + col0 + i) : 0.f;
     }
@@ -288,7 +292,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
   if (ep.flags & kEpiGelu) {
     float dg[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) gelu_and_grad(v[i], v[i], dg[i]);
+    for (int i = 0; i < 32; i += 2) gelu_and_grad2(v[i], v[i + 1], v[i], v[i + 1], dg[i], dg[i + 1]);
     if (aux_out) {  // GELU', kept for the backward pass
       uint8_t* a = slot + 2048 + lane * 64;
 #pragma unroll
@@ -311,8 +315,8 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const float2 f = unpack_bf16x2(ws[h]);
-        v[8 * q + 2 * h + 0] *= f.x;
-        v[8 * q + 2 * h + 1] *= f.y;
+        f2_unpack(f2_mul(f2_pack(v[8 * q + 2 * h], v[8 * q + 2 * h + 1]), f2_pack(f.x, f.y)),
+                  v[8 * q + 2 * h], v[8 * q + 2 * h + 1]);
       }
     }
   }

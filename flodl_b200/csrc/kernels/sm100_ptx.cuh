@@ -356,6 +356,78 @@ __device__ __forceinline__ float gelu_erf_grad(float x) {
   return cdf + x * pdf;
 }
 
+// ---------------------------------------------------------------- packed f32x2
+// sm_100 executes add/mul/fma on a pair of f32 values held in one 64-bit
+// register pair as one instruction (`.f32x2`, round-to-nearest like the scalar
+// forms), halving the issue slots of elementwise epilogue math.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_splat(float a) { return f2_pack(a, a); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// GELU and GELU' of two values with packed math: the same A&S 7.1.28 erf as
+// gelu_and_grad, with the 1/sqrt(2) argument scale folded into the
+// coefficients (b_k = a_k 2^(-k/2)), so the polynomial runs on |x| directly
+// (clamped at 8 sqrt(2), where Phi is 1 to single precision).
+//   Phi(x) = [x >= 0] - sign(x) * r / 2,  r = (1 + sum b_k |x|^k)^-16
+//   GELU(x) = x Phi(x),  GELU'(x) = Phi(x) + x exp(-x^2/2) / sqrt(2 pi)
+__device__ __forceinline__ void gelu_and_grad2(float x0, float x1, float& g0, float& g1,
+                                               float& d0, float& d1) {
+  constexpr float kR = 0.70710678118654752f;
+  constexpr float b1 = 0.0705230784f * kR, b2 = 0.0422820123f * 0.5f,
+                  b3 = 0.0092705272f * 0.5f * kR, b4 = 0.0001520143f * 0.25f,
+                  b5 = 0.0002765672f * 0.25f * kR, b6 = 0.0000430638f * 0.125f;
+  constexpr float kClamp = 8.0f * 1.41421356237309505f;
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t ax = f2_pack(fminf(fabsf(x0), kClamp), fminf(fabsf(x1), kClamp));
+  uint64_t p = f2_fma(f2_splat(b6), ax, f2_splat(b5));
+  p = f2_fma(p, ax, f2_splat(b4));
+  p = f2_fma(p, ax, f2_splat(b3));
+  p = f2_fma(p, ax, f2_splat(b2));
+  p = f2_fma(p, ax, f2_splat(b1));
+  p = f2_fma(p, ax, f2_splat(1.0f));
+  p = f2_mul(p, p);  // ^2
+  p = f2_mul(p, p);  // ^4
+  p = f2_mul(p, p);  // ^8
+  p = f2_mul(p, p);  // ^16
+  float p0, p1, r0, r1;
+  f2_unpack(p, p0, p1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(p0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(p1));
+  const uint64_t base = f2_pack(x0 >= 0.f ? 1.f : 0.f, x1 >= 0.f ? 1.f : 0.f);
+  const uint64_t nhalf = f2_pack(x0 >= 0.f ? -0.5f : 0.5f, x1 >= 0.f ? -0.5f : 0.5f);
+  const uint64_t cdf = f2_fma(nhalf, f2_pack(r0, r1), base);
+  f2_unpack(f2_mul(x, cdf), g0, g1);
+  // exp(-x^2/2) = 2^(-x^2 log2(e) / 2)
+  const uint64_t arg = f2_mul(f2_mul(x, x), f2_splat(-0.72134752044448170f));
+  float a0, a1, e0, e1;
+  f2_unpack(arg, a0, a1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+  const uint64_t xe = f2_mul(x, f2_pack(e0, e1));
+  f2_unpack(f2_fma(xe, f2_splat(0.39894228040143268f), cdf), d0, d1);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
