@@ -16,6 +16,9 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace flodl {
 
@@ -52,6 +55,59 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 constexpr int kWarps = 8;
+
+// cp.async staging for the backward pass: each lane copies its own column
+// chunks of the next row into its warp's shared-memory slot and later reads
+// back only what it copied itself, so no warp barrier is needed - only the
+// per-thread cp.async group wait.
+__device__ __forceinline__ void cp_async_8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+template <typename T>
+__device__ __forceinline__ void cp_async_4elems(void* dst, const T* src);
+template <>
+__device__ __forceinline__ void cp_async_4elems<float>(void* dst, const float* src) {
+  cp_async_16(dst, src);
+}
+template <>
+__device__ __forceinline__ void cp_async_4elems<__nv_bfloat16>(void* dst, const __nv_bfloat16* src) {
+  cp_async_8(dst, src);
+}
+template <typename T>
+__device__ __forceinline__ void lds4(const uint8_t* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void lds4<float>(const uint8_t* p, float (&v)[4]) {
+  const float4 f = *reinterpret_cast<const float4*>(p);
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+template <>
+__device__ __forceinline__ void lds4<__nv_bfloat16>(const uint8_t* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+// Rows up to kStagedMaxNV * 128 columns take the staged path; one slot holds
+// x, dy and the skip-path gradient of one row for one warp.
+constexpr int kStagedMaxNV = 4;
+template <typename TIn, int NV>
+struct LnBwdSlot {
+  static constexpr int kX = 4 * (int)sizeof(TIn);  // bytes per lane chunk
+  static constexpr int kXOff = 0;
+  static constexpr int kDyOff = NV * 32 * kX;
+  static constexpr int kROff = kDyOff + NV * 32 * 8;
+  static constexpr int kBytes = kROff + NV * 32 * 16;
+  static constexpr int kBlockBytes = NV <= kStagedMaxNV ? kWarps * 2 * kBytes : 0;
+};
 
 // NV = number of 128-element column groups (C <= NV*128); lane owns columns
 // lane*4 + 128*j .. +3 for j < NV.
@@ -135,19 +191,63 @@ __global__ void __launch_bounds__(kWarps * 32, 2) ln_bwd_kernel(
   for (int j = 0; j < NV; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc_dg[j][e] = acc_db[j][e] = acc_cs[j][e] = 0.f;
-  for (int r = warp_global; r < rows; r += nwarps) {
-    // issue every load of the row up front (x, dy, skip-path gradient)
-    float xh[NV][4], dyv[NV][4], rv[NV][4];
+  using Slot = LnBwdSlot<TIn, NV>;
+  constexpr bool kStaged = NV <= kStagedMaxNV;
+  extern __shared__ __align__(16) uint8_t ln_stage[];
+  uint8_t* wslots = ln_stage + (size_t)wib * 2 * Slot::kBytes;
+  // the next row of this warp goes into the other slot while this one is used
+  auto stage_row = [&](int r, int slot) {
+    uint8_t* b = wslots + slot * Slot::kBytes;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = lane * 4 + 128 * j;
+      const int k = j * 32 + lane;
       if (c < C) {
-        load4<TIn>(x + (size_t)r * C + c, xh[j]);
-        load4<__nv_bfloat16>(dy + (size_t)r * C + c, dyv[j]);
-        if (dres) load4<float>(dres + (size_t)r * C + c, rv[j]);
+        cp_async_4elems<TIn>(b + Slot::kXOff + k * Slot::kX, x + (size_t)r * C + c);
+        cp_async_8(b + Slot::kDyOff + k * 8, dy + (size_t)r * C + c);
+        if (dres) cp_async_16(b + Slot::kROff + k * 16, dres + (size_t)r * C + c);
+      }
+    }
+    cp_async_commit();  // every lane commits, copies or not: group counts stay uniform
+  };
+  int slot = 0;
+  if (kStaged && warp_global < rows) stage_row(warp_global, 0);
+  for (int r = warp_global; r < rows; r += nwarps, slot ^= 1) {
+    float xh[NV][4], dyv[NV][4], rv[NV][4];
+    if constexpr (kStaged) {
+      if (r + nwarps < rows) {
+        stage_row(r + nwarps, slot ^ 1);
+        cp_async_wait<1>();
       } else {
+        cp_async_wait<0>();
+      }
+      const uint8_t* b = wslots + slot * Slot::kBytes;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
+      for (int j = 0; j < NV; ++j) {
+        const int c = lane * 4 + 128 * j;
+        const int k = j * 32 + lane;
+        if (c < C) {
+          lds4<TIn>(b + Slot::kXOff + k * Slot::kX, xh[j]);
+          lds4<__nv_bfloat16>(b + Slot::kDyOff + k * 8, dyv[j]);
+          if (dres) lds4<float>(b + Slot::kROff + k * 16, rv[j]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
+        }
+      }
+    } else {
+      // issue every load of the row up front (x, dy, skip-path gradient)
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int c = lane * 4 + 128 * j;
+        if (c < C) {
+          load4<TIn>(x + (size_t)r * C + c, xh[j]);
+          load4<__nv_bfloat16>(dy + (size_t)r * C + c, dyv[j]);
+          if (dres) load4<float>(dres + (size_t)r * C + c, rv[j]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xh[j][e] = dyv[j][e] = 0.f;
+        }
       }
     }
     if (pre_add && dres) {
@@ -346,15 +446,30 @@ int grid_for_rows(int rows) {
 
 }  // namespace
 
-#define FL_LN_DISPATCH_NV(C, KERNEL_CALL) \
+// Dynamic shared memory above the 48 KB default needs a per-device,
+// per-function opt-in; done once per (function, device).
+static cudaError_t opt_in_smem(const void* fn, int bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({fn, dev})) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({fn, dev});
+  return e;
+}
+
+#define FL_LN_DISPATCH_NV(C, ...) \
   do {                                   \
     int nv_ = ((C) + 127) / 128;         \
-    if (nv_ <= 1) { constexpr int NV = 1; KERNEL_CALL; } \
-    else if (nv_ <= 2) { constexpr int NV = 2; KERNEL_CALL; } \
-    else if (nv_ <= 4) { constexpr int NV = 4; KERNEL_CALL; } \
-    else if (nv_ <= 6) { constexpr int NV = 6; KERNEL_CALL; } \
-    else if (nv_ <= 8) { constexpr int NV = 8; KERNEL_CALL; } \
-    else if (nv_ <= 16) { constexpr int NV = 16; KERNEL_CALL; } \
+    if (nv_ <= 1) { constexpr int NV = 1; __VA_ARGS__; } \
+    else if (nv_ <= 2) { constexpr int NV = 2; __VA_ARGS__; } \
+    else if (nv_ <= 4) { constexpr int NV = 4; __VA_ARGS__; } \
+    else if (nv_ <= 6) { constexpr int NV = 6; __VA_ARGS__; } \
+    else if (nv_ <= 8) { constexpr int NV = 8; __VA_ARGS__; } \
+    else if (nv_ <= 16) { constexpr int NV = 16; __VA_ARGS__; } \
     else return cudaErrorInvalidValue;   \
   } while (0)
 
@@ -380,15 +495,25 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
   // per column and block (grid capped at two blocks per SM)
   const int grid = a.partials ? a.partial_blocks : std::min(grid_for_rows(a.rows), num_sms() * 2);
   if (a.x_bf16) {
-    FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
-                               a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma, a.dres,
-                               a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C,
-                               a.partials, a.pre_add ? 1 : 0)));
+    FL_LN_DISPATCH_NV(a.C, {
+      auto k = ln_bwd_kernel<__nv_bfloat16, NV>;
+      constexpr int smem = LnBwdSlot<__nv_bfloat16, NV>::kBlockBytes;
+      cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(k), smem);
+      if (e != cudaSuccess) return e;
+      k<<<grid, kWarps * 32, smem, st>>>(a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma,
+                                          a.dres, a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum,
+                                          a.rows, a.C, a.partials, a.pre_add ? 1 : 0);
+    });
   } else {
-    FL_LN_DISPATCH_NV(a.C, (ln_bwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
-                               a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres, a.dx_f32,
-                               a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials,
-                               a.pre_add ? 1 : 0)));
+    FL_LN_DISPATCH_NV(a.C, {
+      auto k = ln_bwd_kernel<float, NV>;
+      constexpr int smem = LnBwdSlot<float, NV>::kBlockBytes;
+      cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(k), smem);
+      if (e != cudaSuccess) return e;
+      k<<<grid, kWarps * 32, smem, st>>>(a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres,
+                                          a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows,
+                                          a.C, a.partials, a.pre_add ? 1 : 0);
+    });
   }
   note_launch();
   if (a.partials) {
