@@ -21,7 +21,7 @@ import torch
 
 from ._common import C, bf16_shadow, grad_buffer, grad_ready, splitk_for
 from .attention import attn_bwd_packed, attn_fwd_packed
-from .transformer import _empty, _wgrad
+from .transformer import WgradLane, _empty, _wgrad
 
 
 class PostBlockParams:
@@ -71,11 +71,14 @@ def post_block_forward(x, x16, p: PostBlockParams, B, S, H, key_pad):
     return x2, x2_16, saved
 
 
-def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, key_pad):
+def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, key_pad,
+                        lane=None):
     """g2: f32 skip-path gradient of the block output, extra16: bf16 GEMM-path
     gradient of the block output (or None). Returns (g_in f32, g_in_extra bf16)
-    for the previous block."""
+    for the previous block. With ``lane`` the weight-gradient GEMMs run on its
+    stream."""
     K = C()
+    wg = lane.wgrad if lane is not None else _wgrad
     x16, qkv, attn, lse, y1, m1, r1, x1_16, a, pre, y2, m2, r2 = saved
     T, Cd = y1.shape
     dev = y1.device
@@ -91,12 +94,12 @@ def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, 
         K.ln_bwd(extra16, y2, m2, r2, ln2.weight.detach(), g2, dy2, dy2_16, grad_buffer(ln2.weight),
                  grad_buffer(ln2.bias), grad_buffer(p.b2), True)
     # FFN
-    _wgrad(dy2_16, a, p.w2)
+    wg(dy2_16, a, p.w2)
     da = _empty((T, F4), torch.bfloat16, dev)
     # da = (dy W2) * GELU'; the epilogue also adds column sums of da to fc1's bias gradient
     K.gemm(dy2_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU,
            colsum=grad_buffer(p.b1))
-    _wgrad(da, x1_16, p.w1)
+    wg(da, x1_16, p.w1)
     dx1 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(da, bf16_shadow(p.w1), dx1, T, Cd, F4, False, True)
     # LN1 backward of (dx1 + dy2) -> dy1, bo grad
@@ -105,12 +108,12 @@ def post_block_backward(g2, g2_16, extra16, p: PostBlockParams, saved, B, S, H, 
     K.ln_bwd(dx1, y1, m1, r1, p.ln1_w.detach(), dy2, dy1, dy1_16, grad_buffer(p.ln1_w),
              grad_buffer(p.ln1_b), grad_buffer(p.bo), True)
     # attention
-    _wgrad(dy1_16, attn, p.wo)
+    wg(dy1_16, attn, p.wo)
     dattn = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dy1_16, bf16_shadow(p.wo), dattn, T, Cd, Cd, False, True)
     dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, False, key_pad,
                            bias_grad=grad_buffer(p.bqkv))
-    _wgrad(dqkv, x16, p.wqkv)
+    wg(dqkv, x16, p.wqkv)
     dxq = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dqkv, bf16_shadow(p.wqkv), dxq, T, Cd, 3 * Cd, False, True)
     return dy1, dxq  # skip-path gradient (f32) and GEMM-path gradient (bf16) of the block input
@@ -220,13 +223,16 @@ class _BertMLMTrainFn(torch.autograd.Function):
         gskip = torch.zeros((T, Cd), dtype=torch.float32, device=dev)
         extra = gx16
         blocks = ctx.blocks
+        lane = WgradLane(dev)
         for li in range(len(blocks) - 1, -1, -1):
             p = blocks[li]
             gskip, extra = post_block_backward(gskip, None, extra, p, ctx.saved_blocks[li], B, S, H,
-                                               key_pad)
+                                               key_pad, lane=lane)
             ctx.saved_blocks[li] = None
-            for q in p.all():
-                grad_ready(q)
+            lane.ready(p.all())
+        # the word-embedding gradient below also receives the tied decoder's
+        # weight gradient (main stream): the lane is joined first
+        lane.join()
         # embedding LayerNorm (input grad = skip + GEMM path) and the three tables
         de = _empty((T, Cd), torch.float32, dev)
         K.ln_bwd(extra, e, me, re_, emb.LayerNorm.weight.detach(), gskip, de, None,

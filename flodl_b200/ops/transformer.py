@@ -36,6 +36,56 @@ from ._common import C, bf16_shadow, grad_buffer, grad_ready, splitk_for
 from .attention import attn_bwd_packed, attn_fwd_packed
 
 
+class WgradLane:
+    """Weight-gradient GEMMs on a second stream. They read activations and
+    output gradients that are already final and write only parameter
+    gradients, so they run beside the input-gradient chain (whose kernels
+    leave SMs idle in their last wave) instead of in series with it. Inputs
+    read on the lane are kept referenced until ``join`` (after which the main
+    stream is ordered behind the lane), so the caching allocator cannot hand
+    their memory to a later kernel while the lane still reads it. Used as is
+    inside CUDA-graph capture: the lane forks from and joins the capturing
+    stream."""
+
+    _streams = {}
+
+    def __init__(self, dev):
+        self.enabled = dev.type == "cuda"
+        self.keep = []
+        if self.enabled:
+            self.main = torch.cuda.current_stream(dev)
+            s = WgradLane._streams.get(dev.index)
+            if s is None:
+                s = WgradLane._streams[dev.index] = torch.cuda.Stream(dev)
+            self.side = s
+
+    def wgrad(self, dy16, x16, w, alpha_t=None):
+        if not self.enabled:
+            return _wgrad(dy16, x16, w, alpha_t)
+        self.side.wait_stream(self.main)
+        with torch.cuda.stream(self.side):
+            _wgrad(dy16, x16, w, alpha_t)
+        self.keep += [dy16, x16]
+
+    def ready(self, params):
+        """Gradient-ready listeners for ``params``: issued on the lane after it
+        has caught up with the main stream, so a listener that orders its
+        collective after the current stream sees every gradient complete."""
+        if not self.enabled:
+            for t in params:
+                grad_ready(t)
+            return
+        self.side.wait_stream(self.main)
+        with torch.cuda.stream(self.side):
+            for t in params:
+                grad_ready(t)
+
+    def join(self):
+        if self.enabled:
+            self.main.wait_stream(self.side)
+        self.keep = []
+
+
 def _wgrad(dy16, x16, w, alpha_t=None):
     """w.grad += dy16^T @ x16 (f32, split-K accumulate)."""
     T, N = dy16.shape
@@ -96,23 +146,25 @@ def block_forward(x, p: BlockParams, B, S, H, causal, key_pad=None):
 
 
 def block_backward(dx3, dx3_16, p: BlockParams, saved, B, S, H, causal, prev_bias_grad,
-                   key_pad=None):
+                   key_pad=None, lane=None):
     """Given the f32 gradient of the block output (and its bf16 copy), returns
     (dx f32, dx bf16). ``prev_bias_grad`` receives the column sum of dx (the
-    bias gradient of the previous block's fc2), or None."""
+    bias gradient of the previous block's fc2), or None. With ``lane`` the
+    weight-gradient GEMMs run on its stream."""
     K = C()
+    wg = lane.wgrad if lane is not None else _wgrad
     x, mean1, rstd1, h1, qkv, attn, lse, x2, mean2, rstd2, h2, pre, a = saved
     T, Cd = x.shape
     F4 = p.w1.shape[0]
     dev = x.device
     # fc2
-    _wgrad(dx3_16, a, p.w2)
+    wg(dx3_16, a, p.w2)
     da = _empty((T, F4), torch.bfloat16, dev)
     # da = (dy W2) * GELU'; the epilogue also adds column sums of da to fc1's bias gradient
     K.gemm(dx3_16, bf16_shadow(p.w2), da, T, F4, Cd, False, True, aux=pre, flags=K.EPI_DGELU,
            colsum=grad_buffer(p.b1))
     # fc1
-    _wgrad(da, h2, p.w1)
+    wg(da, h2, p.w1)
     dh2 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(da, bf16_shadow(p.w1), dh2, T, Cd, F4, False, True)
     # ln2 (+ skip path), bias grad of proj
@@ -121,12 +173,12 @@ def block_backward(dx3, dx3_16, p: BlockParams, saved, B, S, H, causal, prev_bia
     K.ln_bwd(dh2, x2, mean2, rstd2, p.ln2_w.detach(), dx3, dx2, dx2_16, grad_buffer(p.ln2_w),
              grad_buffer(p.ln2_b), grad_buffer(p.bo))
     # attention output projection
-    _wgrad(dx2_16, attn, p.wo)
+    wg(dx2_16, attn, p.wo)
     dattn = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dx2_16, bf16_shadow(p.wo), dattn, T, Cd, Cd, False, True)
     dqkv = attn_bwd_packed(dattn, qkv, attn, lse, B, S, H, causal, key_pad,
                            bias_grad=grad_buffer(p.bqkv))
-    _wgrad(dqkv, h1, p.wqkv)
+    wg(dqkv, h1, p.wqkv)
     dh1 = _empty((T, Cd), torch.bfloat16, dev)
     K.gemm(dqkv, bf16_shadow(p.wqkv), dh1, T, Cd, 3 * Cd, False, True)
     dx = _empty((T, Cd), torch.float32, dev)
@@ -186,7 +238,8 @@ class _LMTrainFn(torch.autograd.Function):
         g = g.detach().reshape(()).float().contiguous()
         # head
         head = model.head
-        _wgrad(dlogits, hf, head.weight, alpha_t=g)
+        lane = WgradLane(dev)
+        lane.wgrad(dlogits, hf, head.weight, alpha_t=g)
         K.colsum(dlogits, grad_buffer(head.bias), g)
         dhf = _empty((T, Cd), torch.bfloat16, dev)
         K.gemm(dlogits, bf16_shadow(head.weight), dhf, T, Cd, model.vocab_size, False, True,
@@ -197,16 +250,14 @@ class _LMTrainFn(torch.autograd.Function):
         last_b2 = grad_buffer(blocks[-1].b2) if blocks else None
         K.ln_bwd(dhf, xL, meanf, rstdf, model.ln_f.weight.detach(), None, dx, dx16,
                  grad_buffer(model.ln_f.weight), grad_buffer(model.ln_f.bias), last_b2)
-        for p in (head.weight, head.bias, model.ln_f.weight, model.ln_f.bias):
-            grad_ready(p)
+        lane.ready((head.weight, head.bias, model.ln_f.weight, model.ln_f.bias))
         for li in range(len(blocks) - 1, -1, -1):
             p = blocks[li]
             prev_b2 = grad_buffer(blocks[li - 1].b2) if li > 0 else None
             dx, dx16 = block_backward(dx, dx16, p, ctx.saved_blocks[li], B, S, H, model.causal,
-                                      prev_b2)
+                                      prev_b2, lane=lane)
             ctx.saved_blocks[li] = None
-            for t in p.all():
-                grad_ready(t)
+            lane.ready(p.all())
         # embeddings
         tokw = model.tok_emb.weight
         V = tokw.shape[0]
@@ -218,6 +269,7 @@ class _LMTrainFn(torch.autograd.Function):
         else:
             K.embed_bwd_atomic(ids_f, dx, grad_buffer(tokw))
         K.pos_grad(dx, grad_buffer(model.pos_emb), B, S)
+        lane.join()
         grad_ready(tokw)
         grad_ready(model.pos_emb)
         ctx.saved_blocks = None
