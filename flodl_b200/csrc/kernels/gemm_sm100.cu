@@ -26,6 +26,7 @@
 
 #include <cstdio>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -40,26 +41,32 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;     // producer + MMA + epilogue
 
 __device__ uint64_t g_wait_limit_ns = 2000000000ull;  // 2 s
 
-// Epilogue staging: each epilogue warp owns two 4 KB slots of shared memory.
-// A slot holds one 32x32 output chunk (f32, 128B swizzle) or one bf16 output
-// chunk plus one bf16 GELU' chunk (2 KB each, 64B swizzle). Chunks
-// leave through TMA stores (full, coalesced lines); epilogue inputs (residual,
-// GELU' operand) arrive through TMA loads into the slot of the chunk that
-// needs them while the previous chunk is being computed. Two slots let the
-// store of chunk j drain while chunk j+1 is staged.
+// Epilogue staging: each epilogue warp owns kSlots 4 KB slots of shared
+// memory. A slot holds one 32x32 output chunk (f32, 128B swizzle) or one bf16
+// output chunk plus one bf16 GELU' chunk (2 KB each, 64B swizzle). Chunks
+// leave through TMA stores (full, coalesced lines). Epilogues with an input
+// (residual, GELU' operand) take two slots: the input of chunk j+1 arrives by
+// TMA into the other slot while chunk j is computed. Epilogues without one
+// take a single slot (the store of chunk j-1 reads it while chunk j is
+// computed), which leaves shared memory for one more operand stage.
 constexpr int kSlotBytes = 4096;
-constexpr int kStageWarpBytes = 2 * kSlotBytes;
-constexpr int kStagingBytes = kEpiWarps * kStageWarpBytes;
 
-template <int BN>
+// kPair: a CTA pair computes a 256 x BN tile with one cta_group::2 MMA; each
+// CTA stages 128 rows of A and BN/2 rows of B per K step.
+template <int BN, int kSlots, bool kPair = false>
 struct GemmCfg {
-  static constexpr int kStages = (BN == 256) ? 3 : 5;
-  static constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
-  static constexpr int kBTileBytes = BN * kBK * 2;   // 32 KB or 16 KB
+  static constexpr int kStagingBytes = kEpiWarps * kSlots * kSlotBytes;
+  static constexpr int kATileBytes = kBM * kBK * 2;                      // 16 KB
+  static constexpr int kBTileBytes = (kPair ? BN / 2 : BN) * kBK * 2;  // 32 or 16 KB
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  // as many operand stages as fit beside the staging slots (at most 8)
+  static constexpr int kFit = (227 * 1024 - kStagingBytes - 1024 - 512) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 512 /*barriers*/;
+  static_assert(kStages <= 8, "barrier arrays");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
 
 struct SmemCtl {
@@ -262,7 +269,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
                                                    const CUtensorMap* tmOut,
                                                    const CUtensorMap* tmAux, uint8_t* slot,
                                                    int row0, int col0, int lane, int N,
-                                                   const uint32_t (&acc)[32]) {
+                                                   const uint32_t (&acc)[32], bool wait_slot) {
   float v[32];
   if (ep.bias && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0) {
     // v = acc * alpha + bias, two columns per packed FMA
@@ -289,10 +296,20 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
   const int sw64 = (lane >> 1) & 3;
   const int sw128 = lane & 7;
   const bool aux_out = (ep.flags & kEpiGelu) && ep.aux;
+  // single-slot staging: the previous chunk's store must have read the slot
+  // (it did so while this chunk's accumulator was read and its math ran)
+  auto slot_free = [&]() {
+    if (wait_slot) {
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+    }
+  };
   if (ep.flags & kEpiGelu) {
     float dg[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 2) gelu_and_grad2(v[i], v[i + 1], v[i], v[i + 1], dg[i], dg[i + 1]);
+    slot_free();
+    wait_slot = false;
     if (aux_out) {  // GELU', kept for the backward pass
       uint8_t* a = slot + 2048 + lane * 64;
 #pragma unroll
@@ -324,6 +341,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
     const float s = chunk_column_sum(v, lane);
     if (col0 + lane < N) atomicAdd(ep.colsum + col0 + lane, s);
   }
+  slot_free();
   if (ep.out_f32) {
     uint8_t* o = slot + lane * 128;
     if (ep.residual) {  // staged f32 residual at the output positions
@@ -364,7 +382,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int kSlots, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
@@ -372,19 +390,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmAux,
                       const __grid_constant__ CUtensorMap tmIn, GemmEpilogue ep, int M, int N,
                       int K, int k_splits, int use_tma_store, int in_kind, uint32_t* err) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, kSlots, kPair>;
   constexpr int S = Cfg::kStages;
+  // Work units: single CTAs over 128 x BN tiles, or CTA pairs over 256 x BN
+  // tiles (this CTA's rows start at crank * 128 within the tile).
+  constexpr int kTM = kPair ? 2 * kBM : kBM;
+  const uint32_t crank = kPair ? cluster_ctarank() : 0u;
+  const int unit = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128B-swizzled tiles need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + S * Cfg::kStageBytes;
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(staging + kStagingBytes);
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(staging + Cfg::kStagingBytes);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_m = (M + kTM - 1) / kTM;
   const int tiles_n = (N + BN - 1) / BN;
   const int k_blocks_total = (K + kBK - 1) / kBK;
   const int kb_per_split = (k_blocks_total + k_splits - 1) / k_splits;
@@ -398,7 +422,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->tmem_full[a], 1);
-      mbar_init(&ctl->tmem_empty[a], kEpiWarps);
+      // pair: the even CTA's barrier collects the epilogue warps of both CTAs
+      mbar_init(&ctl->tmem_empty[a], kPair ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(&ctl->drain, 1);
     for (int i = 0; i < kEpiWarps * 2; ++i) mbar_init(&ctl->epi_in[i], 1);
@@ -415,11 +440,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc<Cfg::kTmemCols>(&ctl->tmem_base);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair<Cfg::kTmemCols>(&ctl->tmem_base);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc<Cfg::kTmemCols>(&ctl->tmem_base);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // pair: both CTAs' barriers are initialised before either signals the other
+  if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile uint32_t* abort_flag = &ctl->abort;
@@ -436,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one_sync()) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < num_tiles && ok; t += units) {
         int tm, tn, ks;
         tile_coords(t, tm, tn, ks);
         const int kb0 = ks * kb_per_split;
@@ -450,8 +482,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* a_dst = smem + s * Cfg::kStageBytes;
           uint8_t* b_dst = a_dst + Cfg::kATileBytes;
-          mbar_arrive_expect_tx(&ctl->full[s], Cfg::kStageBytes);
           const int k0 = kb * kBK;
+          if constexpr (kPair) {
+            // both CTAs' bytes complete on the even CTA's barrier; only the
+            // even CTA arrives (with the pair's byte count)
+            if (crank == 0) mbar_arrive_expect_tx(&ctl->full[s], 2 * Cfg::kStageBytes);
+            const int m0 = tm * kTM + (int)crank * kBM;
+            const int n0 = tn * BN + (int)crank * (BN / 2);
+            if (A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, &ctl->full[s], m0, k0);
+              tma_load_2d_pair(a_dst + 64 * 128, &tmA, &ctl->full[s], m0 + 64, k0);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, &ctl->full[s], k0, m0);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 128; ++c)
+                tma_load_2d_pair(b_dst + c * 64 * 128, &tmB, &ctl->full[s], n0 + c * 64, k0);
+            } else {
+              tma_load_2d_pair(b_dst, &tmB, &ctl->full[s], k0, n0);
+            }
+            continue;
+          }
+          mbar_arrive_expect_tx(&ctl->full[s], Cfg::kStageBytes);
           if (A_MN) {
             tma_load_2d(a_dst, &tmA, &ctl->full[s], tm * kBM, k0);
             tma_load_2d(a_dst + 64 * 128, &tmA, &ctl->full[s], tm * kBM + 64, k0);
@@ -480,13 +533,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();  // reconverge the warp before the CTA-wide barrier below
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one_sync()) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    // pair: the even CTA issues the pair's MMAs; the odd CTA's MMA warp idles
+    if ((!kPair || crank == 0) && elect_one_sync()) {
+      constexpr uint32_t idesc = make_idesc_bf16(kTM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
       uint32_t it = 0;
       uint32_t local_tile = 0;
       bool ok = true;
       bool issued = false;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local_tile) {
+      for (int t = unit; t < num_tiles && ok; t += units, ++local_tile) {
         int tm, tn, ks;
         tile_coords(t, tm, tn, ks);
         const int kb0 = ks * kb_per_split;
@@ -520,16 +574,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               bdesc = make_sdesc_sw128(b_addr + j * 2048, 64 * 128, 1024);
             else
               bdesc = make_sdesc_sw128(b_addr + j * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            if constexpr (kPair)
+              umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            else
+              umma_bf16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
             issued = true;
           }
-          umma_commit(&ctl->empty[s]);  // smem stage free once these MMAs finish
+          // smem stage free once these MMAs finish (pair: in both CTAs)
+          if constexpr (kPair)
+            umma_commit_pair(&ctl->empty[s], 0x3);
+          else
+            umma_commit(&ctl->empty[s]);
         }
         if (!ok) break;
-        umma_commit(&ctl->tmem_full[acc]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (pair: both CTAs' halves)
+        if constexpr (kPair)
+          umma_commit_pair(&ctl->tmem_full[acc], 0x3);
+        else
+          umma_commit(&ctl->tmem_full[acc]);
       }
       if (!ok && issued) {
-        umma_commit(&ctl->drain);
+        if constexpr (kPair)
+          umma_commit_pair(&ctl->drain, 0x1);
+        else
+          umma_commit(&ctl->drain);
         uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&ctl->drain, 0)) {
           if (global_timer_ns() - t0 > 100000000ull) break;
@@ -543,18 +611,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;              // epilogue warp 0..7
     const int half = ew / 4;              // which half of the tile's columns
     constexpr int kChunks = BN / 32 / 2;  // 32-column chunks per warp and tile
-    uint8_t* stage = staging + ew * kStageWarpBytes;
+    uint8_t* stage = staging + ew * kSlots * kSlotBytes;
     uint64_t* in_bar = &ctl->epi_in[ew * 2];
     const float alpha = ep.alpha_ptr ? ep.alpha * __ldg(ep.alpha_ptr) : ep.alpha;
     const bool tma_in = use_tma_store && in_kind != kInNone;
-    const int my_tiles =
-        (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int my_tiles = unit < num_tiles ? (num_tiles - 1 - unit) / units + 1 : 0;
     const int total = my_tiles * kChunks;
-    // chunk j of this warp: tile blockIdx.x + (j / kChunks) * gridDim.x, column chunk j % kChunks
+    // chunk j of this warp: tile unit + (j / kChunks) * units, column chunk j % kChunks
     auto chunk_at = [&](int j, int& row0, int& col0) -> bool {
       int tm, tn, ks;
-      tile_coords((int)blockIdx.x + (j / kChunks) * (int)gridDim.x, tm, tn, ks);
-      row0 = tm * kBM + q * 32;
+      tile_coords(unit + (j / kChunks) * units, tm, tn, ks);
+      row0 = tm * kTM + (int)crank * kBM + q * 32;
       col0 = tn * BN + (half * kChunks + j % kChunks) * 32;
       return col0 < N && row0 < M && ks * kb_per_split < k_blocks_total;
     };
@@ -601,10 +668,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                      r);
       tmem_ld_wait();
       if (cc == kChunks - 1) {
-        // Last read of this accumulator by this warp: hand it back early.
+        // Last read of this accumulator by this warp: hand it back early
+        // (pair: to the even CTA, whose MMA warp reuses both halves).
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->tmem_empty[acc]);
+        if (lane == 0) {
+          if constexpr (kPair)
+            mbar_arrive_cluster(&ctl->tmem_empty[acc], 0);
+          else
+            mbar_arrive(&ctl->tmem_empty[acc]);
+        }
       }
       if (use_tma_store) {
         // Slot j&1 was last read by the store of chunk j-2. With epilogue
@@ -612,19 +685,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         // receive chunk j+1's input, so every store must have read its slot.
         // Without inputs only chunk j-2's store must have: chunk j-1's store
         // (the newest group) may still be reading while chunk j is computed.
-        if (lane == 0) {
-          if (tma_in || !prev_stored)
-            bulk_wait_group_read<0>();
-          else
-            bulk_wait_group_read<1>();
+        if (kSlots == 2) {
+          if (lane == 0) {
+            if (tma_in || !prev_stored)
+              bulk_wait_group_read<0>();
+            else
+              bulk_wait_group_read<1>();
+          }
+          __syncwarp();
         }
-        __syncwarp();
         if (tma_in && j + 1 < total && issue_in(j + 1)) pending |= 1u << ((j + 1) & 1);
       }
       prev_stored = live && use_tma_store;
       if (!live) continue;
       if (use_tma_store) {
-        uint8_t* slot = stage + (j & 1) * kSlotBytes;
+        uint8_t* slot = stage + (kSlots == 2 ? (j & 1) : 0) * kSlotBytes;
         if (tma_in) {
           const uint32_t sb = (uint32_t)(j & 1);
           const bool ok = mbar_wait_bounded(&in_bar[sb], (in_ph >> sb) & 1u, abort_flag, err, limit);
@@ -635,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
         }
-        epilogue_chunk_tma(ep, alpha, &tmOut, &tmAux, slot, row0, col0, lane, N, r);
+        epilogue_chunk_tma(ep, alpha, &tmOut, &tmAux, slot, row0, col0, lane, N, r, kSlots == 1);
       } else {
         epilogue_chunk(ep, row0 + lane, col0, M, N, r);
       }
@@ -656,9 +731,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // pair: neither CTA leaves (freeing the shared memory and TMEM the other's
+  // MMAs and barriers address) before both are done
+  if constexpr (kPair) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
+    if constexpr (kPair)
+      tmem_dealloc_pair<Cfg::kTmemCols>(tmem_base);
+    else
+      tmem_dealloc<Cfg::kTmemCols>(tmem_base);
   }
 }
 
@@ -791,9 +872,60 @@ static bool make_out_tmap(CUtensorMap* map, void* base, bool f32, uint64_t cols,
 static thread_local const char* g_gemm_fail = nullptr;
 const char* gemm_failure_detail() { return g_gemm_fail ? g_gemm_fail : ""; }
 
-template <int BN, bool A_MN, bool B_MN>
+// One dynamic shared-memory opt-in per kernel instance and device (the
+// template parameters key the static: every instance has the same type).
+template <int BN, bool A_MN, bool B_MN, int kSlots, bool kPair>
+static cudaError_t smem_opt_in() {
+  auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN, kSlots, kPair>;
+  const int bytes = GemmCfg<BN, kSlots, kPair>::kSmemBytes;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
+}
+
+// Launch one kernel instance: plain grid, or (pair) a grid of (2,1,1) clusters.
+template <int BN, bool A_MN, bool B_MN, int kSlots, bool kPair>
+static cudaError_t launch_instance(const GemmArgs& g, cudaStream_t stream, const CUtensorMap& tmA,
+                                   const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                                   const CUtensorMap& tmAux, const CUtensorMap& tmIn, int use_tma,
+                                   int in_kind, uint32_t* err) {
+  auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN, kSlots, kPair>;
+  constexpr int smem = GemmCfg<BN, kSlots, kPair>::kSmemBytes;
+  cudaError_t e = smem_opt_in<BN, A_MN, B_MN, kSlots, kPair>();
+  if (e != cudaSuccess) return e;
+  constexpr int tm = kPair ? 2 * kBM : kBM;
+  const int tiles = ((g.M + tm - 1) / tm) * ((g.N + BN - 1) / BN) * g.k_splits;
+  if constexpr (kPair) {
+    const int pairs = std::min(tiles, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N, g.K,
+                              g.k_splits, use_tma, in_kind, err);
+  } else {
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N, g.K,
+                                           g.k_splits, use_tma, in_kind, err);
+    return cudaSuccess;
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool kPair = false>
 static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
   CUtensorMap tmA, tmB;
   // A tile: 128 (M) x 64 (K)
   bool ok;
@@ -808,7 +940,7 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   if (B_MN)
     ok = make_tmap_bf16_2d(&tmB, g.B, g.N, g.K, g.ldb, 64, kBK);
   else
-    ok = make_tmap_bf16_2d(&tmB, g.B, g.K, g.N, g.ldb, kBK, BN);
+    ok = make_tmap_bf16_2d(&tmB, g.B, g.K, g.N, g.ldb, kBK, kPair ? BN / 2 : BN);
   if (!ok) {
     g_gemm_fail = tmap_failure_detail();
     return cudaErrorInvalidValue;
@@ -848,25 +980,26 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     g_gemm_fail = "fused column sums need the TMA-store epilogue (aligned output/aux)";
     return cudaErrorInvalidValue;
   }
-  auto kern = gemm_bf16_tcgen05<BN, A_MN, B_MN>;
-  // the dynamic shared-memory opt-in is a per-device function attribute
-  static std::atomic<uint64_t> attr_done{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_done.load(std::memory_order_relaxed) & bit)) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_done.fetch_or(bit);
-  }
-  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.k_splits;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N,
-                                                     g.K, g.k_splits, use_tma ? 1 : 0, in_kind,
-                                                     g.err ? g.err : default_err_word());
+  uint32_t* err = g.err ? g.err : default_err_word();
+  // single staging slot (one more operand stage) when the epilogue has no input
+  cudaError_t e =
+      in_kind == kInNone
+          ? launch_instance<BN, A_MN, B_MN, 1, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
+                                                      use_tma ? 1 : 0, in_kind, err)
+          : launch_instance<BN, A_MN, B_MN, 2, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
+                                                      use_tma ? 1 : 0, in_kind, err);
+  if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
+}
+
+// FLODL_GEMM_PAIR=0 turns the CTA-pair tiles off (read once per process).
+static bool pair_tiles_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLODL_GEMM_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
@@ -876,10 +1009,19 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   }
   const bool wide = g.N >= 256 && g.bn != 128;
+  // CTA pairs (256-row tiles, half the operand bytes per CTA and K step) for
+  // wide problems with enough rows and a long reduction per tile: with
+  // K >= 1024 the main loop is bound by operand bytes per SM, which the pair
+  // halves; shorter loops (K = 512) measured faster on single-CTA tiles,
+  // where fill latency and the epilogue dominate. bn = 128 / 256 force the
+  // single-CTA tiles.
+  const bool pair = wide && g.bn == 0 && g.M >= 512 && g.K / g.k_splits >= 1024 &&
+                    pair_tiles_enabled();
 #define FL_GEMM_CASE(AMN, BMN)                                                   \
   if (g.a_mn == AMN && g.b_mn == BMN)                                           \
-    return wide ? launch_gemm_t<256, AMN, BMN>(g, stream)                      \
-                : launch_gemm_t<128, AMN, BMN>(g, stream);
+    return pair ? launch_gemm_t<256, AMN, BMN, true>(g, stream)                \
+                : wide ? launch_gemm_t<256, AMN, BMN>(g, stream)               \
+                       : launch_gemm_t<128, AMN, BMN>(g, stream);
   FL_GEMM_CASE(false, false)
   FL_GEMM_CASE(false, true)
   FL_GEMM_CASE(true, false)

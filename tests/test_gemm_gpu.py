@@ -107,3 +107,38 @@ def test_gemm_fused_column_sums(M, N, K, b_mn):
     out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     C.gemm(A, Bm, out2, M, N, K, False, b_mn, colsum=cs2)
     torch.testing.assert_close(cs2, ref.sum(0), rtol=1e-3, atol=1e-2 * (M ** 0.5))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (1000, 768, 2048), (2048, 1536, 1536)])
+def test_cta_pair_tiles_match_fp32(M, N, K):
+    """Long reductions (K >= 1024, M >= 512) run on CTA-pair tiles (one
+    cta_group::2 MMA per 256-row tile): every operand layout and epilogue
+    against a plain fp32 reference."""
+    from flodl_b200._ext import cuda_ext
+    C = cuda_ext()
+    torch.manual_seed(1)
+    bf = lambda *s: (torch.randn(*s, device="cuda") * 0.5).bfloat16()
+    A, B, Bt, At = bf(M, K), bf(N, K), bf(K, N), bf(K, M)
+    bias = torch.randn(N, device="cuda")
+
+    def close(got, ref, tol=2e-2):
+        err = (got.float() - ref).abs().max().item() / ref.abs().max().item()
+        assert err < tol, err
+
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, M, N, K, False, False, bias=bias)
+    close(out, A.float() @ B.float().T + bias)
+    C.gemm(A, Bt, out, M, N, K, False, True)
+    close(out, A.float() @ Bt.float())
+    res = torch.randn(M, N, device="cuda")
+    o32 = torch.empty(M, N, device="cuda")
+    C.gemm(A, B, o32, M, N, K, False, False, bias=bias, residual=res)
+    close(o32, A.float() @ B.float().T + bias + res, 1e-3)
+    aux = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, M, N, K, False, False, bias=bias, aux=aux, flags=C.EPI_GELU)
+    close(out, torch.nn.functional.gelu(A.float() @ B.float().T + bias))
+    g = torch.zeros(M, N, device="cuda")
+    C.gemm(At, Bt, g, M, N, K, True, True, flags=C.EPI_ACCUMULATE)
+    close(g, At.float().T @ Bt.float(), 1e-3)
+    assert C.kernel_error() == 0
