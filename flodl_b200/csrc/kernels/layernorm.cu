@@ -16,6 +16,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -112,23 +113,15 @@ struct LnBwdSlot {
 // NV = number of 128-element column groups (C <= NV*128); lane owns columns
 // lane*4 + 128*j .. +3 for j < NV.
 template <typename TIn, int NV>
-__global__ void __launch_bounds__(kWarps * 32) ln_fwd_kernel(
+__global__ void __launch_bounds__(kWarps * 32, NV <= 4 ? 4 : 1) ln_fwd_kernel(
     const TIn* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
     __nv_bfloat16* __restrict__ y_bf16, float* __restrict__ y_f32, float* __restrict__ mean_out,
     float* __restrict__ rstd_out, int rows, int C, float eps) {
   const int lane = threadIdx.x & 31;
   const int warp_global = blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * kWarps;
-  float g[NV][4], b[NV][4];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = lane * 4 + 128 * j;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      g[j][e] = (c + e < C) ? (gamma ? gamma[c + e] : 1.f) : 0.f;
-      b[j][e] = (c + e < C) ? (beta ? beta[c + e] : 0.f) : 0.f;
-    }
-  }
+  // gamma/beta are read per row through the read-only cache (L1-resident):
+  // holding them in registers cost a quarter of the resident warps.
   for (int r = warp_global; r < rows; r += nwarps) {
     const TIn* xr = x + (size_t)r * C;
     float v[NV][4];
@@ -165,9 +158,14 @@ __global__ void __launch_bounds__(kWarps * 32) ln_fwd_kernel(
     for (int j = 0; j < NV; ++j) {
       const int c = lane * 4 + 128 * j;
       if (c < C) {
+        const float4 g4 = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
+                                : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 b4 = beta ? __ldg(reinterpret_cast<const float4*>(beta + c))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
         float o[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = (v[j][e] - mean) * rstd * g[j][e] + b[j][e];
+        for (int e = 0; e < 4; ++e) o[e] = (v[j][e] - mean) * rstd * gv[e] + bv[e];
         if (y_bf16) store4_bf16(y_bf16 + (size_t)r * C + c, o);
         if (y_f32) store4_f32(y_f32 + (size_t)r * C + c, o);
       }
@@ -473,17 +471,43 @@ static cudaError_t opt_in_smem(const void* fn, int bytes) {
     else return cudaErrorInvalidValue;   \
   } while (0)
 
+// One wave of resident blocks: the grid is capped at what the SMs hold at
+// once (occupancy of this kernel instance, cached per device), and each warp
+// strides over its rows. A grid of 1.6 waves left the second wave's SMs
+// partly idle.
+template <typename Kern>
+static int resident_grid(Kern kern, int rows, std::atomic<int>& cache) {
+  int per_sm = cache.load(std::memory_order_relaxed);
+  if (per_sm <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, 0) !=
+            cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 2;
+    cache.store(per_sm, std::memory_order_relaxed);
+  }
+  const int blocks = (rows + kWarps - 1) / kWarps;
+  const int cap = num_sms() * per_sm;
+  return blocks < cap ? blocks : cap;
+}
+
 cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st) {
   if (a.C % 4 != 0) return cudaErrorInvalidValue;
-  const int grid = grid_for_rows(a.rows);
   if (a.x_bf16) {
-    FL_LN_DISPATCH_NV(a.C, (ln_fwd_kernel<__nv_bfloat16, NV><<<grid, kWarps * 32, 0, st>>>(
-                               (const __nv_bfloat16*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32,
-                               a.mean, a.rstd, a.rows, a.C, a.eps)));
+    FL_LN_DISPATCH_NV(a.C, {
+      auto k = ln_fwd_kernel<__nv_bfloat16, NV>;
+      static std::atomic<int> occ{0};
+      k<<<resident_grid(k, a.rows, occ), kWarps * 32, 0, st>>>(
+          (const __nv_bfloat16*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean, a.rstd, a.rows,
+          a.C, a.eps);
+    });
   } else {
-    FL_LN_DISPATCH_NV(a.C, (ln_fwd_kernel<float, NV><<<grid, kWarps * 32, 0, st>>>(
-                               (const float*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean,
-                               a.rstd, a.rows, a.C, a.eps)));
+    FL_LN_DISPATCH_NV(a.C, {
+      auto k = ln_fwd_kernel<float, NV>;
+      static std::atomic<int> occ{0};
+      k<<<resident_grid(k, a.rows, occ), kWarps * 32, 0, st>>>(
+          (const float*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean, a.rstd, a.rows, a.C,
+          a.eps);
+    });
   }
   note_launch();
   return cudaGetLastError();

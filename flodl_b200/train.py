@@ -91,3 +91,45 @@ class StepRunner:
         else:
             loss = self.step_fn()
         return float(loss.item())
+
+    def step_pipelined(self, *host_inputs: torch.Tensor) -> Optional[float]:
+        """One step whose loss is read back one step late: the inputs are
+        copied in (pinned host memory -> device, asynchronous), the step is
+        launched, its loss is copied into a pinned host slot behind an event,
+        and the PREVIOUS step's loss is returned (None on the first call) once
+        its event completed. The host never waits for the step it just
+        launched, so the next step's copies and launch overlap this step's
+        execution; every step's loss still reaches the host. ``flush()``
+        returns the last one."""
+        if len(host_inputs) != len(self.inputs):
+            raise ValueError(f"expected {len(self.inputs)} inputs, got {len(host_inputs)}")
+        if not hasattr(self, "_loss_host"):
+            self._loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+            self._loss_ev = [torch.cuda.Event(), torch.cuda.Event()]
+            self._slot = 0
+            self._pending = False
+        for dst, src in zip(self.inputs, host_inputs):
+            dst.copy_(src, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            loss = self.graph_loss
+        else:
+            loss = self.step_fn()
+        prev = self._slot
+        self._slot ^= 1
+        self._loss_host[self._slot].copy_(loss.detach().reshape(()).float(), non_blocking=True)
+        self._loss_ev[self._slot].record()
+        out = None
+        if self._pending:
+            self._loss_ev[prev].synchronize()
+            out = float(self._loss_host[prev])
+        self._pending = True
+        return out
+
+    def flush(self) -> Optional[float]:
+        """Loss of the last ``step_pipelined`` call (waits for it)."""
+        if not getattr(self, "_pending", False):
+            return None
+        self._loss_ev[self._slot].synchronize()
+        self._pending = False
+        return float(self._loss_host[self._slot])

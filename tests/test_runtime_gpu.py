@@ -100,3 +100,32 @@ def test_captured_training_step_with_loop():
     cap = [r.replay(x, y).item() for _ in range(6)]
     torch.testing.assert_close(torch.tensor(cap), torch.tensor(eager[3:]), rtol=2e-2, atol=2e-3)
     assert cap[-1] < cap[0]
+
+
+def test_step_pipelined_reads_every_loss_one_step_late():
+    """step_pipelined returns the previous step's loss; with flush() the
+    sequence equals what step() reads synchronously."""
+    from flodl_b200.graph import FlowBuilder
+    from flodl_b200.nn import GELU, Linear
+    from flodl_b200.optim import Adam
+    from flodl_b200.train import StepRunner
+
+    def make():
+        torch.manual_seed(0)
+        g = FlowBuilder.from_(Linear(64, 128, device="cuda")).through(GELU()).through(
+            Linear(128, 64, device="cuda")).build()
+        return g, Adam(g.parameters(), lr=1e-3)
+
+    x = torch.randn(256, 64).pin_memory()
+    y = torch.randn(256, 64).pin_memory()
+    lf = lambda out, t: torch.nn.functional.mse_loss(out.float(), t)
+    g1, o1 = make()
+    r1 = StepRunner.capture_training(g1, o1, lf, [x.cuda(), y.cuda()])
+    sync = [r1.step(x, y) for _ in range(6)]
+    g2, o2 = make()
+    r2 = StepRunner.capture_training(g2, o2, lf, [x.cuda(), y.cuda()])
+    got = [r2.step_pipelined(x, y) for _ in range(6)]
+    assert got[0] is None
+    piped = got[1:] + [r2.flush()]
+    assert r2.flush() is None
+    torch.testing.assert_close(torch.tensor(piped), torch.tensor(sync), rtol=1e-5, atol=1e-6)
