@@ -512,14 +512,14 @@ constexpr int kBwdWarps = 8;
 constexpr int kBwdThreads = 64 + 32 * kBwdWarps;
 
 struct BwdSmem {
-  uint8_t k[kTileBytes];
-  uint8_t v[kTileBytes];
+  uint8_t k[2][kTileBytes];  // K/V of two work items: the next item's tile
+  uint8_t v[2][kTileBytes];  // loads while this item runs
   uint8_t q[2][kTileBytes];
   uint8_t dout[2][kTileBytes];
   uint8_t p[2 * kTileBytes];   // P^T: 128 keys x 128 queries (two 64-query SW128 blocks)
   uint8_t ds[2 * kTileBytes];  // dS^T, same layout
   float stat[kBwdWarps][2][64];  // per compute warp: lse2 and delta of its 64 queries
-  uint64_t kv_full, kv_empty;
+  uint64_t kv_full[2], kv_empty[2];
   uint64_t qdo_full[2], qdo_empty[2];
   uint64_t s_full, s_free, p_ready, pds_free, dq_full, dq_free, dkv_full, dkv_free;
   uint64_t drain;
@@ -659,8 +659,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   auto first_q = [&](int kt) { return causal ? kt : 0; };
 
   if (threadIdx.x == 0) {
-    mbar_init(&sm.kv_full, 1);
-    mbar_init(&sm.kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qdo_full[i], 1);
       mbar_init(&sm.qdo_empty[i], 1);
@@ -699,10 +701,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int kt, h, b;
         bwd_decode(item, H * B, H, kt, h, b);
-        if (!(ok = mbar_wait_bounded(&sm.kv_empty, (n & 1) ^ 1, abort_flag, err, limit))) break;
-        mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
-        tma_load_3d(sm.k, &tm_qkv, &sm.kv_full, C + h * kD, kt * kTile, b);
-        tma_load_3d(sm.v, &tm_qkv, &sm.kv_full, 2 * C + h * kD, kt * kTile, b);
+        const int kb = n & 1;
+        if (!(ok = mbar_wait_bounded(&sm.kv_empty[kb], ((n >> 1) & 1) ^ 1, abort_flag, err,
+                                     limit)))
+          break;
+        mbar_arrive_expect_tx(&sm.kv_full[kb], 2 * kTileBytes);
+        tma_load_3d(sm.k[kb], &tm_qkv, &sm.kv_full[kb], C + h * kD, kt * kTile, b);
+        tma_load_3d(sm.v[kb], &tm_qkv, &sm.kv_full[kb], 2 * C + h * kD, kt * kTile, b);
         for (int i = first_q(kt); i < n_t; ++i, ++qdo_it) {
           const int st = qdo_it & 1;
           if (!(ok = mbar_wait_bounded(&sm.qdo_empty[st], ((qdo_it >> 1) & 1) ^ 1, abort_flag, err,
@@ -721,7 +726,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idesc_kq = make_idesc_bf16(128, 128, 0, 0);  // M=keys, N=queries
       constexpr uint32_t idesc_kd = make_idesc_bf16(128, kD, 0, 1);   // M=keys, N=D, B MN-major
       constexpr uint32_t idesc_qd = make_idesc_bf16(128, kD, 1, 1);   // M=queries, N=D, A,B MN-major
-      const uint32_t k_addr = smem_u32(sm.k), v_addr = smem_u32(sm.v);
       const uint32_t p_addr = smem_u32(sm.p), ds_addr = smem_u32(sm.ds);
       uint32_t qdo_it = 0, t = 0;
       bool ok = true, issued = false;
@@ -729,7 +733,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
         int kt, h, b;
         bwd_decode(item, H * B, H, kt, h, b);
-        if (!(ok = mbar_wait_bounded(&sm.kv_full, n & 1, abort_flag, err, limit))) break;
+        const int kb = n & 1;
+        const uint32_t k_addr = smem_u32(sm.k[kb]), v_addr = smem_u32(sm.v[kb]);
+        if (!(ok = mbar_wait_bounded(&sm.kv_full[kb], (n >> 1) & 1, abort_flag, err, limit))) break;
         if (!(ok = mbar_wait_bounded(&sm.dkv_free, (n & 1) ^ 1, abort_flag, err, limit))) break;
         int it = 0;
         for (int i = first_q(kt); i < n_t; ++i, ++it, ++qdo_it, ++t) {
@@ -772,7 +778,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_commit(&sm.qdo_empty[st]);
         }
         if (!ok) break;
-        umma_commit(&sm.kv_empty);
+        umma_commit(&sm.kv_empty[n & 1]);
         umma_commit(&sm.dkv_full);
       }
       if (!ok && issued) {
