@@ -116,7 +116,7 @@ class ClockSampler:
 def reference_arm(args):
     ref = os.path.join(ROOT, "baseline", "_ref")
     msg = ("reference fab2s/floDl is a Rust/cargo workspace (no setup.py/pyproject); "
-           "pip install of /root/reference fails and this image has no Rust toolchain")
+           "pip install of the reference source tree fails and this image has no Rust toolchain")
     if not os.path.isdir(ref) or not os.listdir(ref):
         print(json.dumps({"impl": "reference", "unavailable": msg}))
         return 0
