@@ -497,7 +497,9 @@ __device__ __forceinline__ void gelu_and_grad2(float x0, float x1, float& g0, fl
   const uint64_t nhalf = f2_pack(x0 >= 0.f ? -0.5f : 0.5f, x1 >= 0.f ? -0.5f : 0.5f);
   const uint64_t cdf = f2_fma(nhalf, f2_pack(r0, r1), base);
   f2_unpack(f2_mul(x, cdf), g0, g1);
-  // exp(-x^2/2) = 2^(-x^2 log2(e) / 2)
+  // exp(-x^2/2) = 2^(-x^2 log2(e) / 2): the identity folded into one packed
+  // multiply, then the hardware base-2 exponential (the same base-2 form the
+  // attention softmax uses)
   const uint64_t arg = f2_mul(f2_mul(x, x), f2_splat(-0.72134752044448170f));
   float a0, a1, e0, e1;
   f2_unpack(arg, a0, a1);
