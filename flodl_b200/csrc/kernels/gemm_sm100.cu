@@ -62,7 +62,9 @@ struct GemmCfg {
   // as many operand stages as fit beside the staging slots (at most 8)
   static constexpr int kFit = (227 * 1024 - kStagingBytes - 1024 - 512) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  // double-buffered accumulator, allocated as a power of two (BN = 192: 512)
+  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+  static_assert(BN % 64 == 0 && BN <= 256, "tile width");
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 512 /*barriers*/;
   static_assert(kStages <= 8, "barrier arrays");
@@ -1009,6 +1011,15 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   }
   const bool wide = g.N >= 256 && g.bn != 128;
+  // 192-column tiles when they leave fewer idle SM-slots in the last wave:
+  // estimated time ~ waves(tiles) * tile width (e.g. N = 1536 at M = 16384:
+  // 6 waves of 256 vs 7 waves of 192, 7/8 of the time)
+  bool w192 = false;
+  if (wide && g.bn == 0 && g.k_splits == 1) {
+    const int tm = (g.M + kBM - 1) / kBM, sms = num_sms();
+    const long t256 = (long)tm * ((g.N + 255) / 256), t192 = (long)tm * ((g.N + 191) / 192);
+    w192 = ((t192 + sms - 1) / sms) * 192 < ((t256 + sms - 1) / sms) * 256;
+  }
   // CTA pairs (256-row tiles, half the operand bytes per CTA and K step) for
   // wide problems with enough rows and a long reduction per tile: with
   // K >= 1024 the main loop is bound by operand bytes per SM, which the pair
@@ -1020,8 +1031,9 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
 #define FL_GEMM_CASE(AMN, BMN)                                                   \
   if (g.a_mn == AMN && g.b_mn == BMN)                                           \
     return pair ? launch_gemm_t<256, AMN, BMN, true>(g, stream)                \
-                : wide ? launch_gemm_t<256, AMN, BMN>(g, stream)               \
-                       : launch_gemm_t<128, AMN, BMN>(g, stream);
+                : w192 ? launch_gemm_t<192, AMN, BMN>(g, stream)               \
+                       : wide ? launch_gemm_t<256, AMN, BMN>(g, stream)        \
+                              : launch_gemm_t<128, AMN, BMN>(g, stream);
   FL_GEMM_CASE(false, false)
   FL_GEMM_CASE(false, true)
   FL_GEMM_CASE(true, false)

@@ -142,3 +142,36 @@ def test_cta_pair_tiles_match_fp32(M, N, K):
     C.gemm(At, Bt, g, M, N, K, True, True, flags=C.EPI_ACCUMULATE)
     close(g, At.float().T @ Bt.float(), 1e-3)
     assert C.kernel_error() == 0
+
+
+@pytest.mark.gpu
+def test_192_column_tiles_match_fp32():
+    """M = 4096, N = 1536 takes 192-column tiles (2 waves of 256 tiles of
+    192 columns beat 2 waves of 192 tiles of 256 on 148 SMs): forward with
+    bias, GELU, f32 residual, DGELU and an MN-major B against fp32."""
+    from flodl_b200._ext import cuda_ext
+    C = cuda_ext()
+    torch.manual_seed(2)
+    M, N, K = 4096, 1536, 512
+    bf = lambda *s: (torch.randn(*s, device="cuda") * 0.5).bfloat16()
+    A, B, Bt = bf(M, K), bf(N, K), bf(K, N)
+    bias = torch.randn(N, device="cuda")
+
+    def close(got, ref, tol=2e-2):
+        err = (got.float() - ref).abs().max().item() / ref.abs().max().item()
+        assert err < tol, err
+
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, M, N, K, False, False, bias=bias)
+    close(out, A.float() @ B.float().T + bias)
+    aux = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, M, N, K, False, False, bias=bias, aux=aux, flags=C.EPI_GELU)
+    close(out, torch.nn.functional.gelu(A.float() @ B.float().T + bias))
+    res = torch.randn(M, N, device="cuda")
+    o32 = torch.empty(M, N, device="cuda")
+    C.gemm(A, B, o32, M, N, K, False, False, residual=res)
+    close(o32, A.float() @ B.float().T + res, 1e-3)
+    g = bf(M, N)
+    C.gemm(A, Bt, out, M, N, K, False, True, aux=g, flags=C.EPI_DGELU)
+    close(out, (A.float() @ Bt.float()) * g.float())
+    assert C.kernel_error() == 0
