@@ -569,17 +569,17 @@ __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
   }
 }
 
-// dqkv[:, q cols] = bf16(dq_acc * scale). With dbias, also the bias gradient
-// of the packed projection: dbias[c] += sum over rows of dqkv[:, c] for all
-// 3C columns (the dK/dV columns were written by the main kernel), one atomic
-// per column and row slice. Thread = 8 consecutive columns of a row; a block
-// is `lanes` row lanes of `gw` threads each (gw = the 3C/8 column groups
-// rounded up to a warp), so (almost) every thread has a column group.
+// dqkv[:, q cols] = bf16(dq_acc * scale). With dbias, also the Q part of the
+// packed projection's bias gradient: dbias[c] += sum over rows of the bf16 dQ
+// for the C query columns, one atomic per column and row slice (the main
+// kernel adds the K and V parts while it reads dK/dV out of TMEM). Thread = 8
+// consecutive columns of a row; a block is `lanes` row lanes of `gw` threads
+// each (gw = the C/8 column groups rounded up to a warp).
 constexpr int kPostMaxThreads = 1024;
 __global__ void __launch_bounds__(kPostMaxThreads) flash_bwd_post_kernel(
     const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int T, int C, float scale,
     float* __restrict__ dbias, int rows_per_block, int gw) {
-  const int groups = 3 * C / 8;
+  const int groups = C / 8;  // dQ columns (the K/V bias sums come from the main kernel)
   const int lanes = blockDim.x / gw;
   const int g = blockIdx.y * gw + (int)(threadIdx.x % gw);
   const int rl = (int)(threadIdx.x / gw);  // row lane
@@ -594,19 +594,13 @@ __global__ void __launch_bounds__(kPostMaxThreads) flash_bwd_post_kernel(
     for (int r = r0 + rl; r < r1; r += lanes) {
       uint4* dst = reinterpret_cast<uint4*>(dqkv + (size_t)r * 3 * C + c0);
       uint4 w;
-      if (c0 < C) {
-        const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * C + c0);
-        const float4 a = src[0], b = src[1];
-        w.x = pack_bf16x2(a.x * scale, a.y * scale);
-        w.y = pack_bf16x2(a.z * scale, a.w * scale);
-        w.z = pack_bf16x2(b.x * scale, b.y * scale);
-        w.w = pack_bf16x2(b.z * scale, b.w * scale);
-        *dst = w;
-      } else if (dbias) {
-        w = *dst;
-      } else {
-        continue;
-      }
+      const float4* src = reinterpret_cast<const float4*>(dq_acc + (size_t)r * C + c0);
+      const float4 a = src[0], b = src[1];
+      w.x = pack_bf16x2(a.x * scale, a.y * scale);
+      w.y = pack_bf16x2(a.z * scale, a.w * scale);
+      w.z = pack_bf16x2(b.x * scale, b.y * scale);
+      w.w = pack_bf16x2(b.z * scale, b.w * scale);
+      *dst = w;
       if (dbias) {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -646,7 +640,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                      const __grid_constant__ CUtensorMap tm_dout, const float* __restrict__ lse2,
                      const float* __restrict__ delta, float* __restrict__ dq_acc,
                      __nv_bfloat16* __restrict__ dqkv, const uint8_t* __restrict__ key_pad, int B,
-                     int S, int H, int causal, float scale, uint32_t* err) {
+                     int S, int H, int causal, float scale, float* __restrict__ dbias,
+                     uint32_t* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -928,6 +923,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.dkv_free);
+      if (dbias) {
+        // K and V bias gradients: column sums of this warp's 32 key rows x 32
+        // columns (rows past S hold zeros), one atomic per column and warp
+        float ck[32], cv[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          ck[c] = kj < S ? __uint_as_float(rk[c]) * scale : 0.f;
+          cv[c] = kj < S ? __uint_as_float(rv[c]) : 0.f;
+        }
+        const float sk = chunk_column_sum(ck, lane);
+        const float sv = chunk_column_sum(cv, lane);
+        atomicAdd(dbias + C + h * kD + hh * 32 + lane, sk);
+        atomicAdd(dbias + 2 * C + h * kD + hh * 32 + lane, sv);
+      }
       if (kj < S) {
         __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD + hh * 32;
         __nv_bfloat16* vrow = krow + C;
@@ -1015,9 +1024,9 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   const int grid = (int)std::min<int64_t>(items, (int64_t)num_sms());
   flash_bwd_kernel<<<grid, kBwdThreads, smem, st>>>(tm_qkv, tm_do, a.lse2, a.delta, a.dq_acc, a.dqkv,
                                             a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
-                                            a.err ? a.err : default_err_word());
+                                            a.dbias, a.err ? a.err : default_err_word());
   const int T = a.B * a.S;
-  const int groups = 3 * C / 8;
+  const int groups = C / 8;  // dQ column groups
   const int gw = std::min(kPostMaxThreads, (groups + 31) / 32 * 32);  // threads per row lane
   const int gy = (groups + gw - 1) / gw;
   const int lanes = kPostMaxThreads / gw;

@@ -216,57 +216,6 @@ enum EpiInput : int { kInNone = 0, kInResidual = 1, kInAux = 2 };
 // positions the outputs use, so each lane reads and writes its own row only.
 // Out-of-range rows/columns need no checks: TMA loads fill them with zeros and
 // TMA stores clip them; only the bias needs a bound.
-// Column sums of a 32x32 chunk held one row per lane (v[c] = element (lane, c)):
-// a butterfly reduce-scatter leaves the sum of column `lane` in lane `lane`
-// after 31 shuffles (each stage halves the columns a lane keeps; lanes with
-// the stage's bit set keep the upper half).
-__device__ __forceinline__ float chunk_column_sum(const float (&v)[32], int lane) {
-  float a[16];
-  {
-    const bool up = lane & 16;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float send = up ? v[k] : v[k + 16];
-      const float keep = up ? v[k + 16] : v[k];
-      a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-  }
-  float b[8];
-  {
-    const bool up = lane & 8;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float send = up ? a[k] : a[k + 8];
-      const float keep = up ? a[k + 8] : a[k];
-      b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-  }
-  float c[4];
-  {
-    const bool up = lane & 4;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float send = up ? b[k] : b[k + 4];
-      const float keep = up ? b[k + 4] : b[k];
-      c[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-  }
-  float d[2];
-  {
-    const bool up = lane & 2;
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float send = up ? c[k] : c[k + 2];
-      const float keep = up ? c[k + 2] : c[k];
-      d[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-  }
-  const bool up = lane & 1;
-  const float send = up ? d[0] : d[1];
-  const float keep = up ? d[1] : d[0];
-  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
-}
-
 __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float alpha,
                                                    const CUtensorMap* tmOut,
                                                    const CUtensorMap* tmAux, uint8_t* slot,
