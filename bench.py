@@ -12,9 +12,11 @@ wd 0.1. Weak scaling: global batch = 64 x N.
 ``--model bert`` runs BASELINE config 4 instead (BERT-base MLM, seq 512,
 batch 32 per GPU, 15% of positions masked, AdamW).
 
-N > 1 runs under torchrun (one rank per GPU, NCCL bootstrap). The timed region
-is exactly K steps bracketed by barrier + synchronize, timed with CUDA events
-on the launching stream, max over ranks; rank 0 prints one JSON line.
+N > 1 runs under torchrun (one rank per GPU, NCCL bootstrap). Each timed
+window is exactly K steps bracketed by barrier + synchronize, timed with CUDA
+events on the launching stream, max over ranks; ``--windows`` (5) such windows
+run back to back and the median is reported with the spread; rank 0 prints
+one JSON line.
 
 ``value`` is the device-timed whole-step throughput of the captured step (CUDA
 graph replay: forward, backward, gradient all-reduce, AdamW). ``e2e`` runs the
@@ -54,6 +56,8 @@ def parse():
     ap.add_argument("--engine", default="auto", choices=["auto", "nccl", "peer"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--windows", type=int, default=5,
+                    help="timed windows of --steps steps each; the median window is reported")
     ap.add_argument("--model", default="lm", choices=["lm", "bert", "resnet20"],
                     help="lm = BASELINE config 3 (the headline); bert = config 4; resnet20 = config 2")
     return ap.parse_args()
@@ -125,11 +129,12 @@ def reference_arm(args):
 
 
 def main():
-    from flodl_b200.utils.crash import install_crash_handler
-    install_crash_handler()
     args = parse()
     if args.impl == "reference":
+        # the reference arm never imports this package (nor maps its .so files)
         return reference_arm(args)
+    from flodl_b200.utils.crash import install_crash_handler
+    install_crash_handler()
     import torch
     import torch.distributed as dist
 
@@ -189,27 +194,36 @@ def main():
     torch.cuda.synchronize()
 
     # ---------------------------------------------------------------- timed (device)
+    # `--windows` windows of exactly K steps, each bracketed by barrier +
+    # synchronize and timed with CUDA events on the launching stream; a
+    # window's time is the max over ranks; the reported value is the median
+    # window, with the spread of all windows alongside.
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    windows = []
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    for _ in range(max(1, args.windows)):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        windows.append(float(t.item()))
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = statistics.median(windows)
+    spread = {"windows": len(windows), "ms_per_step_min": min(windows),
+              "ms_per_step_max": max(windows),
+              "rel_spread": (max(windows) - min(windows)) / ms if ms > 0 else None}
 
     # ---------------------------------------------------------------- e2e (public API)
     e2e = None
@@ -254,6 +268,7 @@ def main():
                        "l2": "inputs larger than L2: ~2 GB of activations per step per GPU"},
             "impl": args.impl,
             "clocks": clocks,
+            "timing": spread,
             "e2e": e2e,
             "gpu_launches": (per_step_launches * args.steps) if per_step_launches is not None else None,
         }

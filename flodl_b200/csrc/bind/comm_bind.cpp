@@ -84,7 +84,9 @@ void fused_launch(int64_t op, py::dict cfg, const std::vector<int64_t>& data,
   a.end = geti("end", 0);
   a.blocks = (int)geti("blocks", 0);
   a.threads = (int)geti("threads", 512);
+  a.oneshot = geti("oneshot", 0) != 0;
   FL_CHECK(a.threads == 128 || a.threads == 256 || a.threads == 512, "threads must be 128, 256 or 512");
+  FL_CHECK(a.bucket >= 0 && a.bucket < flodl::kMaxSlots, "signal slot out of range");
   a.m = reinterpret_cast<float*>(getp("m"));
   a.v = reinterpret_cast<float*>(getp("v"));
   a.lr = reinterpret_cast<const float*>(getp("lr"));
@@ -100,16 +102,30 @@ void fused_launch(int64_t op, py::dict cfg, const std::vector<int64_t>& data,
   a.nesterov = geti("nesterov", 0) != 0;
   a.average = geti("average", 1) != 0;
   a.mass = (float)getf("mass", 1.0);
-  a.gamma = (float)getf("gamma", 1.0);
+  a.mover = (float)getf("mover", 1.0);
+  a.buf_start = geti("buf_start", -1);
+  a.div = reinterpret_cast<float*>(getp("div"));
+  a.sumsq = reinterpret_cast<float*>(getp("sumsq"));
+  a.norm_out = reinterpret_cast<float*>(getp("norm_out"));
+  a.max_norm = (float)getf("max_norm", 0.0);
+  a.table = reinterpret_cast<const int64_t*>(getp("table"));
+  a.nb = (int)geti("nb", 0);
   a.timeout_ns = (uint64_t)geti("timeout_ns", 10000000000LL);
   a.err = reinterpret_cast<uint32_t*>(getp("err"));
   FL_CHECK(a.world >= 1 && a.world <= flodl::kMaxRanks, "world size out of range");
+  FL_CHECK(a.rank >= 0 && a.rank < a.world, "rank out of range");
   FL_CHECK((int)data.size() == a.world && (int)grad.size() == a.world &&
                (int)shadow.size() == a.world && (int)sig.size() == a.world,
            "one pointer per rank required");
-  if (op == (int64_t)flodl::FusedOp::kArAdamW)
+  if (op == (int64_t)flodl::FusedOp::kArAdamW || op == (int64_t)flodl::FusedOp::kClipApplyAdamW)
     FL_CHECK(a.m && a.v && a.lr && a.step, "fused AdamW needs m, v, lr, step");
-  if (op == (int64_t)flodl::FusedOp::kArSgd) FL_CHECK(a.lr, "fused SGD needs lr");
+  if (op == (int64_t)flodl::FusedOp::kArSgd || op == (int64_t)flodl::FusedOp::kClipApplySgd)
+    FL_CHECK(a.lr, "fused SGD needs lr");
+  if (op == (int64_t)flodl::FusedOp::kReduceScatter || op == (int64_t)flodl::FusedOp::kClipApplyAdamW ||
+      op == (int64_t)flodl::FusedOp::kClipApplySgd)
+    FL_CHECK(a.sumsq, "clip mode needs the sum-of-squares accumulator");
+  if (op == (int64_t)flodl::FusedOp::kClipApplyAdamW || op == (int64_t)flodl::FusedOp::kClipApplySgd)
+    FL_CHECK(a.table && a.nb > 0, "clip apply needs the bucket table");
   flodl::PeerPtrs ptrs;
   for (int p = 0; p < flodl::kMaxRanks; ++p) {
     ptrs.data[p] = p < a.world ? reinterpret_cast<float*>(data[p]) : nullptr;
@@ -136,6 +152,11 @@ void register_comm(py::module& m) {
   m.attr("FUSED_ALL_REDUCE") = (int)flodl::FusedOp::kAllReduce;
   m.attr("FUSED_WEIGHTED_AVG") = (int)flodl::FusedOp::kWeightedAverage;
   m.attr("FUSED_BROADCAST") = (int)flodl::FusedOp::kBroadcast;
+  m.attr("FUSED_REDUCE_SCATTER") = (int)flodl::FusedOp::kReduceScatter;
+  m.attr("FUSED_CLIP_APPLY_ADAMW") = (int)flodl::FusedOp::kClipApplyAdamW;
+  m.attr("FUSED_CLIP_APPLY_SGD") = (int)flodl::FusedOp::kClipApplySgd;
   m.attr("MAX_RANKS") = flodl::kMaxRanks;
   m.attr("MAX_BUCKETS") = flodl::kMaxBuckets;
+  m.attr("MAX_SLOTS") = flodl::kMaxSlots;
+  m.attr("MAX_BLOCKS") = flodl::kMaxBlocks;
 }

@@ -96,8 +96,8 @@ void softmax_ce(const Tensor& logits, const Tensor& targets, Tensor& loss, Tenso
   const int T = (int)logits.size(0), V = (int)logits.size(1);
   c10::cuda::CUDAGuard guard(logits.device());
   auto st = cur_stream();
-  FL_CUDA_OK(flodl::launch_ce_count(ptr<int64_t>(targets), T, ignore_index, ptr<float>(inv_count),
-                                    ptr<float>(loss), st));
+  FL_CUDA_OK(flodl::launch_ce_count(ptr<int64_t>(targets), T, V, ignore_index,
+                                    ptr<float>(inv_count), ptr<float>(loss), nullptr, st));
   flodl::CeArgs a;
   a.logits = ptr<__nv_bfloat16>(logits);
   a.ld = (int)logits.stride(0);

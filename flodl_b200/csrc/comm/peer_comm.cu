@@ -7,26 +7,44 @@
 // from / store to any rank's region over NVLink. NCCL (or the torch.distributed
 // store) is only used to exchange the handles.
 //
-// Kernels (all spin-waits are bounded by %globaltimer; on expiry they record
-// an error code in host-mapped memory and return):
+// Synchronisation: there is no grid-wide handshake. Block b of a launch meets
+// block b of the same launch on every peer (all ranks launch the same grid):
+// it publishes a per-(slot, block) phase counter into every peer's flag word
+// with a system-scope release store (lane p stores to peer p, so the world
+// stores go out in parallel) and waits until every peer's counter for that
+// block reached the same phase (lane p polls the word peer p writes). A launch
+// has a start meeting (inputs of every rank are ready) and an end meeting
+// (every peer finished reading this rank's inputs and writing its results
+// here). The element mapping of block b is identical on every rank, so what a
+// block may overwrite after its end meeting is exactly what the peers' block b
+// read. Every wait is bounded by %globaltimer (and gives up early once the
+// communicator's error word is set); on expiry the kernel records an error
+// code in host-mapped memory and returns.
 //
-//  fused_ar_adamw / fused_ar_sgd   per DDP bucket, the reference's
+// Sharding: a range of n float4 is cut into `world` shards of ceil(n/world);
+// rank r owns shard r. Only rank r reads or writes the shard-r elements of any
+// rank's gradient or parameter buffer during a two-shot launch, which is why
+// a reduce-scatter can write its result straight back in place.
+//
+// Kernels:
+//  ar_update (AdamW / SGD)   per DDP bucket, the reference's
 //      "all_reduce_gradients (Avg) then optimizer.step()" (flodl/src/distributed/
-//      ddp.rs:249-260 + nn/optim/adam.rs:183-245) as ONE launch:
-//        1. every block announces "rank r reached bucket k" on all peers
-//        2. rank r reduce-scatters: sums shard r of the bucket's gradients
-//           from all peers by peer loads (scaled by 1/world)
-//        3. applies AdamW / SGD-momentum to its shard
-//        4. stores the updated f32 weights and their bf16 shadow into every
-//           peer's arenas (all-gather by peer stores)
-//        5. counts completion on every peer; waits until all peers' shards
-//           landed locally, then zeroes its local gradient bucket
-//  weighted_average   cluster parameter averaging (ElChe NCCL modes,
-//      worker/sync.rs:130-236): out = sum_i (n_i^gamma / sum_j n_j^gamma) W_i
-//      with the count exchange folded into the signal words.
-//  broadcast_pull     initial parameter broadcast: every rank pulls rank 0's
-//      buffer (rank_entry.rs:619-623).
-//  all_reduce         plain sum/avg all-reduce of a symmetric buffer (sweeps).
+//      ddp.rs:249-260 + nn/optim/adam.rs:183-245, sgd.rs) as ONE launch:
+//      two-shot: reduce shard r from all peers (peer loads), update it, store
+//      the f32 weights and bf16 shadow into every rank (peer stores);
+//      one-shot (small buckets): every rank reduces the whole bucket in the
+//      same peer order and updates it locally (bitwise-identical replicas).
+//      After the end meeting each rank clears its gradient bucket.
+//  reduce_scatter + clip_apply   the same with global-norm clipping
+//      (flodl-sys/ops_training.cpp:948-985): buckets only average their shard
+//      in place and add its sum of squares; the apply launch exchanges the
+//      partial sums, derives the clip coefficient and updates every bucket.
+//  weighted_average   cluster parameter averaging (worker/sync.rs:130-236):
+//      params <- sum_i (m_i / sum m) W_i with m_i = n_i^gamma, f32 buffers
+//      <- mover-weighted mean; the mass exchange rides the start meeting and
+//      the divergence partials of every rank are computed in the same pass.
+//  broadcast_pull     initial parameter broadcast (rank_entry.rs:619-623).
+//  all_reduce         plain sum/avg all-reduce of a symmetric buffer.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -40,7 +58,7 @@ namespace flodl {
 
 namespace {
 
-constexpr int kIlp = 2;  // float4 elements per thread and loop iteration
+constexpr int kIlp = 4;  // float4 elements per thread in flight per loop iteration
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -50,23 +68,38 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_add_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ float4 ld_cg4(const float* p) {
   return __ldcg(reinterpret_cast<const float4*>(p));
 }
+__device__ __forceinline__ void add4(float4& a, const float4 b) {
+  a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+}
+__device__ __forceinline__ void scale4(float4& a, float s) {
+  a.x *= s; a.y *= s; a.z *= s; a.w *= s;
+}
+__device__ __forceinline__ float dot4(const float4 a) {
+  return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+}
+__device__ __forceinline__ uint2 bf16x4(const float4 v) {
+  uint2 s;
+  s.x = pack_bf16x2(v.x, v.y);
+  s.y = pack_bf16x2(v.z, v.w);
+  return s;
+}
 
-// Wait until *p >= target (wrap-safe) or the deadline passes.
+// Wait until *p >= target (wrap-safe). Gives up when the deadline passes or
+// the communicator's error word is already set (another block timed out).
 __device__ __forceinline__ bool wait_ge(const uint32_t* p, uint32_t target, uint64_t limit_ns,
-                                        uint32_t* err, uint32_t code) {
+                                        uint32_t* err) {
   uint64_t t0 = 0;
   uint32_t spins = 0;
   while ((int32_t)(ld_acquire_sys(p) - target) < 0) {
     if ((++spins & 255u) == 0u) {
-      if (t0 == 0) t0 = global_timer_ns();
-      else if (global_timer_ns() - t0 > limit_ns) {
-        if (err) atomicCAS_system(err, 0u, code);
+      if (err && *reinterpret_cast<volatile uint32_t*>(err) != 0u) return false;
+      if (t0 == 0) {
+        t0 = global_timer_ns();
+      } else if (global_timer_ns() - t0 > limit_ns) {
+        if (err) atomicCAS_system(err, 0u, (uint32_t)kErrPeerTimeout);
         return false;
       }
     }
@@ -74,25 +107,19 @@ __device__ __forceinline__ bool wait_ge(const uint32_t* p, uint32_t target, uint
   return true;
 }
 
-// Signal layout (u32 words of the symmetric signal region):
-//   [ready  + k*kMaxRanks + src] : epoch at which rank src reached bucket k
-//   [done   + k]                 : completion counter of bucket k (peers add)
-//   [epoch  + k]                 : local: completed launches of bucket k
-//   [finish + k]                 : local: blocks finished in the current launch
-//   [base + k]                   : local: value of done[k] when the previous launch ended
-// The completion target of a launch is base + world * gridDim, so launches of
-// one slot may use different grid sizes.
+// Signal words (u32) of one rank's symmetric signal region:
+//   flags[slot][block][src] : phase counter of (slot, block) on rank src (peer stores)
+//   phase[slot][block]      : this rank's phase counter of (slot, block) (local)
+//   mass[slot][src][2]      : f32 bits published by rank src (mass, mover / sumsq)
+//   part[block][src][2]     : f32 divergence partials computed by rank src for this rank
+//   count[slot]             : local: blocks that consumed the clip accumulator
 struct SigLayout {
-  static constexpr int kReady = 0;
-  static constexpr int kDone = kReady + kMaxBuckets * kMaxRanks;
-  static constexpr int kEpoch = kDone + kMaxBuckets;
-  static constexpr int kFinish = kEpoch + kMaxBuckets;
-  static constexpr int kCount = kFinish + kMaxBuckets;  // count/mass exchange (f32 bits)
-  static constexpr int kBase = kCount + kMaxBuckets * kMaxRanks * 2;
-  static constexpr int kGo = kBase + kMaxBuckets;       // local: all peers ready (epoch)
-  static constexpr int kFinCnt = kGo + kMaxBuckets;     // local: blocks done with a phase
-  static constexpr int kFinGo = kFinCnt + kMaxBuckets;  // local: phase complete everywhere
-  static constexpr int kWords = kFinGo + kMaxBuckets;
+  static constexpr int kFlags = 0;
+  static constexpr int kPhase = kFlags + kMaxSlots * kMaxBlocks * kMaxRanks;
+  static constexpr int kMass = kPhase + kMaxSlots * kMaxBlocks;
+  static constexpr int kPart = kMass + kMaxSlots * kMaxRanks * 2;
+  static constexpr int kCount = kPart + kMaxBlocks * kMaxRanks * 2;
+  static constexpr int kWords = kCount + kMaxSlots;
 };
 
 struct Handles {
@@ -102,453 +129,518 @@ struct Handles {
   uint32_t* sig[kMaxRanks];
 };
 
-// Start-of-launch handshake. Only block 0 of each rank talks to the peers: it
-// publishes "rank r reached this launch of slot k" on every peer and waits
-// until every peer did the same, then opens a local gate that the other
-// blocks of the launch wait on. Returns the launch epoch (1, 2, ... per slot).
-__device__ __forceinline__ uint32_t announce(const Handles& h, int rank, int world, int bucket,
-                                             uint32_t* sig_local) {
-  __shared__ uint32_t epoch_sh;
-  if (threadIdx.x == 0) {
-    const uint32_t e = *(volatile uint32_t*)(sig_local + SigLayout::kEpoch + bucket) + 1;
-    epoch_sh = e;
-    if (blockIdx.x == 0) {
-      __threadfence_system();
-      for (int p = 0; p < world; ++p)
-        st_release_sys(h.sig[p] + SigLayout::kReady + bucket * kMaxRanks + rank, e);
-    }
-  }
-  __syncthreads();
-  return epoch_sh;
+__device__ __forceinline__ int flag_idx(int slot, int block, int src) {
+  return SigLayout::kFlags + (slot * kMaxBlocks + block) * kMaxRanks + src;
 }
 
-__device__ __forceinline__ bool wait_all_ready(const Handles& h, int world, int bucket,
-                                               uint32_t epoch, uint32_t* sig_local,
-                                               uint64_t limit, uint32_t* err) {
-  __shared__ int ok_sh;
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    if (blockIdx.x == 0) {
-      for (int p = 0; p < world && ok; ++p)
-        ok = wait_ge(sig_local + SigLayout::kReady + bucket * kMaxRanks + p, epoch, limit, err,
-                     kErrPeerTimeout);
-      if (ok) st_release_sys(sig_local + SigLayout::kGo + bucket, epoch);
-    } else {
-      ok = wait_ge(sig_local + SigLayout::kGo + bucket, epoch, limit, err, kErrPeerTimeout);
-    }
-    ok_sh = ok;
-  }
-  __syncthreads();
-  return ok_sh != 0;
-}
-
-// End-of-phase handshake on completion slot `slot` (the bucket, or bucket + 1
-// for a second phase). Every block makes its peer-memory writes visible and
-// counts itself; the last block of this rank signals each peer once and waits
-// until all peers did, then opens a local gate for the other blocks. The
-// completion target is base + world, base = the slot's count when the
-// previous launch ended (recorded by end_launch).
-__device__ __forceinline__ bool phase_done(const Handles& h, int world, int slot, uint32_t epoch,
-                                           uint32_t* sig_local, uint64_t limit, uint32_t* err) {
-  __shared__ int ok_sh;
+// Meeting of block blockIdx.x with the same block of every peer on `slot`.
+// Everything this block wrote before (locally or into peers) is visible to a
+// peer block that passed the meeting, and vice versa. CTA-uniform result.
+__device__ __forceinline__ bool meet(const Handles& h, int rank, int world, int slot,
+                                  uint64_t limit, uint32_t* err) {
+  __shared__ uint32_t ph_sh;
+  uint32_t* sig = h.sig[rank];
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    const uint32_t prev = atomicAdd(sig_local + SigLayout::kFinCnt + slot, 1u);
-    bool ok;
-    if (prev == gridDim.x - 1) {
-      sig_local[SigLayout::kFinCnt + slot] = 0;
-      __threadfence_system();
-      for (int p = 0; p < world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + slot, 1u);
-      const uint32_t target =
-          *(volatile uint32_t*)(sig_local + SigLayout::kBase + slot) + (uint32_t)world;
-      ok = wait_ge(sig_local + SigLayout::kDone + slot, target, limit, err, kErrPeerTimeout);
-      if (ok) st_release_sys(sig_local + SigLayout::kFinGo + slot, epoch);
-    } else {
-      ok = wait_ge(sig_local + SigLayout::kFinGo + slot, epoch, limit, err, kErrPeerTimeout);
-    }
-    ok_sh = ok;
+    uint32_t* c = sig + SigLayout::kPhase + slot * kMaxBlocks + blockIdx.x;
+    const uint32_t ph = *c + 1u;
+    *c = ph;
+    ph_sh = ph;
   }
   __syncthreads();
-  return ok_sh != 0;
-}
-
-__device__ __forceinline__ bool finish_bucket(const Handles& h, int world, int bucket,
-                                              uint32_t epoch, uint32_t* sig_local, uint64_t limit,
-                                              uint32_t* err) {
-  return phase_done(h, world, bucket, epoch, sig_local, limit, err);
-}
-
-// The last local block of a launch records the done counters (slot and
-// slot + 1, which the all-reduce uses for its second round) as the base of
-// the next launch, then advances the epoch. No peer can add to them before
-// this rank announces its next launch.
-__device__ __forceinline__ void end_launch(int bucket, uint32_t* sig_local) {
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(sig_local + SigLayout::kFinish + bucket, 1u);
-    if (prev == gridDim.x - 1) {
-      sig_local[SigLayout::kFinish + bucket] = 0;
-      for (int k = bucket; k < bucket + 2 && k < kMaxBuckets; ++k)
-        sig_local[SigLayout::kBase + k] = *(volatile uint32_t*)(sig_local + SigLayout::kDone + k);
-      __threadfence();
-      atomicAdd(sig_local + SigLayout::kEpoch + bucket, 1u);
-    }
+  bool ok = true;
+  if ((int)threadIdx.x < world) {
+    const uint32_t ph = ph_sh;
+    st_release_sys(h.sig[threadIdx.x] + flag_idx(slot, blockIdx.x, rank), ph);
+    ok = wait_ge(sig + flag_idx(slot, blockIdx.x, threadIdx.x), ph, limit, err);
   }
+  return __syncthreads_and(ok) != 0;
 }
 
-__device__ __forceinline__ void adamw4(float4& p, float4 g, float4& m, float4& v, float lr,
-                                       float b1, float b2, float eps, float wd, float bc1,
-                                       float bc2s) {
-  float* pp = &p.x;
-  float* gg = &g.x;
-  float* mm = &m.x;
-  float* vv = &v.x;
+// Shard of `rank` in float4 units: [s0, s1); `per` = shard length.
+struct Shard {
+  int64_t b0, b1;  // whole range (float4)
+  int64_t per;
+  __device__ Shard(const FusedArgs& a) {
+    b0 = a.start / 4;
+    b1 = a.end / 4;
+    per = (b1 - b0 + a.world - 1) / a.world;
+  }
+  __device__ int64_t s0(int r) const { return b0 + per * r; }
+  __device__ int64_t s1(int r) const { return min(b1, b0 + per * (r + 1)); }
+};
+
+__device__ __forceinline__ float block_sum(float v, float* sh) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    mm[i] = b1 * mm[i] + (1.f - b1) * gg[i];
-    vv[i] = b2 * vv[i] + (1.f - b2) * gg[i] * gg[i];
-    const float denom = sqrtf(vv[i]) / bc2s + eps;
-    pp[i] = pp[i] * (1.f - lr * wd) - (lr / bc1) * mm[i] / denom;
-  }
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r += sh[i];
+  __syncthreads();
+  return r;
 }
 
-// ------------------------------------------------------------------ fused AR + AdamW
-__global__ void __launch_bounds__(512) fused_ar_adamw_kernel(FusedArgs a, Handles h) {
-  uint32_t* sig = h.sig[a.rank];
-  const uint32_t epoch = announce(h, a.rank, a.world, a.bucket, sig);
-  const uint64_t limit = a.timeout_ns;
-  if (!wait_all_ready(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
+// ------------------------------------------------------------------ updates
+// Per-element optimizer updates on a float4 of weights. `i` indexes the
+// float4 in the arena (m/v/momentum buffers are arena-sized and local).
+struct AdamWUpdate {
+  float lr, b1, b2, eps, wd, bc1, bc2s;
+  float* m;
+  float* v;
+  __device__ AdamWUpdate(const FusedArgs& a) {
+    lr = *a.lr;
+    const float t = *a.step;
+    b1 = a.beta1;
+    b2 = a.beta2;
+    eps = a.eps;
+    wd = a.wd;
+    bc1 = 1.f - powf(a.beta1, t);
+    bc2s = sqrtf(1.f - powf(a.beta2, t));
+    m = a.m;
+    v = a.v;
   }
-  // shard of this rank (in float4 units)
-  const int64_t n4 = (a.end - a.start) / 4;
-  const int64_t per = (n4 + a.world - 1) / a.world;
-  const int64_t s0 = a.start / 4 + per * a.rank;
-  const int64_t s1 = min(a.start / 4 + n4, s0 + per);
-  const float lr = *a.lr;
-  const float t = *a.step;
-  const float bc1 = 1.f - powf(a.beta1, t);
-  const float bc2s = sqrtf(1.f - powf(a.beta2, t));
-  const float gs = (a.gscale ? *a.gscale : 1.f) / (float)a.world;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  // two float4 per thread and iteration: all peer loads of both are issued
-  // before any use, doubling the bytes in flight over NVLink
-  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
-       i0 += kIlp * stride) {
-    float4 g[kIlp];
+  __device__ __forceinline__ void operator()(float4& p, const float4 g, int64_t i) const {
+    float4 mv = reinterpret_cast<const float4*>(m)[i];
+    float4 vv = reinterpret_cast<const float4*>(v)[i];
+    float* pp = &p.x;
+    const float* gg = &g.x;
+    float* mm = &mv.x;
+    float* vq = &vv.x;
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int p = 0; p < a.world; ++p) {
+    for (int k = 0; k < 4; ++k) {
+      mm[k] = b1 * mm[k] + (1.f - b1) * gg[k];
+      vq[k] = b2 * vq[k] + (1.f - b2) * gg[k] * gg[k];
+      const float denom = sqrtf(vq[k]) / bc2s + eps;
+      pp[k] = pp[k] * (1.f - lr * wd) - (lr / bc1) * mm[k] / denom;
+    }
+    reinterpret_cast<float4*>(m)[i] = mv;
+    reinterpret_cast<float4*>(v)[i] = vv;
+  }
+};
+
+struct SgdUpdate {
+  float lr, wd, mom, damp;
+  bool first, nesterov;
+  float* buf;
+  __device__ SgdUpdate(const FusedArgs& a) {
+    lr = *a.lr;
+    wd = a.wd;
+    mom = a.momentum;
+    damp = a.dampening;
+    first = a.first ? (*a.first != 0.f) : false;
+    nesterov = a.nesterov;
+    buf = a.m;
+  }
+  __device__ __forceinline__ void operator()(float4& p, const float4 g, int64_t i) const {
+    float4 bv = buf ? reinterpret_cast<const float4*>(buf)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float* pp = &p.x;
+    const float* gg = &g.x;
+    float* bb = &bv.x;
 #pragma unroll
-      for (int j = 0; j < kIlp; ++j) {
-        const int64_t i = i0 + j * stride;
-        if (i < s1) {
-          const float4 x = ld_cg4(h.grad[p] + 4 * i);
-          g[j].x += x.x; g[j].y += x.y; g[j].z += x.z; g[j].w += x.w;
-        }
+    for (int k = 0; k < 4; ++k) {
+      float d = gg[k] + wd * pp[k];
+      if (buf) {
+        bb[k] = first ? d : mom * bb[k] + (1.f - damp) * d;
+        d = nesterov ? d + mom * bb[k] : bb[k];
       }
+      pp[k] -= lr * d;
     }
+    if (buf) reinterpret_cast<float4*>(buf)[i] = bv;
+  }
+};
+
+__device__ __forceinline__ float grad_scale(const FusedArgs& a) {
+  return (a.gscale ? *a.gscale : 1.f) / (float)a.world;
+}
+
+// Sum of the world gradients at float4 index i (fixed peer order 0..world-1,
+// so every rank that sums the same element gets the same bits).
+__device__ __forceinline__ void gather_sum(const Handles& h, int world, const int64_t* idx,
+                                           const bool* live, float4* acc) {
+#pragma unroll
+  for (int j = 0; j < kIlp; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+  for (int p = 0; p < world; ++p) {
+    float4 x[kIlp];
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j)
+      x[j] = live[j] ? ld_cg4(h.grad[p] + 4 * idx[j]) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) add4(acc[j], x[j]);
+  }
+}
+
+// Clear this rank's gradient elements that the peers' block blockIdx.x read:
+// the block's positions in every shard (two-shot) or in the whole range.
+__device__ __forceinline__ void clear_local_grads(const Handles& h, const FusedArgs& a,
+                                                  const Shard& sh) {
+  float4* gl = reinterpret_cast<float4*>(h.grad[a.rank]);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (a.oneshot) {
+    for (int64_t i = sh.b0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < sh.b1; i += stride)
+      gl[i] = z;
+  } else {
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < sh.per; j += stride)
+      for (int s = 0; s < a.world; ++s) {
+        const int64_t i = sh.s0(s) + j;
+        if (i < sh.s1(s)) gl[i] = z;
+      }
+  }
+}
+
+// ------------------------------------------------------------------ fused AR + update
+template <class U>
+__global__ void __launch_bounds__(512) ar_update_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  const Shard sh(a);
+  const int64_t lo = a.oneshot ? sh.b0 : sh.s0(a.rank);
+  const int64_t hi = a.oneshot ? sh.b1 : sh.s1(a.rank);
+  const U upd(a);
+  const float gs = grad_scale(a);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
+       i0 += kIlp * stride) {
+    int64_t idx[kIlp];
+    bool live[kIlp];
 #pragma unroll
     for (int j = 0; j < kIlp; ++j) {
-      const int64_t i = i0 + j * stride;
-      if (i >= s1) break;
+      idx[j] = i0 + j * stride;
+      live[j] = idx[j] < hi;
+    }
+    float4 g[kIlp];
+    gather_sum(h, a.world, idx, live, g);
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) {
+      if (!live[j]) break;
+      const int64_t i = idx[j];
       float4 gj = g[j];
-      gj.x *= gs; gj.y *= gs; gj.z *= gs; gj.w *= gs;
-      float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
-      float4 m = reinterpret_cast<float4*>(a.m)[i];
-      float4 v = reinterpret_cast<float4*>(a.v)[i];
-      adamw4(pv, gj, m, v, lr, a.beta1, a.beta2, a.eps, a.wd, bc1, bc2s);
-      reinterpret_cast<float4*>(a.m)[i] = m;
-      reinterpret_cast<float4*>(a.v)[i] = v;
-      uint2 sh;
-      sh.x = pack_bf16x2(pv.x, pv.y);
-      sh.y = pack_bf16x2(pv.z, pv.w);
-      for (int p = 0; p < a.world; ++p) {
-        const int q = (a.rank + p) % a.world;  // stagger destinations across ranks
-        reinterpret_cast<float4*>(h.data[q])[i] = pv;
-        reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
+      scale4(gj, gs);
+      float4 pv = reinterpret_cast<const float4*>(h.data[a.rank])[i];
+      upd(pv, gj, i);
+      const uint2 s = bf16x4(pv);
+      if (a.oneshot) {
+        reinterpret_cast<float4*>(h.data[a.rank])[i] = pv;
+        if (h.shadow[a.rank]) reinterpret_cast<uint2*>(h.shadow[a.rank])[i] = s;
+      } else {
+        for (int p = 0; p < a.world; ++p) {
+          const int q = (a.rank + p) % a.world;  // stagger destinations across ranks
+          reinterpret_cast<float4*>(h.data[q])[i] = pv;
+          if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = s;
+        }
       }
     }
   }
-  if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  // every peer has read our gradients and written its shard: clear the bucket
-  float4* gl = reinterpret_cast<float4*>(h.grad[a.rank]);
-  for (int64_t i = a.start / 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-       i < a.start / 4 + n4; i += stride)
-    gl[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  end_launch(a.bucket, sig);
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  clear_local_grads(h, a, sh);
 }
 
-// ------------------------------------------------------------------ fused AR + SGD
-__global__ void __launch_bounds__(512) fused_ar_sgd_kernel(FusedArgs a, Handles h) {
-  uint32_t* sig = h.sig[a.rank];
-  const uint32_t epoch = announce(h, a.rank, a.world, a.bucket, sig);
-  const uint64_t limit = a.timeout_ns;
-  if (!wait_all_ready(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  const int64_t n4 = (a.end - a.start) / 4;
-  const int64_t per = (n4 + a.world - 1) / a.world;
-  const int64_t s0 = a.start / 4 + per * a.rank;
-  const int64_t s1 = min(a.start / 4 + n4, s0 + per);
-  const float lr = *a.lr;
-  const bool first = a.first ? (*a.first != 0.f) : false;
-  const float gs = (a.gscale ? *a.gscale : 1.f) / (float)a.world;
+// ------------------------------------------------------------------ clip mode
+// Bucket launch: average shard r of the bucket in place (this rank's own
+// gradient buffer holds the result) and add its sum of squares to *a.sumsq.
+// No end meeting: the shard-r elements are touched by rank r only, and the
+// peers' gradients are cleared by the apply launch, which follows this one on
+// every rank's stream.
+__global__ void __launch_bounds__(512) reduce_scatter_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
+  __shared__ float red[32];
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  const Shard sh(a);
+  const int64_t lo = sh.s0(a.rank), hi = sh.s1(a.rank);
+  const float gs = grad_scale(a);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
+  float ss = 0.f;
+  for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
        i0 += kIlp * stride) {
-    float4 gv[kIlp];
+    int64_t idx[kIlp];
+    bool live[kIlp];
 #pragma unroll
-    for (int jj = 0; jj < kIlp; ++jj) gv[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int p = 0; p < a.world; ++p) {
-#pragma unroll
-      for (int jj = 0; jj < kIlp; ++jj) {
-        const int64_t i = i0 + jj * stride;
-        if (i < s1) {
-          const float4 x = ld_cg4(h.grad[p] + 4 * i);
-          gv[jj].x += x.x; gv[jj].y += x.y; gv[jj].z += x.z; gv[jj].w += x.w;
-        }
-      }
+    for (int j = 0; j < kIlp; ++j) {
+      idx[j] = i0 + j * stride;
+      live[j] = idx[j] < hi;
     }
+    float4 g[kIlp];
+    gather_sum(h, a.world, idx, live, g);
 #pragma unroll
-    for (int jj = 0; jj < kIlp; ++jj) {
-      const int64_t i = i0 + jj * stride;
-      if (i >= s1) break;
-      float4 g = gv[jj];
-      float4 pv = reinterpret_cast<float4*>(h.data[a.rank])[i];
-      float* pp = &pv.x;
-      float* gg = &g.x;
-      float4 bv = a.m ? reinterpret_cast<float4*>(a.m)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      float* bb = &bv.x;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float d = gg[e] * gs + a.wd * pp[e];
-        if (a.m) {
-          bb[e] = first ? d : a.momentum * bb[e] + (1.f - a.dampening) * d;
-          d = a.nesterov ? d + a.momentum * bb[e] : bb[e];
-        }
-        pp[e] -= lr * d;
-      }
-      if (a.m) reinterpret_cast<float4*>(a.m)[i] = bv;
-      uint2 sh;
-      sh.x = pack_bf16x2(pv.x, pv.y);
-      sh.y = pack_bf16x2(pv.z, pv.w);
-      for (int p = 0; p < a.world; ++p) {
-        const int q = (a.rank + p) % a.world;
-        reinterpret_cast<float4*>(h.data[q])[i] = pv;
-        if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
-      }
+    for (int j = 0; j < kIlp; ++j) {
+      if (!live[j]) break;
+      scale4(g[j], gs);
+      ss += dot4(g[j]);
+      reinterpret_cast<float4*>(h.grad[a.rank])[idx[j]] = g[j];
     }
   }
-  if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0 && a.sumsq) atomicAdd(a.sumsq, ss);
+}
+
+// Apply launch: publish this rank's sum of squares, meet, derive the global
+// norm and the clip coefficient (max_norm / (norm + 1e-6) when the norm
+// exceeds max_norm), update shard r of every bucket of the table, all-gather
+// the weights, clear every local gradient, meet again.
+template <class U>
+__global__ void __launch_bounds__(512) clip_apply_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
+  uint32_t* sig = h.sig[a.rank];
+  __shared__ float local_ss;
+  if (threadIdx.x == 0) {
+    local_ss = *reinterpret_cast<volatile float*>(a.sumsq);
+    __threadfence();
+    // the last block to read the accumulator resets it for the next step
+    const uint32_t n = atomicAdd(sig + SigLayout::kCount + a.bucket, 1u);
+    if (n == gridDim.x - 1) {
+      *a.sumsq = 0.f;
+      sig[SigLayout::kCount + a.bucket] = 0u;
+    }
   }
+  __syncthreads();
+  if ((int)threadIdx.x < a.world)
+    h.sig[threadIdx.x][SigLayout::kMass + (a.bucket * kMaxRanks + a.rank) * 2] =
+        __float_as_uint(local_ss);
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  float total = 0.f;
+  for (int p = 0; p < a.world; ++p)
+    total += __uint_as_float(ld_acquire_sys(sig + SigLayout::kMass + (a.bucket * kMaxRanks + p) * 2));
+  const float norm = sqrtf(total);
+  const float coef = (a.max_norm > 0.f && norm > a.max_norm) ? a.max_norm / (norm + 1e-6f) : 1.f;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.norm_out) *a.norm_out = norm;
+  const U upd(a);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
   float4* gl = reinterpret_cast<float4*>(h.grad[a.rank]);
-  for (int64_t i = a.start / 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-       i < a.start / 4 + n4; i += stride)
-    gl[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  end_launch(a.bucket, sig);
+  for (int k = 0; k < a.nb; ++k) {
+    FusedArgs ab = a;
+    ab.start = a.table[2 * k];
+    ab.end = a.table[2 * k + 1];
+    const Shard sh(ab);
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < sh.per; j += stride) {
+      for (int s = 0; s < a.world; ++s) {
+        const int64_t i = sh.s0(s) + j;
+        if (i >= sh.s1(s)) continue;
+        if (s == a.rank) {
+          float4 g = gl[i];
+          scale4(g, coef);
+          float4 pv = reinterpret_cast<const float4*>(h.data[a.rank])[i];
+          upd(pv, g, i);
+          const uint2 sb = bf16x4(pv);
+          for (int p = 0; p < a.world; ++p) {
+            const int q = (a.rank + p) % a.world;
+            reinterpret_cast<float4*>(h.data[q])[i] = pv;
+            if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = sb;
+          }
+        }
+        gl[i] = z;
+      }
+    }
+  }
+  meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err);
 }
 
 // ------------------------------------------------------------------ plain all-reduce
-// In place over h.grad (the symmetric buffer): out = sum (or avg) over ranks.
-__global__ void __launch_bounds__(512) all_reduce_kernel(FusedArgs a, Handles h) {
-  uint32_t* sig = h.sig[a.rank];
-  const uint32_t epoch = announce(h, a.rank, a.world, a.bucket, sig);
-  const uint64_t limit = a.timeout_ns;
-  if (!wait_all_ready(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  const int64_t n4 = (a.end - a.start) / 4;
-  const int64_t per = (n4 + a.world - 1) / a.world;
-  const int64_t s0 = a.start / 4 + per * a.rank;
-  const int64_t s1 = min(a.start / 4 + n4, s0 + per);
+// In place over h.grad. Two-shot: rank r reduces shard r from every peer and
+// writes the result into every peer's shard r (only rank r touches shard r).
+// One-shot: every rank reduces the whole range into its data region (scratch),
+// meets, and copies it into its gradient buffer.
+__global__ void __launch_bounds__(512) all_reduce_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  const Shard sh(a);
+  const int64_t lo = a.oneshot ? sh.b0 : sh.s0(a.rank);
+  const int64_t hi = a.oneshot ? sh.b1 : sh.s1(a.rank);
   const float sc = a.average ? 1.f / (float)a.world : 1.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  // reduce into registers first, then a second barrier before writing so no
-  // rank overwrites a shard another rank is still reading
-  for (int64_t i0 = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < s1;
+  for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
        i0 += kIlp * stride) {
+    int64_t idx[kIlp];
+    bool live[kIlp];
+#pragma unroll
+    for (int j = 0; j < kIlp; ++j) {
+      idx[j] = i0 + j * stride;
+      live[j] = idx[j] < hi;
+    }
     float4 g[kIlp];
+    gather_sum(h, a.world, idx, live, g);
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int p = 0; p < a.world; ++p) {
-#pragma unroll
-      for (int j = 0; j < kIlp; ++j) {
-        const int64_t i = i0 + j * stride;
-        if (i < s1) {
-          const float4 x = ld_cg4(h.grad[p] + 4 * i);
-          g[j].x += x.x; g[j].y += x.y; g[j].z += x.z; g[j].w += x.w;
+    for (int j = 0; j < kIlp; ++j) {
+      if (!live[j]) break;
+      scale4(g[j], sc);
+      if (a.oneshot) {
+        reinterpret_cast<float4*>(h.data[a.rank])[idx[j]] = g[j];
+      } else {
+        for (int p = 0; p < a.world; ++p) {
+          const int q = (a.rank + p) % a.world;
+          reinterpret_cast<float4*>(h.grad[q])[idx[j]] = g[j];
         }
       }
     }
-#pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
-      const int64_t i = i0 + j * stride;
-      if (i < s1) {
-        float4 gj = g[j];
-        gj.x *= sc; gj.y *= sc; gj.z *= sc; gj.w *= sc;
-        reinterpret_cast<float4*>(h.data[a.rank])[i] = gj;  // staging (data region)
-      }
-    }
   }
-  if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  if (a.oneshot) {
+    const float4* src = reinterpret_cast<const float4*>(h.data[a.rank]);
+    float4* dst = reinterpret_cast<float4*>(h.grad[a.rank]);
+    for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += stride)
+      dst[i] = src[i];
   }
-  // all reads done everywhere: broadcast the reduced shard back into every grad buffer
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    const float4 g = reinterpret_cast<const float4*>(h.data[a.rank])[i];
-    for (int p = 0; p < a.world; ++p) {
-      const int q = (a.rank + p) % a.world;
-      reinterpret_cast<float4*>(h.grad[q])[i] = g;
-    }
-  }
-  // second completion round on a separate slot (bucket + 1): every rank's
-  // result is in every buffer before anyone reuses them
-  phase_done(h, a.world, a.bucket + 1, epoch, sig, limit, a.err);
-  end_launch(a.bucket, sig);
 }
 
 // ------------------------------------------------------------------ weighted average
-// data <- sum_p w_p data_p with w_p = n_p^gamma / sum_q n_q^gamma, where each
-// rank publishes its n (work count) through the signal words. Optionally also
-// writes divergence partials sum((pre - post)^2), sum(post^2) into a.m[0..1].
-__global__ void __launch_bounds__(512) weighted_average_kernel(FusedArgs a, Handles h) {
+// data <- sum_p (m_p / sum m) data_p over the parameter part and
+// sum_p (mover_p / sum mover) data_p over the buffer part (elements at or past
+// buf_start). Every rank publishes (m, mover) into every peer's mass slot of
+// this launch before the start meeting. When no rank did any work (sum m == 0)
+// nothing changes (the reference skips both reduces). Divergence: rank r
+// computes, over shard r, sum (data_p - avg)^2 for every p and sum avg^2, and
+// stores them into rank p's partial slots; after the end meeting each rank
+// adds its partials into a.div.
+__global__ void __launch_bounds__(512) weighted_average_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
   uint32_t* sig = h.sig[a.rank];
-  // publish my mass before announcing readiness
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    for (int p = 0; p < a.world; ++p)
-      st_release_sys(h.sig[p] + SigLayout::kCount + a.bucket * kMaxRanks * 2 + a.rank,
-                     __float_as_uint(a.mass));
+  __shared__ float w_sh[kMaxRanks], wb_sh[kMaxRanks];
+  __shared__ float red[32];
+  __shared__ int skip_sh;
+  if ((int)threadIdx.x < a.world) {
+    uint32_t* dst = h.sig[threadIdx.x] + SigLayout::kMass + (a.bucket * kMaxRanks + a.rank) * 2;
+    dst[0] = __float_as_uint(a.mass);
+    dst[1] = __float_as_uint(a.mover);
   }
-  __syncthreads();
-  const uint32_t epoch = announce(h, a.rank, a.world, a.bucket, sig);
-  const uint64_t limit = a.timeout_ns;
-  if (!wait_all_ready(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  __shared__ float w_sh[kMaxRanks];
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
   if (threadIdx.x == 0) {
-    float tot = 0.f;
+    float tot = 0.f, totb = 0.f;
     for (int p = 0; p < a.world; ++p) {
-      const float n = __uint_as_float(ld_acquire_sys(sig + SigLayout::kCount + a.bucket * kMaxRanks * 2 + p));
-      w_sh[p] = powf(fmaxf(n, 0.f), a.gamma);
+      const uint32_t* src = sig + SigLayout::kMass + (a.bucket * kMaxRanks + p) * 2;
+      w_sh[p] = fmaxf(__uint_as_float(ld_acquire_sys(src)), 0.f);
+      wb_sh[p] = fmaxf(__uint_as_float(ld_acquire_sys(src + 1)), 0.f);
       tot += w_sh[p];
+      totb += wb_sh[p];
     }
-    for (int p = 0; p < a.world; ++p) w_sh[p] = tot > 0.f ? w_sh[p] / tot : 1.f / a.world;
+    skip_sh = !(tot > 0.f);
+    for (int p = 0; p < a.world; ++p) {
+      w_sh[p] = tot > 0.f ? w_sh[p] / tot : 0.f;
+      wb_sh[p] = totb > 0.f ? wb_sh[p] / totb : w_sh[p];
+    }
   }
   __syncthreads();
-  const int64_t n4 = (a.end - a.start) / 4;
-  const int64_t per = (n4 + a.world - 1) / a.world;
-  const int64_t s0 = a.start / 4 + per * a.rank;
-  const int64_t s1 = min(a.start / 4 + n4, s0 + per);
+  const Shard sh(a);
+  const int64_t lo = sh.s0(a.rank), hi = sh.s1(a.rank);
+  const int64_t bstart = a.buf_start >= 0 ? a.buf_start / 4 : sh.b1;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  float d2 = 0.f, p2 = 0.f;
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < a.world; ++p) {
-      const float4 x = ld_cg4(h.data[p] + 4 * i);
-      const float w = w_sh[p];
-      acc.x += w * x.x; acc.y += w * x.y; acc.z += w * x.z; acc.w += w * x.w;
-    }
-    reinterpret_cast<float4*>(h.grad[a.rank])[i] = acc;  // staging in the scratch region
-  }
-  if (!finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride) {
-    const float4 g = reinterpret_cast<const float4*>(h.grad[a.rank])[i];
-    const float4 pre = reinterpret_cast<const float4*>(h.data[a.rank])[i];
-    d2 += (pre.x - g.x) * (pre.x - g.x) + (pre.y - g.y) * (pre.y - g.y) +
-          (pre.z - g.z) * (pre.z - g.z) + (pre.w - g.w) * (pre.w - g.w);
-    p2 += g.x * g.x + g.y * g.y + g.z * g.z + g.w * g.w;
-    uint2 sh;
-    sh.x = pack_bf16x2(g.x, g.y);
-    sh.y = pack_bf16x2(g.z, g.w);
-    for (int p = 0; p < a.world; ++p) {
-      const int q = (a.rank + p) % a.world;
-      reinterpret_cast<float4*>(h.data[q])[i] = g;
-      if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = sh;
-    }
-  }
-  if (a.m) {  // divergence partials of this rank's shard
+  float d2[kMaxRanks];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      d2 += __shfl_xor_sync(0xffffffffu, d2, o);
-      p2 += __shfl_xor_sync(0xffffffffu, p2, o);
-    }
-    if ((threadIdx.x & 31) == 0) {
-      atomicAdd(a.m, d2);
-      atomicAdd(a.m + 1, p2);
+  for (int p = 0; p < kMaxRanks; ++p) d2[p] = 0.f;
+  float p2 = 0.f;
+  if (!skip_sh) {
+    for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += stride) {
+      const bool is_buf = i >= bstart;
+      float4 x[kMaxRanks];
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.world) x[p] = ld_cg4(h.data[p] + 4 * i);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) {
+        if (p < a.world) {
+          const float w = is_buf ? wb_sh[p] : w_sh[p];
+          acc.x += w * x[p].x; acc.y += w * x[p].y; acc.z += w * x[p].z; acc.w += w * x[p].w;
+        }
+      }
+      if (!is_buf) {
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p) {
+          if (p < a.world) {
+            const float4 d = make_float4(x[p].x - acc.x, x[p].y - acc.y, x[p].z - acc.z,
+                                         x[p].w - acc.w);
+            d2[p] += dot4(d);
+          }
+        }
+        p2 += dot4(acc);
+      }
+      const uint2 s = bf16x4(acc);
+      for (int p = 0; p < a.world; ++p) {
+        const int q = (a.rank + p) % a.world;
+        reinterpret_cast<float4*>(h.data[q])[i] = acc;
+        if (h.shadow[q]) reinterpret_cast<uint2*>(h.shadow[q])[i] = s;
+      }
     }
   }
-  const int b2 = a.bucket + 1;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < a.world; ++p) red_add_release_sys(h.sig[p] + SigLayout::kDone + b2, 1u);
-    wait_ge(sig + SigLayout::kDone + b2,
-            *(volatile uint32_t*)(sig + SigLayout::kBase + b2) + (uint32_t)(a.world * gridDim.x),
-            limit, a.err, kErrPeerTimeout);
+  if (a.div) {
+    // partials for every rank p: (sum over shard r of (data_p - avg)^2, sum avg^2)
+    __shared__ float part_sh[kMaxRanks][2];
+    for (int p = 0; p < a.world; ++p) {
+      const float v = block_sum(d2[p], red);
+      if (threadIdx.x == 0) part_sh[p][0] = v;
+    }
+    const float pp = block_sum(p2, red);
+    if (threadIdx.x == 0)
+      for (int p = 0; p < a.world; ++p) part_sh[p][1] = pp;
+    __syncthreads();
+    if ((int)threadIdx.x < a.world) {
+      const int p = threadIdx.x;
+      uint32_t* dst = h.sig[p] + SigLayout::kPart + (blockIdx.x * kMaxRanks + a.rank) * 2;
+      dst[0] = __float_as_uint(part_sh[p][0]);
+      dst[1] = __float_as_uint(part_sh[p][1]);
+    }
   }
-  __syncthreads();
-  // the gradient arena served as staging for this rank's shard: clear it
-  for (int64_t i = s0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < s1; i += stride)
-    reinterpret_cast<float4*>(h.grad[a.rank])[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  end_launch(a.bucket, sig);
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  if (a.div && threadIdx.x == 0) {
+    float dd = 0.f, pp = 0.f;
+    for (int p = 0; p < a.world; ++p) {
+      const uint32_t* src = sig + SigLayout::kPart + (blockIdx.x * kMaxRanks + p) * 2;
+      dd += __uint_as_float(ld_acquire_sys(src));
+      pp += __uint_as_float(ld_acquire_sys(src + 1));
+    }
+    atomicAdd(a.div, dd);
+    atomicAdd(a.div + 1, pp);
+  }
 }
 
 // ------------------------------------------------------------------ broadcast pull
-__global__ void __launch_bounds__(512) broadcast_pull_kernel(FusedArgs a, Handles h) {
-  uint32_t* sig = h.sig[a.rank];
-  const uint32_t epoch = announce(h, a.rank, a.world, a.bucket, sig);
-  const uint64_t limit = a.timeout_ns;
-  if (!wait_all_ready(h, a.world, a.bucket, epoch, sig, limit, a.err)) {
-    end_launch(a.bucket, sig);
-    return;
-  }
-  const int64_t n4 = (a.end - a.start) / 4;
+__global__ void __launch_bounds__(512) broadcast_pull_kernel(const __grid_constant__ FusedArgs a,
+                                                 const __grid_constant__ Handles h) {
+  if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
+  const Shard sh(a);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (a.rank != a.root) {
     const float4* src = reinterpret_cast<const float4*>(h.data[a.root]);
     float4* dst = reinterpret_cast<float4*>(h.data[a.rank]);
-    for (int64_t i = a.start / 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-         i < a.start / 4 + n4; i += stride) {
-      const float4 v = __ldcg(src + i);
-      dst[i] = v;
-      if (h.shadow[a.rank]) {
-        uint2 sh;
-        sh.x = pack_bf16x2(v.x, v.y);
-        sh.y = pack_bf16x2(v.z, v.w);
-        reinterpret_cast<uint2*>(h.shadow[a.rank])[i] = sh;
+    uint2* shd = reinterpret_cast<uint2*>(h.shadow[a.rank]);
+    for (int64_t i0 = sh.b0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < sh.b1;
+         i0 += kIlp * stride) {
+      float4 v[kIlp];
+#pragma unroll
+      for (int j = 0; j < kIlp; ++j) {
+        const int64_t i = i0 + j * stride;
+        v[j] = i < sh.b1 ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < kIlp; ++j) {
+        const int64_t i = i0 + j * stride;
+        if (i < sh.b1) {
+          dst[i] = v[j];
+          if (shd) shd[i] = bf16x4(v[j]);
+        }
       }
     }
+  } else if (h.shadow[a.rank]) {
+    // the root refreshes its own shadow so every rank ends with the same bits
+    const float4* src = reinterpret_cast<const float4*>(h.data[a.rank]);
+    uint2* shd = reinterpret_cast<uint2*>(h.shadow[a.rank]);
+    for (int64_t i = sh.b0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < sh.b1; i += stride)
+      shd[i] = bf16x4(src[i]);
   }
   // the root must not change its buffer until everyone has pulled
-  finish_bucket(h, a.world, a.bucket, epoch, sig, limit, a.err);
-  end_launch(a.bucket, sig);
+  meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err);
 }
 
 }  // namespace
 
 cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, cudaStream_t st) {
-  if (a.world < 1 || a.world > kMaxRanks || a.bucket < 0 || a.bucket + 1 >= kMaxBuckets)
+  if (a.world < 1 || a.world > kMaxRanks || a.rank < 0 || a.rank >= a.world || a.bucket < 0 ||
+      a.bucket >= kMaxSlots)
     return cudaErrorInvalidValue;
   if ((a.start & 3) || (a.end & 3) || a.end < a.start) return cudaErrorInvalidValue;
+  if (a.threads != 128 && a.threads != 256 && a.threads != 512) return cudaErrorInvalidValue;
   Handles h;
   for (int p = 0; p < kMaxRanks; ++p) {
     h.data[p] = p < a.world ? ptrs.data[p] : nullptr;
@@ -558,29 +650,43 @@ cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, c
   }
   const int threads = a.threads;
   const void* fn = nullptr;
+  bool sharded = true;  // work per rank = one shard (false: the whole range)
   switch (op) {
-    case FusedOp::kArAdamW: fn = (const void*)fused_ar_adamw_kernel; break;
-    case FusedOp::kArSgd: fn = (const void*)fused_ar_sgd_kernel; break;
+    case FusedOp::kArAdamW: fn = (const void*)ar_update_kernel<AdamWUpdate>; break;
+    case FusedOp::kArSgd: fn = (const void*)ar_update_kernel<SgdUpdate>; break;
     case FusedOp::kAllReduce: fn = (const void*)all_reduce_kernel; break;
     case FusedOp::kWeightedAverage: fn = (const void*)weighted_average_kernel; break;
-    case FusedOp::kBroadcast: fn = (const void*)broadcast_pull_kernel; break;
+    case FusedOp::kBroadcast: fn = (const void*)broadcast_pull_kernel; sharded = false; break;
+    case FusedOp::kReduceScatter: fn = (const void*)reduce_scatter_kernel; break;
+    case FusedOp::kClipApplyAdamW: fn = (const void*)clip_apply_kernel<AdamWUpdate>; break;
+    case FusedOp::kClipApplySgd: fn = (const void*)clip_apply_kernel<SgdUpdate>; break;
   }
   if (fn == nullptr) return cudaErrorInvalidValue;
-  // Every block waits (bounded) for all blocks of all ranks, so the grid must
-  // be co-resident: cap it by the occupancy of this kernel (0 = the cap).
+  if ((op == FusedOp::kArAdamW || op == FusedOp::kClipApplyAdamW) && (!a.m || !a.v || !a.lr || !a.step))
+    return cudaErrorInvalidValue;
+  if ((op == FusedOp::kArSgd || op == FusedOp::kClipApplySgd) && !a.lr) return cudaErrorInvalidValue;
+  if ((op == FusedOp::kReduceScatter || op == FusedOp::kClipApplyAdamW ||
+       op == FusedOp::kClipApplySgd) && !a.sumsq)
+    return cudaErrorInvalidValue;
+  if ((op == FusedOp::kClipApplyAdamW || op == FusedOp::kClipApplySgd) && (!a.table || a.nb <= 0))
+    return cudaErrorInvalidValue;
+  if (a.oneshot) sharded = false;
+  // Blocks of a launch meet their counterparts on the peers, so the grid is
+  // kept co-resident: capped by the occupancy of this kernel.
   int per_sm = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
-  const int cap = per_sm * num_sms();
-  // default: enough blocks for about two float4 pairs per thread of this
-  // rank's shard (small messages: few blocks, less start/finish overhead)
-  const int64_t shard4 = ((a.end - a.start) / 4 + a.world - 1) / a.world;
-  const int64_t want = std::max<int64_t>(1, (shard4 + threads * kIlp * 2 - 1) / (threads * kIlp * 2));
-  int blocks = a.blocks > 0 ? std::min(a.blocks, cap) : (int)std::min<int64_t>(want, cap);
-  FusedArgs al = a;
-  al.blocks = blocks;
-  void* args[] = {(void*)&al, (void*)&h};
+  const int cap = std::min(kMaxBlocks, per_sm * num_sms());
+  // default: enough blocks for kIlp float4 per thread of this rank's work
+  int64_t work4 = (a.end - a.start) / 4;
+  if (op == FusedOp::kClipApplyAdamW || op == FusedOp::kClipApplySgd) work4 = 1 << 30;
+  if (sharded) work4 = (work4 + a.world - 1) / a.world;
+  const int64_t want = std::max<int64_t>(1, (work4 + (int64_t)threads * kIlp - 1) / ((int64_t)threads * kIlp));
+  // an explicit grid is an upper bound: small messages keep few blocks
+  const int64_t lim = a.blocks > 0 ? std::min(a.blocks, cap) : cap;
+  const int blocks = (int)std::min<int64_t>(want, lim);
+  void* args[] = {(void*)&a, (void*)&h};
   cudaError_t e = cudaLaunchKernel(fn, dim3(blocks), dim3(threads), args, 0, st);
   if (e != cudaSuccess) return e;
   note_launch();

@@ -65,9 +65,13 @@ struct CeArgs {
   float* loss = nullptr;                  // device scalar, accumulated mean loss
   __nv_bfloat16* dlogits = nullptr;       // [T, V] gradient of the mean loss (nullable)
   int ld_d = 0;                           // row pitch of dlogits (0: V)
+  uint32_t* err = nullptr;                // error word: kErrBadLabel for a target outside [0, V)
 };
-cudaError_t launch_ce_count(const int64_t* targets, int T, int64_t ignore_index, float* inv_count,
-                            float* loss_zero, cudaStream_t st);
+// inv_count = 1 / #rows whose target is in [0, V) (ignore_index and out-of-range
+// targets do not count; an out-of-range target that is not ignore_index also
+// records kErrBadLabel in *err).
+cudaError_t launch_ce_count(const int64_t* targets, int T, int V, int64_t ignore_index,
+                            float* inv_count, float* loss_zero, uint32_t* err, cudaStream_t st);
 cudaError_t launch_softmax_ce(const CeArgs& a, cudaStream_t st);
 
 // ------------------------------------------------------------- embedding

@@ -46,6 +46,7 @@ enum KernelError : uint32_t {
   kErrMbarTimeout = 1,
   kErrPeerTimeout = 2,
   kErrBadArgs = 3,
+  kErrBadLabel = 4,  // a class target outside [0, V) that is not ignore_index
 };
 
 __device__ __forceinline__ void report_error(uint32_t* err, uint32_t code) {

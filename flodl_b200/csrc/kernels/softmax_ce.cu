@@ -6,6 +6,9 @@
 // and its gradient dz = (softmax(z) - (1-eps) onehot(y) - eps/V) / N are both
 // produced here, so backward is a scale (by the upstream scalar) folded into
 // the consuming GEMMs. Rows whose target equals ignore_index contribute nothing.
+// A target outside [0, V) that is not ignore_index is never used as an index:
+// the row is skipped like an ignored one and kErrBadLabel is recorded in the
+// error word, which the host reads (the reference's cross-entropy raises).
 #include "sm100_ptx.cuh"
 #include "kernels.h"
 
@@ -39,11 +42,20 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
   return r;
 }
 
-__global__ void ce_count_kernel(const int64_t* __restrict__ targets, int T, int64_t ignore,
-                                float* inv_count, float* loss_zero) {
+__device__ __forceinline__ bool target_in_range(int64_t y, int V) { return y >= 0 && y < V; }
+
+__global__ void ce_count_kernel(const int64_t* __restrict__ targets, int T, int V, int64_t ignore,
+                                float* inv_count, float* loss_zero, uint32_t* err) {
   __shared__ float sh[32];
   float c = 0.f;
-  for (int i = threadIdx.x; i < T; i += blockDim.x) c += (targets[i] != ignore) ? 1.f : 0.f;
+  bool bad = false;
+  for (int i = threadIdx.x; i < T; i += blockDim.x) {
+    const int64_t y = targets[i];
+    if (y == ignore) continue;
+    if (target_in_range(y, V)) c += 1.f;
+    else bad = true;
+  }
+  if (bad) report_error(err, kErrBadLabel);
   float tot = block_reduce_sum(c, sh);
   if (threadIdx.x == 0) {
     *inv_count = tot > 0.f ? 1.f / tot : 0.f;
@@ -58,7 +70,8 @@ __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
     const __nv_bfloat16* z = a.logits + (size_t)t * a.ld;
     const int64_t y = a.targets[t];
-    const bool valid = (y != a.ignore_index);
+    // out-of-range targets were reported by the count kernel; skip the row
+    const bool valid = (y != a.ignore_index) && target_in_range(y, a.V);
     // pass 1: max and sum of logits
     float mx = -INFINITY, sz = 0.f;
     for (int j = threadIdx.x; j < a.V; j += kThreads) {
@@ -97,9 +110,10 @@ __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
 
 }  // namespace
 
-cudaError_t launch_ce_count(const int64_t* targets, int T, int64_t ignore_index, float* inv_count,
-                            float* loss_zero, cudaStream_t st) {
-  ce_count_kernel<<<1, kThreads, 0, st>>>(targets, T, ignore_index, inv_count, loss_zero);
+cudaError_t launch_ce_count(const int64_t* targets, int T, int V, int64_t ignore_index,
+                            float* inv_count, float* loss_zero, uint32_t* err, cudaStream_t st) {
+  ce_count_kernel<<<1, kThreads, 0, st>>>(targets, T, V, ignore_index, inv_count, loss_zero,
+                                          err ? err : default_err_word());
   note_launch();
   return cudaGetLastError();
 }

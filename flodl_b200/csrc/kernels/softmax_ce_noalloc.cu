@@ -24,10 +24,14 @@
 //    that device. Make that first call before any stream capture begins.
 //  * Every call on a device shares the same array and leaves the last call's
 //    contents in it. All scratch slots a call reads are written earlier in
-//    the same call (the count, then one loss per row, ignored rows as 0), so
-//    nothing has to start at zero. Calls that overlap on the GPU (different
-//    streams, or a second call launched before the first finished on another
-//    stream) race on the array; serialise them on one stream.
+//    the same call (the count and the bad-row count, then one loss per row,
+//    ignored rows as 0), so nothing has to start at zero.
+//  * A target outside [0, V) that is not ignore_index is never used as an
+//    index: that row is skipped like an ignored one and counted in scratch
+//    slot 1, which flodl_softmax_ce_noalloc_bad_rows reads back.
+//  * Calls that overlap on the GPU (different streams, or a second call
+//    launched before the first finished on another stream) race on the
+//    array; serialise them on one stream.
 //  * The mean loss is the deterministic sum of per-row losses (no atomics);
 //    dlogits (nullable) receives the gradient of the mean loss, as the
 //    regular entry point writes it.
@@ -38,17 +42,25 @@
 
 #include <mutex>
 
+#include "softmax_ce_noalloc.h"
+
 namespace {
 
 constexpr int kNoAllocMaxRows = 262144;  // rows (tokens) per call
-constexpr int kScratchHeader = 64;       // floats: [0] = 1/count, rest reserved
+constexpr int kScratchHeader = 64;       // floats: [0] = 1/count, [1] = bad rows (u32 bits)
 constexpr int kMaxDevices = 64;
 constexpr int kThreads = 256;
 
 static __device__ __align__(256) float g_ce_noalloc_scratch[kScratchHeader + kNoAllocMaxRows];
 
-float* g_scratch_ptr[kMaxDevices] = {nullptr};
+struct DeviceSetup {
+  float* scratch = nullptr;  // device address of g_ce_noalloc_scratch on this device
+  int sms = 0;               // multiprocessor count of this device
+};
+DeviceSetup g_setup[kMaxDevices];
 std::mutex g_setup_mu;
+
+__device__ __forceinline__ bool target_in_range(int64_t y, int V) { return y >= 0 && y < V; }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -80,14 +92,24 @@ __device__ float block_max(float v, float* sh) {
   return r;
 }
 
-// scratch[0] = 1 / number of rows whose target is not ignore_index
-__global__ void noalloc_count_kernel(const int64_t* __restrict__ targets, int T, int64_t ignore,
-                                     float* scratch) {
+// scratch[0] = 1 / number of rows whose target is in [0, V);
+// scratch[1] = number of rows whose target is out of range and not ignore_index
+__global__ void noalloc_count_kernel(const int64_t* __restrict__ targets, int T, int V,
+                                     int64_t ignore, float* scratch) {
   __shared__ float sh[32];
-  float c = 0.f;
-  for (int i = threadIdx.x; i < T; i += blockDim.x) c += (targets[i] != ignore) ? 1.f : 0.f;
+  float c = 0.f, bad = 0.f;
+  for (int i = threadIdx.x; i < T; i += blockDim.x) {
+    const int64_t y = targets[i];
+    if (y == ignore) continue;
+    if (target_in_range(y, V)) c += 1.f;
+    else bad += 1.f;
+  }
   const float tot = block_sum(c, sh);
-  if (threadIdx.x == 0) scratch[0] = tot > 0.f ? 1.f / tot : 0.f;
+  const float nbad = block_sum(bad, sh);
+  if (threadIdx.x == 0) {
+    scratch[0] = tot > 0.f ? 1.f / tot : 0.f;
+    reinterpret_cast<uint32_t*>(scratch)[1] = (uint32_t)nbad;
+  }
 }
 
 // scratch[kScratchHeader + t] = loss of row t / count (0 for ignored rows)
@@ -100,7 +122,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     const __nv_bfloat16* z = logits + (size_t)t * ld;
     const int64_t y = targets[t];
-    const bool valid = (y != ignore);
+    const bool valid = (y != ignore) && target_in_range(y, V);  // z[y] is read only when valid
     float mx = -INFINITY, sz = 0.f;
     for (int j = threadIdx.x; j < V; j += kThreads) {
       const float v = __bfloat162float(z[j]);
@@ -146,51 +168,48 @@ __global__ void noalloc_reduce_kernel(const float* __restrict__ scratch, int T, 
   if (threadIdx.x == 0) *loss_out = tot;
 }
 
-// Looks up (once per device) the device address of the scratch array.
-cudaError_t scratch_for_current_device(float** out) {
+// Looks up (once per device, with that device current) the device address of
+// the scratch array and the device's multiprocessor count.
+cudaError_t setup_for_current_device(DeviceSetup* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  DeviceSetup& s = g_setup[dev];
+  if (s.scratch == nullptr) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    if (sms <= 0) return cudaErrorInvalidDevice;
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
     if (e != cudaSuccess) return e;
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    s.sms = sms;
+    s.scratch = static_cast<float*>(p);
   }
-  *out = g_scratch_ptr[dev];
+  *out = s;
   return cudaSuccess;
 }
 
 }  // namespace
 
-#define FLODL_NOALLOC_ERR_TOO_MANY_ROWS (-1)
-#define FLODL_NOALLOC_ERR_BAD_ARGS (-2)
-
-// Fused softmax cross-entropy that allocates nothing.
-//   logits   : bf16 [T, V], row pitch `ld` elements (device)
-//   targets  : int64 [T] (device); rows equal to ignore_index are skipped
-//   loss_out : f32 scalar (device), receives the mean loss
-//   dlogits  : bf16 [T, V] contiguous (device) or NULL, receives d(mean loss)/dlogits
-//   stream   : CUDA stream to launch on (0 = legacy default stream)
-// Returns 0 on success, FLODL_NOALLOC_ERR_TOO_MANY_ROWS when T exceeds the
-// fixed scratch capacity (262144 rows), FLODL_NOALLOC_ERR_BAD_ARGS for invalid
-// sizes or null pointers, or a positive cudaError_t value.
+// Arguments and return codes: softmax_ce_noalloc.h. Returns 0 on success,
+// FLODL_NOALLOC_ERR_TOO_MANY_ROWS when T exceeds the fixed scratch capacity
+// (262144 rows), FLODL_NOALLOC_ERR_BAD_ARGS for invalid sizes or null
+// pointers, or a positive cudaError_t value.
 extern "C" __attribute__((visibility("default"))) int flodl_softmax_ce_noalloc(
     const void* logits, int ld, const int64_t* targets, int T, int V, int64_t ignore_index,
     float smoothing, float* loss_out, void* dlogits, cudaStream_t stream) {
   if (T <= 0 || V <= 0 || ld < V || !logits || !targets || !loss_out)
     return FLODL_NOALLOC_ERR_BAD_ARGS;
   if (T > kNoAllocMaxRows) return FLODL_NOALLOC_ERR_TOO_MANY_ROWS;
-  float* scratch = nullptr;
-  cudaError_t e = scratch_for_current_device(&scratch);
+  DeviceSetup dev;
+  cudaError_t e = setup_for_current_device(&dev);
   if (e != cudaSuccess) return (int)e;
-  noalloc_count_kernel<<<1, kThreads, 0, stream>>>(targets, T, ignore_index, scratch);
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = T < sms * 8 ? T : sms * 8;
+  float* scratch = dev.scratch;
+  noalloc_count_kernel<<<1, kThreads, 0, stream>>>(targets, T, V, ignore_index, scratch);
+  const int grid = T < dev.sms * 8 ? T : dev.sms * 8;
   noalloc_rows_kernel<<<grid, kThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(logits), ld, targets, T, V, ignore_index, smoothing,
       scratch, static_cast<__nv_bfloat16*>(dlogits));
@@ -200,6 +219,23 @@ extern "C" __attribute__((visibility("default"))) int flodl_softmax_ce_noalloc(
 }
 
 // Capacity of the fixed scratch array, in rows.
-extern "C" __attribute__((visibility("default"))) int flodl_softmax_ce_noalloc_max_rows() {
+extern "C" __attribute__((visibility("default"))) int flodl_softmax_ce_noalloc_max_rows(void) {
   return kNoAllocMaxRows;
+}
+
+// Bad-row count of the last call on the current device (scratch slot 1).
+extern "C" __attribute__((visibility("default"))) int flodl_softmax_ce_noalloc_bad_rows(
+    cudaStream_t stream, int* out) {
+  if (!out) return FLODL_NOALLOC_ERR_BAD_ARGS;
+  DeviceSetup dev;
+  cudaError_t e = setup_for_current_device(&dev);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return (int)e;
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, reinterpret_cast<const uint32_t*>(dev.scratch) + 1, sizeof(v),
+                 cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return (int)e;
+  *out = (int)v;
+  return 0;
 }

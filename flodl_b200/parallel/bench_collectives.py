@@ -6,9 +6,10 @@ lines. All times are CUDA-event device times, max over ranks.
 
 Modes:
 
-* ``sweep``     all-reduce (sum) of fp32 and bf16 buffers from 1 KiB to 1 GiB:
-                the peer-memory kernel (fp32) and NCCL (fp32, bf16); algorithmic
-                and bus bandwidth (2 (n-1)/n x bytes / time).
+* ``sweep``     all-reduce (sum) of fp32 and bf16 buffers from 4 KiB to 1 GiB:
+                the peer-memory kernel (fp32, two-shot and one-shot) and NCCL
+                (fp32, bf16); algorithmic and bus bandwidth (2 (n-1)/n x bytes
+                / time).
 * ``fused``     the fused gradient all-reduce + AdamW kernel on a parameter
                 arena the size of the LM benchmark (or ``--numel``), reported
                 against its NVLink roofline: each rank reads (n-1)/n of the f32
@@ -22,6 +23,7 @@ Modes:
                 rank did (the reference's realized-work mass), through the fused
                 weighted-average kernel (``--engine peer``) or NCCL
                 (``--engine nccl``: scale, all-reduce, divide).
+* ``avgkernel`` the weighted-average kernel alone against its NVLink roofline.
 """
 from __future__ import annotations
 
@@ -66,18 +68,25 @@ def _time(fn, iters, warmup, world):
 
 
 def sweep(rank, world, dev, args):
+    """Two-shot and one-shot peer all-reduce against NCCL. One-shot reads
+    every peer's whole buffer (world x the bytes of two-shot) and is timed up
+    to ``--oneshot-max-log2``."""
     from .peer import PeerComm
     max_bytes = 1 << args.max_log2
     comm = PeerComm(max_bytes // 4, dev, with_shadow=False, timeout_s=10.0)
     buf = torch.empty(max_bytes // 4, device=dev)
     buf16 = torch.empty(max_bytes // 2, device=dev, dtype=torch.bfloat16)
-    nb = 10
+    nb = args.min_log2
     while nb <= args.max_log2:
         nbytes = 1 << nb
         iters = 50 if nbytes <= (64 << 20) else 10
         n32 = max(nbytes // 4, 4)
         comm.grad[:n32].fill_(1.0)
         t_peer = _time(lambda: comm.all_reduce_(n32, average=False, slot=0), iters, 3, world)
+        t_one = None
+        if nb <= args.oneshot_max_log2:
+            t_one = _time(lambda: comm.all_reduce_(n32, average=False, slot=1, oneshot=True),
+                          iters, 3, world)
         comm.check()
         t_nccl = _time(lambda: dist.all_reduce(buf[:n32]), iters, 3, world)
         n16 = max(nbytes // 2, 8)
@@ -85,11 +94,16 @@ def sweep(rank, world, dev, args):
         if rank == 0:
             f = 2.0 * (world - 1) / world
             rec = {"mode": "sweep", "n_gpus": world, "bytes": nbytes}
-            for name, t in (("peer_f32", t_peer), ("nccl_f32", t_nccl), ("nccl_bf16", t_nccl16)):
+            for name, t in (("peer_f32", t_peer), ("peer_oneshot_f32", t_one),
+                            ("nccl_f32", t_nccl), ("nccl_bf16", t_nccl16)):
+                if t is None:
+                    continue
                 rec[name] = {"us": round(t * 1e3, 2), "algbw_gbs": round(nbytes / t / 1e6, 2),
                              "busbw_gbs": round(f * nbytes / t / 1e6, 2)}
+            best = min(t for t in (t_peer, t_one) if t is not None)
+            rec["peer_best_over_nccl"] = round(t_nccl / best, 3)
             print(json.dumps(rec), flush=True)
-        nb += 2
+        nb += args.step_log2
     comm.close()
 
 
@@ -113,8 +127,9 @@ def fused(rank, world, dev, args):
             s1 = min(n, s0 + per)
             if s0 >= s1:
                 break
-            comm.launch(C.FUSED_AR_ADAMW, bucket=2 * i, start=s0, end=s1, blocks=args.blocks,
-                        m=m, v=v, lr=lr, step=step, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.1)
+            comm.launch(C.FUSED_AR_ADAMW, bucket=i, start=s0, end=s1, blocks=args.blocks,
+                        m=m, v=v, lr=lr, step=step, beta1=0.9, beta2=0.999, eps=1e-8, wd=0.1,
+                        oneshot=int(args.oneshot))
 
     t = _time(run, 20, 3, world)
     comm.check()
@@ -124,7 +139,8 @@ def fused(rank, world, dev, args):
     target_ms = max(in_bytes, out_bytes) / (LINK_GBS * 1e9) * 1e3
     if rank == 0:
         print(json.dumps({"mode": "fused_allreduce_adamw", "n_gpus": world, "numel": n,
-                          "buckets": buckets, "us": round(t * 1e3, 2),
+                          "buckets": buckets, "oneshot": bool(args.oneshot),
+                          "us": round(t * 1e3, 2),
                           "nvlink_roofline_us": round(target_ms * 1e3, 2),
                           "frac_of_roofline": round(target_ms / t, 3) if world > 1 else None,
                           "link_gbs_assumed": LINK_GBS}), flush=True)
@@ -135,22 +151,19 @@ def averaging(rank, world, dev, args):
     from ..models import ResNet20
     from ..optim import SGD
     from ..utils.arena import ParamArena
+    from .config import AverageBackend
     torch.manual_seed(0)
     model = ResNet20(device=dev)
     params = list(model.parameters())
-    comm = None
+    avg = None
+    opt = SGD(params, lr=0.1, momentum=0.9, weight_decay=1e-4)
     if args.engine == "peer" and world > 1:
-        from .peer import PeerComm
-        numel = sum((p.numel() + 63) // 64 * 64 for p in params)
-        comm = PeerComm(numel, dev, timeout_s=10.0)
-        arena = ParamArena(params, alloc=comm.data_alloc, grad_alloc=comm.grad_alloc,
-                           with_shadow=False)
-        arena.shadow = comm.shadow[:arena.numel]
-        arena.rebind()
-        arena.refresh_shadow()
+        from .trainer import _Averager
+        # parameters and BatchNorm statistics averaged by one fused kernel
+        avg = _Averager(model, opt, AverageBackend.NCCL, rank, world, dev)
+        arena = avg.fused[1]
     else:
         arena = ParamArena(params)
-    opt = SGD(params, lr=0.1, momentum=0.9, weight_decay=1e-4)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(128, 3, 32, 32, device=dev, generator=g)
     y = torch.randint(0, 10, (128,), device=dev, generator=g)
@@ -160,7 +173,7 @@ def averaging(rank, world, dev, args):
         all_steps = [None] * world
         dist.all_gather_object(all_steps, local_steps)
         steps = all_steps
-    bufs = [b for b in model.buffers() if b.is_floating_point()]
+    bufs = [b for b in model.buffers() if b.dtype == torch.float32]
 
     def round_():
         for _ in range(local_steps):
@@ -171,20 +184,17 @@ def averaging(rank, world, dev, args):
         if world == 1:
             return
         mass = float(local_steps)
-        if comm is not None:
-            comm.weighted_average_(arena.numel, mass, 1.0, slot=0)
+        if avg is not None:
+            avg.average(local_steps)
         else:
-            arena.data.mul_(mass)
+            arena.data.mul_(mass / float(sum(steps)))
             dist.all_reduce(arena.data)
-            arena.data.div_(float(sum(steps)))
             arena.refresh_shadow()
-        for b in bufs:  # batch-norm running statistics, same weighting
-            b.mul_(mass / float(sum(steps)))
-            dist.all_reduce(b)
+            for b in bufs:  # batch-norm running statistics: mean over the ranks that moved
+                b.mul_(1.0 / world)
+                dist.all_reduce(b)
 
     t = _time(round_, args.rounds, 2, world)
-    if comm is not None:
-        comm.check()
     samples = 128 * sum(steps)
     if rank == 0:
         print(json.dumps({"mode": "averaging", "engine": args.engine if world > 1 else "none",
@@ -193,14 +203,46 @@ def averaging(rank, world, dev, args):
                           "samples_per_s": round(samples / (t / 1e3), 1),
                           "note": "device time per round (local steps + weighted average), max over ranks"}),
               flush=True)
-    if comm is not None:
-        comm.close()
+    if avg is not None:
+        avg.close()
+
+
+def avgkernel(rank, world, dev, args):
+    """The weighted-average kernel alone (parameters + an f32 buffer tail,
+    divergence partials on) against its NVLink roofline: rank r reads shard r
+    of every peer ((n-1)/n x 4 bytes per element) and writes the average and
+    its bf16 shadow into every peer ((n-1)/n x 6 bytes per element)."""
+    from .peer import PeerComm
+    n = (args.numel + 63) // 64 * 64
+    nbuf = 4096
+    comm = PeerComm(n + nbuf, dev, timeout_s=10.0)
+    comm.data.normal_()
+    div = torch.zeros(2, device=dev)
+
+    def run():
+        comm.weighted_average_(n + nbuf, float(1 + rank), slot=0, div=div, buf_start=n)
+
+    t = _time(run, 20, 3, world)
+    comm.check()
+    frac = (world - 1) / world
+    target_ms = frac * 6 * (n + nbuf) / (LINK_GBS * 1e9) * 1e3
+    if rank == 0:
+        print(json.dumps({"mode": "weighted_average_kernel", "n_gpus": world,
+                          "numel": n, "buffer_numel": nbuf, "us": round(t * 1e3, 2),
+                          "nvlink_roofline_us": round(target_ms * 1e3, 2),
+                          "frac_of_roofline": round(target_ms / t, 3) if world > 1 else None,
+                          "link_gbs_assumed": LINK_GBS}), flush=True)
+    comm.close()
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", default="sweep", choices=["sweep", "fused", "averaging"])
+    ap.add_argument("--mode", default="sweep", choices=["sweep", "fused", "averaging", "avgkernel"])
     ap.add_argument("--max-log2", type=int, default=30)
+    ap.add_argument("--min-log2", type=int, default=12)
+    ap.add_argument("--step-log2", type=int, default=2)
+    ap.add_argument("--oneshot-max-log2", type=int, default=24)
+    ap.add_argument("--oneshot", action="store_true")
     ap.add_argument("--numel", type=int, default=19_000_000)
     ap.add_argument("--buckets", type=int, default=4)
     ap.add_argument("--blocks", type=int, default=0)
@@ -208,7 +250,8 @@ def main():
     ap.add_argument("--rounds", type=int, default=10)
     args = ap.parse_args()
     rank, world, dev = _init()
-    {"sweep": sweep, "fused": fused, "averaging": averaging}[args.mode](rank, world, dev, args)
+    {"sweep": sweep, "fused": fused, "averaging": averaging,
+     "avgkernel": avgkernel}[args.mode](rank, world, dev, args)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -2,19 +2,28 @@
 
 ``FusedDdp(model, optimizer)`` re-homes the model's parameters, gradients and
 bf16 weight shadows into symmetric peer-mapped arenas, broadcasts rank 0's
-weights with the pull kernel, and cuts the arena into buckets in reverse
-parameter order. During backward, the fused ops report each parameter's
-gradient as complete; when a bucket is complete its fused kernel is launched on
-the communication stream (overlapping the rest of backward): reduce-scatter
-over NVLink, AdamW/SGD on this rank's shard, all-gather of the updated f32
-weights and bf16 shadows into every rank, gradient clear. ``finish()`` joins
-the communication stream; there is no separate ``optimizer.step()`` or
-``zero_grad()`` in this mode.
+weights with the pull kernel, and cuts the arena into buckets. During
+backward, the fused ops report each parameter's gradient as complete; when a
+bucket is complete its fused kernel is launched on the communication stream
+(overlapping the rest of backward): reduce-scatter over NVLink, AdamW/SGD on
+this rank's shard, all-gather of the updated f32 weights and bf16 shadows into
+every rank, gradient clear. Buckets below ``oneshot_kb`` run the one-shot form
+instead (every rank reduces the whole bucket and updates it locally: no
+all-gather, fewer bytes in flight, the lowest latency). ``finish()`` launches
+what is left and joins the communication stream; there is no separate
+``optimizer.step()`` or ``zero_grad()`` in this mode.
+
+With ``max_grad_norm`` the buckets only reduce-scatter their gradients (the
+average lands in this rank's shard, its sum of squares in an accumulator) and
+``finish()`` launches one apply kernel that exchanges the partial sums, takes
+the global norm, scales by ``max_norm / (norm + 1e-6)`` when the norm is above
+``max_norm`` (the reference's ``clip_grad_norm``, flodl-sys/ops_training.cpp:
+948-985) and then updates and all-gathers every bucket.
 
 Semantics equal the reference's ``Ddp::wrap`` + ``all_reduce_gradients`` (Avg)
 + ``optimizer.step()`` (flodl/src/distributed/ddp.rs:249-260): every rank ends
-the step with identical parameters. Optimizer moments are held only for the
-shard each rank owns (the other ranks' slices of m/v stay unused).
+the step with identical parameters. Optimizer moments of a two-shot bucket are
+held only for the shard each rank owns (the other ranks' slices stay unused).
 """
 from __future__ import annotations
 
@@ -35,17 +44,23 @@ class FusedDdp:
 
     def __init__(self, model: torch.nn.Module, optimizer, bucket_mb: Optional[float] = None,
                  blocks: int = 0, group=None, timeout_s: float = 10.0,
-                 overlap_threads: Optional[int] = None, overlap_blocks: Optional[int] = None):
+                 overlap_threads: Optional[int] = None, overlap_blocks: Optional[int] = None,
+                 oneshot_kb: Optional[float] = None, tail_mb: Optional[float] = None,
+                 max_grad_norm: Optional[float] = None):
         # tuning knobs (constructor arguments win over the environment):
-        #   FLODL_DDP_BUCKET_MB        bucket size in MiB of f32 gradients (64)
+        #   FLODL_DDP_BUCKET_MB        bucket size in MiB of f32 gradients (16)
+        #   FLODL_DDP_TAIL_MB          size of the bucket holding the first parameters,
+        #                              which completes last in backward (2)
+        #   FLODL_DDP_ONESHOT_KB       buckets up to this size run the one-shot form (1024)
         #   FLODL_DDP_OVERLAP_THREADS  threads per CTA of in-backward launches (256)
         #   FLODL_DDP_OVERLAP_BLOCKS   CTAs of in-backward launches (0: two per SM)
-        # Measured on the 19M-parameter LM (B200, NVSwitch): 64 MiB buckets of
-        # 256-thread CTAs, two per SM, beat smaller buckets at 2 and 8 GPUs;
-        # 128-thread grids overlap with backward but move too few bytes.
         env = os.environ
         if bucket_mb is None:
-            bucket_mb = float(env.get("FLODL_DDP_BUCKET_MB", "64"))
+            bucket_mb = float(env.get("FLODL_DDP_BUCKET_MB", "16"))
+        if tail_mb is None:
+            tail_mb = float(env.get("FLODL_DDP_TAIL_MB", "2"))
+        if oneshot_kb is None:
+            oneshot_kb = float(env.get("FLODL_DDP_ONESHOT_KB", "1024"))
         if overlap_threads is None:
             overlap_threads = int(env.get("FLODL_DDP_OVERLAP_THREADS", "256"))
         if overlap_blocks is None:
@@ -72,6 +87,8 @@ class FusedDdp:
         self.blocks = blocks
         self.overlap_threads = overlap_threads
         self.overlap_blocks = overlap_blocks or 2 * self.comm.C.num_sms()
+        self.oneshot_elems = int(oneshot_kb * 1024 / 4)
+        self.max_grad_norm = float(max_grad_norm) if max_grad_norm else 0.0
         # optimizer state (device scalars + moments) for the whole arena
         optimizer._device_scalars(self.group)
         self.kind = "adamw" if isinstance(optimizer, Adam) else "sgd" if isinstance(optimizer, SGD) else None
@@ -84,7 +101,12 @@ class FusedDdp:
             # step_t holds the number of the update the next bucket kernels apply
             self.comm.C.add_scalar(self.group.step_t, 1.0)
         self.comm_stream = torch.cuda.Stream(self.device)
-        self._build_buckets(bucket_mb)
+        self._build_buckets(bucket_mb, tail_mb)
+        if self.max_grad_norm:
+            self.sumsq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            self.grad_norm = torch.zeros(1, dtype=torch.float32, device=self.device)
+            self.table = torch.tensor([[b["start"], b["end"]] for b in self.buckets],
+                                      dtype=torch.int64, device=self.device)
         for p in params:
             clear_grad_ready_listeners(p)
             add_grad_ready_listener(p, self._on_ready)
@@ -99,32 +121,42 @@ class FusedDdp:
                     dist.broadcast(b, src=0)
         self._launched: set = set()
 
-    def _build_buckets(self, bucket_mb: float) -> None:
+    def _build_buckets(self, bucket_mb: float, tail_mb: float) -> None:
+        """Buckets over the arena in forward parameter order: the first
+        (holding the earliest parameters, whose gradients complete last) is
+        capped at ``tail_mb``, the others at ``bucket_mb``; they launch in
+        reverse order as backward completes them."""
         a = self.arena
-        cap = int(bucket_mb * (1 << 20) / 4)
-        order = list(range(len(a.params)))[::-1]
+        caps = (int(tail_mb * (1 << 20) / 4), int(bucket_mb * (1 << 20) / 4))
+        groups: List[List[int]] = []
+        cur, size = [], 0
+        for i in range(len(a.params)):
+            n = a.params[i].numel()
+            cap = caps[0] if not groups else caps[1]
+            if cur and size + n > cap:
+                groups.append(cur)
+                cur, size = [], 0
+            cur.append(i)
+            size += n
+        if cur:
+            groups.append(cur)
         self.buckets: List[dict] = []
         self._bucket_of: Dict[int, dict] = {}
-        cur, size = [], 0
-        for i in order:
-            cur.append(i)
-            size += a.params[i].numel()
-            if size >= cap:
-                self._close(cur)
-                cur, size = [], 0
-        if cur:
-            self._close(cur)
-        self._slot_bcast = 2 * len(self.buckets)
-        self._slot_avg = self._slot_bcast + 2
-        if self._slot_avg + 2 >= self.comm.C.MAX_BUCKETS:
+        for idx in reversed(groups):
+            self._close(idx)
+        self._slot_bcast = len(self.buckets)
+        self._slot_avg = self._slot_bcast + 1
+        self._slot_apply = self._slot_bcast + 2
+        if self._slot_apply >= self.comm.C.MAX_SLOTS:
             raise ValueError("too many buckets; raise bucket_mb")
 
     def _close(self, idx: List[int]) -> None:
         a = self.arena
         start = min(a.offsets[i] for i in idx)
         end = max(a.offsets[i] + ((a.params[i].numel() + 63) // 64) * 64 for i in idx)
-        b = {"slot": 2 * len(self.buckets), "start": start, "end": end,
-             "params": [a.params[i] for i in idx], "pending": len(idx)}
+        b = {"slot": len(self.buckets), "start": start, "end": end,
+             "params": [a.params[i] for i in idx], "pending": len(idx),
+             "oneshot": (end - start) <= self.oneshot_elems and not self.max_grad_norm}
         self.buckets.append(b)
         for i in idx:
             self._bucket_of[id(a.params[i])] = b
@@ -137,6 +169,16 @@ class FusedDdp:
         if b["pending"] == 0:
             self._launch(b)
 
+    def _update_args(self) -> dict:
+        g = self.group
+        h = g.hyper
+        if self.kind == "adamw":
+            return dict(m=g.m, v=g.v, lr=g.lr_t, step=g.step_t, gscale=self.opt.gscale_t,
+                        beta1=h["beta1"], beta2=h["beta2"], eps=h["eps"], wd=h["weight_decay"])
+        return dict(m=g.buf, lr=g.lr_t, first=g.first_t, gscale=self.opt.gscale_t,
+                    wd=h["weight_decay"], momentum=h["momentum"], dampening=h["dampening"],
+                    nesterov=int(h["nesterov"]))
+
     def _launch(self, b, tail: bool = False) -> None:
         """Launch bucket b's fused kernel on the communication stream. Buckets
         that complete during backward run a grid of small CTAs that fits beside
@@ -144,24 +186,19 @@ class FusedDdp:
         tail launched by finish() takes the full grid."""
         cur = torch.cuda.current_stream(self.device)
         self.comm_stream.wait_stream(cur)
-        g = self.group
-        h = g.hyper
         if tail:
             geo = {"blocks": self.blocks, "threads": 512}
         else:
             geo = {"blocks": self.overlap_blocks, "threads": self.overlap_threads}
+        C = self.comm.C
         with torch.cuda.stream(self.comm_stream):
-            if self.kind == "adamw":
-                self.comm.launch(self.comm.C.FUSED_AR_ADAMW, bucket=b["slot"], start=b["start"],
-                                 end=b["end"], m=g.m, v=g.v, lr=g.lr_t,
-                                 step=g.step_t, gscale=self.opt.gscale_t, beta1=h["beta1"],
-                                 beta2=h["beta2"], eps=h["eps"], wd=h["weight_decay"], **geo)
+            if self.max_grad_norm:
+                self.comm.launch(C.FUSED_REDUCE_SCATTER, bucket=b["slot"], start=b["start"],
+                                 end=b["end"], sumsq=self.sumsq, gscale=self.opt.gscale_t, **geo)
             else:
-                self.comm.launch(self.comm.C.FUSED_AR_SGD, bucket=b["slot"], start=b["start"],
-                                 end=b["end"], m=g.buf, lr=g.lr_t,
-                                 first=g.first_t, gscale=self.opt.gscale_t, wd=h["weight_decay"],
-                                 momentum=h["momentum"], dampening=h["dampening"],
-                                 nesterov=int(h["nesterov"]), **geo)
+                op = C.FUSED_AR_ADAMW if self.kind == "adamw" else C.FUSED_AR_SGD
+                self.comm.launch(op, bucket=b["slot"], start=b["start"], end=b["end"],
+                                 oneshot=int(b["oneshot"]), **self._update_args(), **geo)
         self._launched.add(b["slot"])
 
     def finish(self) -> None:
@@ -169,6 +206,16 @@ class FusedDdp:
         for b in self.buckets:
             if b["slot"] not in self._launched:
                 self._launch(b, tail=True)
+        if self.max_grad_norm:
+            C = self.comm.C
+            op = C.FUSED_CLIP_APPLY_ADAMW if self.kind == "adamw" else C.FUSED_CLIP_APPLY_SGD
+            args = self._update_args()
+            args.pop("gscale", None)  # the buckets already applied it
+            with torch.cuda.stream(self.comm_stream):
+                self.comm.launch(op, bucket=self._slot_apply, start=0, end=0, sumsq=self.sumsq,
+                                 norm_out=self.grad_norm, max_norm=self.max_grad_norm,
+                                 table=self.table, nb=len(self.buckets), blocks=self.blocks,
+                                 threads=512, **args)
         torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
         if self.kind == "adamw":
             self.comm.C.add_scalar(self.group.step_t, 1.0)
@@ -180,9 +227,10 @@ class FusedDdp:
 
     all_reduce_gradients = finish
 
-    def average_params(self, mass: float = 1.0, gamma: float = 1.0) -> None:
-        """Weighted parameter average across ranks (cluster averaging)."""
-        self.comm.weighted_average_(self.arena.numel, mass, gamma, slot=self._slot_avg,
+    def average_params(self, mass: float = 1.0) -> None:
+        """Weighted parameter average across ranks (cluster averaging);
+        ``mass`` is this rank's gamma-mass."""
+        self.comm.weighted_average_(self.arena.numel, mass, slot=self._slot_avg,
                                     blocks=self.blocks)
 
     def close(self) -> None:

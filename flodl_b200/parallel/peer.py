@@ -117,21 +117,35 @@ class PeerComm:
         if code:
             raise PeerTimeout(f"peer communicator: {ERR_NAMES.get(code, code)} on rank {self.rank}")
 
-    def all_reduce_(self, n: int, average: bool = True, slot: int = 0, blocks: int = 0) -> None:
-        """In-place all-reduce of grad[:n] (uses data[:n] as scratch)."""
+    def all_reduce_(self, n: int, average: bool = True, slot: int = 0, blocks: int = 0,
+                    oneshot: bool = False, threads: int = 512) -> None:
+        """In-place all-reduce of grad[:n]. The one-shot form reads every
+        peer's whole range and uses data[:n] as scratch."""
         self.launch(self.C.FUSED_ALL_REDUCE, bucket=slot, start=0, end=(n + 3) // 4 * 4,
-                    average=int(average), blocks=blocks)
+                    average=int(average), blocks=blocks, oneshot=int(oneshot), threads=threads)
 
     def broadcast_(self, n: int, root: int = 0, slot: int = 0, blocks: int = 0) -> None:
         """Every rank pulls data[:n] (and refreshes its bf16 shadow) from ``root``."""
         self.launch(self.C.FUSED_BROADCAST, bucket=slot, start=0, end=(n + 3) // 4 * 4, root=root,
                     blocks=blocks)
 
-    def weighted_average_(self, n: int, mass: float, gamma: float = 1.0, slot: int = 0,
-                          divergence: Optional[torch.Tensor] = None, blocks: int = 0) -> None:
-        """data[:n] <- sum_i (mass_i^gamma / sum mass^gamma) data_i[:n]."""
+    def weighted_average_(self, n: int, mass: float, slot: int = 0,
+                          div: Optional[torch.Tensor] = None, blocks: int = 0,
+                          mover: Optional[float] = None, buf_start: int = -1) -> None:
+        """Cluster averaging over data[:n] (flodl/src/distributed/ddp_run/worker/
+        sync.rs:130-236): data[:buf_start] <- sum_i (mass_i / sum mass) data_i
+        (``mass`` is this rank's gamma-mass n^gamma, 0 for an idle rank) and
+        data[buf_start:n] (f32 buffers) <- mean over the ranks that did work
+        (``mover``, default 1 if mass > 0). Nothing changes when no rank did
+        work. ``div`` (f32 [2], zeroed by the caller) receives this rank's
+        ||pre - post||^2 and ||post||^2 over the parameter part."""
+        if mover is None:
+            mover = 1.0 if mass > 0 else 0.0
+        if buf_start >= 0 and buf_start % 4:
+            raise ValueError("buf_start must be a multiple of 4 elements")
         self.launch(self.C.FUSED_WEIGHTED_AVG, bucket=slot, start=0, end=(n + 3) // 4 * 4,
-                    mass=float(mass), gamma=float(gamma), m=divergence, blocks=blocks)
+                    mass=float(mass), mover=float(mover), buf_start=int(buf_start), div=div,
+                    blocks=blocks)
 
     def close(self) -> None:
         if self.closed:

@@ -7,8 +7,9 @@ trainer auto-promotes to one process per GPU; each rank owns a model and
 optimizer replica and trains on its shard of the data. Averaging follows the
 ``ElCheMode``:
 
-* Sync:    every rank steps its optimizer, then parameters (and f32 buffers)
-           are averaged every window of one step.
+* Sync:    every rank steps its optimizer, then parameters (work-weighted)
+           and f32 buffers (mean over the ranks that moved) are averaged
+           every window of one step.
 * Cadence: rank r runs ``batch_counts[r]`` steps per window (ElChe balances
            the counts from measured ms/batch and the averaging overhead), then
            the work-weighted average ``sum_r n_r^gamma W_r / sum n^gamma``.
@@ -83,30 +84,46 @@ def _unflat_(params, flat: torch.Tensor) -> None:
 
 
 class _Averager:
-    """Weighted parameter average across ranks for one replica."""
+    """Weighted parameter (and f32 buffer) average across ranks for one replica.
+
+    Parameters are averaged with the work mass n^gamma of each rank; f32
+    buffers (BatchNorm running statistics and the like) with equal weight over
+    the ranks that did any work, as the reference's buffer round does
+    (flodl/src/distributed/ddp_run/worker/sync.rs:214-226). When no rank did
+    any work nothing changes. On CUDA both rounds are one fused peer-memory
+    kernel whose divergence partials come back with the result; on CPU ranks
+    they are gloo all-reduces (or the CPU reducer's rounds). ``easgd_alpha``
+    blends the consensus into the local replica, ``(1 - a) local + a center``
+    (the CpuAsync load, worker/sync.rs:451), instead of overwriting it."""
 
     def __init__(self, model, opt, backend: AverageBackend, rank: int, world: int, device,
-                 cpu_client=None, gamma: float = 1.0):
+                 cpu_client=None, gamma: float = 1.0, easgd_alpha: Optional[float] = None):
         self.model, self.opt = model, opt
         self.backend, self.rank, self.world = backend, rank, world
         self.device = device
         self.params = [p for p in model.parameters()]
+        self.buffers = [b for b in model.buffers() if b.dtype == torch.float32]
         self.cpu = cpu_client
         self.gamma = gamma
+        self.alpha = easgd_alpha
         self.fused = None
         self.round = 0
         if backend == AverageBackend.NCCL and device.type == "cuda" and world > 1:
-            from ..utils.arena import ParamArena, arena_of
+            from ..utils.arena import ParamArena
             from .peer import PeerComm
 
-            numel = sum((p.numel() + 63) // 64 * 64 for p in self.params)
-            comm = PeerComm(numel, device)
+            nparam = sum((p.numel() + 63) // 64 * 64 for p in self.params)
+            self.nbuf = sum(b.numel() for b in self.buffers)
+            comm = PeerComm(nparam + (self.nbuf + 63) // 64 * 64, device)
             arena = ParamArena(self.params, alloc=comm.data_alloc, grad_alloc=comm.grad_alloc,
                                with_shadow=False)
             arena.shadow = comm.shadow[:arena.numel]
             arena.rebind()
             arena.refresh_shadow()
             self.fused = (comm, arena)
+            self.buf_start = arena.numel
+            self.buf_view = comm.data[self.buf_start:self.buf_start + self.nbuf]
+            self.div = torch.zeros(2, dtype=torch.float32, device=device)
             for g in opt.groups:
                 if all(any(q is p for q in arena.params) for p in g.params) and len(opt.groups) == 1:
                     g.arena = arena
@@ -116,29 +133,68 @@ class _Averager:
             return self.fused[1].data.clone()
         return _flat(self.params)
 
+    def _buffers_flat(self) -> Optional[torch.Tensor]:
+        if not self.buffers:
+            return None
+        return torch.cat([b.detach().reshape(-1) for b in self.buffers])
+
+    def _load_buffers(self, flat: torch.Tensor) -> None:
+        off = 0
+        with torch.no_grad():
+            for b in self.buffers:
+                n = b.numel()
+                b.copy_(flat[off:off + n].view_as(b))
+                off += n
+
     def average(self, batches: int) -> float:
-        """Average parameters weighted by this rank's work; returns divergence."""
+        """Average with this rank's work; returns ||pre - post|| / ||post||."""
         mass = realized_mass(batches, self.gamma)
+        mover = 1.0 if batches > 0 else 0.0
         self.round += 1
         if self.world == 1:
             return 0.0
         if self.fused is not None:
             comm, arena = self.fused
-            pre = arena.data.clone()
-            comm.weighted_average_(arena.numel, mass, 1.0, slot=0)
-            torch.cuda.synchronize(self.device)
+            n = arena.numel
+            if self.buffers:
+                with torch.no_grad():
+                    self.buf_view.copy_(self._buffers_flat())
+                n = self.buf_start + self.nbuf
+            self.div.zero_()
+            comm.weighted_average_(n, mass, slot=0, div=self.div, mover=mover,
+                                   buf_start=self.buf_start if self.buffers else -1)
+            if self.buffers:
+                self._load_buffers(self.buf_view)
+            d2, p2 = self.div.tolist()  # synchronises
             comm.check()
-            return divergence(pre, arena.data)
+            return (d2 ** 0.5) / max(p2 ** 0.5, 1e-12)
         pre = _flat(self.params)
+        bpre = self._buffers_flat()
         if self.backend == AverageBackend.CPU and self.cpu is not None:
-            post = self.cpu.all_reduce_scaled(pre.cpu(), mass, self.round).to(pre.device)
+            post = self.cpu.all_reduce_scaled(pre.cpu(), mass, 2 * self.round).to(pre.device)
+            bpost = (self.cpu.all_reduce_scaled(bpre.cpu(), mover, 2 * self.round + 1).to(bpre.device)
+                     if bpre is not None else None)
         else:
-            num = pre * mass
-            m = torch.tensor([mass], dtype=torch.float32, device=pre.device)
+            tot = torch.tensor([mass, mover], dtype=torch.float64, device=pre.device)
+            dist.all_reduce(tot)
+            if float(tot[0]) <= 0.0:
+                return 0.0  # nobody moved: the consensus already holds
+            num = pre * (mass / float(tot[0]))
             dist.all_reduce(num)
-            dist.all_reduce(m)
-            post = num / m.clamp_min(1e-30)
+            post = num
+            bpost = None
+            if bpre is not None:
+                bnum = bpre * (mover / float(tot[1]))
+                dist.all_reduce(bnum)
+                bpost = bnum
+        if self.alpha is not None:
+            a = float(self.alpha)
+            post = (1.0 - a) * pre + a * post
+            if bpost is not None:
+                bpost = (1.0 - a) * bpre + a * bpost
         _unflat_(self.params, post)
+        if bpost is not None:
+            self._load_buffers(bpost)
         return divergence(pre, post)
 
     def broadcast_initial(self) -> None:
@@ -147,7 +203,7 @@ class _Averager:
         if self.fused is not None:
             comm, arena = self.fused
             torch.cuda.synchronize(self.device)
-            comm.broadcast_(arena.numel, root=0, slot=4)
+            comm.broadcast_(arena.numel, root=0, slot=1)
             torch.cuda.synchronize(self.device)
             comm.check()
         else:
@@ -220,7 +276,10 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
         from .bundle import load_bundle
         meta = load_bundle(cfg.resume_from_, model, opt)
         start_epoch, global_step = meta.epoch + 1, meta.global_step
-    avg = _Averager(model, opt, backend, rank, world, device, cpu_client, ec.gamma_)
+    # CpuAsync blends the consensus into each replica (EASGD); every other
+    # mode overwrites with it (config.rs:283-313)
+    alpha = ec.easgd_alpha_ if policy == ApplyPolicy.ASYNC else None
+    avg = _Averager(model, opt, backend, rank, world, device, cpu_client, ec.gamma_, alpha)
     avg.broadcast_initial()
     sampler = DistributedSampler(rank, world, seed=spec.get("seed", 0))
     loader = (DataLoader.from_dataset(spec["dataset"]).batch_size(cfg.batch_size_).device(device)
@@ -289,8 +348,6 @@ def _train_rank(rank, world, device, key, spec) -> TrainedState:
                 break
             s0 = time.perf_counter()
             div = avg.average(done)
-            if policy == ApplyPolicy.ASYNC:
-                pass  # consensus already loaded; EASGD blend happens in the backend below
             sync_ms = (time.perf_counter() - s0) * 1e3
             st.syncs += 1
             st.divergence.append(div)

@@ -124,6 +124,72 @@ def test_flash_attention_padding_mask():
     torch.testing.assert_close(qkv.grad.float(), qr.grad, rtol=5e-2, atol=5e-2)
 
 
+def _attn_ref_chunked(qkv, dout, B, S, H, causal, key_pad=None, chunk=8):
+    """fp32 attention output and input gradient, computed batch chunk by batch
+    chunk so the [B, H, S, S] score tensors stay small."""
+    outs, grads = [], []
+    for b0 in range(0, B, chunk):
+        b1 = min(B, b0 + chunk)
+        q = qkv[b0 * S:b1 * S].detach().float().requires_grad_()
+        kp = None if key_pad is None else key_pad[b0:b1]
+        o = _attn_ref(q, b1 - b0, S, H, causal, kp)
+        o.backward(dout[b0 * S:b1 * S].float())
+        outs.append(o.detach())
+        grads.append(q.grad)
+    return torch.cat(outs), torch.cat(grads)
+
+
+@pytest.mark.parametrize("B,S,H,causal,padded", [(64, 256, 8, True, False), (32, 512, 12, False, True)])
+def test_flash_attention_production_shapes(B, S, H, causal, padded):
+    """The LM (B64 H8 S256 causal) and BERT (B32 H12 S512, padding mask) shapes:
+    hundreds of work items per launch, so every CTA of the persistent kernels
+    walks several items (item-parity buffers, next-item K/V prefetch and the
+    heaviest-first order all run)."""
+    torch.manual_seed(11)
+    from flodl_b200.ops.attention import attention_packed
+    D = 64
+    items = B * H * ((S + 127) // 128)
+    assert items >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16().requires_grad_()
+    pad = None
+    if padded:
+        lens = torch.randint(S // 4, S + 1, (B,), device="cuda")
+        lens[0] = S
+        pad = torch.arange(S, device="cuda")[None, :] >= lens[:, None]
+    out = attention_packed(qkv, B, S, H, causal, pad)
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    ref_out, ref_grad = _attn_ref_chunked(qkv, dout, B, S, H, causal, pad)
+    torch.testing.assert_close(out.float(), ref_out, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(qkv.grad.float(), ref_grad, rtol=5e-2, atol=5e-2)
+
+
+def test_softmax_ce_out_of_range_target_reports_error():
+    """A target outside [0, V) is skipped (never read as an index) and recorded
+    as kErrBadLabel (4) in the kernel error word."""
+    torch.manual_seed(12)
+    C = _C()
+    from flodl_b200.ops.loss import cross_entropy
+    T, V = 300, 50
+    logits = torch.randn(T, V, device="cuda").bfloat16()
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    tgt[5] = V
+    tgt[T - 1] = 1 << 40
+    torch.cuda.synchronize()
+    C.clear_kernel_error()
+    loss = cross_entropy(logits, tgt)
+    torch.cuda.synchronize()
+    assert C.kernel_error() == 4
+    C.clear_kernel_error()
+    ref_t = tgt.clone()
+    ref_t[[5, T - 1]] = -100
+    ref = F.cross_entropy(logits.float(), ref_t, ignore_index=-100)
+    torch.testing.assert_close(loss, ref, rtol=1e-4, atol=1e-4)
+    cross_entropy(logits, ref_t)
+    torch.cuda.synchronize()
+    assert C.kernel_error() == 0
+
+
 def test_adamw_kernel_matches_torch():
     torch.manual_seed(5)
     C = _C()

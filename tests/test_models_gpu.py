@@ -54,6 +54,26 @@ def test_transformer_lm_fused_matches_fp32(S, causal):
     _compare(gpu, cpu, lg, lc, loss_tol=2e-2, grad_tol=4e-2)
 
 
+def test_transformer_lm_bench_width_matches_fp32():
+    """The benchmarked LM width (6 layers, d512, 8 heads, d_ff 2048, S 256)
+    against the fp32 CPU model: loss and every parameter gradient."""
+    from flodl_b200.models import TransformerLM
+
+    torch.manual_seed(0)
+    cpu = TransformerLM(vocab_size=256, d_model=512, n_layers=6, n_heads=8, d_ff=2048,
+                        max_seq=256, causal=True)
+    gpu = copy.deepcopy(cpu)
+    gpu.move_to_device(torch.device("cuda"))
+    ids = torch.randint(0, 256, (4, 256))
+    tgt = torch.randint(0, 256, (4, 256))
+    lc = cpu.loss(ids, tgt)
+    lc.backward()
+    lg = gpu.loss(ids.cuda(), tgt.cuda())
+    lg.backward()
+    torch.cuda.synchronize()
+    _compare(gpu, cpu, lg, lc, loss_tol=2e-2, grad_tol=5e-2)
+
+
 def test_bert_mlm_fused_matches_fp32():
     from flodl_b200.models.bert import BertConfig, BertForMaskedLM
 

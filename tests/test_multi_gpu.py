@@ -1,8 +1,17 @@
-"""Peer-memory collectives and fused DDP on 2+ GPUs of one node.
+"""Peer-memory collectives and fused DDP on 2, 4 and 8 GPUs of one node.
 
 Each test spawns one process per GPU (NCCL bootstrap on 127.0.0.1, NVLS off
-so no rank ever binds memory to a multicast object). Skipped when fewer than
-two GPUs are visible.
+so no rank ever binds memory to a multicast object) and is skipped, with the
+reason, when fewer GPUs are visible. Every result is checked against NCCL or
+against a single-GPU run of the same model on the full batch.
+
+Covered: two-shot and one-shot all-reduce at sizes that are not multiples of
+world x 4, broadcast from a non-zero root, the weighted average with a
+gamma-mass, an idle rank, an f32 buffer part averaged over the ranks that
+moved, the divergence partials, and the all-idle no-op; fused DDP with AdamW
+and SGD over at least three buckets that mix the one-shot and two-shot forms,
+the bf16 shadow after the all-gather, global-norm clipping, and a
+CUDA-graph-captured step against the eager one.
 """
 import os
 import socket
@@ -12,6 +21,8 @@ import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
+
+WORLDS = [2, 4, 8]
 
 
 def _free_port():
@@ -27,7 +38,7 @@ def _need_gpus(n=2):
         pytest.skip(f"needs {n} GPUs (have {torch.cuda.device_count()})")
 
 
-def _collect(q, procs, world, timeout=240.0):
+def _collect(q, procs, world, timeout=300.0):
     """Results from every worker; fails fast if a worker died without one."""
     import queue
     import time
@@ -48,6 +59,19 @@ def _collect(q, procs, world, timeout=240.0):
     return out
 
 
+def _spawn(target, world, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(_collect(q, procs, world), key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
 def _init(rank, world, port):
     import datetime
     from flodl_b200.utils.crash import install_crash_handler
@@ -56,137 +80,223 @@ def _init(rank, world, port):
 
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
 
 
+# ----------------------------------------------------------------------------- collectives
 def _collectives_worker(rank, world, port, q):
     import torch.distributed as dist
 
+    from flodl_b200.parallel.convergence import realized_mass
     from flodl_b200.parallel.peer import PeerComm
 
+    checks = {}
     try:
         _init(rank, world, port)
-        n = 1 << 20
-        comm = PeerComm(n, torch.device("cuda", rank), timeout_s=5.0)
-        g = torch.Generator(device="cuda").manual_seed(rank)
-        x = torch.randn(n, device="cuda", generator=g)
-        comm.grad[:n].copy_(x)
-        ref = x.clone()
-        dist.all_reduce(ref)
-        comm.all_reduce_(n, average=False, slot=0)
+        dev = torch.device("cuda", rank)
+        nmax = (1 << 20) + 36
+        comm = PeerComm(nmax + 64, dev, timeout_s=5.0)
+        slot = 0
+        for n in (1000, 4096 + 12, nmax):
+            for oneshot in (False, True):
+                g = torch.Generator(device="cuda").manual_seed(1000 * rank + n)
+                x = torch.randn(n, device="cuda", generator=g)
+                comm.grad[:n].copy_(x)
+                ref = x.clone()
+                dist.all_reduce(ref)
+                comm.all_reduce_(n, average=False, slot=slot, oneshot=oneshot)
+                slot += 1
+                torch.cuda.synchronize()
+                comm.check()
+                checks[f"allreduce n={n} oneshot={oneshot}"] = bool(
+                    torch.allclose(comm.grad[:n], ref, atol=1e-4, rtol=1e-5))
+        # broadcast from the last rank; the shadow follows the pulled weights
+        n = nmax
+        comm.data[:n].fill_(float(rank + 1))
+        comm.broadcast_(n, root=world - 1, slot=slot)
+        slot += 1
+        torch.cuda.synchronize()
+        checks["broadcast"] = bool((comm.data[:n] == float(world)).all())
+        checks["broadcast shadow"] = bool((comm.shadow[:n].float() == float(world)).all())
+        # weighted average: gamma 0.5 mass, the last rank idle, a buffer tail
+        gamma = 0.5
+        nparam, nbuf = 100_000, 1000  # nparam is a multiple of 4
+        n = nparam + nbuf
+        g = torch.Generator(device="cuda").manual_seed(77 + rank)
+        mine = torch.randn(n, device="cuda", generator=g)
+        comm.data[:n].copy_(mine)
+        batches = [0 if r == world - 1 else r + 1 for r in range(world)]
+        masses = [realized_mass(b, gamma) for b in batches]
+        allx = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allx, mine)
+        X = torch.stack(allx).double()
+        w = torch.tensor(masses, dtype=torch.float64, device="cuda")
+        movers = torch.tensor([1.0 if b > 0 else 0.0 for b in batches], dtype=torch.float64,
+                              device="cuda")
+        expect = torch.empty(n, dtype=torch.float64, device="cuda")
+        expect[:nparam] = (w[:, None] * X[:, :nparam]).sum(0) / w.sum()
+        expect[nparam:] = (movers[:, None] * X[:, nparam:]).sum(0) / movers.sum()
+        div = torch.zeros(2, device="cuda")
+        comm.weighted_average_(n, masses[rank], slot=slot, div=div, buf_start=nparam)
+        slot += 1
         torch.cuda.synchronize()
         comm.check()
-        ok_ar = torch.allclose(comm.grad[:n], ref, atol=1e-4)
-        # broadcast from rank 0
-        comm.data[:n].fill_(float(rank + 1))
-        comm.broadcast_(n, root=0, slot=4)
+        checks["weighted average"] = bool(torch.allclose(comm.data[:n].double(), expect,
+                                                         atol=1e-5, rtol=1e-5))
+        d2 = float(((X[rank, :nparam] - expect[:nparam]) ** 2).sum())
+        p2 = float((expect[:nparam] ** 2).sum())
+        checks["divergence partials"] = (abs(div[0].item() - d2) <= 1e-3 * max(d2, 1e-6)
+                                         and abs(div[1].item() - p2) <= 1e-3 * p2)
+        checks["weighted average shadow"] = bool(torch.equal(comm.shadow[:n],
+                                                             comm.data[:n].bfloat16()))
+        # nobody moved: nothing changes
+        before = comm.data[:n].clone()
+        comm.weighted_average_(n, 0.0, slot=slot, buf_start=nparam)
         torch.cuda.synchronize()
-        ok_bc = bool((comm.data[:n] == 1.0).all())
-        # weighted average with masses 1 and 3 (ranks 0,1,...)
-        comm.data[:n].fill_(float(rank))
-        comm.grad[:n].zero_()
-        comm.weighted_average_(n, mass=float(rank + 1), gamma=1.0, slot=8)
-        torch.cuda.synchronize()
-        masses = [float(r + 1) for r in range(world)]
-        expect = sum(r * m for r, m in enumerate(masses)) / sum(masses)
-        ok_avg = torch.allclose(comm.data[:n], torch.full((n,), expect, device="cuda"), atol=1e-5)
+        comm.check()
+        checks["all idle is a no-op"] = bool(torch.equal(before, comm.data[:n]))
         comm.close()
-        q.put((rank, ok_ar, ok_bc, ok_avg, None))
+        q.put((rank, checks, None))
         dist.destroy_process_group()
-    except Exception as e:  # pragma: no cover - reported to the parent
-        q.put((rank, False, False, False, repr(e)))
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+        q.put((rank, checks, traceback.format_exc()))
 
 
-def test_peer_collectives():
-    _need_gpus(2)
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_collectives_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = _collect(q, procs, world)
-    for p in procs:
-        p.join(timeout=60)
-    for rank, a, b, c, err in res:
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_collectives(world):
+    _need_gpus(world)
+    for rank, checks, err in _spawn(_collectives_worker, world):
         assert err is None, err
-        assert a, f"rank {rank}: all-reduce mismatch"
-        assert b, f"rank {rank}: broadcast mismatch"
-        assert c, f"rank {rank}: weighted average mismatch"
+        bad = [k for k, v in checks.items() if not v]
+        assert not bad, f"rank {rank}: failed {bad}"
 
 
-def _fused_ddp_worker(rank, world, port, q):
+# ----------------------------------------------------------------------------- fused DDP
+def _lm(dev):
+    from flodl_b200.models import TransformerLM
+
+    torch.manual_seed(0)
+    return TransformerLM(vocab_size=256, d_model=256, n_layers=2, n_heads=4, d_ff=1024,
+                         max_seq=128, device=dev)
+
+
+def _batch(world, dev):
+    g = torch.Generator(device="cuda").manual_seed(100)
+    return torch.randint(0, 256, (4 * world, 128), device=dev, generator=g)
+
+
+def _make_opt(kind, params):
+    from flodl_b200.optim import SGD, AdamW
+
+    if kind == "sgd":
+        return SGD(params, lr=0.05, momentum=0.9, weight_decay=1e-4)
+    return AdamW(params, lr=1e-3, weight_decay=0.1)
+
+
+STEPS = 3
+
+
+def _fused_ddp_worker(rank, world, port, q, kind, clip, graph):
     import torch.distributed as dist
 
-    from flodl_b200.models import TransformerLM
-    from flodl_b200.optim import AdamW
     from flodl_b200.parallel.fused import FusedDdp
 
     try:
         _init(rank, world, port)
         dev = torch.device("cuda", rank)
-        torch.manual_seed(0)
-        model = TransformerLM(vocab_size=256, d_model=256, n_layers=2, n_heads=4, d_ff=1024,
-                              max_seq=128, device=dev)
-        opt = AdamW(model.parameters(), lr=1e-3, weight_decay=0.1)
-        ddp = FusedDdp(model, opt, bucket_mb=1.0, blocks=16, timeout_s=5.0)
-        g = torch.Generator(device="cuda").manual_seed(100)
-        ids = torch.randint(0, 256, (4 * world, 128), device=dev, generator=g)
-        mine = ids[rank * 4:(rank + 1) * 4]
-        for _ in range(2):
+        model = _lm(dev)
+        opt = _make_opt(kind, model.parameters())
+        # 1 MiB buckets with a 64 KiB tail and one-shot up to 256 KiB: the
+        # 0.8M-parameter model gives several buckets of both forms
+        ddp = FusedDdp(model, opt, bucket_mb=1.0, tail_mb=0.0625, oneshot_kb=256,
+                       timeout_s=5.0, max_grad_norm=0.5 if clip else None)
+        nb = len(ddp.buckets)
+        forms = {b["oneshot"] for b in ddp.buckets}
+        ids = _batch(world, dev)
+        mine = ids[rank * 4:(rank + 1) * 4].clone()
+
+        def step():
             loss = model.loss(mine, mine)
             loss.backward()
             ddp.finish()
+            return loss
+
+        if graph:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                step()  # warm-up step (counts as step 1)
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                step()
+            for _ in range(STEPS - 1):
+                g.replay()
+        else:
+            for _ in range(STEPS):
+                step()
         torch.cuda.synchronize()
         ddp.comm.check()
         flat = ddp.arena.data.clone()
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         same = all(torch.equal(gathered[0], t) for t in gathered[1:])
-        q.put((rank, same, flat.cpu().numpy(), None))
+        shadow_ok = bool(torch.equal(ddp.arena.shadow, ddp.arena.data.bfloat16()))
+        norm = float(ddp.grad_norm.item()) if clip else None
+        if graph:
+            del g
+        q.put((rank, {"replicas equal": same, "shadow equals weights": shadow_ok,
+                      "buckets >= 3": nb >= 3, "both forms": len(forms) == 2 or clip},
+               flat.cpu(), norm, None))
         ddp.close()
         dist.destroy_process_group()
-    except Exception as e:  # pragma: no cover
-        q.put((rank, False, None, repr(e)))
+    except Exception:  # pragma: no cover
+        import traceback
+        q.put((rank, {}, None, None, traceback.format_exc()))
 
 
-def test_fused_ddp_matches_single_gpu_full_batch():
-    _need_gpus(2)
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_fused_ddp_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = sorted(_collect(q, procs, world), key=lambda t: t[0])
-    for p in procs:
-        p.join(timeout=60)
-    for rank, same, _, err in res:
-        assert err is None, err
-        assert same, f"rank {rank}: replicas diverged"
-    # single-GPU reference: same init, full batch, two AdamW steps
-    from flodl_b200.models import TransformerLM
-    from flodl_b200.optim import AdamW
-    from flodl_b200.utils.arena import ParamArena
-
+def _reference(world, kind, clip):
+    """Single GPU, full batch, the same number of steps."""
     dev = torch.device("cuda", 0)
-    torch.manual_seed(0)
-    model = TransformerLM(vocab_size=256, d_model=256, n_layers=2, n_heads=4, d_ff=1024,
-                          max_seq=128, device=dev)
-    opt = AdamW(model.parameters(), lr=1e-3, weight_decay=0.1)
-    g = torch.Generator(device="cuda").manual_seed(100)
-    ids = torch.randint(0, 256, (4 * world, 128), device=dev, generator=g)
-    for _ in range(2):
+    model = _lm(dev)
+    opt = _make_opt(kind, model.parameters())
+    ids = _batch(world, dev)
+    norm = None
+    for _ in range(STEPS):
         loss = model.loss(ids, ids)
         loss.backward()
+        if clip:
+            grads = [p.grad for p in model.parameters() if p.grad is not None]
+            norm = float(torch.linalg.vector_norm(torch.stack(
+                [torch.linalg.vector_norm(g.float()) for g in grads])))
+            if norm > 0.5:
+                for gr in grads:
+                    gr.mul_(0.5 / (norm + 1e-6))
         opt.step()
         opt.zero_grad()
-    ref = opt.groups[0].arena.data.cpu()
-    got = torch.from_numpy(res[0][2])
+    return opt.groups[0].arena.data.cpu(), norm
+
+
+@pytest.mark.parametrize("world", WORLDS)
+@pytest.mark.parametrize("kind,clip,graph", [("adamw", False, False), ("sgd", False, False),
+                                             ("adamw", True, False), ("adamw", False, True)])
+def test_fused_ddp_matches_single_gpu_full_batch(world, kind, clip, graph):
+    _need_gpus(world)
+    res = _spawn(_fused_ddp_worker, world, kind, clip, graph)
+    for rank, checks, _, _, err in res:
+        assert err is None, err
+        bad = [k for k, v in checks.items() if not v]
+        assert not bad, f"rank {rank}: failed {bad}"
+    ref, ref_norm = _reference(world, kind, clip)
+    got = res[0][2]
     torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=2e-3)
+    if clip:
+        got_norm = res[0][3]
+        assert abs(got_norm - ref_norm) <= 0.03 * ref_norm, (got_norm, ref_norm)
