@@ -236,6 +236,13 @@ def load_bundle(stem: str, model, optimizer=None) -> CheckpointMeta:
     return meta
 
 
+def read_meta(stem: str) -> CheckpointMeta:
+    """The ``.meta.json`` of a bundle without loading any tensors."""
+    path = CheckpointBundle.meta_path(stem)
+    with open(path) as f:
+        return CheckpointMeta.from_json(json.load(f), path)
+
+
 def bundle_complete(stem: str) -> bool:
     return all(os.path.exists(p) for p in (CheckpointBundle.model_path(stem),
                                            CheckpointBundle.meta_path(stem)))

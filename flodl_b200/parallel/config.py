@@ -60,7 +60,7 @@ class ElCheConfig:
     anchor_: int = 10
     max_anchor_: int = 0
     min_anchor_: int = 1
-    overhead_target_: float = 0.10
+    overhead_target_: float = 0.05
     max_batch_diff_: int = 0
     relax_up_: bool = False
     partition_ratios_: Optional[List[float]] = None

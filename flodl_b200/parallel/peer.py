@@ -174,3 +174,25 @@ class PeerComm:
         self.closed = True
 
     abort = close
+
+    def abandon(self) -> None:
+        """Give the communicator up without any peer: waits for this rank's
+        own work, unmaps the peers' regions and frees this rank's regions. No
+        kernel touches a peer's memory again and no collective runs, so this
+        is safe after a peer left or died (survivor re-formation)."""
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                try:
+                    self.C.peer_close(p)
+                except Exception:
+                    pass
+            for p in self._own:
+                try:
+                    self.C.peer_free(p)
+                except Exception:
+                    pass
+        self._opened, self._own = [], []
+        self.closed = True

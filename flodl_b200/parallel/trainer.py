@@ -2,10 +2,13 @@
 
 Reference: ``Trainer::builder(model_factory, optim_factory, train_fn)`` ->
 ``DdpBuilder`` -> ``.run()`` -> ``DdpHandle::join()`` -> ``TrainedState``
-(flodl/src/distributed/ddp.rs:408-560, ddp_run/*). With two or more GPUs the
-trainer auto-promotes to one process per GPU; each rank owns a model and
-optimizer replica and trains on its shard of the data. Averaging follows the
-``ElCheMode``:
+(flodl/src/distributed/ddp.rs:408-560, ddp_run/*). With two or more devices
+(or ``devices([...])``) the trainer runs one process per rank under a cluster
+coordinator (``parallel/runtime.py``) hosted by the launching process: the
+coordinator dispatches each rank's window from the epoch's chunk pool, decides
+when the ranks average, feeds the timings to ElChe and the divergence to the
+convergence guard, and re-forms the survivors when a rank leaves or stops
+answering. Averaging follows the ``ElCheMode``:
 
 * Sync:    every rank steps its optimizer, then parameters (work-weighted)
            and f32 buffers (mean over the ranks that moved) are averaged
@@ -13,15 +16,19 @@ optimizer replica and trains on its shard of the data. Averaging follows the
 * Cadence: rank r runs ``batch_counts[r]`` steps per window (ElChe balances
            the counts from measured ms/batch and the averaging overhead), then
            the work-weighted average ``sum_r n_r^gamma W_r / sum n^gamma``.
-* Async (CPU backend): each rank blends with the current consensus
-           (EASGD) instead of overwriting.
+* Async (CPU backend): ranks that finish early keep training for up to
+           ``max_overshoot`` batches, and each rank blends the consensus into
+           its replica (EASGD, ``easgd_alpha``) instead of overwriting.
 
 Device averaging runs the fused peer-memory weighted-average kernel on CUDA
-(the count exchange rides its signal words); on CPU ranks (gloo) it is a
-weighted ``all_reduce``. The CPU backend goes through the signed-frame CPU
-reducer hosted by rank 0. Divergence ||pre-post||/||post|| feeds the
-convergence guard, which can nudge the ElChe anchor down. Outer optimizers
-(SlowMo / DiLoCo) apply to each consensus.
+(the mass exchange rides its signal words, the divergence partials come back
+with it); on CPU ranks it is a gloo all-reduce. The CPU backend goes through
+the signed-frame CPU reducer that the coordinator hosts. Each session's
+process group is gloo (bootstrap only: the device data path is the peer
+kernels), so survivors can re-form without a device communicator abort. A
+round that fails (a peer wait ran out, a collective timed out) is retried on
+the re-formed session after every rank restored its pre-round parameters.
+Outer optimizers (SlowMo / DiLoCo) apply to each consensus.
 
 ``model_factory(device)``, ``optim_factory(params)`` and ``train_fn(model,
 batch) -> loss`` must be picklable (module-level) for multi-process runs.
@@ -60,6 +67,7 @@ class TrainedState:
     divergence: List[float] = field(default_factory=list)
     start_epoch: int = 0
     meta_nudges: List[float] = field(default_factory=list)
+    record: Dict[str, Any] = field(default_factory=dict)  # the coordinator's run record
 
 
 def _free_port() -> int:
@@ -109,24 +117,7 @@ class _Averager:
         self.fused = None
         self.round = 0
         if backend == AverageBackend.NCCL and device.type == "cuda" and world > 1:
-            from ..utils.arena import ParamArena
-            from .peer import PeerComm
-
-            nparam = sum((p.numel() + 63) // 64 * 64 for p in self.params)
-            self.nbuf = sum(b.numel() for b in self.buffers)
-            comm = PeerComm(nparam + (self.nbuf + 63) // 64 * 64, device)
-            arena = ParamArena(self.params, alloc=comm.data_alloc, grad_alloc=comm.grad_alloc,
-                               with_shadow=False)
-            arena.shadow = comm.shadow[:arena.numel]
-            arena.rebind()
-            arena.refresh_shadow()
-            self.fused = (comm, arena)
-            self.buf_start = arena.numel
-            self.buf_view = comm.data[self.buf_start:self.buf_start + self.nbuf]
-            self.div = torch.zeros(2, dtype=torch.float32, device=device)
-            for g in opt.groups:
-                if all(any(q is p for q in arena.params) for p in g.params) and len(opt.groups) == 1:
-                    g.arena = arena
+            self._make_fused()
 
     def flat(self) -> torch.Tensor:
         if self.fused is not None:
@@ -146,11 +137,75 @@ class _Averager:
                 b.copy_(flat[off:off + n].view_as(b))
                 off += n
 
-    def average(self, batches: int) -> float:
-        """Average with this rank's work; returns ||pre - post|| / ||post||."""
+    def snapshot(self) -> None:
+        """Keep this rank's pre-round parameters and buffers (restored when a
+        round fails, before it is retried on a re-formed session)."""
+        with torch.no_grad():
+            self._pre = self.flat()
+            self._pre_buf = self._buffers_flat()
+
+    def restore(self) -> None:
+        pre = getattr(self, "_pre", None)
+        if pre is None:
+            return
+        with torch.no_grad():
+            if self.fused is not None:
+                self.fused[1].data.copy_(pre)
+                self.fused[1].refresh_shadow()
+            else:
+                _unflat_(self.params, pre)
+            if self._pre_buf is not None:
+                self._load_buffers(self._pre_buf)
+
+    def rebuild(self, rank: int, world: int) -> None:
+        """Re-form over the current default process group (a survivor set):
+        a new symmetric region holds the parameters, the old communicator is
+        abandoned without touching any peer's memory."""
+        self.rank, self.world = rank, world
+        if self.fused is None:
+            return
+        old_comm, old_arena = self.fused
+        torch.cuda.synchronize(self.device)
+        self.fused = None
+        if world > 1:
+            self._make_fused()
+        else:
+            # alone: the parameters move to private memory
+            from ..utils.arena import ParamArena
+            arena = ParamArena(self.params)
+            for g in self.opt.groups:
+                if getattr(g, "arena", None) is old_arena:
+                    g.arena = arena
+        old_comm.abandon()
+
+    def _make_fused(self) -> None:
+        from ..utils.arena import ParamArena
+        from .peer import PeerComm
+
+        nparam = sum((p.numel() + 63) // 64 * 64 for p in self.params)
+        self.nbuf = sum(b.numel() for b in self.buffers)
+        comm = PeerComm(nparam + (self.nbuf + 63) // 64 * 64, self.device)
+        arena = ParamArena(self.params, alloc=comm.data_alloc, grad_alloc=comm.grad_alloc,
+                           with_shadow=False)
+        arena.shadow = comm.shadow[:arena.numel]
+        arena.rebind()
+        arena.refresh_shadow()
+        self.fused = (comm, arena)
+        self.buf_start = arena.numel
+        self.buf_view = comm.data[self.buf_start:self.buf_start + self.nbuf]
+        self.div = torch.zeros(2, dtype=torch.float32, device=self.device)
+        opt = self.opt
+        for g in opt.groups:
+            if all(any(q is p for q in arena.params) for p in g.params) and len(opt.groups) == 1:
+                g.arena = arena
+
+    def average(self, batches: int, rnd: Optional[int] = None) -> float:
+        """Average with this rank's work; returns ||pre - post|| / ||post||.
+        ``rnd`` names the round for the CPU reducer (every rank passes the same)."""
         mass = realized_mass(batches, self.gamma)
         mover = 1.0 if batches > 0 else 0.0
         self.round += 1
+        rnd = self.round if rnd is None else int(rnd)
         if self.world == 1:
             return 0.0
         if self.fused is not None:
@@ -171,8 +226,8 @@ class _Averager:
         pre = _flat(self.params)
         bpre = self._buffers_flat()
         if self.backend == AverageBackend.CPU and self.cpu is not None:
-            post = self.cpu.all_reduce_scaled(pre.cpu(), mass, 2 * self.round).to(pre.device)
-            bpost = (self.cpu.all_reduce_scaled(bpre.cpu(), mover, 2 * self.round + 1).to(bpre.device)
+            post = self.cpu.all_reduce_scaled(pre.cpu(), mass, 2 * rnd).to(pre.device)
+            bpost = (self.cpu.all_reduce_scaled(bpre.cpu(), mover, 2 * rnd + 1).to(bpre.device)
                      if bpre is not None else None)
         else:
             tot = torch.tensor([mass, mover], dtype=torch.float64, device=pre.device)
@@ -218,28 +273,18 @@ class _Averager:
             self.fused[0].close()
 
 
-def _rank_main(rank: int, world: int, port: int, key: bytes, spec: dict, out_q) -> None:
-    """One training rank (a spawned process, or the caller for world == 1)."""
+def _rank_main(rank: int, world: int, host: str, port: int, key: bytes, spec: dict,
+               out_q) -> None:
+    """One training rank process: follows the coordinator's control messages."""
     try:
-        dev_kind = spec["device_kind"]
-        if world > 1:
-            os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-            if dev_kind == "cuda":
-                torch.cuda.set_device(rank)
-                dist.init_process_group("nccl", rank=rank, world_size=world,
-                                        timeout=datetime.timedelta(seconds=spec["timeout_s"]),
-                                        device_id=torch.device("cuda", rank))
-            else:
-                dist.init_process_group("gloo", rank=rank, world_size=world,
-                                        timeout=datetime.timedelta(seconds=spec["timeout_s"]))
-        device = torch.device("cuda", rank) if dev_kind == "cuda" else torch.device("cpu")
+        device = (torch.device("cuda", rank) if spec["device_kind"] == "cuda"
+                  else torch.device("cpu"))
+        if device.type == "cuda":
+            torch.cuda.set_device(device)
         log.set_label(f"rank {rank}")
-        state = _train_rank(rank, world, device, key, spec)
-        if rank == 0:
-            out_q.put(("ok", state))
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
+        report = _RankWorker(rank, world, host, port, key, spec, device).run()
+        if report is not None:
+            out_q.put(("ok", report))
     except Exception as e:
         cfg = spec.get("config")
         if cfg is not None and getattr(cfg, "save_path_", None):
@@ -250,180 +295,343 @@ def _rank_main(rank: int, world: int, port: int, key: bytes, spec: dict, out_q) 
             except OSError:
                 pass
         out_q.put(("err", f"rank {rank}: " + traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
 
 
-def _train_rank(rank, world, device, key, spec) -> TrainedState:
+class _RankWorker:
+    """The GpuWorker role (ddp_run/worker/*): model and optimizer replica, the
+    training of dispatched windows, averaging rounds with restore-and-retry,
+    session re-formation and epoch callbacks."""
+
+    def __init__(self, rank, world, host, port, key, spec, device):
+        from .runtime import RankAgent
+
+        self.rank, self.world, self.spec, self.device = rank, world, spec, device
+        self.key = key
+        cfg: TrainerConfig = spec["config"]
+        self.cfg = cfg
+        ec = cfg.elche_
+        self.policy, self.backend = ec.mode_.split()
+        torch.manual_seed(spec.get("seed", 0))
+        self.model = spec["model_factory"](device)
+        self.opt = spec["optim_factory"](self.model.parameters())
+        self.train_fn = spec["train_fn"]
+        self.global_step = 0
+        if cfg.resume_from_:
+            from .bundle import load_bundle
+            meta = load_bundle(cfg.resume_from_, self.model, self.opt)
+            self.global_step = meta.global_step
+        self.loader = (DataLoader.from_dataset(spec["dataset"]).batch_size(cfg.batch_size_)
+                       .device(device).build())
+        self.seed = spec.get("seed", 0)
+        self.avg: Optional[_Averager] = None
+        self.cpu_client = None
+        self.since_sync = 0
+        self.windows = 0
+        self.syncs = 0
+        self.epoch_losses: List[float] = []
+        self._loss_sum = 0.0
+        self._loss_n = 0
+        self.divs: List[float] = []
+        self.outer = OuterStepper(spec.get("outer") or OuterAvg())
+        hb = max(0.05, min(1.0, cfg.heartbeat_timeout_secs_ / 5.0))
+        self.agent = RankAgent(host, port, key, rank, heartbeat_s=hb)
+        hooks = spec.get("test_hooks") or {}
+        self.leave_after = (hooks.get("leave_after_syncs") or {}).get(rank)
+        self.hang_after = (hooks.get("hang_after_windows") or {}).get(rank)
+        self.slow_ms = (hooks.get("slow_ms_per_batch") or {}).get(rank, 0.0)
+
+    # -------------------------------------------------------------- control loop
+    def run(self) -> Optional[TrainedState]:
+        from .runtime import (K_DEAD, K_DONE, K_EPOCH, K_EPOCH_ACK, K_PLAN, K_REBUILT,
+                              K_SESSION, K_STOP, K_SYNC, K_SYNCED)
+        try:
+            while True:
+                kind, body = self.agent.recv()
+                if kind == K_SESSION:
+                    self._session(body)
+                    self.agent.send(K_REBUILT, {"session": body["session"]})
+                elif kind == K_PLAN:
+                    self.agent.send(K_DONE, self._train(body))
+                    self.windows += 1
+                    if self.hang_after is not None and self.windows >= self.hang_after:
+                        self.agent.pause_heartbeat()  # a rank that stops answering
+                        while True:
+                            time.sleep(3600)
+                elif kind == K_SYNC:
+                    self.agent.send(K_SYNCED, self._sync(body))
+                    if self.leave_after is not None and self.syncs >= self.leave_after:
+                        # leave between windows: nothing of ours is in flight
+                        if self.device.type == "cuda":
+                            torch.cuda.synchronize(self.device)
+                        self.agent.close(bye=True)
+                        self._close()
+                        return None
+                elif kind == K_EPOCH:
+                    self._epoch_end(body)
+                    self.agent.send(K_EPOCH_ACK, {"epoch": body["epoch"]})
+                elif kind == K_DEAD:
+                    log.verbose(f"rank {body.get('rank')} declared dead")
+                elif kind == K_STOP:
+                    if body.get("error"):
+                        raise RuntimeError(f"coordinator stopped the run: {body['error']}")
+                    if body.get("report_rank") == self.rank:
+                        return self._report()
+                    return None
+        finally:
+            self._close()
+
+    def _close(self) -> None:
+        if self.avg is not None:
+            try:
+                if self.avg.fused is not None:
+                    self.avg.fused[0].abandon()
+                    self.avg.fused = None
+            except Exception:
+                pass
+        if self.cpu_client is not None:
+            try:
+                self.cpu_client.close()
+            except Exception:
+                pass
+            self.cpu_client = None
+        try:
+            self.agent.close()
+        except Exception:
+            pass
+
+    # -------------------------------------------------------------- session
+    def _session(self, body: dict) -> None:
+        ranks = [int(r) for r in body["ranks"]]
+        me, n = ranks.index(self.rank), len(ranks)
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+        dist.init_process_group(
+            "gloo", init_method=f"tcp://127.0.0.1:{int(body['port'])}", rank=me, world_size=n,
+            timeout=datetime.timedelta(seconds=float(self.spec.get("group_timeout_s", 60.0))))
+        if self.backend == AverageBackend.CPU and self.cpu_client is None and body.get("cpu_port"):
+            from .cpu_reduce import CpuReduceClient
+            self.cpu_client = CpuReduceClient(self.rank, "127.0.0.1", int(body["cpu_port"]), self.key)
+        if self.avg is None:
+            alpha = self.cfg.elche_.easgd_alpha_ if self.policy == ApplyPolicy.ASYNC else None
+            self.avg = _Averager(self.model, self.opt, self.backend, me, n, self.device,
+                                 self.cpu_client, self.cfg.elche_.gamma_, alpha)
+            self.avg.broadcast_initial()
+        else:
+            self.avg.rebuild(me, n)
+            self.avg.cpu = self.cpu_client
+
+    # -------------------------------------------------------------- training
+    def _train(self, plan: dict) -> dict:
+        from ..data.sampler import ChunkSampler
+        cfg = self.cfg
+        self.loader.sampler_ = ChunkSampler([(a, a + n) for a, n in plan["spans"]], self.seed)
+        limit = int(plan["batches"])
+        self.model.train()
+        dev = self.device
+        t0 = time.perf_counter()
+        first_ms = None
+        n = samples = 0
+        loss_acc = torch.zeros((), dtype=torch.float32, device=dev)
+        for batch in self.loader.epoch(int(plan["epoch"])):
+            if n >= limit:
+                break
+            loss = self.train_fn(self.model, batch)
+            loss.backward()
+            if cfg.max_grad_norm_:
+                from ..nn.clip import clip_grad_norm
+                clip_grad_norm(self.model.parameters(), cfg.max_grad_norm_, self.opt)
+            if cfg.scheduler_fn_ is not None:
+                self.opt.set_lr(cfg.scheduler_fn_(self.syncs))
+            self.opt.step()
+            self.opt.zero_grad()
+            loss_acc += loss.detach().float()
+            n += 1
+            self.global_step += 1
+            b0 = batch[0] if isinstance(batch, (list, tuple)) else next(iter(batch))
+            samples += int(b0.shape[0])
+            if self.slow_ms:
+                time.sleep(self.slow_ms / 1e3)
+            if first_ms is None:
+                if dev.type == "cuda":
+                    torch.cuda.synchronize(dev)
+                first_ms = (time.perf_counter() - t0) * 1e3
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+        wall = (time.perf_counter() - t0) * 1e3
+        ls = float(loss_acc.item())
+        self._loss_sum += ls
+        self._loss_n += n
+        self.since_sync += n
+        return {"wid": plan["wid"], "batches": n, "samples": samples, "wall_ms": wall,
+                "first_ms": first_ms or 0.0, "loss_sum": ls, "n_loss": n}
+
+    # -------------------------------------------------------------- averaging
+    def _sync(self, body: dict) -> dict:
+        rnd = int(body["round"]) * 64 + int(body.get("attempt", 1))
+        t0 = time.perf_counter()
+        ok, err, div = True, None, 0.0
+        self.avg.snapshot()
+        try:
+            div = self.avg.average(self.since_sync, rnd=rnd)
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+        except Exception as e:  # a peer timeout or a process-group error
+            ok, err = False, repr(e)
+            self.avg.restore()
+        sync_ms = (time.perf_counter() - t0) * 1e3
+        if ok:
+            self.since_sync = 0
+            self.syncs += 1
+            self.divs.append(div)
+            if not isinstance(self.outer.opt, OuterAvg):
+                flat = self.avg.flat()
+                newg = self.outer.step(flat)
+                if self.avg.fused is not None:
+                    self.avg.fused[1].data.copy_(newg)
+                    self.avg.fused[1].refresh_shadow()
+                else:
+                    _unflat_(self.avg.params, newg)
+                if self.outer.opt.resets_inner:
+                    self.opt.reset_state()
+        lr = self.opt.lr() if hasattr(self.opt, "lr") else 0.0
+        return {"round": body["round"], "ok": ok, "err": err, "sync_ms": sync_ms, "div": div,
+                "lr": float(lr)}
+
+    # -------------------------------------------------------------- epochs
+    def _epoch_end(self, body: dict) -> None:
+        epoch = int(body["epoch"])
+        if self._loss_n:
+            self.epoch_losses.append(self._loss_sum / self._loss_n)
+        self._loss_sum, self._loss_n = 0.0, 0
+        mine = int(body.get("callback_rank", 0)) == self.rank
+        if mine and self.cfg.epoch_fn_ is not None:
+            self.cfg.epoch_fn_(epoch, self.model, self._report())
+        if mine and body.get("save") and self.cfg.save_path_:
+            from .bundle import (CheckpointMeta, CoverageBlock, ElCheState, EpochCoverage,
+                                 SaveReason, save_bundle)
+            es = body.get("elche_state")
+            st = ElCheState(int(es["anchor"]), es["anchor_rank"],
+                            [float(x) for x in es["smoothed_ms_per_batch"]], es["phase"],
+                            int(es["calibration_count"])) if es else None
+            cov = CoverageBlock(self.seed, self.cfg.batch_size_,
+                                [EpochCoverage(epoch, len(self.spec["dataset"]),
+                                               [tuple(r) for r in body.get("coverage", [])])])
+            save_bundle(self.cfg.save_path_, self.model, self.opt,
+                        CheckpointMeta(epoch, self.global_step, int(body.get("syncs", 0)),
+                                       self.world, SaveReason.Checkpoint, st, cov))
+
+    def _report(self) -> TrainedState:
+        st = TrainedState(world=self.world, mode=self.cfg.elche_.mode_.value)
+        st.params = [(n, p.detach().cpu().clone()) for n, p in self.model.named_parameters()]
+        st.buffers = [(n, b.detach().cpu().clone()) for n, b in self.model.named_buffers()]
+        st.losses = list(self.epoch_losses)
+        st.syncs = self.syncs
+        st.divergence = list(self.divs)
+        return st
+
+
+def _train_single(spec) -> TrainedState:
+    """One device, no averaging: the single-device fallback of the trainer."""
     cfg: TrainerConfig = spec["config"]
-    ec: ElCheConfig = cfg.elche_
-    policy, backend = ec.mode_.split()
+    dev = (torch.device("cuda", 0) if spec["device_kind"] == "cuda" else torch.device("cpu"))
     torch.manual_seed(spec.get("seed", 0))
-    model = spec["model_factory"](device)
+    model = spec["model_factory"](dev)
     opt = spec["optim_factory"](model.parameters())
-    train_fn = spec["train_fn"]
-    cpu_ctl = cpu_client = None
-    if backend == AverageBackend.CPU and world > 1:
-        from .cpu_reduce import CpuReduceClient, CpuReduceController
-
-        port_t = torch.zeros(1, dtype=torch.int64, device=device if device.type == "cuda" else "cpu")
-        if rank == 0:
-            cpu_ctl = CpuReduceController(world, key, heartbeat_timeout=cfg.heartbeat_timeout_secs_)
-            port_t[0] = cpu_ctl.port
-        dist.broadcast(port_t, src=0)
-        cpu_client = CpuReduceClient(rank, "127.0.0.1", int(port_t.item()), key)
     start_epoch, global_step = 0, 0
     if cfg.resume_from_:
-        # every rank loads the same bundle; the initial broadcast then agrees anyway
         from .bundle import load_bundle
         meta = load_bundle(cfg.resume_from_, model, opt)
         start_epoch, global_step = meta.epoch + 1, meta.global_step
-    # CpuAsync blends the consensus into each replica (EASGD); every other
-    # mode overwrites with it (config.rs:283-313)
-    alpha = ec.easgd_alpha_ if policy == ApplyPolicy.ASYNC else None
-    avg = _Averager(model, opt, backend, rank, world, device, cpu_client, ec.gamma_, alpha)
-    avg.broadcast_initial()
-    sampler = DistributedSampler(rank, world, seed=spec.get("seed", 0))
-    loader = (DataLoader.from_dataset(spec["dataset"]).batch_size(cfg.batch_size_).device(device)
-              .sampler(sampler).build())
-    native = None
-    if policy == ApplyPolicy.CADENCE and world > 1:
-        from .._ext import native as _native
-
-        native = _native().ElChe(world, ec.anchor_)
-        native.set_overhead_target(ec.overhead_target_)
-        if ec.max_anchor_:
-            native.set_max_anchor(ec.max_anchor_)
-        native.set_min_anchor(ec.min_anchor_)
-        if ec.max_batch_diff_:
-            native.set_max_batch_diff(ec.max_batch_diff_)
-        native.set_max_total(max(1, loader.num_batches() * world))
-    guard = (NoGuard() if not ec.divergence_guard_ else LevelGuard(ec.divergence_threshold_))
-    from .meta import LrEventMeta
-    meta = LrEventMeta()
-    outer = OuterStepper(spec.get("outer") or OuterAvg())
-    st = TrainedState(world=world, mode=ec.mode_.value)
-    counts = [1] * world if policy != ApplyPolicy.CADENCE else [ec.anchor_] * world
-    st.start_epoch = start_epoch
+    loader = (DataLoader.from_dataset(spec["dataset"]).batch_size(cfg.batch_size_).device(dev)
+              .seed(spec.get("seed", 0)).build())
+    st = TrainedState(world=1, mode=cfg.elche_.mode_.value, start_epoch=start_epoch)
     for epoch in range(start_epoch, cfg.num_epochs_):
         model.train()
-        losses = []
-        it = iter(loader.epoch(epoch))
-        exhausted = False
-        while not exhausted:
-            window = counts[rank] if world > 1 else 1
-            t0 = time.perf_counter()
-            done = 0
-            for _ in range(window):
-                try:
-                    batch = next(it)
-                except StopIteration:
-                    exhausted = True
-                    break
-                loss = train_fn(model, batch)
-                loss.backward()
-                if cfg.max_grad_norm_:
-                    from ..nn.clip import clip_grad_norm
-
-                    clip_grad_norm(model.parameters(), cfg.max_grad_norm_, opt)
-                if cfg.scheduler_fn_ is not None:
-                    opt.set_lr(cfg.scheduler_fn_(st.syncs))
-                opt.step()
-                opt.zero_grad()
-                losses.append(float(loss.detach().float().item()))
-                done += 1
-                global_step += 1
-            if device.type == "cuda":
-                torch.cuda.synchronize(device)
-            wall_ms = (time.perf_counter() - t0) * 1e3
-            if world == 1:
-                continue
-            # every rank must enter the same number of averaging rounds; one
-            # exchange carries (more data?, work done) of every rank
-            flags = torch.tensor([0 if exhausted else 1, done], dtype=torch.int64,
-                                 device=device if device.type == "cuda" else "cpu")
-            allf = [torch.zeros_like(flags) for _ in range(world)]
-            dist.all_gather(allf, flags)
-            more = torch.tensor(min(int(f[0]) for f in allf))
-            if sum(int(f[1]) for f in allf) == 0:
-                # the cohort did no work in this window: skip the reduce
-                break
-            s0 = time.perf_counter()
-            div = avg.average(done)
-            sync_ms = (time.perf_counter() - s0) * 1e3
-            st.syncs += 1
-            st.divergence.append(div)
-            if outer is not None and not isinstance(outer.opt, OuterAvg):
-                flat = avg.flat()
-                newg = outer.step(flat)
-                if avg.fused is not None:
-                    avg.fused[1].data.copy_(newg)
-                    avg.fused[1].refresh_shadow()
-                else:
-                    _unflat_(avg.params, newg)
-                if outer.opt.resets_inner:
-                    opt.reset_state()
-            if native is not None:
-                t = torch.tensor([wall_ms, float(done)], dtype=torch.float64,
-                                 device=device if device.type == "cuda" else "cpu")
-                gathered = [torch.zeros_like(t) for _ in range(world)]
-                dist.all_gather(gathered, t)
-                verdict = guard.observe(div)
-                if ec.meta_controller_:
-                    lr_now = opt.lr() if hasattr(opt, "lr") else 0.0
-                    f = meta.observe(lr_now, int(native.anchor()),
-                                     "shrink" if verdict == Verdict.SHRINK else "ok", native.phase())
-                    if f is not None:
-                        native.nudge_anchor_down(f)
-                        st.meta_nudges.append(f)
-                native.report_timing([float(g[0]) for g in gathered],
-                                     [int(g[1]) for g in gathered], sync_ms)
-                counts = list(native.batch_counts())
-                st.batch_counts.append(counts)
-            if int(more.item()) == 0:
-                exhausted = True
-        if losses:
-            st.losses.append(sum(losses) / len(losses))
-        if cfg.epoch_fn_ is not None and rank == 0:
+        acc = torch.zeros((), device=dev)
+        n = 0
+        for batch in loader.epoch(epoch):
+            loss = spec["train_fn"](model, batch)
+            loss.backward()
+            if cfg.max_grad_norm_:
+                from ..nn.clip import clip_grad_norm
+                clip_grad_norm(model.parameters(), cfg.max_grad_norm_, opt)
+            if cfg.scheduler_fn_ is not None:
+                opt.set_lr(cfg.scheduler_fn_(global_step))
+            opt.step()
+            opt.zero_grad()
+            acc += loss.detach().float()
+            n += 1
+            global_step += 1
+        if n:
+            st.losses.append(float(acc.item()) / n)
+        if cfg.epoch_fn_ is not None:
             cfg.epoch_fn_(epoch, model, st)
-        if cfg.save_path_ and cfg.checkpoint_every_ and (epoch + 1) % cfg.checkpoint_every_ == 0 and rank == 0:
-            from .bundle import save_bundle
-
-            from .bundle import CheckpointMeta, ElCheState, SaveReason
-            es = None
-            if native is not None:
-                ph = native.phase()
-                es = ElCheState(int(native.anchor()), int(native.anchor_rank()),
-                                [float(x) for x in native.ms_per_batch()],
-                                ph.lower() if isinstance(ph, str) else
-                                ("probe", "warmup", "stable", "mature")[int(ph)],
-                                int(native.calibrations()))
+        if cfg.save_path_ and cfg.checkpoint_every_ and (epoch + 1) % cfg.checkpoint_every_ == 0:
+            from .bundle import CheckpointMeta, SaveReason, save_bundle
             save_bundle(cfg.save_path_, model, opt,
-                        CheckpointMeta(epoch, global_step, st.syncs, world, SaveReason.Checkpoint, es))
-    st.params = [(n, p.detach().cpu().clone()) for n, p in model.named_parameters()]
-    st.buffers = [(n, b.detach().cpu().clone()) for n, b in model.named_buffers()]
-    avg.close()
-    if cpu_client is not None:
-        cpu_client.close()
-    if cpu_ctl is not None:
-        cpu_ctl.close()
+                        CheckpointMeta(epoch, global_step, 0, 1, SaveReason.Checkpoint, None))
+    st.params = [(n_, p.detach().cpu().clone()) for n_, p in model.named_parameters()]
+    st.buffers = [(n_, b.detach().cpu().clone()) for n_, b in model.named_buffers()]
     return st
 
 
 class DdpHandle:
-    def __init__(self, procs, q, inline_state=None):
+    """A running job: ``join()`` waits for it and returns the trained state
+    with the coordinator's record (batch counts, divergence, verdicts, deaths)."""
+
+    def __init__(self, procs, q, inline_state=None, coordinator=None):
         self.procs, self.q, self.inline_state = procs, q, inline_state
+        self.coordinator = coordinator
 
     def join(self, timeout: float = 3600.0) -> TrainedState:
         if self.inline_state is not None:
             return self.inline_state
-        status, payload = self.q.get(timeout=timeout)
+        import queue as _queue
+        deadline = time.time() + timeout
+        status = payload = None
+        while status is None:
+            try:
+                status, payload = self.q.get(timeout=1.0)
+            except _queue.Empty:
+                if self.coordinator is not None and self.coordinator._done.is_set() \
+                        and self.coordinator.error:
+                    status, payload = "err", self.coordinator.error
+                elif time.time() > deadline:
+                    status, payload = "err", "training did not finish in time"
+        rec = None
+        if self.coordinator is not None:
+            try:
+                rec = self.coordinator.result(timeout=60)
+            except RuntimeError as e:
+                if status == "ok":
+                    status, payload = "err", str(e)
         for p in self.procs:
-            p.join(timeout=120)
+            p.join(timeout=30)
+        for p in self.procs:
+            if p.is_alive():
+                p.terminate()  # a rank the test told to hang
+                p.join(timeout=10)
         if status != "ok":
-            for p in self.procs:
-                if p.is_alive():
-                    p.terminate()
             raise RuntimeError(payload)
-        return payload
+        st: TrainedState = payload
+        if rec is not None:
+            st.world = self.coordinator.world
+            st.syncs = rec["syncs"]
+            st.batch_counts = rec["batch_counts"]
+            st.divergence = rec["divergence"]
+            st.meta_nudges = rec.get("meta_nudges", [])
+            st.start_epoch = self.coordinator.start_epoch
+            st.record = rec
+        return st
 
 
 class DdpBuilder:
@@ -474,22 +682,37 @@ class DdpBuilder:
         self.spec["device_kind"] = kind
         key = os.urandom(16)
         if world == 1:
-            q: "queue.Queue" = queue.Queue()
-            _rank_main(0, 1, 0, key, self.spec, q)
-            status, payload = q.get()
-            if status != "ok":
-                raise RuntimeError(payload)
-            return DdpHandle([], None, payload)
+            return DdpHandle([], None, _train_single(self.spec))
         import torch.multiprocessing as mp
+        from .runtime import Coordinator
 
+        ds = self.spec.get("dataset")
+        if ds is None:
+            raise ValueError("DdpBuilder: dataset(...) is required")
+        coord = Coordinator(world, key, len(ds), self.spec["config"],
+                            seed=self.spec.get("seed", 0)).start()
+        host, port = coord.address()
         ctx = mp.get_context("spawn")
         q = ctx.Queue()
-        port = _free_port()
-        procs = [ctx.Process(target=_rank_main, args=(r, world, port, key, self.spec, q), daemon=False)
-                 for r in range(world)]
+        procs = [ctx.Process(target=_rank_main, args=(r, world, host, port, key, self.spec, q),
+                             daemon=False) for r in range(world)]
         for p in procs:
             p.start()
-        return DdpHandle(procs, q)
+        return DdpHandle(procs, q, coordinator=coord)
+
+    def test_hooks(self, **hooks):
+        """Failure-injection seams for tests, all on the host: ``leave_after_syncs``
+        {rank: n} (the rank leaves cleanly after its n-th averaging round),
+        ``hang_after_windows`` {rank: n} (the rank stops heart-beating and
+        sleeps), ``slow_ms_per_batch`` {rank: ms}."""
+        self.spec["test_hooks"] = hooks
+        return self
+
+    def group_timeout(self, seconds: float):
+        """Timeout of the per-session process group (a collective with a lost
+        peer fails after it and the round is retried on the survivors)."""
+        self.spec["group_timeout_s"] = float(seconds)
+        return self
 
     def into_worker(self, rank: Optional[int] = None, world: Optional[int] = None) -> "Worker":
         return Worker(self.spec, rank, world)
