@@ -255,22 +255,48 @@ __device__ __forceinline__ float grad_scale(const FusedArgs& a) {
   return (a.gscale ? *a.gscale : 1.f) / (float)a.world;
 }
 
-// Sum of the world gradients at float4 index i (fixed peer order 0..world-1,
-// so every rank that sums the same element gets the same bits).
+// Sum of the world gradients at the float4 indices idx[0..ILP) (fixed peer
+// order 0..world-1, so every rank that sums the same element gets the same
+// bits). W > 0: the world size is a compile-time constant and the loads of
+// every peer are issued before the first add (W x ILP float4 in flight per
+// thread); W == 0: any world size, one peer's loads in flight at a time.
+template <int W, int ILP>
 __device__ __forceinline__ void gather_sum(const Handles& h, int world, const int64_t* idx,
                                            const bool* live, float4* acc) {
+  if constexpr (W > 0) {
+    float4 x[W][ILP];
 #pragma unroll
-  for (int j = 0; j < kIlp; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < W; ++p)
+#pragma unroll
+      for (int j = 0; j < ILP; ++j)
+        x[p][j] = live[j] ? ld_cg4(h.grad[p] + 4 * idx[j]) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < ILP; ++j) {
+      acc[j] = x[0][j];
+#pragma unroll
+      for (int p = 1; p < W; ++p) add4(acc[j], x[p][j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < ILP; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-  for (int p = 0; p < world; ++p) {
-    float4 x[kIlp];
+    for (int p = 0; p < world; ++p) {
+      float4 x[ILP];
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j)
-      x[j] = live[j] ? ld_cg4(h.grad[p] + 4 * idx[j]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < ILP; ++j)
+        x[j] = live[j] ? ld_cg4(h.grad[p] + 4 * idx[j]) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) add4(acc[j], x[j]);
+      for (int j = 0; j < ILP; ++j) add4(acc[j], x[j]);
+    }
   }
 }
+
+// float4 per thread and loop iteration for a compile-time world size (the
+// gather keeps W x ILP float4 loads in flight).
+template <int W>
+struct IlpFor {
+  static constexpr int value = W == 0 ? 4 : (W <= 2 ? 4 : (W <= 4 ? 2 : 1));
+};
 
 // Clear this rank's gradient elements that the peers' block blockIdx.x read:
 // the block's positions in every shard (two-shot) or in the whole range.
@@ -292,9 +318,10 @@ __device__ __forceinline__ void clear_local_grads(const Handles& h, const FusedA
 }
 
 // ------------------------------------------------------------------ fused AR + update
-template <class U>
-__global__ void __launch_bounds__(512) ar_update_kernel(const __grid_constant__ FusedArgs a,
+template <class U, int W>
+__global__ void __launch_bounds__(512, 2) ar_update_kernel(const __grid_constant__ FusedArgs a,
                                                  const __grid_constant__ Handles h) {
+  constexpr int ILP = IlpFor<W>::value;
   if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
   const Shard sh(a);
   const int64_t lo = a.oneshot ? sh.b0 : sh.s0(a.rank);
@@ -303,18 +330,18 @@ __global__ void __launch_bounds__(512) ar_update_kernel(const __grid_constant__ 
   const float gs = grad_scale(a);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
-       i0 += kIlp * stride) {
-    int64_t idx[kIlp];
-    bool live[kIlp];
+       i0 += ILP * stride) {
+    int64_t idx[ILP];
+    bool live[ILP];
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       idx[j] = i0 + j * stride;
       live[j] = idx[j] < hi;
     }
-    float4 g[kIlp];
-    gather_sum(h, a.world, idx, live, g);
+    float4 g[ILP];
+    gather_sum<W, ILP>(h, a.world, idx, live, g);
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       if (!live[j]) break;
       const int64_t i = idx[j];
       float4 gj = g[j];
@@ -344,8 +371,10 @@ __global__ void __launch_bounds__(512) ar_update_kernel(const __grid_constant__ 
 // No end meeting: the shard-r elements are touched by rank r only, and the
 // peers' gradients are cleared by the apply launch, which follows this one on
 // every rank's stream.
-__global__ void __launch_bounds__(512) reduce_scatter_kernel(const __grid_constant__ FusedArgs a,
+template <int W>
+__global__ void __launch_bounds__(512, 2) reduce_scatter_kernel(const __grid_constant__ FusedArgs a,
                                                  const __grid_constant__ Handles h) {
+  constexpr int ILP = IlpFor<W>::value;
   __shared__ float red[32];
   if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
   const Shard sh(a);
@@ -354,18 +383,18 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(const __grid_consta
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   float ss = 0.f;
   for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
-       i0 += kIlp * stride) {
-    int64_t idx[kIlp];
-    bool live[kIlp];
+       i0 += ILP * stride) {
+    int64_t idx[ILP];
+    bool live[ILP];
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       idx[j] = i0 + j * stride;
       live[j] = idx[j] < hi;
     }
-    float4 g[kIlp];
-    gather_sum(h, a.world, idx, live, g);
+    float4 g[ILP];
+    gather_sum<W, ILP>(h, a.world, idx, live, g);
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       if (!live[j]) break;
       scale4(g[j], gs);
       ss += dot4(g[j]);
@@ -443,8 +472,10 @@ __global__ void __launch_bounds__(512) clip_apply_kernel(const __grid_constant__
 // writes the result into every peer's shard r (only rank r touches shard r).
 // One-shot: every rank reduces the whole range into its data region (scratch),
 // meets, and copies it into its gradient buffer.
-__global__ void __launch_bounds__(512) all_reduce_kernel(const __grid_constant__ FusedArgs a,
+template <int W>
+__global__ void __launch_bounds__(512, 2) all_reduce_kernel(const __grid_constant__ FusedArgs a,
                                                  const __grid_constant__ Handles h) {
+  constexpr int ILP = IlpFor<W>::value;
   if (!meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err)) return;
   const Shard sh(a);
   const int64_t lo = a.oneshot ? sh.b0 : sh.s0(a.rank);
@@ -452,18 +483,18 @@ __global__ void __launch_bounds__(512) all_reduce_kernel(const __grid_constant__
   const float sc = a.average ? 1.f / (float)a.world : 1.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i0 = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < hi;
-       i0 += kIlp * stride) {
-    int64_t idx[kIlp];
-    bool live[kIlp];
+       i0 += ILP * stride) {
+    int64_t idx[ILP];
+    bool live[ILP];
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       idx[j] = i0 + j * stride;
       live[j] = idx[j] < hi;
     }
-    float4 g[kIlp];
-    gather_sum(h, a.world, idx, live, g);
+    float4 g[ILP];
+    gather_sum<W, ILP>(h, a.world, idx, live, g);
 #pragma unroll
-    for (int j = 0; j < kIlp; ++j) {
+    for (int j = 0; j < ILP; ++j) {
       if (!live[j]) break;
       scale4(g[j], sc);
       if (a.oneshot) {
@@ -494,7 +525,7 @@ __global__ void __launch_bounds__(512) all_reduce_kernel(const __grid_constant__
 // computes, over shard r, sum (data_p - avg)^2 for every p and sum avg^2, and
 // stores them into rank p's partial slots; after the end meeting each rank
 // adds its partials into a.div.
-__global__ void __launch_bounds__(512) weighted_average_kernel(const __grid_constant__ FusedArgs a,
+__global__ void __launch_bounds__(512, 2) weighted_average_kernel(const __grid_constant__ FusedArgs a,
                                                  const __grid_constant__ Handles h) {
   uint32_t* sig = h.sig[a.rank];
   __shared__ float w_sh[kMaxRanks], wb_sh[kMaxRanks];
@@ -633,6 +664,30 @@ __global__ void __launch_bounds__(512) broadcast_pull_kernel(const __grid_consta
   meet(h, a.rank, a.world, a.bucket, a.timeout_ns, a.err);
 }
 
+// Kernel selection by world size: 2, 4 and 8 ranks get the compile-time
+// gather (every peer's loads in flight at once), other sizes the generic one.
+struct ArAdamWK {
+  template <int W> static const void* fn() { return (const void*)ar_update_kernel<AdamWUpdate, W>; }
+};
+struct ArSgdK {
+  template <int W> static const void* fn() { return (const void*)ar_update_kernel<SgdUpdate, W>; }
+};
+struct AllReduceK {
+  template <int W> static const void* fn() { return (const void*)all_reduce_kernel<W>; }
+};
+struct ReduceScatterK {
+  template <int W> static const void* fn() { return (const void*)reduce_scatter_kernel<W>; }
+};
+template <class K>
+const void* pick_world(int world, int* ilp) {
+  switch (world) {
+    case 2: *ilp = IlpFor<2>::value; return K::template fn<2>();
+    case 4: *ilp = IlpFor<4>::value; return K::template fn<4>();
+    case 8: *ilp = IlpFor<8>::value; return K::template fn<8>();
+    default: *ilp = IlpFor<0>::value; return K::template fn<0>();
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, cudaStream_t st) {
@@ -651,13 +706,14 @@ cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, c
   const int threads = a.threads;
   const void* fn = nullptr;
   bool sharded = true;  // work per rank = one shard (false: the whole range)
+  int ilp = IlpFor<0>::value;
   switch (op) {
-    case FusedOp::kArAdamW: fn = (const void*)ar_update_kernel<AdamWUpdate>; break;
-    case FusedOp::kArSgd: fn = (const void*)ar_update_kernel<SgdUpdate>; break;
-    case FusedOp::kAllReduce: fn = (const void*)all_reduce_kernel; break;
+    case FusedOp::kArAdamW: fn = pick_world<ArAdamWK>(a.world, &ilp); break;
+    case FusedOp::kArSgd: fn = pick_world<ArSgdK>(a.world, &ilp); break;
+    case FusedOp::kAllReduce: fn = pick_world<AllReduceK>(a.world, &ilp); break;
     case FusedOp::kWeightedAverage: fn = (const void*)weighted_average_kernel; break;
     case FusedOp::kBroadcast: fn = (const void*)broadcast_pull_kernel; sharded = false; break;
-    case FusedOp::kReduceScatter: fn = (const void*)reduce_scatter_kernel; break;
+    case FusedOp::kReduceScatter: fn = pick_world<ReduceScatterK>(a.world, &ilp); break;
     case FusedOp::kClipApplyAdamW: fn = (const void*)clip_apply_kernel<AdamWUpdate>; break;
     case FusedOp::kClipApplySgd: fn = (const void*)clip_apply_kernel<SgdUpdate>; break;
   }
@@ -682,7 +738,7 @@ cudaError_t launch_fused(FusedOp op, const FusedArgs& a, const PeerPtrs& ptrs, c
   int64_t work4 = (a.end - a.start) / 4;
   if (op == FusedOp::kClipApplyAdamW || op == FusedOp::kClipApplySgd) work4 = 1 << 30;
   if (sharded) work4 = (work4 + a.world - 1) / a.world;
-  const int64_t want = std::max<int64_t>(1, (work4 + (int64_t)threads * kIlp - 1) / ((int64_t)threads * kIlp));
+  const int64_t want = std::max<int64_t>(1, (work4 + (int64_t)threads * ilp - 1) / ((int64_t)threads * ilp));
   // an explicit grid is an upper bound: small messages keep few blocks
   const int64_t lim = a.blocks > 0 ? std::min(a.blocks, cap) : cap;
   const int blocks = (int)std::min<int64_t>(want, lim);

@@ -12,10 +12,12 @@ Modes:
                 / time).
 * ``fused``     the fused gradient all-reduce + AdamW kernel on a parameter
                 arena the size of the LM benchmark (or ``--numel``), reported
-                against its NVLink roofline: each rank reads (n-1)/n of the f32
-                gradients from its peers and writes (n-1)/n of the updated f32
-                weights and bf16 shadows to them; the target time is the larger
-                direction over the measured 770 GB/s per-direction peer copy
+                against its NVLink roofline. Out of each GPU go the peers' reads
+                of their shards of its f32 gradients ((n-1)/n x 4 B per
+                element) and its shard's f32 weights and bf16 shadows written
+                into every peer ((n-1)/n x 6 B); both use the same direction of
+                the GPU's NVLink port, so the target time is (n-1)/n x 10 B x
+                elements over the measured 770 GB/s per-direction peer copy
                 bandwidth.
 * ``averaging`` cluster parameter averaging with uneven work: ResNet-20,
                 rank r runs 4 + r local SGD steps per round on its own batch,
@@ -133,10 +135,13 @@ def fused(rank, world, dev, args):
 
     t = _time(run, 20, 3, world)
     comm.check()
+    # bytes leaving each GPU (and, by symmetry, arriving): the peers read
+    # their shards of this rank's f32 gradients ((n-1)/n x 4 B per element)
+    # and this rank writes its shard's f32 weights and bf16 shadow into every
+    # peer ((n-1)/n x 6 B); both share the link direction out of this GPU
     frac = (world - 1) / world
-    in_bytes = frac * 4 * n            # f32 gradient shards read from peers
-    out_bytes = frac * (4 + 2) * n     # f32 weights + bf16 shadows written to peers
-    target_ms = max(in_bytes, out_bytes) / (LINK_GBS * 1e9) * 1e3
+    link_bytes = frac * (4 + 6) * n
+    target_ms = link_bytes / (LINK_GBS * 1e9) * 1e3
     if rank == 0:
         print(json.dumps({"mode": "fused_allreduce_adamw", "n_gpus": world, "numel": n,
                           "buckets": buckets, "oneshot": bool(args.oneshot),
@@ -225,7 +230,10 @@ def avgkernel(rank, world, dev, args):
     t = _time(run, 20, 3, world)
     comm.check()
     frac = (world - 1) / world
-    target_ms = frac * 6 * (n + nbuf) / (LINK_GBS * 1e9) * 1e3
+    # out of each GPU: the peers' reads of their shards of this rank's data
+    # (4 B per element) plus this rank's average and shadow written into
+    # every peer (6 B per element), each (n-1)/n of the elements
+    target_ms = frac * 10 * (n + nbuf) / (LINK_GBS * 1e9) * 1e3
     if rank == 0:
         print(json.dumps({"mode": "weighted_average_kernel", "n_gpus": world,
                           "numel": n, "buffer_numel": nbuf, "us": round(t * 1e3, 2),

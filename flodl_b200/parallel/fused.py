@@ -48,7 +48,7 @@ class FusedDdp:
                  oneshot_kb: Optional[float] = None, tail_mb: Optional[float] = None,
                  max_grad_norm: Optional[float] = None):
         # tuning knobs (constructor arguments win over the environment):
-        #   FLODL_DDP_BUCKET_MB        bucket size in MiB of f32 gradients (16)
+        #   FLODL_DDP_BUCKET_MB        bucket size in MiB of f32 gradients (64)
         #   FLODL_DDP_TAIL_MB          size of the bucket holding the first parameters,
         #                              which completes last in backward (2)
         #   FLODL_DDP_ONESHOT_KB       buckets up to this size run the one-shot form (1024)
@@ -56,7 +56,7 @@ class FusedDdp:
         #   FLODL_DDP_OVERLAP_BLOCKS   CTAs of in-backward launches (0: two per SM)
         env = os.environ
         if bucket_mb is None:
-            bucket_mb = float(env.get("FLODL_DDP_BUCKET_MB", "16"))
+            bucket_mb = float(env.get("FLODL_DDP_BUCKET_MB", "64"))
         if tail_mb is None:
             tail_mb = float(env.get("FLODL_DDP_TAIL_MB", "2"))
         if oneshot_kb is None:
