@@ -68,7 +68,7 @@ def _sources(*patterns):
 ext_modules = [
     CUDAExtension(
         name="flodl_b200._C",
-        sources=_sources("bind/*.cpp", "kernels/*.cu", "comm/*.cu"),
+        sources=_sources("bind/*.cpp", "capi/*.cpp", "kernels/*.cu", "comm/*.cu"),
         include_dirs=[os.path.join(ROOT, CSRC)],
         extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
         extra_link_args=LINK_FLAGS,

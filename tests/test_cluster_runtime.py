@@ -128,8 +128,10 @@ def _averager_worker(rank, world, port, batches, alpha, q):
     avg = _Averager(net, None, AverageBackend.NCCL, rank, world, torch.device("cpu"),
                     gamma=1.0, easgd_alpha=alpha)
     avg.average(batches[rank])
-    q.put((rank, [p.detach().clone() for p in net.parameters()],
-           net.bn.running_mean.clone(), net.bn.running_var.clone()))
+    # plain lists: a tensor in the queue is shared through a file descriptor
+    # that dies with this process, which may exit before the parent reads it
+    q.put((rank, [p.detach().tolist() for p in net.parameters()],
+           net.bn.running_mean.tolist(), net.bn.running_var.tolist()))
     dist.destroy_process_group()
 
 
@@ -142,7 +144,9 @@ def _run_averager(batches, alpha=None):
           for r in range(world)]
     for p in ps:
         p.start()
-    out = dict((r, rest) for r, *rest in [q.get(timeout=120) for _ in range(world)])
+    out = {}
+    for r, params, rm, rv in [q.get(timeout=120) for _ in range(world)]:
+        out[r] = ([torch.tensor(p) for p in params], torch.tensor(rm), torch.tensor(rv))
     for p in ps:
         p.join(timeout=60)
     return out
