@@ -120,7 +120,8 @@ class ClockSampler:
 def reference_arm(args):
     ref = os.path.join(ROOT, "baseline", "_ref")
     msg = ("reference fab2s/floDl is a Rust/cargo workspace (no setup.py/pyproject); "
-           "pip install of the reference source tree fails and this image has no Rust toolchain")
+           "pip install of the reference source tree fails and no Rust toolchain (cargo/rustc) "
+           "exists on this image or on the GPU box (probed)")
     if not os.path.isdir(ref) or not os.listdir(ref):
         print(json.dumps({"impl": "reference", "unavailable": msg}))
         return 0
