@@ -148,11 +148,105 @@ def case_adamw(_):
     return fn, 0.0, n * (4 * 4 + 3 * 4 + 2)
 
 
+def case_sgd(_):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    n = 19 * (1 << 20)
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    buf = torch.zeros(n, device="cuda")
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    lr = torch.full((), 0.1, device="cuda")
+    first = torch.zeros((), device="cuda")
+    fn = lambda: C.sgd(p, g, buf, sh, lr, None, first, 0.9, 0.0, 0.0, False, False)
+    return fn, 0.0, n * (3 * 4 + 2 * 4 + 2)
+
+
+def case_softmax_ce(_):
+    # the LM head's loss: 16384 rows x 256 byte classes, bf16 logits, dlogits out
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    V = 256
+    logits = _bf(T, V)
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    loss = torch.zeros((), device="cuda")
+    inv = torch.zeros((), device="cuda")
+    dl = torch.empty(T, V, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: C.softmax_ce(logits, tgt, loss, inv, dl, -100, 0.0)
+    return fn, 0.0, T * V * 2 * 2 + T * 8
+
+
+def case_embed(kind):
+    # token + position embedding of the LM batch (f32 residual stream and bf16 copy)
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    V = 256
+    ids = torch.randint(0, V, (B, S), device="cuda")
+    tok = torch.randn(V, D, device="cuda")
+    pos = torch.randn(S, D, device="cuda")
+    out = torch.empty(T, D, device="cuda")
+    out16 = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    if kind == "embed_fwd":
+        fn = lambda: C.embed_fwd(ids, tok, pos, None, None, out, out16, S)
+        return fn, 0.0, T * D * (4 + 2) + T * 8
+    dy = torch.randn(T, D, device="cuda")
+    dtok = torch.zeros(V, D, device="cuda")
+    fn = lambda: C.embed_bwd_atomic(ids, dy, dtok)
+    return fn, 0.0, T * D * 4 + T * 8
+
+
+# ResNet-20 stage-1 activation of the config-2 batch: 128 x 32 x 32 x 16 (NHWC bf16)
+RN, RH, RC = 128, 32, 16
+
+
+def case_conv(kind):
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    x = _bf(RN, RH, RH, RC)
+    M = RN * RH * RH
+    if kind in ("im2col", "col2im"):
+        cols = torch.empty(M, 9 * RC, device="cuda", dtype=torch.bfloat16)
+        if kind == "im2col":
+            fn = lambda: C.im2col(x, cols, 3, 1, 1)
+            return fn, 0.0, M * RC * 2 + M * 9 * RC * 2
+        dcols = _bf(M, 9 * RC)
+        dx = torch.empty_like(x)
+        fn = lambda: C.col2im(dcols, dx, 3, 1, 1, None, None)
+        return fn, 0.0, M * 9 * RC * 2 + M * RC * 2
+    mean = torch.empty(RC, device="cuda")
+    rstd = torch.empty(RC, device="cuda")
+    rm = torch.zeros(RC, device="cuda")
+    rv = torch.ones(RC, device="cuda")
+    ws = torch.zeros(2 * RC + 1, device="cuda")
+    gamma = torch.ones(RC, device="cuda")
+    beta = torch.zeros(RC, device="cuda")
+    C.bn_stats(x, mean, rstd, rm, rv, ws, 1e-5, 0.1)
+    if kind == "bn_stats":
+        fn = lambda: C.bn_stats(x, mean, rstd, rm, rv, ws, 1e-5, 0.1)
+        return fn, 0.0, M * RC * 2
+    if kind == "bn_apply":
+        y = torch.empty_like(x)
+        ident = _bf(RN, RH, RH, RC)
+        fn = lambda: C.bn_apply(x, mean, rstd, gamma, beta, ident, True, y)
+        return fn, 0.0, 3 * M * RC * 2
+    dy = _bf(RN, RH, RH, RC)
+    ymask = _bf(RN, RH, RH, RC)
+    dg = torch.zeros(RC, device="cuda")
+    db = torch.zeros(RC, device="cuda")
+    sums = torch.zeros(2 * RC, device="cuda")
+    dx = torch.empty_like(x)
+    fn = lambda: C.bn_bwd(dy, ymask, x, mean, rstd, gamma, dg, db, sums, ws, dx, None)
+    return fn, 0.0, 2 * (3 * M * RC * 2) + M * RC * 2
+
+
 CASES = {
     "gemm_qkv": case_gemm, "gemm_fc1_gelu": case_gemm, "gemm_fc2_residual": case_gemm,
     "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm,
     "flash_fwd": case_flash, "flash_bwd": case_flash,
-    "ln_fwd": case_ln, "ln_bwd": case_ln, "adamw": case_adamw,
+    "ln_fwd": case_ln, "ln_bwd": case_ln, "adamw": case_adamw, "sgd": case_sgd,
+    "softmax_ce": case_softmax_ce, "embed_fwd": case_embed, "embed_bwd": case_embed,
+    "im2col": case_conv, "col2im": case_conv, "bn_stats": case_conv, "bn_apply": case_conv,
+    "bn_bwd": case_conv,
 }
 
 

@@ -25,7 +25,10 @@
 #include "sm100_ptx.cuh"
 #include "flash_attn.h"
 
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace flodl {
@@ -495,6 +498,341 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
+// ============================================================== forward, two CTAs per SM
+// The same computation with one query row per thread and P kept in tensor
+// memory. Two CTAs share each SM (97 KB of shared memory, 256 TMEM columns
+// and 192 threads each): inside a CTA the chain S -> softmax -> P V is serial
+// per key tile, and the other CTA's MMAs, loads and softmax fill its gaps.
+//
+// Warps: 0 = TMA producer, 1 = MMA issuer, 2..5 = softmax. Softmax warp w owns
+// TMEM lane quarter w & 3; a thread owns one query row and all 128 keys of a
+// tile, so no exchange between warps is needed. The row maximum takes a first
+// pass over S (32 columns at a time), the exponentials a second pass.
+//
+// TMEM (256 columns): S at 0 (128 columns). The softmax writes P (bf16 pairs,
+// 64 columns) over S in place: P columns [16c, 16c + 16) replace S columns
+// that pass c has already read. The P V MMA takes P as its A operand straight
+// from TMEM. O double buffer (by item parity) at 128 / 192, rescaled lazily
+// in TMEM like the 8-warp kernel. The MMAs of one thread execute in issue
+// order, so S of the next key tile, issued after P V, cannot overwrite P
+// before P V has read it; and the commit that signals S(j) also covers P V of
+// tile j-1, so a rescale of O never races an MMA.
+constexpr int kF2Warps = 4;
+constexpr int kF2Threads = 64 + 32 * kF2Warps;
+
+struct Fwd2Smem {
+  uint8_t q[2][kTileBytes];
+  uint8_t k[2][kTileBytes];
+  uint8_t v[2][kTileBytes];
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full, p_full;
+  uint64_t o_full[2], o_free[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+// Key-padding mask of 32 columns: -inf where the key is padded (BERT-style
+// batches; the causal/range part is handled by the per-row limit).
+__device__ __forceinline__ void f2_pad_mask32(float (&v)[32], int kc0, int S,
+                                              const uint8_t* kp_row) {
+#pragma unroll
+  for (int w4 = 0; w4 < 8; ++w4) {
+    const int k = kc0 + 4 * w4;
+    uint32_t word;
+    if (k + 3 < S && ((reinterpret_cast<uintptr_t>(kp_row + k) & 3) == 0)) {
+      word = __ldg(reinterpret_cast<const uint32_t*>(kp_row + k));
+    } else {
+      word = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        word |= (uint32_t)((k + t < S) ? __ldg(kp_row + k + t) : 0) << (8 * t);
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      if ((word >> (8 * t)) & 0xffu) v[4 * w4 + t] = -INFINITY;
+  }
+}
+
+__global__ void __launch_bounds__(kF2Threads, 2)
+    flash_fwd2_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
+                      float* __restrict__ lse2, const uint8_t* __restrict__ key_pad, int B, int S,
+                      int H, int causal, float scale, uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Fwd2Smem& sm = *reinterpret_cast<Fwd2Smem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int C = H * kD;
+  const int n_qt = (S + kTile - 1) / kTile;
+  const int n_items = n_qt * H * B;
+  const uint64_t limit = g_fa_wait_limit_ns;
+  volatile uint32_t* abort_flag = &sm.abort;
+  auto kv_tiles = [&](int qt) { return causal ? min(qt + 1, n_qt) : n_qt; };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], 1);
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.o_full[i], 1);
+      mbar_init(&sm.o_free[i], kF2Warps);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.p_full, kF2Warps);
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<256>(&sm.tmem_base);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tm_qkv);
+      uint32_t kv_it = 0;
+      bool ok = true;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int qt, h, b;
+        fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
+        const int qb = n & 1;
+        if (!(ok = mbar_wait_bounded(&sm.q_empty[qb], ((n >> 1) & 1) ^ 1, abort_flag, err, limit)))
+          break;
+        mbar_arrive_expect_tx(&sm.q_full[qb], kTileBytes);
+        tma_load_3d(sm.q[qb], &tm_qkv, &sm.q_full[qb], h * kD, qt * kTile, b);
+        const int nkv = kv_tiles(qt);
+        for (int j = 0; j < nkv; ++j, ++kv_it) {
+          const int st = kv_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.kv_empty[st], ((kv_it >> 1) & 1) ^ 1, abort_flag, err,
+                                       limit)))
+            break;
+          mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kTileBytes);
+          tma_load_3d(sm.k[st], &tm_qkv, &sm.kv_full[st], C + h * kD, j * kTile, b);
+          tma_load_3d(sm.v[st], &tm_qkv, &sm.kv_full[st], 2 * C + h * kD, j * kTile, b);
+        }
+      }
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier at the end
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc_bf16(128, kD, 0, 1);
+      uint32_t kv_it = 0, t_it = 0;
+      bool ok = true, issued = false;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        int qt, h, b;
+        fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
+        const int qb = n & 1;
+        const uint32_t t_o = tmem + 128 + (uint32_t)qb * kD;
+        if (!(ok = mbar_wait_bounded(&sm.q_full[qb], (n >> 1) & 1, abort_flag, err, limit))) break;
+        const uint32_t q_addr = smem_u32(sm.q[qb]);
+        const int nkv = kv_tiles(qt);
+        for (int j = 0; j < nkv; ++j, ++kv_it, ++t_it) {
+          const uint32_t st = kv_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.kv_full[st], (kv_it >> 1) & 1, abort_flag, err, limit)))
+            break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm.k[st]);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            umma_bf16(tmem, make_sdesc_sw128(q_addr + kk * 32, 16, 1024),
+                      make_sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0);
+          issued = true;
+          umma_commit(&sm.s_full);
+          if (j == nkv - 1) umma_commit(&sm.q_empty[qb]);  // Q no longer read
+          // the O buffer of this parity was read out (item n - 2)
+          if (j == 0 && !(ok = mbar_wait_bounded(&sm.o_free[qb], ((n >> 1) & 1) ^ 1, abort_flag,
+                                                 err, limit)))
+            break;
+          // P (written over S by the softmax) times V
+          if (!(ok = mbar_wait_bounded(&sm.p_full, t_it & 1, abort_flag, err, limit))) break;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sm.v[st]);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_bf16_tmem_a(t_o, tmem + (uint32_t)(kk * 8),
+                             make_sdesc_sw128(v_addr + kk * 2048, kTileBytes, 1024), idesc_o,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&sm.kv_empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&sm.o_full[qb]);
+      }
+      if (!ok && issued) {
+        umma_commit(&sm.drain);
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&sm.drain, 0) && global_timer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier at the end
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // query row within the tile
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t t_s = tmem + lane_off;
+    const float sl2 = scale * kLog2e;
+    uint32_t t_it = 0;
+    bool ok = true;
+    int n = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      int qt, h, b;
+      fwd_decode(item, n_qt, H, H * B, causal != 0, qt, h, b);
+      const int qb = n & 1;
+      const uint32_t t_o = tmem + 128 + (uint32_t)qb * kD + lane_off;
+      const int q0 = qt * kTile;
+      const int qi = q0 + r;
+      const int nkv = kv_tiles(qt);
+      const uint8_t* kp_row = key_pad ? key_pad + (size_t)b * S : nullptr;
+      float m_ref = -INFINITY;  // reference max (scaled, log2 units)
+      float l = 0.f;            // row sum relative to m_ref
+      for (int j = 0; j < nkv; ++j, ++t_it) {
+        ok = mbar_wait_bounded(&sm.s_full, t_it & 1, abort_flag, err, limit);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        const int k0 = j * kTile;
+        // valid keys of this row in this tile: [k0, k0 + lim) (range and causal)
+        const int lim = max(0, min((causal ? min(qi + 1, S) : S) - k0, kTile));
+        const bool ranged = lim < kTile;  // warp-uniform only on tiles without masking
+        // pass 1: row maximum of the raw scores (scale > 0 commutes with max)
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t raw[32];
+          tmem_ld_32cols(t_s + (uint32_t)(c * 32), raw);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+          if (ranged) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (c * 32 + i < lim) ? v[i] : -INFINITY;
+          }
+          if (kp_row) f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
+        }
+        const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        const float mx = mraw == -INFINITY ? -INFINITY : mraw * sl2;
+        // lazy rescale: move the reference only when the max grew by > threshold
+        const bool move = mx > m_ref + kRescaleThreshold;
+        const float m_new = move ? mx : m_ref;
+        const float corr = (move && m_ref != -INFINITY) ? ex2_approx(m_ref - m_new) : 1.f;
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        m_ref = m_new;
+        // pass 2: P = 2^(s * scale - m) as bf16 over S (masked keys 0), row sum
+        const uint64_t neg_m = f2_splat(-m_use);
+        const uint64_t sl2x2 = f2_splat(sl2);
+        uint64_t la = f2_splat(0.f), lb = f2_splat(0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t raw[32];
+          tmem_ld_32cols(t_s + (uint32_t)(c * 32), raw);
+          tmem_ld_wait();
+          float p[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float a0, a1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1])),
+                             sl2x2, neg_m),
+                      a0, a1);
+            p[i] = ex2_approx(a0);
+            p[i + 1] = ex2_approx(a1);
+          }
+          if (ranged) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) p[i] = (c * 32 + i < lim) ? p[i] : 0.f;
+          }
+          if (kp_row) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) p[i] = v[i] == -INFINITY ? 0.f : p[i];
+          }
+          uint32_t pw[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            if (i & 2)
+              lb = f2_add(lb, f2_pack(p[i], p[i + 1]));
+            else
+              la = f2_add(la, f2_pack(p[i], p[i + 1]));
+            pw[i / 2] = pack_bf16x2(p[i], p[i + 1]);
+          }
+          tmem_st_16cols(t_s + (uint32_t)(c * 16), pw);
+        }
+        float la0, la1, lb0, lb1;
+        f2_unpack(la, la0, la1);
+        f2_unpack(lb, lb0, lb1);
+        l = l * corr + ((la0 + la1) + (lb0 + lb1));
+        // rescale O when a row's reference moved (P V of tile j - 1 is complete:
+        // the commit behind s_full follows it)
+        if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < kD / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld_16cols(t_o + (uint32_t)(c * 16), o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st_16cols(t_o + (uint32_t)(c * 16), o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full);
+      }
+      if (!ok) break;
+      // ---- output of this item: O / l and lse
+      ok = mbar_wait_bounded(&sm.o_full[qb], (n >> 1) & 1, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld_32cols(t_o, o[0]);
+      tmem_ld_32cols(t_o + 32, o[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.o_free[qb]);
+      if (qi < S) {
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        uint4* orow = reinterpret_cast<uint4*>(out + ((size_t)b * S + qi) * C + h * kD);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t* oo = &o[q >> 2][(q & 3) * 8];
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(oo[0]) * inv_l, __uint_as_float(oo[1]) * inv_l);
+          w.y = pack_bf16x2(__uint_as_float(oo[2]) * inv_l, __uint_as_float(oo[3]) * inv_l);
+          w.z = pack_bf16x2(__uint_as_float(oo[4]) * inv_l, __uint_as_float(oo[5]) * inv_l);
+          w.w = pack_bf16x2(__uint_as_float(oo[6]) * inv_l, __uint_as_float(oo[7]) * inv_l);
+          orow[q] = w;
+        }
+        lse2[((size_t)b * H + h) * S + qi] = (l > 0.f) ? (m_ref + log2f(l)) : -INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<256>(tmem);
+  }
+}
+
 // ============================================================== backward
 // Persistent over work items (128-key tile, head, batch). Per item the CTA
 // walks the query tiles that see these keys (all, or those at/after the key
@@ -731,7 +1069,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int kb = n & 1;
         const uint32_t k_addr = smem_u32(sm.k[kb]), v_addr = smem_u32(sm.v[kb]);
         if (!(ok = mbar_wait_bounded(&sm.kv_full[kb], (n >> 1) & 1, abort_flag, err, limit))) break;
-        if (!(ok = mbar_wait_bounded(&sm.dkv_free, (n & 1) ^ 1, abort_flag, err, limit))) break;
         int it = 0;
         for (int i = first_q(kt); i < n_t; ++i, ++it, ++qdo_it, ++t) {
           const int st = qdo_it & 1;
@@ -751,6 +1088,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           issued = true;
           umma_commit(&sm.s_full);
           if (!(ok = mbar_wait_bounded(&sm.p_ready, t & 1, abort_flag, err, limit))) break;
+          // dV/dK of the previous item read out: waited only here, so this
+          // item's first S^T / dP^T overlap that read-out
+          if (it == 0 &&
+              !(ok = mbar_wait_bounded(&sm.dkv_free, (n & 1) ^ 1, abort_flag, err, limit)))
+            break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk) {
@@ -972,10 +1314,63 @@ void set_flash_wait_limit_ns(uint64_t ns) {
   cudaMemcpyToSymbol(g_fa_wait_limit_ns, &ns, sizeof(ns));
 }
 
+// FLODL_FLASH_FWD=v1 selects the one-CTA-per-SM forward (8 softmax warps, P
+// in shared memory) instead of the two-CTA-per-SM kernel with P in TMEM.
+static bool use_fwd_v1() {
+  static const bool v1 = [] {
+    const char* e = std::getenv("FLODL_FLASH_FWD");
+    return e != nullptr && std::strcmp(e, "v1") == 0;
+  }();
+  return v1;
+}
+
+static cudaError_t launch_flash_fwd2(const FlashArgs& a, const CUtensorMap& tm, cudaStream_t st) {
+  const int smem = (int)sizeof(Fwd2Smem) + 1024;
+  static std::atomic<uint64_t> done{0};
+  static std::atomic<int> per_sm{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(done.load(std::memory_order_relaxed) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd2_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    // the largest shared-memory carveout, so that two CTAs fit on an SM
+    e = cudaFuncSetAttribute(flash_fwd2_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    // CTAs per SM from the shared memory and register budgets (the runtime's
+    // occupancy query answered 1 here although two fit)
+    int smem_sm = 0, reserved = 0, regs_sm = 0;
+    cudaFuncAttributes fa{};
+    if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) !=
+            cudaSuccess ||
+        cudaFuncGetAttributes(&fa, flash_fwd2_kernel) != cudaSuccess)
+      return cudaGetLastError();
+    const int by_smem = smem_sm / (smem + reserved);
+    const int regs_cta = ((fa.numRegs + 7) / 8 * 8) * kF2Threads;
+    const int by_regs = regs_cta > 0 ? regs_sm / regs_cta : 1;
+    per_sm.store(std::max(1, std::min(2, std::min(by_smem, by_regs))));
+    done.fetch_or(bit);
+  }
+  const int64_t items = (int64_t)((a.S + kTile - 1) / kTile) * a.H * a.B;
+  const int grid = (int)std::min<int64_t>(items, (int64_t)num_sms() * per_sm.load());
+  flash_fwd2_kernel<<<grid, kF2Threads, smem, st>>>(tm, a.out, a.lse2, a.key_pad, a.B, a.S, a.H,
+                                                    a.causal ? 1 : 0, a.scale,
+                                                    a.err ? a.err : default_err_word());
+  note_launch();
+  return cudaGetLastError();
+}
+
 cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st) {
   if (a.D != kD || a.S <= 0 || a.B <= 0 || a.H <= 0) return cudaErrorInvalidValue;
   CUtensorMap tm;
   if (!make_map_3d(&tm, a.qkv, a.B, a.S, 3 * a.H * kD)) return cudaErrorInvalidValue;
+  if (!use_fwd_v1()) return launch_flash_fwd2(a, tm, st);
   const int smem = (int)sizeof(FwdSmem) + 1024;
   {
     // the dynamic shared-memory opt-in is a per-device function attribute

@@ -12,6 +12,8 @@
 #include "sm100_ptx.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace flodl {
 
 namespace {
@@ -44,23 +46,127 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
 
 __device__ __forceinline__ bool target_in_range(int64_t y, int V) { return y >= 0 && y < V; }
 
-__global__ void ce_count_kernel(const int64_t* __restrict__ targets, int T, int V, int64_t ignore,
-                                float* inv_count, float* loss_zero, uint32_t* err) {
+// 1 / (number of rows whose target is in [0, V)). One block; every thread
+// issues its loads kCountUnroll at a time so the whole target vector is in
+// flight at once instead of one dependent load per iteration.
+constexpr int kCountThreads = 1024;
+constexpr int kCountUnroll = 8;
+__global__ void __launch_bounds__(kCountThreads) ce_count_kernel(
+    const int64_t* __restrict__ targets, int T, int V, int64_t ignore, float* inv_count,
+    float* loss_zero, uint32_t* err) {
   __shared__ float sh[32];
   float c = 0.f;
   bool bad = false;
-  for (int i = threadIdx.x; i < T; i += blockDim.x) {
-    const int64_t y = targets[i];
-    if (y == ignore) continue;
-    if (target_in_range(y, V)) c += 1.f;
-    else bad = true;
+  for (int base = threadIdx.x; base < T; base += kCountThreads * kCountUnroll) {
+    int64_t y[kCountUnroll];
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int i = base + u * kCountThreads;
+      y[u] = i < T ? __ldg(targets + i) : ignore;
+    }
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      if (y[u] == ignore) continue;
+      if (target_in_range(y[u], V)) c += 1.f;
+      else bad = true;
+    }
   }
   if (bad) report_error(err, kErrBadLabel);
-  float tot = block_reduce_sum(c, sh);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = c;
+  __syncthreads();
   if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < kCountThreads / 32; ++i) tot += sh[i];
     *inv_count = tot > 0.f ? 1.f / tot : 0.f;
     if (loss_zero) *loss_zero = 0.f;
   }
+}
+
+// Warp per row for vocabularies up to 32 x 8 x NC columns (NC 16-byte chunks
+// of 8 bf16 per lane held in registers): one read of the row, shuffle
+// reductions, no block barriers. Rows, pitches and V are multiples of 8.
+template <int NC>
+__global__ void __launch_bounds__(256) softmax_ce_warp_kernel(CeArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int n_warps = (gridDim.x * blockDim.x) >> 5;
+  const float inv_n = *a.inv_count;
+  const float eps = a.smoothing;
+  const float off = eps / a.V;
+  const int ldd = a.ld_d > 0 ? a.ld_d : a.V;
+  float loss_acc = 0.f;
+  for (int t = warp_g; t < a.T; t += n_warps) {
+    const __nv_bfloat16* z = a.logits + (size_t)t * a.ld;
+    const int64_t y = __ldg(a.targets + t);
+    const bool valid = (y != a.ignore_index) && target_in_range(y, a.V);
+    float v[NC][8];
+    float mx = -INFINITY, sz = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < a.V) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(z + col));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16x2(ws[k]);
+          v[c][2 * k] = f.x;
+          v[c][2 * k + 1] = f.y;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          mx = fmaxf(mx, v[c][k]);
+          sz += v[c][k];
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[c][k] = -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      sz += __shfl_xor_sync(0xffffffffu, sz, o);
+    }
+    float se = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[c][k] = __expf(v[c][k] - mx);  // exp(-inf) = 0 past V
+        se += v[c][k];
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+    const float inv_se = 1.f / se;
+    if (valid && lane == 0) {
+      const float zt = __bfloat162float(z[y]);
+      loss_acc += (mx + __logf(se) - (1.f - eps) * zt - off * sz) * inv_n;
+    }
+    if (a.dlogits) {
+      __nv_bfloat16* dz = a.dlogits + (size_t)t * ldd;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < a.V) {
+          float g[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            g[k] = valid ? (v[c][k] * inv_se - off - (col + k == y ? (1.f - eps) : 0.f)) * inv_n
+                         : 0.f;
+          uint4 w;
+          w.x = pack_bf16x2(g[0], g[1]);
+          w.y = pack_bf16x2(g[2], g[3]);
+          w.z = pack_bf16x2(g[4], g[5]);
+          w.w = pack_bf16x2(g[6], g[7]);
+          *reinterpret_cast<uint4*>(dz + col) = w;
+        }
+      }
+    }
+  }
+  if (lane == 0 && loss_acc != 0.f) atomicAdd(a.loss, loss_acc);
 }
 
 __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
@@ -112,14 +218,32 @@ __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
 
 cudaError_t launch_ce_count(const int64_t* targets, int T, int V, int64_t ignore_index,
                             float* inv_count, float* loss_zero, uint32_t* err, cudaStream_t st) {
-  ce_count_kernel<<<1, kThreads, 0, st>>>(targets, T, V, ignore_index, inv_count, loss_zero,
-                                          err ? err : default_err_word());
+  ce_count_kernel<<<1, kCountThreads, 0, st>>>(targets, T, V, ignore_index, inv_count,
+                                                loss_zero, err ? err : default_err_word());
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_softmax_ce(const CeArgs& a, cudaStream_t st) {
   if (a.T <= 0 || a.V <= 0) return cudaErrorInvalidValue;
+  const int ldd = a.ld_d > 0 ? a.ld_d : a.V;
+  const bool aligned = a.V % 8 == 0 && a.ld % 8 == 0 && ldd % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.dlogits) & 15) == 0;
+  if (aligned && a.V <= 32 * 8 * 8) {
+    // warp per row; enough warps for every SM, at most one row per warp and pass
+    const int nc = (a.V + 255) / 256;
+    const int64_t warps = std::min<int64_t>(a.T, (int64_t)num_sms() * 64);
+    const int grid = (int)((warps * 32 + 255) / 256);
+    switch (nc) {
+      case 1: softmax_ce_warp_kernel<1><<<grid, 256, 0, st>>>(a); break;
+      case 2: softmax_ce_warp_kernel<2><<<grid, 256, 0, st>>>(a); break;
+      case 3: case 4: softmax_ce_warp_kernel<4><<<grid, 256, 0, st>>>(a); break;
+      default: softmax_ce_warp_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    }
+    note_launch();
+    return cudaGetLastError();
+  }
   int grid = a.T < num_sms() * 8 ? a.T : num_sms() * 8;
   softmax_ce_kernel<<<grid, kThreads, 0, st>>>(a);
   note_launch();

@@ -69,6 +69,38 @@ def _time(fn, iters, warmup, world):
     return float(t.item())  # ms
 
 
+def _time_graph(fn, iters, warmup, world):
+    """Device time per call of `fn` with host launch cost removed: `iters`
+    calls are captured into one CUDA graph and the replay is timed (max over
+    ranks). NCCL and the peer kernels both capture; the graph is released
+    before returning (a graph holding NCCL work must not outlive the group)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())  # ms
+
+
 def sweep(rank, world, dev, args):
     """Two-shot and one-shot peer all-reduce against NCCL. One-shot reads
     every peer's whole buffer (world x the bytes of two-shot) and is timed up
@@ -76,6 +108,7 @@ def sweep(rank, world, dev, args):
     from .peer import PeerComm
     max_bytes = 1 << args.max_log2
     comm = PeerComm(max_bytes // 4, dev, with_shadow=False, timeout_s=10.0)
+    timer = _time_graph if args.graph else _time
     buf = torch.empty(max_bytes // 4, device=dev)
     buf16 = torch.empty(max_bytes // 2, device=dev, dtype=torch.bfloat16)
     nb = args.min_log2
@@ -84,18 +117,19 @@ def sweep(rank, world, dev, args):
         iters = 50 if nbytes <= (64 << 20) else 10
         n32 = max(nbytes // 4, 4)
         comm.grad[:n32].fill_(1.0)
-        t_peer = _time(lambda: comm.all_reduce_(n32, average=False, slot=0), iters, 3, world)
+        t_peer = timer(lambda: comm.all_reduce_(n32, average=False, slot=0), iters, 3, world)
         t_one = None
         if nb <= args.oneshot_max_log2:
-            t_one = _time(lambda: comm.all_reduce_(n32, average=False, slot=1, oneshot=True),
+            t_one = timer(lambda: comm.all_reduce_(n32, average=False, slot=1, oneshot=True),
                           iters, 3, world)
         comm.check()
-        t_nccl = _time(lambda: dist.all_reduce(buf[:n32]), iters, 3, world)
+        t_nccl = timer(lambda: dist.all_reduce(buf[:n32]), iters, 3, world)
         n16 = max(nbytes // 2, 8)
-        t_nccl16 = _time(lambda: dist.all_reduce(buf16[:n16]), iters, 3, world)
+        t_nccl16 = timer(lambda: dist.all_reduce(buf16[:n16]), iters, 3, world)
         if rank == 0:
             f = 2.0 * (world - 1) / world
-            rec = {"mode": "sweep", "n_gpus": world, "bytes": nbytes}
+            rec = {"mode": "sweep", "n_gpus": world, "bytes": nbytes,
+                   "timing": "cuda-graph replay" if args.graph else "eager launches"}
             for name, t in (("peer_f32", t_peer), ("peer_oneshot_f32", t_one),
                             ("nccl_f32", t_nccl), ("nccl_bf16", t_nccl16)):
                 if t is None:
@@ -256,6 +290,8 @@ def main():
     ap.add_argument("--blocks", type=int, default=0)
     ap.add_argument("--engine", default="peer", choices=["peer", "nccl"])
     ap.add_argument("--rounds", type=int, default=10)
+    ap.add_argument("--graph", type=int, default=1,
+                    help="sweep: time CUDA-graph replays (device latency, no host launch cost)")
     args = ap.parse_args()
     rank, world, dev = _init()
     {"sweep": sweep, "fused": fused, "averaging": averaging,

@@ -60,7 +60,8 @@ def test_ln_bwd_fused_extras():
     torch.testing.assert_close(colsum, ref.sum(0), rtol=1e-3, atol=1e-2)
 
 
-@pytest.mark.parametrize("V,smooth,ignore", [(256, 0.0, False), (30522, 0.1, True), (10, 0.0, False)])
+@pytest.mark.parametrize("V,smooth,ignore", [(256, 0.0, False), (30522, 0.1, True), (10, 0.0, False),
+                                             (1000, 0.1, True), (2048, 0.0, True), (520, 0.0, False)])
 def test_softmax_ce(V, smooth, ignore):
     torch.manual_seed(2)
     from flodl_b200.ops.loss import cross_entropy
