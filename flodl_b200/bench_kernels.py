@@ -4,7 +4,9 @@
                                        [--launches K]
 
 Each case builds its inputs once on ``cuda:0`` and times ``iters`` launches
-with CUDA events after ``warmup`` launches (inputs larger than L2 where the
+(captured into one CUDA graph, so that the host cost of the binding call does
+not hide a short kernel; ``--graph 0`` times eager launches) with CUDA events
+after ``warmup`` launches (inputs larger than L2 where the
 case is memory-bound), then prints one JSON line per case: microseconds per
 launch, the algorithmic FLOPs or bytes, the achieved rate, and its fraction
 of the measured peaks in ``MEASURED_PEAKS.json`` (cuBLAS bf16 GEMM burst and
@@ -250,7 +252,7 @@ CASES = {
 }
 
 
-def run(name, iters, warmup, launches):
+def run(name, iters, warmup, launches, graph=True):
     fn, flops, nbytes = CASES[name](name)
     if launches:
         for _ in range(launches):
@@ -261,14 +263,27 @@ def run(name, iters, warmup, launches):
         fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(iters):
-        fn()
-    e1.record()
+    if graph:
+        # `iters` launches captured into one CUDA graph: device time without
+        # the host cost of the binding calls (which exceeds short kernels)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+    else:
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / iters
     tf_peak, bw_peak, src = _peaks()
-    rec = {"case": name, "us": round(us, 2)}
+    rec = {"case": name, "us": round(us, 2), "timing": "graph" if graph else "eager"}
     if flops:
         tf = flops / us / 1e6
         rec.update(tflops=round(tf, 1), frac_of_bf16_peak=round(tf / tf_peak, 3))
@@ -283,10 +298,12 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--launches", type=int, default=0)
+    ap.add_argument("--graph", type=int, default=1,
+                    help="time a CUDA graph of the launches (1) or eager launches (0)")
     a = ap.parse_args()
     names = list(CASES) if a.case == "all" else a.case.split(",")
     for n in names:
-        print(json.dumps(run(n, a.iters, a.warmup, a.launches)), flush=True)
+        print(json.dumps(run(n, a.iters, a.warmup, a.launches, bool(a.graph))), flush=True)
 
 
 if __name__ == "__main__":

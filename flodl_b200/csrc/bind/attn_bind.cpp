@@ -42,7 +42,8 @@ void flash_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const T
   FL_CHECK(D == 64, "flash attention kernels support head_dim 64");
   auto opts = qkv.options().dtype(at::kFloat);
   Tensor delta = at::empty({B, H, S}, opts);
-  Tensor dq_acc = at::empty({B * S, H * D}, opts);
+  Tensor dq_acc;
+  if (flodl::flash_bwd_needs_dq_acc((int)S)) dq_acc = at::empty({B * S, H * D}, opts);
   flodl::FlashArgs a;
   a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -50,7 +51,7 @@ void flash_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const T
   a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.delta = delta.data_ptr<float>();
-  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dq_acc = dq_acc.defined() ? dq_acc.data_ptr<float>() : nullptr;
   if (key_pad) a.key_pad = reinterpret_cast<const uint8_t*>(key_pad->data_ptr());
   if (dbias) {
     FL_CHECK_F32(*dbias);

@@ -200,7 +200,8 @@ FLODL_EXPORT int flodl_flash_attn_bwd(const uint16_t* dout, const uint16_t* qkv,
                                       const uint8_t* key_pad, int B, int S, int H, int D,
                                       int causal, float scale, flodl_stream stream) {
   REQUIRE(dout && qkv && out && lse2 && dqkv, "dout, qkv, out, lse2 and dqkv are required");
-  REQUIRE(delta && dq_acc, "scratch delta and dq_acc are required");
+  REQUIRE(delta, "scratch delta is required");
+  REQUIRE(dq_acc || !flodl::flash_bwd_needs_dq_acc(S), "scratch dq_acc is required for S > 256");
   REQUIRE(B > 0 && S > 0 && H > 0, "B, S and H must be positive");
   if (D != 64) return fail(FLODL_ERR_UNSUPPORTED, __func__, "head_dim must be 64");
   flodl::FlashArgs a;

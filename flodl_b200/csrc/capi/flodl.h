@@ -125,7 +125,8 @@ int flodl_flash_attn_fwd(const uint16_t* qkv, uint16_t* out, float* lse2, const 
                          int B, int S, int H, int D, int causal, float scale,
                          flodl_stream stream);
 /* Backward into dqkv [B*S, 3*H*D] bf16. Scratch: delta f32 [B*H*S], dq_acc
- * f32 [B*S*H*D] (no initial contents needed). dbias f32 [3*H*D] or NULL:
+ * f32 [B*S*H*D] (no initial contents needed; unused, and may be NULL, when
+ * S <= 256: dQ then stays in tensor memory). dbias f32 [3*H*D] or NULL:
  * += column sums of dqkv (the packed projection's bias gradient). */
 int flodl_flash_attn_bwd(const uint16_t* dout, const uint16_t* qkv, const uint16_t* out,
                          const float* lse2, uint16_t* dqkv, float* delta, float* dq_acc,

@@ -865,7 +865,8 @@ struct BwdSmem {
   uint32_t abort;
 };
 
-// delta[b,h,s] = sum_d dO * O ; also zeroes the f32 dQ accumulator rows.
+// delta[b,h,s] = sum_d dO * O ; also zeroes the f32 dQ accumulator rows
+// (when there is one: the per-(batch, head) kernel keeps dQ in TMEM).
 // A warp handles four (token, head) rows per step: eight lanes per row, each
 // with 16-byte loads of dO and O (8 values) and a 3-step shuffle reduction.
 __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
@@ -894,9 +895,11 @@ __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
         const float2 a = unpack_bf16x2(xs[k]), c = unpack_bf16x2(ys[k]);
         s = fmaf(a.x, c.x, fmaf(a.y, c.y, s));
       }
-      float4* dq = reinterpret_cast<float4*>(dq_acc + tok * C + h * kD + part * 8);
-      dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-      dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (dq_acc != nullptr) {
+        float4* dq = reinterpret_cast<float4*>(dq_acc + tok * C + h * kD + part * 8);
+        dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
 #pragma unroll
     for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -1307,6 +1310,404 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ============================================================== backward, one (batch, head) per item
+// For sequences of at most two 128-row tiles (S <= 256, the LM benchmark's
+// shape) a work item is a whole (batch, head): the CTA walks its key tiles
+// and, per key tile, the query tiles that see them. dQ of both query tiles
+// then accumulates in TMEM across the key tiles (two 64-column buffers), so
+// dQ leaves the kernel as bf16 written once: no f32 accumulator to zero, no
+// red.add traffic and no conversion pass. TMEM: S^T 0, dP^T 128, dV 256,
+// dK 320, dQ of query tile 0 / 1 at 384 / 448 (all 512 columns).
+//
+// Warps and per-step math are those of flash_bwd_kernel. Read-outs are
+// deferred by one step: after producing P^T / dS^T of step i, the compute
+// warps read out what step i - 1 completed (dQ of a query tile after its last
+// key tile, dK / dV after a key tile's last query tile), so the tensor cores
+// run step i while the results of step i - 1 leave.
+struct BwdBhSmem {
+  uint8_t k[2][kTileBytes];  // K/V by key-tile parity (the next tile loads early)
+  uint8_t v[2][kTileBytes];
+  uint8_t q[2][kTileBytes];
+  uint8_t dout[2][kTileBytes];
+  uint8_t p[2 * kTileBytes];   // P^T: 128 keys x 128 queries (two 64-query SW128 blocks)
+  uint8_t ds[2 * kTileBytes];  // dS^T, same layout
+  float stat[kBwdWarps][2][64];
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t s_full, s_free, p_ready, pds_free, dkv_full, dkv_free;
+  uint64_t dq_full[2], dq_free[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    flash_bwd_bh_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                        const __grid_constant__ CUtensorMap tm_dout, const float* __restrict__ lse2,
+                        const float* __restrict__ delta, __nv_bfloat16* __restrict__ dqkv,
+                        const uint8_t* __restrict__ key_pad, int B, int S, int H, int causal,
+                        float scale, float* __restrict__ dbias, uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  BwdBhSmem& sm = *reinterpret_cast<BwdBhSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int C = H * kD;
+  const int n_t = (S + kTile - 1) / kTile;  // 1 or 2
+  const int n_items = H * B;
+  const uint64_t limit = g_fa_wait_limit_ns;
+  volatile uint32_t* abort_flag = &sm.abort;
+  auto first_q = [&](int kt) { return causal ? kt : 0; };
+  // the last key tile that contributes to query tile qt
+  auto last_k = [&](int qt) { return causal ? qt : n_t - 1; };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+      mbar_init(&sm.qdo_full[i], 1);
+      mbar_init(&sm.qdo_empty[i], 1);
+      mbar_init(&sm.dq_full[i], 1);
+      mbar_init(&sm.dq_free[i], kBwdWarps);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_free, kBwdWarps);
+    mbar_init(&sm.p_ready, kBwdWarps);
+    mbar_init(&sm.pds_free, 1);
+    mbar_init(&sm.dkv_full, 1);
+    mbar_init(&sm.dkv_free, kBwdWarps);
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<512>(&sm.tmem_base);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 320,
+                 t_dq = tmem + 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_dout);
+      uint32_t kv_it = 0, qdo_it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const int h = item % H, b = item / H;
+        for (int kt = 0; kt < n_t && ok; ++kt, ++kv_it) {
+          const int kb = kv_it & 1;
+          if (!(ok = mbar_wait_bounded(&sm.kv_empty[kb], ((kv_it >> 1) & 1) ^ 1, abort_flag, err,
+                                       limit)))
+            break;
+          mbar_arrive_expect_tx(&sm.kv_full[kb], 2 * kTileBytes);
+          tma_load_3d(sm.k[kb], &tm_qkv, &sm.kv_full[kb], C + h * kD, kt * kTile, b);
+          tma_load_3d(sm.v[kb], &tm_qkv, &sm.kv_full[kb], 2 * C + h * kD, kt * kTile, b);
+          for (int i = first_q(kt); i < n_t; ++i, ++qdo_it) {
+            const int st = qdo_it & 1;
+            if (!(ok = mbar_wait_bounded(&sm.qdo_empty[st], ((qdo_it >> 1) & 1) ^ 1, abort_flag,
+                                         err, limit)))
+              break;
+            mbar_arrive_expect_tx(&sm.qdo_full[st], 2 * kTileBytes);
+            tma_load_3d(sm.q[st], &tm_qkv, &sm.qdo_full[st], h * kD, i * kTile, b);
+            tma_load_3d(sm.dout[st], &tm_dout, &sm.qdo_full[st], h * kD, i * kTile, b);
+          }
+        }
+      }
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier at the end
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_kq = make_idesc_bf16(128, 128, 0, 0);  // M=keys, N=queries
+      constexpr uint32_t idesc_kd = make_idesc_bf16(128, kD, 0, 1);   // M=keys, N=D, B MN-major
+      constexpr uint32_t idesc_qd = make_idesc_bf16(128, kD, 1, 1);   // M=queries, N=D
+      const uint32_t p_addr = smem_u32(sm.p), ds_addr = smem_u32(sm.ds);
+      uint32_t kv_it = 0, qdo_it = 0, t = 0;
+      bool ok = true, issued = false;
+      int n = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+        for (int kt = 0; kt < n_t && ok; ++kt, ++kv_it) {
+          const int kb = kv_it & 1;
+          const uint32_t k_addr = smem_u32(sm.k[kb]), v_addr = smem_u32(sm.v[kb]);
+          if (!(ok = mbar_wait_bounded(&sm.kv_full[kb], (kv_it >> 1) & 1, abort_flag, err, limit)))
+            break;
+          int it = 0;
+          for (int i = first_q(kt); i < n_t; ++i, ++it, ++qdo_it, ++t) {
+            const int st = qdo_it & 1;
+            if (!(ok = mbar_wait_bounded(&sm.qdo_full[st], (qdo_it >> 1) & 1, abort_flag, err,
+                                         limit)))
+              break;
+            if (!(ok = mbar_wait_bounded(&sm.s_free, (t & 1) ^ 1, abort_flag, err, limit))) break;
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(sm.q[st]), do_addr = smem_u32(sm.dout[st]);
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              umma_bf16(t_s, make_sdesc_sw128(k_addr + kk * 32, 16, 1024),
+                        make_sdesc_sw128(q_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
+              umma_bf16(t_dp, make_sdesc_sw128(v_addr + kk * 32, 16, 1024),
+                        make_sdesc_sw128(do_addr + kk * 32, 16, 1024), idesc_kq, kk > 0);
+            }
+            issued = true;
+            umma_commit(&sm.s_full);
+            if (!(ok = mbar_wait_bounded(&sm.p_ready, t & 1, abort_flag, err, limit))) break;
+            // dV/dK of the previous key tile read out (deferred by one step)
+            if (it == 0 &&
+                !(ok = mbar_wait_bounded(&sm.dkv_free, (kv_it & 1) ^ 1, abort_flag, err, limit)))
+              break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk) {
+              const uint32_t aoff = (kk / 4) * kTileBytes + (kk % 4) * 32;
+              umma_bf16(t_dv, make_sdesc_sw128(p_addr + aoff, 16, 1024),
+                        make_sdesc_sw128(do_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
+                        (it > 0 || kk > 0));
+              umma_bf16(t_dk, make_sdesc_sw128(ds_addr + aoff, 16, 1024),
+                        make_sdesc_sw128(q_addr + kk * 2048, kTileBytes, 1024), idesc_kd,
+                        (it > 0 || kk > 0));
+            }
+            // dQ of query tile i: first touched at key tile 0 in this item,
+            // whose buffer the read-out of the previous item must have freed
+            if (kt == 0 &&
+                !(ok = mbar_wait_bounded(&sm.dq_free[i], (n & 1) ^ 1, abort_flag, err, limit)))
+              break;
+            tc_fence_after();
+            const uint32_t t_dqi = t_dq + (uint32_t)(i * kD);
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              umma_bf16(t_dqi, make_sdesc_sw128(ds_addr + kk * 2048, kTileBytes, 1024),
+                        make_sdesc_sw128(k_addr + kk * 2048, kTileBytes, 1024), idesc_qd,
+                        (kt > 0 || kk > 0));
+            umma_commit(&sm.pds_free);
+            umma_commit(&sm.qdo_empty[st]);
+            if (kt == last_k(i)) umma_commit(&sm.dq_full[i]);
+          }
+          if (!ok) break;
+          umma_commit(&sm.kv_empty[kb]);
+          umma_commit(&sm.dkv_full);
+        }
+      }
+      if (!ok && issued) {
+        umma_commit(&sm.drain);
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&sm.drain, 0) && global_timer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier at the end
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int wi = warp - 2;
+    const int q4 = warp & 3;
+    const int hh = wi >> 2;        // query half of each tile (dims half of dQ/dK/dV)
+    const int r = q4 * 32 + lane;  // key row of the tile (query row for dQ)
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    const uint64_t sl2x2 = f2_splat(sl2);
+    float* st_lse = sm.stat[wi][0];
+    float* st_dl = sm.stat[wi][1];
+    uint32_t t = 0, kv_done = 0;
+    bool ok = true;
+    int n = 0;
+    // read-outs completed by the previous step, done after the next step's P^T / dS^T
+    struct Pending {
+      int dq_tile = -1, dq_b = 0, dq_h = 0, dq_n = 0;
+      int kv_tile = -1, kv_b = 0, kv_h = 0;
+    } pend;
+    auto readout_dq = [&](int qt, int b, int h, int nn) -> bool {
+      const bool w = mbar_wait_bounded(&sm.dq_full[qt], nn & 1, abort_flag, err, limit);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      uint32_t raw[32];
+      tmem_ld_32cols(t_dq + (uint32_t)(qt * kD) + lane_off + (uint32_t)(hh * 32), raw);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.dq_free[qt]);
+      const int qi = qt * kTile + r;
+      float vq[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) vq[c] = qi < S ? __uint_as_float(raw[c]) * scale : 0.f;
+      if (dbias) {
+        const float sq = chunk_column_sum(vq, lane);
+        atomicAdd(dbias + h * kD + hh * 32 + lane, sq);
+      }
+      if (qi < S) {
+        uint4* qrow = reinterpret_cast<uint4*>(dqkv + ((size_t)b * S + qi) * 3 * C + h * kD +
+                                               hh * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(vq[8 * q + 0], vq[8 * q + 1]);
+          w.y = pack_bf16x2(vq[8 * q + 2], vq[8 * q + 3]);
+          w.z = pack_bf16x2(vq[8 * q + 4], vq[8 * q + 5]);
+          w.w = pack_bf16x2(vq[8 * q + 6], vq[8 * q + 7]);
+          qrow[q] = w;
+        }
+      }
+      return true;
+    };
+    auto readout_dkv = [&](int kt, int b, int h) -> bool {
+      const bool w = mbar_wait_bounded(&sm.dkv_full, kv_done & 1, abort_flag, err, limit);
+      ++kv_done;
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      uint32_t rk[32], rv[32];
+      tmem_ld_32cols(t_dk + lane_off + (uint32_t)(hh * 32), rk);
+      tmem_ld_32cols(t_dv + lane_off + (uint32_t)(hh * 32), rv);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.dkv_free);
+      const int kj = kt * kTile + r;
+      float ck[32], cv[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        ck[c] = kj < S ? __uint_as_float(rk[c]) * scale : 0.f;
+        cv[c] = kj < S ? __uint_as_float(rv[c]) : 0.f;
+      }
+      if (dbias) {
+        const float sk = chunk_column_sum(ck, lane);
+        const float sv = chunk_column_sum(cv, lane);
+        atomicAdd(dbias + C + h * kD + hh * 32 + lane, sk);
+        atomicAdd(dbias + 2 * C + h * kD + hh * 32 + lane, sv);
+      }
+      if (kj < S) {
+        __nv_bfloat16* krow = dqkv + ((size_t)b * S + kj) * 3 * C + C + h * kD + hh * 32;
+        __nv_bfloat16* vrow = krow + C;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 wk, wv;
+          wk.x = pack_bf16x2(ck[8 * q + 0], ck[8 * q + 1]);
+          wk.y = pack_bf16x2(ck[8 * q + 2], ck[8 * q + 3]);
+          wk.z = pack_bf16x2(ck[8 * q + 4], ck[8 * q + 5]);
+          wk.w = pack_bf16x2(ck[8 * q + 6], ck[8 * q + 7]);
+          wv.x = pack_bf16x2(cv[8 * q + 0], cv[8 * q + 1]);
+          wv.y = pack_bf16x2(cv[8 * q + 2], cv[8 * q + 3]);
+          wv.z = pack_bf16x2(cv[8 * q + 4], cv[8 * q + 5]);
+          wv.w = pack_bf16x2(cv[8 * q + 6], cv[8 * q + 7]);
+          reinterpret_cast<uint4*>(krow)[q] = wk;
+          reinterpret_cast<uint4*>(vrow)[q] = wv;
+        }
+      }
+      return true;
+    };
+    auto flush = [&]() -> bool {
+      bool good = true;
+      if (pend.dq_tile >= 0) good = readout_dq(pend.dq_tile, pend.dq_b, pend.dq_h, pend.dq_n);
+      pend.dq_tile = -1;
+      if (good && pend.kv_tile >= 0) good = readout_dkv(pend.kv_tile, pend.kv_b, pend.kv_h);
+      pend.kv_tile = -1;
+      return good;
+    };
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+      const int h = item % H, b = item / H;
+      for (int kt = 0; kt < n_t && ok; ++kt) {
+        const int kj = kt * kTile + r;
+        const bool key_ok = kj < S && !(key_pad && __ldg(key_pad + (size_t)b * S + kj) != 0);
+        for (int i = first_q(kt); i < n_t; ++i, ++t) {
+          const int q0 = i * kTile;
+          const int qc0 = q0 + hh * 64;  // first query of this warp's half
+          {
+            const float* lrow = lse2 + ((size_t)b * H + h) * S;
+            const float* drow = delta + ((size_t)b * H + h) * S;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int qi = qc0 + u * 32 + lane;
+              st_lse[u * 32 + lane] = qi < S ? -__ldg(lrow + qi) : -INFINITY;
+              st_dl[u * 32 + lane] = qi < S ? -__ldg(drow + qi) : 0.f;
+            }
+            __syncwarp();
+          }
+          ok = mbar_wait_bounded(&sm.s_full, t & 1, abort_flag, err, limit);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          ok = mbar_wait_bounded(&sm.pds_free, (t & 1) ^ 1, abort_flag, err, limit);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+          const bool diag = causal && (qc0 < kt * kTile + kTile);
+          uint8_t* pb = sm.p + hh * kTileBytes;
+          uint8_t* db = sm.ds + hh * kTileBytes;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t rs[32], rdp[32];
+            tmem_ld_32cols(t_s + lane_off + (uint32_t)(hh * 64 + cc * 32), rs);
+            tmem_ld_32cols(t_dp + lane_off + (uint32_t)(hh * 64 + cc * 32), rdp);
+            tmem_ld_wait();
+            float p[32], ds[32];
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 l4 = *reinterpret_cast<const float4*>(st_lse + cc * 32 + 4 * c4);
+              const float4 d4 = *reinterpret_cast<const float4*>(st_dl + cc * 32 + 4 * c4);
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+              const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+              for (int u = 0; u < 4; u += 2) {
+                const int c = 4 * c4 + u;
+                float a0, a1;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])),
+                                 sl2x2, f2_pack(lv[u], lv[u + 1])),
+                          a0, a1);
+                const bool v0 = key_ok && (!diag || kj <= qc0 + cc * 32 + c);
+                const bool v1 = key_ok && (!diag || kj <= qc0 + cc * 32 + c + 1);
+                p[c] = v0 ? ex2_approx(a0) : 0.f;
+                p[c + 1] = v1 ? ex2_approx(a1) : 0.f;
+                const uint64_t dd = f2_add(
+                    f2_pack(__uint_as_float(rdp[c]), __uint_as_float(rdp[c + 1])),
+                    f2_pack(dv[u], dv[u + 1]));
+                f2_unpack(f2_mul(f2_pack(p[c], p[c + 1]), dd), ds[c], ds[c + 1]);
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w, v;
+              w.x = pack_bf16x2(p[8 * q + 0], p[8 * q + 1]);
+              w.y = pack_bf16x2(p[8 * q + 2], p[8 * q + 3]);
+              w.z = pack_bf16x2(p[8 * q + 4], p[8 * q + 5]);
+              w.w = pack_bf16x2(p[8 * q + 6], p[8 * q + 7]);
+              v.x = pack_bf16x2(ds[8 * q + 0], ds[8 * q + 1]);
+              v.y = pack_bf16x2(ds[8 * q + 2], ds[8 * q + 3]);
+              v.z = pack_bf16x2(ds[8 * q + 4], ds[8 * q + 5]);
+              v.w = pack_bf16x2(ds[8 * q + 6], ds[8 * q + 7]);
+              st_sw128_chunk(pb, r, cc * 4 + q, w);
+              st_sw128_chunk(db, r, cc * 4 + q, v);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.s_free);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.p_ready);
+          // results of the previous step, then queue this step's
+          if (!flush()) { ok = false; break; }
+          if (kt == last_k(i)) {
+            pend.dq_tile = i;
+            pend.dq_b = b;
+            pend.dq_h = h;
+            pend.dq_n = n;
+          }
+          if (i == n_t - 1) {
+            pend.kv_tile = kt;
+            pend.kv_b = b;
+            pend.kv_h = h;
+          }
+        }
+      }
+    }
+    if (ok) flush();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
 }  // namespace
 
 
@@ -1393,6 +1794,18 @@ cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// FLODL_FLASH_BWD=v1 keeps the key-tile kernel (f32 dQ accumulator) for
+// every sequence length instead of the per-(batch, head) kernel for S <= 256.
+static bool use_bwd_v1() {
+  static const bool v1 = [] {
+    const char* e = std::getenv("FLODL_FLASH_BWD");
+    return e != nullptr && std::strcmp(e, "v1") == 0;
+  }();
+  return v1;
+}
+
+bool flash_bwd_needs_dq_acc(int S) { return S > 2 * kTile || use_bwd_v1(); }
+
 cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   if (a.D != kD || a.S <= 0 || a.B <= 0 || a.H <= 0) return cudaErrorInvalidValue;
   const int C = a.H * kD;
@@ -1401,6 +1814,29 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   if (!make_map_3d(&tm_do, a.dout, a.B, a.S, C)) return cudaErrorInvalidValue;
   const int64_t rows = (int64_t)a.B * a.S * a.H;
   int pre_blocks = (int)std::min<int64_t>((rows + 31) / 32, (int64_t)num_sms() * 16);
+  if (!flash_bwd_needs_dq_acc(a.S)) {
+    // dQ stays in TMEM: delta only, then one kernel per (batch, head)
+    flash_bwd_pre_kernel<<<pre_blocks, 256, 0, st>>>(a.dout, a.out, a.delta, nullptr, a.B, a.S,
+                                                     a.H);
+    const int smem = (int)sizeof(BwdBhSmem) + 1024;
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load(std::memory_order_relaxed) & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(flash_bwd_bh_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      done.fetch_or(bit);
+    }
+    const int grid = std::min(a.B * a.H, num_sms());
+    flash_bwd_bh_kernel<<<grid, kBwdThreads, smem, st>>>(
+        tm_qkv, tm_do, a.lse2, a.delta, a.dqkv, a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0,
+        a.scale, a.dbias, a.err ? a.err : default_err_word());
+    note_launch(2);
+    return cudaGetLastError();
+  }
+  if (a.dq_acc == nullptr) return cudaErrorInvalidValue;
   flash_bwd_pre_kernel<<<pre_blocks, 256, 0, st>>>(a.dout, a.out, a.delta, a.dq_acc, a.B, a.S, a.H);
   const int smem = (int)sizeof(BwdSmem) + 1024;
   {

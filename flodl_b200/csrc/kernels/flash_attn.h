@@ -17,7 +17,7 @@ struct FlashArgs {
   const __nv_bfloat16* dout = nullptr; // [B*S, H*D]
   __nv_bfloat16* dqkv = nullptr;       // [B*S, 3*H*D]
   float* delta = nullptr;              // [B, H, S] scratch
-  float* dq_acc = nullptr;             // [B*S, H*D] f32 scratch
+  float* dq_acc = nullptr;             // [B*S, H*D] f32 scratch (only if flash_bwd_needs_dq_acc(S))
   float* dbias = nullptr;              // [3*H*D] f32: += column sums of dqkv (nullable)
   int B = 0, S = 0, H = 0, D = 0;
   bool causal = false;
@@ -27,6 +27,9 @@ struct FlashArgs {
 
 cudaError_t launch_flash_fwd(const FlashArgs& a, cudaStream_t st);
 cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st);
+// Whether the backward for sequence length S uses the f32 dQ accumulator
+// (S > 256: key-tile kernel); for S <= 256 dQ stays in tensor memory.
+bool flash_bwd_needs_dq_acc(int S);
 void set_flash_wait_limit_ns(uint64_t ns);
 
 }  // namespace flodl

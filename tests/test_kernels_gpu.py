@@ -310,3 +310,24 @@ def test_linear_odd_features_padded_path(fused_linear_only):
     torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
     for got, ref in ((x.grad, xr.grad), (w.grad, wr.grad), (b.grad, br.grad)):
         assert ((got - ref).norm() / ref.norm()).item() < 2e-2
+
+
+def test_flash_attention_previous_kernels_still_match():
+    """FLODL_FLASH_FWD=v1 / FLODL_FLASH_BWD=v1 select the one-CTA-per-SM
+    forward and the key-tile backward with the f32 dQ accumulator (kept for
+    comparison runs); checked in a child process because the switches are read
+    once per process."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys\n"
+        "sys.path.insert(0, %r)\n"
+        "from tests.test_kernels_gpu import test_flash_attention_fwd_bwd as t\n"
+        "t(2, 256, 2, True); t(1, 200, 3, False)\n"
+        "print('ok')\n" % root)
+    env = dict(os.environ, FLODL_FLASH_FWD="v1", FLODL_FLASH_BWD="v1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=300, cwd=root)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
