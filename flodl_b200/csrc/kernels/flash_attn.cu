@@ -1604,25 +1604,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       pend.kv_tile = -1;
       return good;
     };
+    // softmax statistics of this warp's queries (both query tiles, negated
+    // for the packed FMAs), loaded one item ahead so their latency hides
+    // behind the previous item's steps
+    float cl[2][2], cd[2][2], nl[2][2], nd[2][2];
+    auto load_stats = [&](int item, float (&l)[2][2], float (&d)[2][2]) {
+      const int h = item % H, b = item / H;
+      const float* lrow = lse2 + ((size_t)b * H + h) * S;
+      const float* drow = delta + ((size_t)b * H + h) * S;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int qi = i * kTile + hh * 64 + u * 32 + lane;
+          const bool in = i < n_t && qi < S;
+          l[i][u] = in ? -__ldg(lrow + qi) : -INFINITY;
+          d[i][u] = in ? -__ldg(drow + qi) : 0.f;
+        }
+    };
+    if (blockIdx.x < n_items) load_stats(blockIdx.x, cl, cd);
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
       const int h = item % H, b = item / H;
+      if (item + (int)gridDim.x < n_items) load_stats(item + gridDim.x, nl, nd);
       for (int kt = 0; kt < n_t && ok; ++kt) {
         const int kj = kt * kTile + r;
         const bool key_ok = kj < S && !(key_pad && __ldg(key_pad + (size_t)b * S + kj) != 0);
         for (int i = first_q(kt); i < n_t; ++i, ++t) {
           const int q0 = i * kTile;
           const int qc0 = q0 + hh * 64;  // first query of this warp's half
-          {
-            const float* lrow = lse2 + ((size_t)b * H + h) * S;
-            const float* drow = delta + ((size_t)b * H + h) * S;
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int qi = qc0 + u * 32 + lane;
-              st_lse[u * 32 + lane] = qi < S ? -__ldg(lrow + qi) : -INFINITY;
-              st_dl[u * 32 + lane] = qi < S ? -__ldg(drow + qi) : 0.f;
-            }
-            __syncwarp();
+          for (int u = 0; u < 2; ++u) {
+            st_lse[u * 32 + lane] = i == 0 ? cl[0][u] : cl[1][u];
+            st_dl[u * 32 + lane] = i == 0 ? cd[0][u] : cd[1][u];
           }
+          __syncwarp();
           ok = mbar_wait_bounded(&sm.s_full, t & 1, abort_flag, err, limit);
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
           ok = mbar_wait_bounded(&sm.pds_free, (t & 1) ^ 1, abort_flag, err, limit);
@@ -1697,6 +1712,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       }
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          cl[i][u] = nl[i][u];
+          cd[i][u] = nd[i][u];
+        }
     }
     if (ok) flush();
   }

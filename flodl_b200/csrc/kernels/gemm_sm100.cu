@@ -953,6 +953,15 @@ static bool pair_tiles_enabled() {
   return on;
 }
 
+// Shortest reduction per tile that takes CTA-pair tiles (FLODL_GEMM_PAIR_MIN_K).
+static int pair_min_k() {
+  static const int k = [] {
+    const char* v = std::getenv("FLODL_GEMM_PAIR_MIN_K");
+    return v ? std::max(64, std::atoi(v)) : 1024;
+  }();
+  return k;
+}
+
 cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   g_gemm_fail = nullptr;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.k_splits < 1) {
@@ -975,7 +984,7 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   // halves; shorter loops (K = 512) measured faster on single-CTA tiles,
   // where fill latency and the epilogue dominate. bn = 128 / 256 force the
   // single-CTA tiles.
-  const bool pair = wide && g.bn == 0 && g.M >= 512 && g.K / g.k_splits >= 1024 &&
+  const bool pair = wide && g.bn == 0 && g.M >= 512 && g.K / g.k_splits >= pair_min_k() &&
                     pair_tiles_enabled();
 #define FL_GEMM_CASE(AMN, BMN)                                                   \
   if (g.a_mn == AMN && g.b_mn == BMN)                                           \

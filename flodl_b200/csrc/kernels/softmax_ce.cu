@@ -166,7 +166,16 @@ __global__ void __launch_bounds__(256) softmax_ce_warp_kernel(CeArgs a) {
       }
     }
   }
-  if (lane == 0 && loss_acc != 0.f) atomicAdd(a.loss, loss_acc);
+  // one atomic per block: same-address atomics serialise in L2, one per warp
+  // cost more than the whole row pass
+  __shared__ float warp_loss[8];
+  if (lane == 0) warp_loss[threadIdx.x >> 5] = loss_acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += warp_loss[w];
+    if (tot != 0.f) atomicAdd(a.loss, tot);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
@@ -231,9 +240,9 @@ cudaError_t launch_softmax_ce(const CeArgs& a, cudaStream_t st) {
                        (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(a.dlogits) & 15) == 0;
   if (aligned && a.V <= 32 * 8 * 8) {
-    // warp per row; enough warps for every SM, at most one row per warp and pass
+    // warp per row; 32 warps per SM (a few rows each), 8 warps per block
     const int nc = (a.V + 255) / 256;
-    const int64_t warps = std::min<int64_t>(a.T, (int64_t)num_sms() * 64);
+    const int64_t warps = std::min<int64_t>(a.T, (int64_t)num_sms() * 32);
     const int grid = (int)((warps * 32 + 255) / 256);
     switch (nc) {
       case 1: softmax_ce_warp_kernel<1><<<grid, 256, 0, st>>>(a); break;
