@@ -218,9 +218,41 @@ def _commands(a) -> int:
 
 def _run(a) -> int:
     from .manifest import run, split_env
+    from .schema import load_cached, validate_tail
     env, rest = split_env(a.rest)
     extra = rest[1:] if rest and rest[0] == "--" else rest
+    sch = load_cached(".", a.name)
+    if sch is not None:
+        errs = validate_tail(sch, extra)
+        if errs:
+            for e in errs:
+                print(f"{a.name}: {e}", file=sys.stderr)
+            return 2
     return run(a.name, extra, ".", env, a.dry_run)
+
+
+def _schema(a) -> int:
+    from .schema import main_schema
+    return main_schema(a.rest)
+
+
+def _config(a) -> int:
+    from .manifest import show_config, split_env
+    env, rest = split_env(a.rest)
+    if not rest or rest[0] in ("-h", "--help"):
+        print("usage: config show [<env>|@env]")
+        return 0 if rest else 1
+    if rest[0] != "show":
+        print(f"unknown config sub-command: {rest[0]}", file=sys.stderr)
+        return 1
+    env = rest[1] if len(rest) > 1 else env
+    try:
+        for line in show_config(".", env):
+            print(line)
+    except FileNotFoundError as e:
+        print(f"error: {e}", file=sys.stderr)
+        return 1
+    return 0
 
 
 def _join(a) -> int:
@@ -402,6 +434,10 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("publish", help="validate and publish a run directory")
     p.add_argument("src")
     p.add_argument("dest")
+    p = sub.add_parser("schema", help="cached --fdl-schema outputs: list | clear | refresh")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
+    p = sub.add_parser("config", help="config show [<env>]: the merged fdl.yml with sources")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
     return ap
 
 
@@ -410,4 +446,4 @@ def main(argv=None) -> int:
     return {"probe": _probe, "diagnose": _diagnose, "status": _status, "start": _start,
             "launch": _launch, "init": _init, "completions": _completions,
             "commands": _commands, "run": _run, "join": _join, "api-ref": _api_ref, "add": _add,
-            "publish": _publish}[a.cmd](a)
+            "publish": _publish, "schema": _schema, "config": _config}[a.cmd](a)

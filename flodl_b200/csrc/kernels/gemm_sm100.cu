@@ -875,6 +875,17 @@ static cudaError_t launch_instance(const GemmArgs& g, cudaStream_t stream, const
   }
 }
 
+// FLODL_GEMM_EPI_SLOTS: 0 (unset) = automatic, 1 or 2 = staging slots per
+// epilogue warp for epilogues without an input (read once per process).
+static int epi_slots_override() {
+  static const int v = [] {
+    const char* e = std::getenv("FLODL_GEMM_EPI_SLOTS");
+    const int k = e ? std::atoi(e) : 0;
+    return (k == 1 || k == 2) ? k : 0;
+  }();
+  return v;
+}
+
 template <int BN, bool A_MN, bool B_MN, bool kPair = false>
 static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   CUtensorMap tmA, tmB;
@@ -932,13 +943,18 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   }
   uint32_t* err = g.err ? g.err : default_err_word();
-  // single staging slot (one more operand stage) when the epilogue has no input
+  // Epilogues without an input take two staging slots (chunk j is computed
+  // while chunk j-1's store still reads its slot) when that costs no operand
+  // stage (BN = 192), else one slot and the extra operand stage.
+  // FLODL_GEMM_EPI_SLOTS=1|2 forces the choice.
+  constexpr bool two_free = GemmCfg<BN, 2, kPair>::kStages == GemmCfg<BN, 1, kPair>::kStages;
+  const int forced = epi_slots_override();
+  const bool two = in_kind != kInNone || (forced ? forced == 2 : two_free);
   cudaError_t e =
-      in_kind == kInNone
-          ? launch_instance<BN, A_MN, B_MN, 1, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
-                                                      use_tma ? 1 : 0, in_kind, err)
-          : launch_instance<BN, A_MN, B_MN, 2, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
-                                                      use_tma ? 1 : 0, in_kind, err);
+      !two ? launch_instance<BN, A_MN, B_MN, 1, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
+                                                       use_tma ? 1 : 0, in_kind, err)
+           : launch_instance<BN, A_MN, B_MN, 2, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
+                                                       use_tma ? 1 : 0, in_kind, err);
   if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();

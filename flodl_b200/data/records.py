@@ -1,4 +1,4 @@
-"""Fixed-stride record files: positioned per-record reads.
+"""Record files with a fixed byte stride per record, read one record at a time by offset.
 
 Reference: flodl/src/data/records.rs. Many raw dataset files are fixed-size
 records behind a fixed header (CIFAR-10 binary batches: 3073-byte records;

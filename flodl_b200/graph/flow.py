@@ -71,7 +71,8 @@ class FlowBuilder:
         self.taps: Dict[str, NodeRef] = {}
         self.on_target: Optional[NodeRef] = None
         self.fork_target: Optional[NodeRef] = None
-        self.counters: Dict[str, int] = {}
+        self.counter = 0  # one sequence over every node kind: linear_1, gelu_2, linear_3
+        self.input_names: List[str] = []
         self.err: Optional[str] = None
         self.pending: Dict[str, List[str]] = {}
         self.forward_refs: List[ForwardRef] = []
@@ -81,6 +82,7 @@ class FlowBuilder:
         self._verbose = False
         ref = self._add_module(module if module is not None else Identity())
         self.inputs.append(NodeRef(ref.node_id, DEFAULT_INPUT))
+        self.input_names.append(DEFAULT_INPUT)
         self.on_target = ref
         self.current = [ref]
 
@@ -99,9 +101,11 @@ class FlowBuilder:
             self.err = msg
 
     def next_id(self, prefix: str) -> str:
-        n = self.counters.get(prefix, 0) + 1
-        self.counters[prefix] = n
-        return f"{prefix}_{n}"
+        """Node ids as the reference's builder forms them: the prefix and one
+        counter shared by every node of the graph (flodl/src/graph/flow.rs
+        ``next_id``), so untagged parameters get the same checkpoint keys."""
+        self.counter += 1
+        return f"{prefix}_{self.counter}"
 
     def _add_node(self, node: Node) -> NodeRef:
         self.nodes[node.id] = node
@@ -237,9 +241,10 @@ class FlowBuilder:
             if name in self.taps:
                 self.fail(f"input tag {name!r} conflicts with existing tag")
                 return self
-            ref = self._add_node(Node(self.next_id("input"), "input"))
+            ref = self._add_node(Node(self.next_id(f"input_{name}"), "input"))
             self.taps[name] = ref
             self.inputs.append(NodeRef(ref.node_id, DEFAULT_INPUT))
+            self.input_names.append(name)
             self._resolve_pending(name, ref)
         return self
 

@@ -41,6 +41,7 @@ class Graph(Module):
             [n.module if n.module is not None else torch.nn.Identity() for n in self._node_list])
         self.edges = list(fb.edges)
         self.inputs = list(fb.inputs)
+        self.input_names = list(fb.input_names)
         self.output = fb.current[0]
         self.forward_refs = list(fb.forward_refs)
         self.tag_names = dict(fb.taps)
@@ -313,6 +314,24 @@ class Graph(Module):
                 for s in (e.from_node, e.from_port, e.to_node, e.to_port):
                     h.update_str(s)
                     h.update(b"\0")
+            # tags by name: (node index, output-port index; every node has the
+            # single output port), then the exposed input and output ports
+            h.update_str("TAGS")
+            for name in sorted(self.tag_names):
+                ref = self.tag_names[name]
+                h.update_str(name)
+                h.update(b"\0")
+                h.update_i64(self._index[ref.node_id])
+                h.update_i64(0)
+            h.update_str("INPUTS")
+            for name, ref in zip(self.input_names, self.inputs):
+                for s in (name, ref.node_id, ref.port):
+                    h.update_str(s)
+                    h.update(b"\0")
+            h.update_str("OUTPUTS")
+            for s in ("output", self.output.node_id, self.output.port):
+                h.update_str(s)
+                h.update(b"\0")
             self._hash = h.hexdigest()
         return self._hash
 

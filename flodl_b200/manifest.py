@@ -11,6 +11,7 @@ replaces the base value, and a ``null`` in the overlay deletes the key.
 """
 from __future__ import annotations
 
+import json
 import os
 import shlex
 import subprocess
@@ -48,6 +49,53 @@ def load_manifest(directory: str = ".", env: Optional[str] = None) -> dict:
             m = deep_merge(m, yaml.safe_load(f) or {})
     m.setdefault("commands", {})
     return m
+
+
+def config_layers(directory: str = ".", env: Optional[str] = None) -> List[Tuple[str, dict]]:
+    """The files that make up the resolved manifest, base first: ``fdl.yml``,
+    then the ``fdl.<env>.yml`` overlay when an environment is selected."""
+    layers = []
+    with open(os.path.join(directory, "fdl.yml")) as f:
+        layers.append(("fdl.yml", yaml.safe_load(f) or {}))
+    env = env or os.environ.get(ENV_VAR)
+    if env:
+        op = os.path.join(directory, f"fdl.{env}.yml")
+        if not os.path.exists(op):
+            raise FileNotFoundError(f"overlay fdl.{env}.yml not found in {directory}")
+        with open(op) as f:
+            layers.append((f"fdl.{env}.yml", yaml.safe_load(f) or {}))
+    return layers
+
+
+def show_config(directory: str = ".", env: Optional[str] = None) -> List[str]:
+    """The merged manifest, one leaf per line (``dotted.key: value``), each
+    tagged with the file that set it (the reference's ``fdl config show``)."""
+    layers = config_layers(directory, env)
+    merged, source = {}, {}
+
+    def walk(node, prefix, label):
+        for k, v in (node or {}).items():
+            key = f"{prefix}.{k}" if prefix else str(k)
+            if v is None:  # an overlay null deletes the key
+                for s in [s for s in source if s == key or s.startswith(key + ".")]:
+                    source.pop(s)
+            elif isinstance(v, dict):
+                walk(v, key, label)
+            else:
+                source[key] = label
+
+    for label, data in layers:
+        merged = deep_merge(merged, data)
+        walk(data, "", label)
+
+    def value(key):
+        node = merged
+        for part in key.split("."):
+            node = node[part]
+        return node
+
+    width = max((len(k) for k in source), default=0)
+    return [f"{k:<{width}}  {json.dumps(value(k))}  # {source[k]}" for k in sorted(source)]
 
 
 def split_env(args: List[str]) -> Tuple[Optional[str], List[str]]:

@@ -90,3 +90,76 @@ def test_migrate_renames(tmp_path):
     rep = migrate_checkpoint(src, dst, {"old/w": "new/w"})
     assert rep.renamed == [("old/w", "new/w")]
     assert checkpoint_keys(dst) == ["new/w"]
+
+
+# ------------------------------------------------------------------ reference-format fixture
+def _ref_structural_hash():
+    """SHA-256 over the fields the reference hashes (flodl/src/graph/checkpoint.rs
+    compute_structural_hash), written out field by field for the graph
+    Linear(4, 8) -[tag enc]-> GELU -> Linear(8, 2): nodes in topological order
+    with their module names and sorted (parameter, shape) lists, the edges, the
+    tags with (node index, port index), then the exposed input and output ports.
+    Independent of this package's Graph.structural_hash."""
+    import hashlib
+    h = hashlib.sha256()
+    z = b"\0"
+    i64 = lambda v: struct.pack("<q", v)
+    u64 = lambda v: struct.pack("<Q", v)
+    h.update(b"linear_1" + z + b"linear" + z)
+    h.update(b"P" + b"bias" + z + i64(8))
+    h.update(b"P" + b"weight" + z + i64(8) + i64(4))
+    h.update(b"gelu_2" + z + b"gelu" + z)
+    h.update(b"linear_3" + z + b"linear" + z)
+    h.update(b"P" + b"bias" + z + i64(2))
+    h.update(b"P" + b"weight" + z + i64(2) + i64(8))
+    h.update(b"EDGES")
+    h.update(b"linear_1" + z + b"output" + z + b"gelu_2" + z + b"input" + z)
+    h.update(b"gelu_2" + z + b"output" + z + b"linear_3" + z + b"input" + z)
+    h.update(b"TAGS" + b"enc" + z + u64(0) + u64(0))
+    h.update(b"INPUTS" + b"input" + z + b"linear_1" + z + b"input" + z)
+    h.update(b"OUTPUTS" + b"output" + z + b"linear_3" + z + b"output" + z)
+    return h.hexdigest()
+
+
+def _ref_fdl_bytes(hash_hex, entries):
+    """A .fdl file assembled by hand from the reference's layout
+    (flodl/src/nn/checkpoint.rs save_checkpoint / write_tensor_data):
+    MAGIC | u32 version 2 | 32-byte hash | u32 count | entries, each
+    u32 name_len | name | u32 ndim | i64 dims | u8 dtype tag | u64 nbytes | raw."""
+    out = bytearray(b"FDLC" + struct.pack("<I", 2) + bytes.fromhex(hash_hex) +
+                    struct.pack("<I", len(entries)))
+    for name, t in entries:
+        nb = name.encode()
+        out += struct.pack("<I", len(nb)) + nb + struct.pack("<I", t.dim())
+        out += b"".join(struct.pack("<q", d) for d in t.shape)
+        raw = t.contiguous().numpy().tobytes()
+        out += bytes([3]) + struct.pack("<Q", len(raw)) + raw
+    return bytes(out)
+
+
+def test_structural_hash_matches_the_reference_algorithm():
+    assert _build(0).structural_hash() == _ref_structural_hash()
+
+
+def test_loads_a_hand_assembled_reference_checkpoint(tmp_path):
+    torch.manual_seed(5)
+    want = {"enc/weight": torch.randn(8, 4), "enc/bias": torch.randn(8),
+            "linear_3/weight": torch.randn(2, 8), "linear_3/bias": torch.randn(2)}
+    order = ["enc/weight", "enc/bias", "linear_3/weight", "linear_3/bias"]
+    blob = _ref_fdl_bytes(_ref_structural_hash(), [(k, want[k]) for k in order])
+    p = tmp_path / "ref.fdl"
+    p.write_bytes(blob)
+    g = _build(1)
+    rep = load_model(g, str(p))  # validates the structural hash
+    assert sorted(rep.loaded) == sorted(order) and not rep.missing and not rep.skipped
+    got = dict(g.graph_named_parameters())
+    for k in order:
+        torch.testing.assert_close(got[k].detach(), want[k])
+    # this package writes the same bytes for the same model
+    q = tmp_path / "ours.fdl"
+    save_model(g, str(q))
+    assert q.read_bytes() == blob
+    # a different architecture is refused by the hash
+    other = FlowBuilder.from_(Linear(4, 8)).tag("enc").through(GELU()).through(Linear(8, 3)).build()
+    with pytest.raises(Exception):
+        load_model(other, str(p))

@@ -15,14 +15,16 @@ def test_sequential_and_residual():
     ref = l3(h + l2(h))
     torch.testing.assert_close(g(x), ref)
     names = [n for n, _ in g.graph_named_parameters()]
-    assert names == ["linear_1/weight", "linear_1/bias", "layernorm_1/weight", "layernorm_1/bias",
-                     "linear_2/weight", "linear_2/bias", "linear_3/weight", "linear_3/bias"]
+    # node ids share one counter across node kinds, as the reference's builder
+    # numbers them (linear_1, gelu_2, layernorm_3, linear_4, add_5, linear_6)
+    assert names == ["linear_1/weight", "linear_1/bias", "layernorm_3/weight", "layernorm_3/bias",
+                     "linear_4/weight", "linear_4/bias", "linear_6/weight", "linear_6/bias"]
 
 
 def test_tag_names_parameters_and_tagged_values():
     g = FlowBuilder.from_(Linear(4, 4)).tag("enc").through(ReLU()).tag("act").through(Linear(4, 2)).build()
     names = [n for n, _ in g.graph_named_parameters()]
-    assert names[0] == "enc/weight" and names[-1] == "linear_2/bias"
+    assert names[0] == "enc/weight" and names[-1] == "linear_3/bias"
     x = torch.randn(2, 4)
     g(x)
     assert torch.all(g.tagged("act") >= 0)
@@ -92,7 +94,7 @@ def test_loops_for_while_until():
     assert ctr["n"] == 3
     g3 = FlowBuilder.new().loop_body(Identity()).until_cond(ThresholdHalt(-100.0), 5).build()
     g3(x)
-    assert g3.traces_by_node("loop_1") is not None and len(g3.traces_by_node("loop_1")) == 1
+    assert g3.traces_by_node("loop_2") is not None and len(g3.traces_by_node("loop_2")) == 1
 
 
 def test_gate_and_switch():
