@@ -943,13 +943,11 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   }
   uint32_t* err = g.err ? g.err : default_err_word();
-  // Epilogues without an input take two staging slots (chunk j is computed
-  // while chunk j-1's store still reads its slot) when that costs no operand
-  // stage (BN = 192), else one slot and the extra operand stage.
-  // FLODL_GEMM_EPI_SLOTS=1|2 forces the choice.
-  constexpr bool two_free = GemmCfg<BN, 2, kPair>::kStages == GemmCfg<BN, 1, kPair>::kStages;
-  const int forced = epi_slots_override();
-  const bool two = in_kind != kInNone || (forced ? forced == 2 : two_free);
+  // Epilogues without an input take a single staging slot (the previous
+  // chunk's store reads it while this chunk is computed) and one more operand
+  // stage where that fits; two slots measured slower (qkv 28.5 -> 30.1 us,
+  // fc1 58.8 -> 62.6 us). FLODL_GEMM_EPI_SLOTS=2 selects two slots.
+  const bool two = in_kind != kInNone || epi_slots_override() == 2;
   cudaError_t e =
       !two ? launch_instance<BN, A_MN, B_MN, 1, kPair>(g, stream, tmA, tmB, tmOut, tmAux, tmIn,
                                                        use_tma ? 1 : 0, in_kind, err)

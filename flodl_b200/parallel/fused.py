@@ -20,6 +20,13 @@ the global norm, scales by ``max_norm / (norm + 1e-6)`` when the norm is above
 ``max_norm`` (the reference's ``clip_grad_norm``, flodl-sys/ops_training.cpp:
 948-985) and then updates and all-gathers every bucket.
 
+Several parameter groups (their own lr, weight decay, betas) share one
+symmetric region: group k's arena is a slice of it, buckets never span two
+groups, each bucket launch carries its group's hyper-parameters, and the
+optimizer moments live in region-sized buffers (each group's state a view at
+its base) because the kernels index state by region position. Global-norm
+clipping is fused for a single group.
+
 Semantics equal the reference's ``Ddp::wrap`` + ``all_reduce_gradients`` (Avg)
 + ``optimizer.step()`` (flodl/src/distributed/ddp.rs:249-260): every rank ends
 the step with identical parameters. Optimizer moments of a two-shot bucket are
@@ -67,39 +74,70 @@ class FusedDdp:
             overlap_blocks = int(env.get("FLODL_DDP_OVERLAP_BLOCKS", "0"))
         self.model = model
         self.opt = optimizer
-        if len(optimizer.groups) != 1:
-            raise ValueError("FusedDdp supports one parameter group")
-        self.group = optimizer.groups[0]
-        params = list(self.group.params)
+        self.groups = list(optimizer.groups)
+        self.group = self.groups[0]
+        params = [p for g in self.groups for p in g.params]
         self.params = params
         self.device = params[0].device
-        numel = sum((p.numel() + 63) // 64 * 64 for p in params)
+        self.max_grad_norm = float(max_grad_norm) if max_grad_norm else 0.0
+        if self.max_grad_norm and len(self.groups) > 1:
+            raise ValueError("FusedDdp: global-norm clipping is fused for one parameter group; "
+                             "use one group or clip outside the fused path")
+        sizes = [sum((p.numel() + 63) // 64 * 64 for p in g.params) for g in self.groups]
+        numel = sum(sizes)
         self.comm = PeerComm(numel, self.device, group=group, timeout_s=timeout_s)
         self.rank, self.world = self.comm.rank, self.comm.world
-        arena = ParamArena(params, alloc=self.comm.data_alloc, grad_alloc=self.comm.grad_alloc,
-                           with_shadow=False)
-        # bf16 shadow lives in the symmetric region too
-        arena.shadow = self.comm.shadow[:arena.numel]
-        arena.rebind()
-        arena.refresh_shadow()
-        self.arena = arena
-        self.group.arena = arena
+        # one symmetric region for every group: group k's arena is the slice
+        # [base_k, base_k + size_k) of the peer-mapped data/grad/shadow regions
+        self.arenas: List[ParamArena] = []
+        self.bases: List[int] = []
+        base = 0
+        for g, n in zip(self.groups, sizes):
+            lo = base
+            arena = ParamArena(g.params,
+                               alloc=lambda k, dt, dv, lo=lo: self.comm.data[lo:lo + k],
+                               grad_alloc=lambda k, dt, dv, lo=lo: self.comm.grad[lo:lo + k],
+                               with_shadow=False)
+            arena.shadow = self.comm.shadow[lo:lo + arena.numel]
+            arena.rebind()
+            arena.refresh_shadow()
+            g.arena = arena
+            self.arenas.append(arena)
+            self.bases.append(lo)
+            base += n
+        self.arena = self.arenas[0]
+        self.numel = base
         self.blocks = blocks
         self.overlap_threads = overlap_threads
         self.overlap_blocks = overlap_blocks or 2 * self.comm.C.num_sms()
         self.oneshot_elems = int(oneshot_kb * 1024 / 4)
-        self.max_grad_norm = float(max_grad_norm) if max_grad_norm else 0.0
-        # optimizer state (device scalars + moments) for the whole arena
-        optimizer._device_scalars(self.group)
         self.kind = "adamw" if isinstance(optimizer, Adam) else "sgd" if isinstance(optimizer, SGD) else None
         if self.kind is None:
             raise ValueError("FusedDdp supports Adam/AdamW and SGD")
-        if isinstance(optimizer, Adam) and not isinstance(optimizer, AdamW) and self.group.hyper["weight_decay"]:
-            raise ValueError("FusedDdp: Adam with L2 weight decay is not fused; use AdamW")
-        optimizer._init_fused_state(self.group)
+        # optimizer state (device scalars per group; moments over the whole
+        # region, each group's state a view at its base, because the kernels
+        # index state by the element's position in the region)
+        for g in self.groups:
+            optimizer._device_scalars(g)
+            if (isinstance(optimizer, Adam) and not isinstance(optimizer, AdamW)
+                    and g.hyper["weight_decay"]):
+                raise ValueError("FusedDdp: Adam with L2 weight decay is not fused; use AdamW")
+            optimizer._init_fused_state(g)
+        self._state = {}
+        names = ("m", "v") if self.kind == "adamw" else ("buf",)
+        for name in names:
+            if any(getattr(g, name, None) is None for g in self.groups):
+                continue  # SGD without momentum keeps no buffer
+            whole = torch.zeros(self.numel, device=self.device, dtype=torch.float32)
+            for g, lo in zip(self.groups, self.bases):
+                part = whole[lo:lo + g.arena.numel]
+                part.copy_(getattr(g, name))
+                setattr(g, name, part)
+            self._state[name] = whole
         if self.kind == "adamw":
             # step_t holds the number of the update the next bucket kernels apply
-            self.comm.C.add_scalar(self.group.step_t, 1.0)
+            for g in self.groups:
+                self.comm.C.add_scalar(g.step_t, 1.0)
         self.comm_stream = torch.cuda.Stream(self.device)
         self._build_buckets(bucket_mb, tail_mb)
         if self.max_grad_norm:
@@ -112,7 +150,7 @@ class FusedDdp:
             add_grad_ready_listener(p, self._on_ready)
         # initial state: rank 0's parameters on every rank (pull broadcast)
         torch.cuda.synchronize(self.device)
-        self.comm.broadcast_(arena.numel, root=0, slot=self._slot_bcast, blocks=blocks)
+        self.comm.broadcast_(self.numel, root=0, slot=self._slot_bcast, blocks=blocks)
         torch.cuda.synchronize(self.device)
         self.comm.check()
         if self.world > 1:
@@ -122,39 +160,40 @@ class FusedDdp:
         self._launched: set = set()
 
     def _build_buckets(self, bucket_mb: float, tail_mb: float) -> None:
-        """Buckets over the arena in forward parameter order: the first
-        (holding the earliest parameters, whose gradients complete last) is
-        capped at ``tail_mb``, the others at ``bucket_mb``; they launch in
-        reverse order as backward completes them."""
-        a = self.arena
+        """Buckets over the region in forward parameter order, never spanning
+        two parameter groups: the first (holding the earliest parameters,
+        whose gradients complete last) is capped at ``tail_mb``, the others at
+        ``bucket_mb``; they launch in reverse order as backward completes
+        them."""
         caps = (int(tail_mb * (1 << 20) / 4), int(bucket_mb * (1 << 20) / 4))
-        groups: List[List[int]] = []
-        cur, size = [], 0
-        for i in range(len(a.params)):
-            n = a.params[i].numel()
-            cap = caps[0] if not groups else caps[1]
-            if cur and size + n > cap:
-                groups.append(cur)
-                cur, size = [], 0
-            cur.append(i)
-            size += n
-        if cur:
-            groups.append(cur)
+        chunks: List[tuple] = []  # (group index, [param indices])
+        for gi, a in enumerate(self.arenas):
+            cur, size = [], 0
+            for i in range(len(a.params)):
+                n = a.params[i].numel()
+                cap = caps[0] if not chunks else caps[1]
+                if cur and size + n > cap:
+                    chunks.append((gi, cur))
+                    cur, size = [], 0
+                cur.append(i)
+                size += n
+            if cur:
+                chunks.append((gi, cur))
         self.buckets: List[dict] = []
         self._bucket_of: Dict[int, dict] = {}
-        for idx in reversed(groups):
-            self._close(idx)
+        for gi, idx in reversed(chunks):
+            self._close(gi, idx)
         self._slot_bcast = len(self.buckets)
         self._slot_avg = self._slot_bcast + 1
         self._slot_apply = self._slot_bcast + 2
         if self._slot_apply >= self.comm.C.MAX_SLOTS:
             raise ValueError("too many buckets; raise bucket_mb")
 
-    def _close(self, idx: List[int]) -> None:
-        a = self.arena
-        start = min(a.offsets[i] for i in idx)
-        end = max(a.offsets[i] + ((a.params[i].numel() + 63) // 64) * 64 for i in idx)
-        b = {"slot": len(self.buckets), "start": start, "end": end,
+    def _close(self, gi: int, idx: List[int]) -> None:
+        a, base = self.arenas[gi], self.bases[gi]
+        start = base + min(a.offsets[i] for i in idx)
+        end = base + max(a.offsets[i] + ((a.params[i].numel() + 63) // 64) * 64 for i in idx)
+        b = {"slot": len(self.buckets), "start": start, "end": end, "group": gi,
              "params": [a.params[i] for i in idx], "pending": len(idx),
              "oneshot": (end - start) <= self.oneshot_elems and not self.max_grad_norm}
         self.buckets.append(b)
@@ -169,15 +208,18 @@ class FusedDdp:
         if b["pending"] == 0:
             self._launch(b)
 
-    def _update_args(self) -> dict:
-        g = self.group
+    def _update_args(self, gi: int = 0) -> dict:
+        """Hyper-parameters of group gi; the state buffers are those of the
+        whole region (the kernels index them by region position)."""
+        g = self.groups[gi]
         h = g.hyper
         if self.kind == "adamw":
-            return dict(m=g.m, v=g.v, lr=g.lr_t, step=g.step_t, gscale=self.opt.gscale_t,
-                        beta1=h["beta1"], beta2=h["beta2"], eps=h["eps"], wd=h["weight_decay"])
-        return dict(m=g.buf, lr=g.lr_t, first=g.first_t, gscale=self.opt.gscale_t,
-                    wd=h["weight_decay"], momentum=h["momentum"], dampening=h["dampening"],
-                    nesterov=int(h["nesterov"]))
+            return dict(m=self._state["m"], v=self._state["v"], lr=g.lr_t, step=g.step_t,
+                        gscale=self.opt.gscale_t, beta1=h["beta1"], beta2=h["beta2"],
+                        eps=h["eps"], wd=h["weight_decay"])
+        return dict(m=self._state.get("buf"), lr=g.lr_t, first=g.first_t,
+                    gscale=self.opt.gscale_t, wd=h["weight_decay"], momentum=h["momentum"],
+                    dampening=h["dampening"], nesterov=int(h["nesterov"]))
 
     def _launch(self, b, tail: bool = False) -> None:
         """Launch bucket b's fused kernel on the communication stream. Buckets
@@ -198,7 +240,8 @@ class FusedDdp:
             else:
                 op = C.FUSED_AR_ADAMW if self.kind == "adamw" else C.FUSED_AR_SGD
                 self.comm.launch(op, bucket=b["slot"], start=b["start"], end=b["end"],
-                                 oneshot=int(b["oneshot"]), **self._update_args(), **geo)
+                                 oneshot=int(b["oneshot"]), **self._update_args(b["group"]),
+                                 **geo)
         self._launched.add(b["slot"])
 
     def finish(self) -> None:
@@ -217,10 +260,11 @@ class FusedDdp:
                                  table=self.table, nb=len(self.buckets), blocks=self.blocks,
                                  threads=512, **args)
         torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
-        if self.kind == "adamw":
-            self.comm.C.add_scalar(self.group.step_t, 1.0)
-        else:
-            self.group.first_t.zero_()
+        for g in self.groups:
+            if self.kind == "adamw":
+                self.comm.C.add_scalar(g.step_t, 1.0)
+            else:
+                g.first_t.zero_()
         for b in self.buckets:
             b["pending"] = len(b["params"])
         self._launched = set()
@@ -230,7 +274,7 @@ class FusedDdp:
     def average_params(self, mass: float = 1.0) -> None:
         """Weighted parameter average across ranks (cluster averaging);
         ``mass`` is this rank's gamma-mass."""
-        self.comm.weighted_average_(self.arena.numel, mass, slot=self._slot_avg,
+        self.comm.weighted_average_(self.numel, mass, slot=self._slot_avg,
                                     blocks=self.blocks)
 
     def close(self) -> None:

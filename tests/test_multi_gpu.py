@@ -197,6 +197,13 @@ def _make_opt(kind, params):
 
     if kind == "sgd":
         return SGD(params, lr=0.05, momentum=0.9, weight_decay=1e-4)
+    if kind == "adamw2":
+        # two parameter groups with their own lr / weight decay (matrices vs
+        # vectors), as a decay-exempt bias/norm group is usually set up
+        params = list(params)
+        return AdamW([{"params": [p for p in params if p.dim() >= 2]},
+                      {"params": [p for p in params if p.dim() < 2], "lr": 2e-3,
+                       "weight_decay": 0.0}], lr=1e-3, weight_decay=0.1)
     return AdamW(params, lr=1e-3, weight_decay=0.1)
 
 
@@ -244,17 +251,17 @@ def _fused_ddp_worker(rank, world, port, q, kind, clip, graph):
                 step()
         torch.cuda.synchronize()
         ddp.comm.check()
-        flat = ddp.arena.data.clone()
+        flat = ddp.comm.data[:ddp.numel].clone()
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         same = all(torch.equal(gathered[0], t) for t in gathered[1:])
-        shadow_ok = bool(torch.equal(ddp.arena.shadow, ddp.arena.data.bfloat16()))
+        shadow_ok = bool(torch.equal(ddp.comm.shadow[:ddp.numel], flat.bfloat16()))
         norm = float(ddp.grad_norm.item()) if clip else None
         if graph:
             del g
         q.put((rank, {"replicas equal": same, "shadow equals weights": shadow_ok,
                       "buckets >= 3": nb >= 3, "both forms": len(forms) == 2 or clip},
-               flat.cpu(), norm, None))
+               flat.cpu().numpy(), norm, None))
         ddp.close()
         dist.destroy_process_group()
     except Exception:  # pragma: no cover
@@ -281,12 +288,13 @@ def _reference(world, kind, clip):
                     gr.mul_(0.5 / (norm + 1e-6))
         opt.step()
         opt.zero_grad()
-    return opt.groups[0].arena.data.cpu(), norm
+    return torch.cat([g.arena.data for g in opt.groups]).cpu(), norm
 
 
 @pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("kind,clip,graph", [("adamw", False, False), ("sgd", False, False),
-                                             ("adamw", True, False), ("adamw", False, True)])
+                                             ("adamw", True, False), ("adamw", False, True),
+                                             ("adamw2", False, False)])
 def test_fused_ddp_matches_single_gpu_full_batch(world, kind, clip, graph):
     _need_gpus(world)
     res = _spawn(_fused_ddp_worker, world, kind, clip, graph)
@@ -295,7 +303,7 @@ def test_fused_ddp_matches_single_gpu_full_batch(world, kind, clip, graph):
         bad = [k for k, v in checks.items() if not v]
         assert not bad, f"rank {rank}: failed {bad}"
     ref, ref_norm = _reference(world, kind, clip)
-    got = res[0][2]
+    got = torch.from_numpy(res[0][2])
     torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=2e-3)
     if clip:
         got_norm = res[0][3]
