@@ -52,7 +52,7 @@ def _lm_flodl(dev, world, engine):
     model = TransformerLM(vocab_size=LM_V, d_model=512, n_layers=6, n_heads=8, d_ff=2048,
                           max_seq=LM_S, device=dev)
     ddp = None
-    if world > 1 and engine == "peer":
+    if engine == "peer":
         from .parallel.fused import FusedDdp
         opt = AdamW(model.parameters(), lr=3e-4, weight_decay=0.1)
         ddp = FusedDdp(model, opt)
@@ -141,7 +141,7 @@ def _bert_flodl(dev, world, engine):
 
     model = BertForMaskedLM(BertConfig.bert_base_uncased(), device=dev)
     ddp = None
-    if world > 1 and engine == "peer":
+    if engine == "peer":
         from .parallel.fused import FusedDdp
         opt = AdamW(model.parameters(), lr=1e-4, weight_decay=0.01)
         ddp = FusedDdp(model, opt)
@@ -204,7 +204,7 @@ def _rn_flodl(dev, world, engine):
     model = ResNet20(device=dev)
     ddp = None
     mk = lambda: SGD(model.parameters(), lr=0.1, momentum=0.9, weight_decay=1e-4)
-    if world > 1 and engine == "peer":
+    if engine == "peer":
         from .parallel.fused import FusedDdp
         opt = mk()
         ddp = FusedDdp(model, opt)

@@ -48,6 +48,38 @@ void col2im(const Tensor& dcols, Tensor& dx, int64_t k, int64_t s, int64_t p,
                                   N, H, W, C, (int)k, (int)s, (int)p, cur_stream()));
 }
 
+// Rectangular-kernel forms (per-axis kernel, stride, padding).
+void im2col_geo(const Tensor& x, Tensor& cols, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                int64_t ph, int64_t pw) {
+  check_nhwc(x, "x");
+  FL_CHECK(cols.scalar_type() == at::kBFloat16 && cols.dim() == 2 && cols.is_contiguous(),
+           "cols must be contiguous bf16 [M, kh*kw*C]");
+  const int N = (int)x.size(0), H = (int)x.size(1), W = (int)x.size(2), C = (int)x.size(3);
+  FL_CHECK(C % 8 == 0, "im2col needs a multiple of 8 channels");
+  const int Ho = (H + 2 * (int)ph - (int)kh) / (int)sh + 1;
+  const int Wo = (W + 2 * (int)pw - (int)kw) / (int)sw + 1;
+  FL_CHECK(cols.size(0) == (int64_t)N * Ho * Wo && cols.size(1) == C * kh * kw, "cols shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_im2col_geo(ptr<__nv_bfloat16>(x), ptr<__nv_bfloat16>(cols), N, H, W, C,
+                                      flodl::ConvGeo{(int)kh, (int)kw, (int)sh, (int)sw, (int)ph,
+                                                     (int)pw},
+                                      cur_stream()));
+}
+
+void col2im_geo(const Tensor& dcols, Tensor& dx, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                int64_t ph, int64_t pw) {
+  check_nhwc(dx, "dx");
+  FL_CHECK(dcols.scalar_type() == at::kBFloat16 && dcols.dim() == 2 && dcols.stride(1) == 1,
+           "dcols must be row-major bf16 [M, >= C*kh*kw]");
+  const int N = (int)dx.size(0), H = (int)dx.size(1), W = (int)dx.size(2), C = (int)dx.size(3);
+  c10::cuda::CUDAGuard guard(dx.device());
+  FL_CUDA_OK(flodl::launch_col2im_geo(ptr<__nv_bfloat16>(dcols), (int)dcols.stride(0),
+                                      ptr<__nv_bfloat16>(dx), nullptr, false, nullptr, N, H, W, C,
+                                      flodl::ConvGeo{(int)kh, (int)kw, (int)sh, (int)sw, (int)ph,
+                                                     (int)pw},
+                                      cur_stream()));
+}
+
 void bn_stats(const Tensor& x, Tensor& mean, Tensor& rstd, const optional<Tensor>& run_mean,
               const optional<Tensor>& run_var, Tensor& ws, double eps, double momentum) {
   FL_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x");
@@ -162,6 +194,8 @@ void register_conv(py::module& m) {
         py::arg("pad"));
   m.def("col2im", &col2im, py::arg("dcols"), py::arg("dx"), py::arg("k"), py::arg("stride"),
         py::arg("pad"), py::arg("add") = py::none(), py::arg("mask") = py::none());
+  m.def("im2col_geo", &im2col_geo);
+  m.def("col2im_geo", &col2im_geo);
   m.def("bn_stats", &bn_stats, py::arg("x"), py::arg("mean"), py::arg("rstd"),
         py::arg("run_mean"), py::arg("run_var"), py::arg("ws"), py::arg("eps"),
         py::arg("momentum"));

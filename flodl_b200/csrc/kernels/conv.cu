@@ -40,13 +40,14 @@ int blocks_for(int64_t work, int threads, int per_sm) {
 }
 
 // ---------------------------------------------------------------- im2col / col2im
-// cols[pix, (kh*k + kw)*C + c] = x[n, ho*s - p + kh, wo*s - p + kw, c] (0 outside).
+// cols[pix, (kh*kw_ + kw)*C + c] = x[n, ho*sh - ph + kh, wo*sw - pw + kw, c] (0
+// outside), for a kh_ x kw_ kernel with per-axis stride and padding.
 // Thread = (output pixel, tap, group of 8 channels): one 16-byte load or zero,
 // one 16-byte store.
 __global__ void im2col_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ cols,
-                              int N, int H, int W, int C, int Ho, int Wo, int k, int s, int p) {
+                              int N, int H, int W, int C, int Ho, int Wo, ConvGeo g2) {
   const int G = C / 8;
-  const int kk = k * k;
+  const int kk = g2.kh * g2.kw;
   const int64_t total = (int64_t)N * Ho * Wo * kk * G;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -58,8 +59,8 @@ __global__ void im2col_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16
     t = pix / Wo;
     const int ho = (int)(t % Ho);
     const int n = (int)(t / Ho);
-    const int h = ho * s - p + tap / k;
-    const int w = wo * s - p + tap % k;
+    const int h = ho * g2.sh - g2.ph + tap / g2.kw;
+    const int w = wo * g2.sw - g2.pw + tap % g2.kw;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (h >= 0 && h < H && w >= 0 && w < W)
       v = *reinterpret_cast<const uint4*>(x + (((int64_t)n * H + h) * W + w) * C + g * 8);
@@ -75,7 +76,7 @@ template <typename TAdd>
 __global__ void col2im_kernel(const __nv_bfloat16* __restrict__ dcols, int ldc,
                               __nv_bfloat16* __restrict__ dx, const TAdd* __restrict__ add,
                               const __nv_bfloat16* __restrict__ mask, int N, int H, int W, int C,
-                              int Ho, int Wo, int k, int s, int p) {
+                              int Ho, int Wo, ConvGeo g2) {
   const int G = C / 8;
   const int64_t total = (int64_t)N * H * W * G;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -89,19 +90,19 @@ __global__ void col2im_kernel(const __nv_bfloat16* __restrict__ dcols, int ldc,
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    for (int kh = 0; kh < k; ++kh) {
-      const int hn = h + p - kh;
-      if (hn < 0 || hn % s) continue;
-      const int ho = hn / s;
+    for (int kh = 0; kh < g2.kh; ++kh) {
+      const int hn = h + g2.ph - kh;
+      if (hn < 0 || hn % g2.sh) continue;
+      const int ho = hn / g2.sh;
       if (ho >= Ho) continue;
-      for (int kw = 0; kw < k; ++kw) {
-        const int wn = w + p - kw;
-        if (wn < 0 || wn % s) continue;
-        const int wo = wn / s;
+      for (int kw = 0; kw < g2.kw; ++kw) {
+        const int wn = w + g2.pw - kw;
+        if (wn < 0 || wn % g2.sw) continue;
+        const int wo = wn / g2.sw;
         if (wo >= Wo) continue;
         const int64_t op = ((int64_t)n * Ho + ho) * Wo + wo;
         const uint4 u =
-            *reinterpret_cast<const uint4*>(dcols + op * ldc + (kh * k + kw) * C + g * 8);
+            *reinterpret_cast<const uint4*>(dcols + op * ldc + (kh * g2.kw + kw) * C + g * 8);
         const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -488,30 +489,48 @@ __global__ void cast_pad_kernel(const float* __restrict__ x, __nv_bfloat16* __re
 
 }  // namespace
 
-cudaError_t launch_im2col(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W, int C,
-                          int k, int s, int p, cudaStream_t st) {
-  const int Ho = (H + 2 * p - k) / s + 1, Wo = (W + 2 * p - k) / s + 1;
+static bool geo_ok(const ConvGeo& g) {
+  return g.kh > 0 && g.kw > 0 && g.sh > 0 && g.sw > 0 && g.ph >= 0 && g.pw >= 0;
+}
+
+cudaError_t launch_im2col_geo(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W,
+                              int C, const ConvGeo& g, cudaStream_t st) {
+  if (!geo_ok(g)) return cudaErrorInvalidValue;
+  const int Ho = (H + 2 * g.ph - g.kh) / g.sh + 1, Wo = (W + 2 * g.pw - g.kw) / g.sw + 1;
   if (Ho <= 0 || Wo <= 0 || C % 8) return cudaErrorInvalidValue;
-  im2col_kernel<<<blocks_for((int64_t)N * Ho * Wo * k * k * (C / 8), 256, 16), 256, 0, st>>>(
-      x, cols, N, H, W, C, Ho, Wo, k, s, p);
+  im2col_kernel<<<blocks_for((int64_t)N * Ho * Wo * g.kh * g.kw * (C / 8), 256, 16), 256, 0,
+                  st>>>(x, cols, N, H, W, C, Ho, Wo, g);
   note_launch();
   return cudaGetLastError();
+}
+
+cudaError_t launch_col2im_geo(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx,
+                              const void* add, bool add_f32, const __nv_bfloat16* mask, int N,
+                              int H, int W, int C, const ConvGeo& g, cudaStream_t st) {
+  if (!geo_ok(g)) return cudaErrorInvalidValue;
+  const int Ho = (H + 2 * g.ph - g.kh) / g.sh + 1, Wo = (W + 2 * g.pw - g.kw) / g.sw + 1;
+  if (C % 8) return cudaErrorInvalidValue;
+  const int blocks = blocks_for((int64_t)N * H * W * (C / 8), 256, 16);
+  if (add_f32)
+    col2im_kernel<float><<<blocks, 256, 0, st>>>(dcols, ldc, dx, (const float*)add, mask, N, H, W,
+                                                 C, Ho, Wo, g);
+  else
+    col2im_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        dcols, ldc, dx, (const __nv_bfloat16*)add, mask, N, H, W, C, Ho, Wo, g);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_im2col(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W, int C,
+                          int k, int s, int p, cudaStream_t st) {
+  return launch_im2col_geo(x, cols, N, H, W, C, ConvGeo{k, k, s, s, p, p}, st);
 }
 
 cudaError_t launch_col2im(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx, const void* add,
                           bool add_f32, const __nv_bfloat16* mask, int N, int H, int W, int C,
                           int k, int s, int p, cudaStream_t st) {
-  const int Ho = (H + 2 * p - k) / s + 1, Wo = (W + 2 * p - k) / s + 1;
-  if (C % 8) return cudaErrorInvalidValue;
-  const int blocks = blocks_for((int64_t)N * H * W * (C / 8), 256, 16);
-  if (add_f32)
-    col2im_kernel<float><<<blocks, 256, 0, st>>>(dcols, ldc, dx, (const float*)add, mask, N, H, W,
-                                                 C, Ho, Wo, k, s, p);
-  else
-    col2im_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        dcols, ldc, dx, (const __nv_bfloat16*)add, mask, N, H, W, C, Ho, Wo, k, s, p);
-  note_launch();
-  return cudaGetLastError();
+  return launch_col2im_geo(dcols, ldc, dx, add, add_f32, mask, N, H, W, C, ConvGeo{k, k, s, s, p, p},
+                           st);
 }
 
 cudaError_t launch_pack_conv_weights(const ConvPackEntry* table, int n, int max_elems,

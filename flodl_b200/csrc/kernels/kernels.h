@@ -146,6 +146,16 @@ cudaError_t launch_gelu_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n,
 // cols [N*Ho*Wo, k*k*C], column (kh*k + kw)*C + ci; C a multiple of 8
 cudaError_t launch_im2col(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W, int C,
                           int k, int s, int p, cudaStream_t st);
+// Rectangular kernels with per-axis stride and padding (1-D convolutions run
+// as kh = 1).
+struct ConvGeo {
+  int kh, kw, sh, sw, ph, pw;
+};
+cudaError_t launch_im2col_geo(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W,
+                              int C, const ConvGeo& g, cudaStream_t st);
+cudaError_t launch_col2im_geo(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx,
+                              const void* add, bool add_f32, const __nv_bfloat16* mask, int N,
+                              int H, int W, int C, const ConvGeo& g, cudaStream_t st);
 cudaError_t launch_col2im(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx, const void* add,
                           bool add_f32, const __nv_bfloat16* mask, int N, int H, int W, int C,
                           int k, int s, int p, cudaStream_t st);

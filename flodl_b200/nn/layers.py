@@ -113,6 +113,10 @@ class _ConvNd(Module):
 
     def forward(self, x):
         if self.transposed:
+            if self.nd in (1, 2) and x.is_cuda:
+                fn = ops.conv_transpose2d if self.nd == 2 else ops.conv_transpose1d
+                return fn(x, self.weight, self.bias, self.stride, self.padding,
+                          self.output_padding, self.groups, self.dilation)
             fn = {1: F.conv_transpose1d, 2: F.conv_transpose2d, 3: F.conv_transpose3d}[self.nd]
             x, w, b = self._lib_operands(x)
             return fn(x, w, b, self.stride, self.padding, self.output_padding, self.groups,
@@ -120,6 +124,9 @@ class _ConvNd(Module):
         if self.nd == 2:
             return ops.conv2d(x, self.weight, self.bias, self.stride, self.padding, self.dilation,
                               self.groups)
+        if self.nd == 1 and x.is_cuda:
+            return ops.conv1d(x, self.weight, self.bias, self.stride, self.padding,
+                              self.dilation, self.groups)
         fn = {1: F.conv1d, 3: F.conv3d}[self.nd]
         x, w, b = self._lib_operands(x)
         return fn(x, w, b, self.stride, self.padding, self.dilation, self.groups)

@@ -81,55 +81,59 @@ def _to_nhwc(x, cin_pad):
 
 
 class _Conv2dFn(torch.autograd.Function):
-    """Square-kernel 2-D convolution (groups 1, dilation 1) on the tcgen05 GEMM:
-    im2col (columns (kh, kw, ci)) -> GEMM with the packed weight; backward =
-    dgrad GEMM + col2im and a split-K weight-gradient GEMM. NCHW in/out (the
-    output is a channels-last NCHW view, bf16)."""
+    """2-D convolution (groups 1, dilation 1, any kh x kw kernel with per-axis
+    stride and padding) on the tcgen05 GEMM: im2col (columns (kh, kw, ci)) ->
+    GEMM with the packed weight; backward = dgrad GEMM + col2im and a split-K
+    weight-gradient GEMM. NCHW in/out (the output is a channels-last NCHW
+    view, bf16). 1-D convolutions run as kh = 1 (flodl-sys/ops_nn.cpp:19-275
+    routes every convolution through one entry the same way)."""
 
     @staticmethod
     def forward(ctx, x, weight, bias, stride, padding):
         K_ = C()
         N, Cin, H, W = x.shape
-        Cout, _, k, _ = weight.shape
+        # a 1-D weight [Cout, Cin, k] is the 1 x k kernel; the gradient goes
+        # to the weight as given (the parameter itself, not a view of it)
+        Cout, kh, kw = weight.shape[0], (weight.shape[2] if weight.dim() == 4 else 1), weight.shape[-1]
         cp = (Cin + 7) // 8 * 8
-        s, p = stride, padding
-        Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
-        M, Kc = N * Ho * Wo, k * k * cp
+        (sh, sw), (ph, pw) = stride, padding
+        Ho, Wo = (H + 2 * ph - kh) // sh + 1, (W + 2 * pw - kw) // sw + 1
+        M, Kc = N * Ho * Wo, kh * kw * cp
         xh = _to_nhwc(x, cp)
-        if k == 1 and s == 1 and p == 0:
+        if kh == 1 and kw == 1 and sh == 1 and sw == 1 and ph == 0 and pw == 0:
             cols = xh.view(M, Kc)
         else:
             cols = torch.empty((M, Kc), device=x.device, dtype=torch.bfloat16)
-            K_.im2col(xh, cols, k, s, p)
-        wp = _pack_weight(weight, cp)
+            K_.im2col_geo(xh, cols, kh, kw, sh, sw, ph, pw)
+        wp = _pack_weight(weight.view(Cout, -1, kh, kw), cp)
         y = torch.empty((M, Cout), device=x.device, dtype=torch.bfloat16)
         K_.gemm(cols, wp, y, M, Cout, Kc, False, False,
                 bias=bias.detach().float().contiguous() if bias is not None else None)
         ctx.save_for_backward(cols, wp, weight, bias)
-        ctx.geo = (N, Cin, cp, H, W, Ho, Wo, k, s, p, x.dtype)
+        ctx.geo = (N, Cin, cp, H, W, Ho, Wo, kh, kw, sh, sw, ph, pw, x.dtype)
         return y.view(N, Ho, Wo, Cout).permute(0, 3, 1, 2)
 
     @staticmethod
     def backward(ctx, dy):
         K_ = C()
         cols, wp, weight, bias = ctx.saved_tensors
-        N, Cin, cp, H, W, Ho, Wo, k, s, p, xdt = ctx.geo
+        N, Cin, cp, H, W, Ho, Wo, kh, kw, sh, sw, ph, pw, xdt = ctx.geo
         Cout = weight.shape[0]
-        M, Kc = N * Ho * Wo, k * k * cp
+        M, Kc = N * Ho * Wo, kh * kw * cp
         dyh = dy.permute(0, 2, 3, 1).to(torch.bfloat16).contiguous().view(M, Cout)
         dx = None
         if ctx.needs_input_grad[0]:
             dcols = torch.empty((M, Kc), device=dy.device, dtype=torch.bfloat16)
             K_.gemm(dyh, wp, dcols, M, Kc, Cout, False, True)
             dxh = torch.empty((N, H, W, cp), device=dy.device, dtype=torch.bfloat16)
-            K_.col2im(dcols, dxh, k, s, p)
+            K_.col2im_geo(dcols, dxh, kh, kw, sh, sw, ph, pw)
             dx = dxh[..., :Cin].permute(0, 3, 1, 2).to(xdt)
         if wants_grad(weight):
             gp = torch.zeros((Cout, Kc), device=dy.device, dtype=torch.float32)
             K_.gemm(dyh, cols, gp, Cout, Kc, M, True, True, flags=K_.EPI_ACCUMULATE,
                     k_splits=_splitk(Cout, Kc, M))
-            g = gp.view(Cout, k, k, cp)[..., :Cin].permute(0, 3, 1, 2)
-            grad_buffer(weight).add_(g)
+            g = gp.view(Cout, kh, kw, cp)[..., :Cin].permute(0, 3, 1, 2)
+            grad_buffer(weight).add_(g.reshape(weight.shape))
             grad_ready(weight)
         if bias is not None and wants_grad(bias):
             K_.colsum(dyh, grad_buffer(bias))
@@ -143,17 +147,117 @@ def _splitk(m, n, k):
 
 
 def conv2d(x, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
-    """2-D convolution. CUDA inputs with square kernels, equal strides and
-    paddings, groups 1, dilation 1 and a multiple of 8 output channels run
-    the tcgen05 path; everything else PyTorch's convolution."""
+    """2-D convolution. CUDA inputs with groups 1, dilation 1, integer
+    paddings and a multiple of 8 output channels run the tcgen05 path (any
+    kh x kw kernel, per-axis stride and padding); everything else PyTorch's
+    convolution."""
     st, pd, dl = _pair(stride), _pair(padding), _pair(dilation)
-    k = weight.shape[-1]
     fast = (use_kernels(x) and x.dim() == 4 and groups == 1 and dl == (1, 1)
-            and weight.shape[-2] == k and st[0] == st[1] and pd[0] == pd[1]
-            and weight.shape[0] % 8 == 0 and isinstance(pd[0], int))
+            and weight.shape[0] % 8 == 0 and all(isinstance(v, int) for v in pd))
     if not fast:
         return F.conv2d(x, weight, bias, stride, padding, dilation, groups)
-    return _Conv2dFn.apply(x, weight, bias, st[0], pd[0])
+    return _Conv2dFn.apply(x, weight, bias, st, pd)
+
+
+def conv1d(x, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
+    """1-D convolution over [N, C, L] as a 1 x k 2-D convolution on the
+    tcgen05 path (same conditions as :func:`conv2d`)."""
+    s = stride if isinstance(stride, int) else stride[0]
+    p = padding if isinstance(padding, int) else padding[0]
+    d = dilation if isinstance(dilation, int) else dilation[0]
+    if not (use_kernels(x) and x.dim() == 3 and groups == 1 and d == 1 and isinstance(p, int)
+            and weight.shape[0] % 8 == 0):
+        return F.conv1d(x, weight, bias, stride, padding, dilation, groups)
+    y = _Conv2dFn.apply(x.unsqueeze(2), weight, bias, (1, s), (0, p))
+    return y.squeeze(2)
+
+
+class _ConvTranspose2dFn(torch.autograd.Function):
+    """Transposed 2-D convolution (groups 1, dilation 1) on the tcgen05 GEMM.
+    Its forward is a convolution's data gradient: with the weight [Cin, Cout,
+    kh, kw] read as the weight of a convolution from Cout to Cin channels,
+    cols = x (NHWC rows) x packed weight, then col2im onto the output grid.
+    Backward: the input gradient is that convolution's forward (im2col of dy,
+    GEMM), the weight gradient a split-K GEMM of x against those columns."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, stride, padding, output_padding):
+        K_ = C()
+        N, Cin, H, W = x.shape
+        # a 1-D weight [Cin, Cout, k] is the 1 x k kernel (gradient to the weight as given)
+        w4 = weight if weight.dim() == 4 else weight.unsqueeze(2)
+        Cout, kh, kw = w4.shape[1], w4.shape[2], w4.shape[3]
+        (sh, sw), (ph, pw), (oh, ow) = stride, padding, output_padding
+        Hout = (H - 1) * sh - 2 * ph + kh + oh
+        Wout = (W - 1) * sw - 2 * pw + kw + ow
+        cp = (Cout + 7) // 8 * 8
+        M, Kc = N * H * W, kh * kw * cp
+        xh = x.permute(0, 2, 3, 1).to(torch.bfloat16).contiguous().view(M, Cin)
+        wp = _pack_weight(w4, cp)  # [Cin, kh*kw*cp]: the convolution Cout -> Cin
+        cols = torch.empty((M, Kc), device=x.device, dtype=torch.bfloat16)
+        K_.gemm(xh, wp, cols, M, Kc, Cin, False, True)
+        yh = torch.empty((N, Hout, Wout, cp), device=x.device, dtype=torch.bfloat16)
+        K_.col2im_geo(cols, yh, kh, kw, sh, sw, ph, pw)
+        y = yh[..., :Cout]
+        if bias is not None:
+            y = (y.float() + bias.detach().float()).to(torch.bfloat16)
+        ctx.save_for_backward(xh, wp, weight, bias)
+        ctx.geo = (N, Cin, Cout, cp, H, W, Hout, Wout, kh, kw, sh, sw, ph, pw, x.dtype)
+        return y.permute(0, 3, 1, 2)
+
+    @staticmethod
+    def backward(ctx, dy):
+        K_ = C()
+        xh, wp, weight, bias = ctx.saved_tensors
+        N, Cin, Cout, cp, H, W, Hout, Wout, kh, kw, sh, sw, ph, pw, xdt = ctx.geo
+        M, Kc = N * H * W, kh * kw * cp
+        dyh = _to_nhwc(dy, cp)  # [N, Hout, Wout, cp]
+        cols = torch.empty((M, Kc), device=dy.device, dtype=torch.bfloat16)
+        K_.im2col_geo(dyh, cols, kh, kw, sh, sw, ph, pw)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dxh = torch.empty((M, Cin), device=dy.device, dtype=torch.bfloat16)
+            K_.gemm(cols, wp, dxh, M, Cin, Kc, False, False)
+            dx = dxh.view(N, H, W, Cin).permute(0, 3, 1, 2).to(xdt)
+        if wants_grad(weight):
+            gp = torch.zeros((Cin, Kc), device=dy.device, dtype=torch.float32)
+            K_.gemm(xh, cols, gp, Cin, Kc, M, True, True, flags=K_.EPI_ACCUMULATE,
+                    k_splits=_splitk(Cin, Kc, M))
+            g = gp.view(Cin, kh, kw, cp)[..., :Cout].permute(0, 3, 1, 2)
+            grad_buffer(weight).add_(g.reshape(weight.shape))
+            grad_ready(weight)
+        if bias is not None and wants_grad(bias):
+            K_.colsum(dyh.view(-1, cp)[:, :Cout], grad_buffer(bias))
+            grad_ready(bias)
+        return dx, None, None, None, None, None
+
+
+def conv_transpose2d(x, weight, bias=None, stride=1, padding=0, output_padding=0, groups=1,
+                     dilation=1):
+    """Transposed 2-D convolution; CUDA inputs with groups 1, dilation 1 and a
+    multiple of 8 input channels run the tcgen05 path, everything else
+    PyTorch's."""
+    st, pd, op, dl = _pair(stride), _pair(padding), _pair(output_padding), _pair(dilation)
+    fast = (use_kernels(x) and x.dim() == 4 and groups == 1 and dl == (1, 1)
+            and weight.shape[0] % 8 == 0 and all(isinstance(v, int) for v in pd + op)
+            and op[0] < st[0] and op[1] < st[1])
+    if not fast:
+        return F.conv_transpose2d(x, weight, bias, stride, padding, output_padding, groups,
+                                  dilation)
+    return _ConvTranspose2dFn.apply(x, weight, bias, st, pd, op)
+
+
+def conv_transpose1d(x, weight, bias=None, stride=1, padding=0, output_padding=0, groups=1,
+                     dilation=1):
+    """Transposed 1-D convolution as a 1 x k transposed 2-D convolution."""
+    one = lambda v: v if isinstance(v, int) else v[0]
+    s, p, o, d = one(stride), one(padding), one(output_padding), one(dilation)
+    if not (use_kernels(x) and x.dim() == 3 and groups == 1 and d == 1 and isinstance(p, int)
+            and weight.shape[0] % 8 == 0 and o < s):
+        return F.conv_transpose1d(x, weight, bias, stride, padding, output_padding, groups,
+                                  dilation)
+    y = _ConvTranspose2dFn.apply(x.unsqueeze(2), weight, bias, (1, s), (0, p), (0, o))
+    return y.squeeze(2)
 
 
 class _BatchNorm2dFn(torch.autograd.Function):

@@ -153,3 +153,80 @@ def test_generic_conv2d_and_batchnorm_ops():
     for u, v in ((o.float(), o2), (z.grad, z2.grad), (g.grad, g2.grad), (be.grad, be2.grad)):
         assert ((u - v).norm() / v.norm()).item() < 2e-2
     torch.testing.assert_close(rm, rm2, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("kh,kw,sh,sw,ph,pw", [(3, 5, 1, 2, 1, 2), (1, 7, 1, 1, 0, 3),
+                                               (5, 3, 2, 1, 2, 0)])
+def test_rectangular_conv2d_matches_fp32(kh, kw, sh, sw, ph, pw):
+    """Any kh x kw kernel with per-axis stride and padding on the tcgen05 path,
+    against an fp32 convolution of the bf16-rounded operands."""
+    from flodl_b200 import ops
+    torch.manual_seed(7)
+    x = torch.randn(4, 12, 20, 18, device="cuda", requires_grad=True)
+    w = torch.randn(16, 12, kh, kw, device="cuda", requires_grad=True)
+    b = torch.randn(16, device="cuda", requires_grad=True)
+    y = ops.conv2d(x, w, b, (sh, sw), (ph, pw))
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    x2, w2, b2 = [t.detach().clone().requires_grad_() for t in (x, w, b)]
+    y2 = F.conv2d(x2.bfloat16().float(), w2.bfloat16().float(), b2, (sh, sw), (ph, pw))
+    y2.backward(dy.bfloat16().float())
+    for u, v in ((y.float(), y2), (x.grad, x2.grad), (w.grad, w2.grad), (b.grad, b2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 1e-2
+
+
+def test_conv1d_layer_runs_the_kernels_and_matches_fp32():
+    from flodl_b200._ext import cuda_ext
+    from flodl_b200.nn import Conv1d
+    torch.manual_seed(8)
+    conv = Conv1d(4, 32, 5, stride=2, padding=2, device=torch.device("cuda"))
+    x = torch.randn(8, 4, 200, device="cuda", requires_grad=True)
+    n0 = cuda_ext().launch_count()
+    y = conv(x)
+    assert cuda_ext().launch_count() > n0, "Conv1d did not launch this library's kernels"
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    x2 = x.detach().clone().requires_grad_()
+    w2 = conv.weight.detach().clone().requires_grad_()
+    b2 = conv.bias.detach().clone().requires_grad_()
+    y2 = F.conv1d(x2.bfloat16().float(), w2.bfloat16().float(), b2, 2, 2)
+    y2.backward(dy.bfloat16().float())
+    for u, v in ((y.float(), y2), (x.grad, x2.grad), (conv.weight.grad, w2.grad),
+                 (conv.bias.grad, b2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("k,s,p,op", [(3, 2, 1, 1), (4, 2, 1, 0), (3, 1, 1, 0)])
+def test_conv_transpose2d_matches_fp32(k, s, p, op):
+    from flodl_b200 import ops
+    torch.manual_seed(9)
+    x = torch.randn(4, 16, 9, 11, device="cuda", requires_grad=True)
+    w = torch.randn(16, 12, k, k, device="cuda", requires_grad=True)
+    b = torch.randn(12, device="cuda", requires_grad=True)
+    y = ops.conv_transpose2d(x, w, b, s, p, op)
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    x2, w2, b2 = [t.detach().clone().requires_grad_() for t in (x, w, b)]
+    y2 = F.conv_transpose2d(x2.bfloat16().float(), w2.bfloat16().float(), b2, s, p, op)
+    y2.backward(dy.bfloat16().float())
+    assert y.shape == y2.shape
+    for u, v in ((y.float(), y2), (x.grad, x2.grad), (w.grad, w2.grad), (b.grad, b2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 1e-2
+
+
+def test_conv_transpose1d_layer_matches_fp32():
+    from flodl_b200.nn import ConvTranspose1d
+    torch.manual_seed(10)
+    m = ConvTranspose1d(8, 4, 4, stride=2, padding=1, device=torch.device("cuda"))
+    x = torch.randn(6, 8, 50, device="cuda", requires_grad=True)
+    y = m(x)
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    x2 = x.detach().clone().requires_grad_()
+    w2 = m.weight.detach().clone().requires_grad_()
+    b2 = m.bias.detach().clone().requires_grad_()
+    y2 = F.conv_transpose1d(x2.bfloat16().float(), w2.bfloat16().float(), b2, 2, 1)
+    y2.backward(dy.bfloat16().float())
+    for u, v in ((y.float(), y2), (x.grad, x2.grad), (m.weight.grad, w2.grad),
+                 (m.bias.grad, b2.grad)):
+        assert ((u - v).norm() / v.norm()).item() < 1e-2
