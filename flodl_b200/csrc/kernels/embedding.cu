@@ -18,6 +18,8 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const float* _
                                  const float* __restrict__ type_tab, float* __restrict__ out,
                                  __nv_bfloat16* __restrict__ out_bf16, int T, int S, int C, int V,
                                  uint32_t* err) {
+  pdl_wait();
+  pdl_trigger();
   const int C4 = C / 4;
   const int64_t total = (int64_t)T * C4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -97,8 +99,10 @@ cudaError_t launch_embed_fwd(const int64_t* ids, const float* tok, const float* 
                              const int64_t* type_ids, const float* type_tab, float* out,
                              __nv_bfloat16* out_bf16, int T, int S, int C, int V, cudaStream_t st) {
   if (C % 4) return cudaErrorInvalidValue;
-  embed_fwd_kernel<<<grid_1d((int64_t)T * C / 4, 256), 256, 0, st>>>(
-      ids, tok, pos, type_ids, type_tab, out, out_bf16, T, S, C, V, nullptr);
+  cudaError_t e = launch_pdl(embed_fwd_kernel, dim3(grid_1d((int64_t)T * C / 4, 256)), dim3(256),
+                             0, st, ids, tok, pos, type_ids, type_tab, out, out_bf16, T, S, C, V,
+                             (uint32_t*)nullptr);
+  if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
 }

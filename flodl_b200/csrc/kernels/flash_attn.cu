@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  pdl_wait();  // global memory only after the previous kernel of the stream
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -593,6 +595,8 @@ __global__ void __launch_bounds__(kF2Threads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  pdl_wait();  // global memory only after the previous kernel of the stream
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -872,6 +876,8 @@ struct BwdSmem {
 __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
                                      const __nv_bfloat16* __restrict__ out, float* __restrict__ delta,
                                      float* __restrict__ dq_acc, int B, int S, int H) {
+  pdl_wait();
+  pdl_trigger();
   const int C = H * kD;
   const int64_t rows = (int64_t)B * S * H;
   const int64_t warp_g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -920,6 +926,8 @@ constexpr int kPostMaxThreads = 1024;
 __global__ void __launch_bounds__(kPostMaxThreads) flash_bwd_post_kernel(
     const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int T, int C, float scale,
     float* __restrict__ dbias, int rows_per_block, int gw) {
+  pdl_wait();
+  pdl_trigger();
   const int groups = C / 8;  // dQ columns (the K/V bias sums come from the main kernel)
   const int lanes = blockDim.x / gw;
   const int g = blockIdx.y * gw + (int)(threadIdx.x % gw);
@@ -1023,6 +1031,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  pdl_wait();  // global memory only after the previous kernel of the stream
+  pdl_trigger();
   const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 320,
                  t_dq = tmem + 384;
 
@@ -1387,6 +1397,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  pdl_wait();  // global memory only after the previous kernel of the stream
+  pdl_trigger();
   const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 320,
                  t_dq = tmem + 384;
 
@@ -1782,9 +1794,10 @@ static cudaError_t launch_flash_fwd2(const FlashArgs& a, const CUtensorMap& tm, 
   }
   const int64_t items = (int64_t)((a.S + kTile - 1) / kTile) * a.H * a.B;
   const int grid = (int)std::min<int64_t>(items, (int64_t)num_sms() * per_sm.load());
-  flash_fwd2_kernel<<<grid, kF2Threads, smem, st>>>(tm, a.out, a.lse2, a.key_pad, a.B, a.S, a.H,
-                                                    a.causal ? 1 : 0, a.scale,
-                                                    a.err ? a.err : default_err_word());
+  cudaError_t le = launch_pdl(flash_fwd2_kernel, dim3(grid), dim3(kF2Threads), smem, st, tm, a.out,
+                              a.lse2, a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0, a.scale,
+                              a.err ? a.err : default_err_word());
+  if (le != cudaSuccess) return le;
   note_launch();
   return cudaGetLastError();
 }
@@ -1838,8 +1851,9 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   int pre_blocks = (int)std::min<int64_t>((rows + 31) / 32, (int64_t)num_sms() * 16);
   if (!flash_bwd_needs_dq_acc(a.S)) {
     // dQ stays in TMEM: delta only, then one kernel per (batch, head)
-    flash_bwd_pre_kernel<<<pre_blocks, 256, 0, st>>>(a.dout, a.out, a.delta, nullptr, a.B, a.S,
-                                                     a.H);
+    cudaError_t le = launch_pdl(flash_bwd_pre_kernel, dim3(pre_blocks), dim3(256), 0, st, a.dout,
+                                a.out, a.delta, (float*)nullptr, a.B, a.S, a.H);
+    if (le != cudaSuccess) return le;
     const int smem = (int)sizeof(BwdBhSmem) + 1024;
     static std::atomic<uint64_t> done{0};
     int dev = 0;
@@ -1852,9 +1866,10 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
       done.fetch_or(bit);
     }
     const int grid = std::min(a.B * a.H, num_sms());
-    flash_bwd_bh_kernel<<<grid, kBwdThreads, smem, st>>>(
-        tm_qkv, tm_do, a.lse2, a.delta, a.dqkv, a.key_pad, a.B, a.S, a.H, a.causal ? 1 : 0,
-        a.scale, a.dbias, a.err ? a.err : default_err_word());
+    le = launch_pdl(flash_bwd_bh_kernel, dim3(grid), dim3(kBwdThreads), smem, st, tm_qkv, tm_do,
+                    (const float*)a.lse2, (const float*)a.delta, a.dqkv, a.key_pad, a.B, a.S,
+                    a.H, a.causal ? 1 : 0, a.scale, a.dbias, a.err ? a.err : default_err_word());
+    if (le != cudaSuccess) return le;
     note_launch(2);
     return cudaGetLastError();
   }

@@ -405,6 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  // the prologue above may overlap the previous kernel of the stream; global
+  // memory is touched only from here on
+  pdl_wait();
+  pdl_trigger();
   volatile uint32_t* abort_flag = &ctl->abort;
 
   auto tile_coords = [&](int t, int& tm, int& tn, int& ks) {
@@ -858,20 +862,21 @@ static cudaError_t launch_instance(const GemmArgs& g, cudaStream_t stream, const
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N, g.K,
                               g.k_splits, use_tma, in_kind, err);
   } else {
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, tmOut, tmAux, tmIn, g.ep, g.M, g.N, g.K,
-                                           g.k_splits, use_tma, in_kind, err);
-    return cudaSuccess;
+    return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB, tmOut, tmAux,
+                      tmIn, g.ep, g.M, g.N, g.K, g.k_splits, use_tma, in_kind, err);
   }
 }
 
@@ -956,6 +961,14 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FLODL_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 // FLODL_GEMM_PAIR=0 turns the CTA-pair tiles off (read once per process).

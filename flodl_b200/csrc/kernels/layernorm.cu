@@ -117,6 +117,8 @@ __global__ void __launch_bounds__(kWarps * 32, NV <= 4 ? 4 : 1) ln_fwd_kernel(
     const TIn* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
     __nv_bfloat16* __restrict__ y_bf16, float* __restrict__ y_f32, float* __restrict__ mean_out,
     float* __restrict__ rstd_out, int rows, int C, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp_global = blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * kWarps;
@@ -180,6 +182,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) ln_bwd_kernel(
     const float* __restrict__ gamma, const float* __restrict__ dres, float* __restrict__ dx_f32,
     __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dgamma, float* __restrict__ dbeta,
     float* __restrict__ colsum, int rows, int C, float* __restrict__ partials, int pre_add) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int warp_global = blockIdx.x * kWarps + wib;
@@ -496,17 +500,19 @@ cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st) {
     FL_LN_DISPATCH_NV(a.C, {
       auto k = ln_fwd_kernel<__nv_bfloat16, NV>;
       static std::atomic<int> occ{0};
-      k<<<resident_grid(k, a.rows, occ), kWarps * 32, 0, st>>>(
-          (const __nv_bfloat16*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean, a.rstd, a.rows,
-          a.C, a.eps);
+      cudaError_t le = launch_pdl(k, dim3(resident_grid(k, a.rows, occ)), dim3(kWarps * 32), 0, st,
+                                  (const __nv_bfloat16*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32,
+                                  a.mean, a.rstd, a.rows, a.C, a.eps);
+      if (le != cudaSuccess) return le;
     });
   } else {
     FL_LN_DISPATCH_NV(a.C, {
       auto k = ln_fwd_kernel<float, NV>;
       static std::atomic<int> occ{0};
-      k<<<resident_grid(k, a.rows, occ), kWarps * 32, 0, st>>>(
-          (const float*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean, a.rstd, a.rows, a.C,
-          a.eps);
+      cudaError_t le = launch_pdl(k, dim3(resident_grid(k, a.rows, occ)), dim3(kWarps * 32), 0, st,
+                                  (const float*)a.x, a.gamma, a.beta, a.y_bf16, a.y_f32, a.mean,
+                                  a.rstd, a.rows, a.C, a.eps);
+      if (le != cudaSuccess) return le;
     });
   }
   note_launch();
@@ -524,9 +530,11 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
       constexpr int smem = LnBwdSlot<__nv_bfloat16, NV>::kBlockBytes;
       cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(k), smem);
       if (e != cudaSuccess) return e;
-      k<<<grid, kWarps * 32, smem, st>>>(a.dy, (const __nv_bfloat16*)a.x, a.mean, a.rstd, a.gamma,
-                                          a.dres, a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum,
-                                          a.rows, a.C, a.partials, a.pre_add ? 1 : 0);
+      e = launch_pdl(k, dim3(grid), dim3(kWarps * 32), smem, st, a.dy, (const __nv_bfloat16*)a.x,
+                     (const float*)a.mean, (const float*)a.rstd, a.gamma, a.dres, a.dx_f32,
+                     a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials,
+                     a.pre_add ? 1 : 0);
+      if (e != cudaSuccess) return e;
     });
   } else {
     FL_LN_DISPATCH_NV(a.C, {
@@ -534,9 +542,11 @@ cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st) {
       constexpr int smem = LnBwdSlot<float, NV>::kBlockBytes;
       cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(k), smem);
       if (e != cudaSuccess) return e;
-      k<<<grid, kWarps * 32, smem, st>>>(a.dy, (const float*)a.x, a.mean, a.rstd, a.gamma, a.dres,
-                                          a.dx_f32, a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows,
-                                          a.C, a.partials, a.pre_add ? 1 : 0);
+      e = launch_pdl(k, dim3(grid), dim3(kWarps * 32), smem, st, a.dy, (const float*)a.x,
+                     (const float*)a.mean, (const float*)a.rstd, a.gamma, a.dres, a.dx_f32,
+                     a.dx_bf16, a.dgamma, a.dbeta, a.colsum, a.rows, a.C, a.partials,
+                     a.pre_add ? 1 : 0);
+      if (e != cudaSuccess) return e;
     });
   }
   note_launch();

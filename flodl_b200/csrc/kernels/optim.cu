@@ -35,6 +35,8 @@ __device__ __forceinline__ void adamw_elem(float& p, float g, float& m, float& v
 }
 
 __global__ void __launch_bounds__(256) adamw_kernel(AdamWArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const float lr = *a.lr;
   const float t = *a.step;
   const float bc1 = 1.f - powf(a.beta1, t);
@@ -141,7 +143,8 @@ cudaError_t launch_adamw(const AdamWArgs& a, cudaStream_t st) {
        reinterpret_cast<uintptr_t>(a.m) | reinterpret_cast<uintptr_t>(a.v)) & 15)
     return cudaErrorMisalignedAddress;
   if (a.shadow && (reinterpret_cast<uintptr_t>(a.shadow) & 7)) return cudaErrorMisalignedAddress;
-  adamw_kernel<<<grid_1d(a.n / 4 + 1, 256), 256, 0, st>>>(a);
+  cudaError_t e = launch_pdl(adamw_kernel, dim3(grid_1d(a.n / 4 + 1, 256)), dim3(256), 0, st, a);
+  if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
 }

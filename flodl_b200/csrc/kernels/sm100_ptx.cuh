@@ -12,6 +12,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace flodl {
 
 // ---------------------------------------------------------------- basics
@@ -51,6 +53,37 @@ enum KernelError : uint32_t {
 
 __device__ __forceinline__ void report_error(uint32_t* err, uint32_t code) {
   if (err) atomicCAS(err, 0u, code);
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with launch_pdl may start (their prologue: barrier init,
+// TMEM allocation, descriptor prefetch) while the previous kernel of the
+// stream is still finishing; pdl_wait() blocks until that kernel completed and
+// its memory is visible, so it comes before the first global access.
+// pdl_trigger() lets the next PDL launch of the stream be scheduled once every
+// CTA of this grid has started. Both are no-ops for an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// FLODL_PDL=0 turns programmatic dependent launches off (read once per process).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- mbarrier

@@ -54,6 +54,8 @@ constexpr int kCountUnroll = 8;
 __global__ void __launch_bounds__(kCountThreads) ce_count_kernel(
     const int64_t* __restrict__ targets, int T, int V, int64_t ignore, float* inv_count,
     float* loss_zero, uint32_t* err) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sh[32];
   float c = 0.f;
   bool bad = false;
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(kCountThreads) ce_count_kernel(
 // reductions, no block barriers. Rows, pitches and V are multiples of 8.
 template <int NC>
 __global__ void __launch_bounds__(256) softmax_ce_warp_kernel(CeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int n_warps = (gridDim.x * blockDim.x) >> 5;
@@ -227,8 +231,10 @@ __global__ void __launch_bounds__(kThreads) softmax_ce_kernel(CeArgs a) {
 
 cudaError_t launch_ce_count(const int64_t* targets, int T, int V, int64_t ignore_index,
                             float* inv_count, float* loss_zero, uint32_t* err, cudaStream_t st) {
-  ce_count_kernel<<<1, kCountThreads, 0, st>>>(targets, T, V, ignore_index, inv_count,
-                                                loss_zero, err ? err : default_err_word());
+  cudaError_t le = launch_pdl(ce_count_kernel, dim3(1), dim3(kCountThreads), 0, st, targets, T, V,
+                              ignore_index, inv_count, loss_zero,
+                              err ? err : default_err_word());
+  if (le != cudaSuccess) return le;
   note_launch();
   return cudaGetLastError();
 }
@@ -244,12 +250,16 @@ cudaError_t launch_softmax_ce(const CeArgs& a, cudaStream_t st) {
     const int nc = (a.V + 255) / 256;
     const int64_t warps = std::min<int64_t>(a.T, (int64_t)num_sms() * 32);
     const int grid = (int)((warps * 32 + 255) / 256);
+    cudaError_t e = cudaSuccess;
     switch (nc) {
-      case 1: softmax_ce_warp_kernel<1><<<grid, 256, 0, st>>>(a); break;
-      case 2: softmax_ce_warp_kernel<2><<<grid, 256, 0, st>>>(a); break;
-      case 3: case 4: softmax_ce_warp_kernel<4><<<grid, 256, 0, st>>>(a); break;
-      default: softmax_ce_warp_kernel<8><<<grid, 256, 0, st>>>(a); break;
+      case 1: e = launch_pdl(softmax_ce_warp_kernel<1>, dim3(grid), dim3(256), 0, st, a); break;
+      case 2: e = launch_pdl(softmax_ce_warp_kernel<2>, dim3(grid), dim3(256), 0, st, a); break;
+      case 3: case 4:
+        e = launch_pdl(softmax_ce_warp_kernel<4>, dim3(grid), dim3(256), 0, st, a);
+        break;
+      default: e = launch_pdl(softmax_ce_warp_kernel<8>, dim3(grid), dim3(256), 0, st, a); break;
     }
+    if (e != cudaSuccess) return e;
     note_launch();
     return cudaGetLastError();
   }
