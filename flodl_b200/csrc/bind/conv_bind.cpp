@@ -93,6 +93,28 @@ void bn_stats(const Tensor& x, Tensor& mean, Tensor& rstd, const optional<Tensor
                                     cur_stream()));
 }
 
+// Batch norm from the statistics a convolution GEMM accumulated into ws
+// (sum, sum of squares; ws[2C] is the ticket word, left zeroed).
+void bn_apply_sums(const Tensor& x, Tensor& ws, Tensor& mean, Tensor& rstd,
+                   const optional<Tensor>& run_mean, const optional<Tensor>& run_var,
+                   const optional<Tensor>& gamma, const optional<Tensor>& beta,
+                   const optional<Tensor>& identity, bool relu, Tensor& y, double eps,
+                   double momentum) {
+  FL_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x");
+  const int C = (int)x.size(-1);
+  FL_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= 2 * C + 1, "ws needs 2C+1 f32");
+  FL_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.numel() == x.numel(), "y");
+  if (identity) FL_CHECK(identity->scalar_type() == at::kBFloat16 && identity->is_contiguous() &&
+                             identity->numel() == x.numel(), "identity");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_bn_apply_sums(
+      ptr<__nv_bfloat16>(x), x.numel() / C, C, ptr<float>(ws),
+      reinterpret_cast<unsigned*>(ptr<float>(ws) + 2 * C), (float)eps, (float)momentum,
+      ptr<float>(mean), ptr<float>(rstd), opt_ptr<float>(run_mean), opt_ptr<float>(run_var),
+      opt_ptr<const float>(gamma), opt_ptr<const float>(beta),
+      opt_ptr<const __nv_bfloat16>(identity), relu, ptr<__nv_bfloat16>(y), cur_stream()));
+}
+
 void bn_apply(const Tensor& x, const Tensor& mean, const Tensor& rstd, const optional<Tensor>& gamma,
               const optional<Tensor>& beta, const optional<Tensor>& identity, bool relu, Tensor& y) {
   FL_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x");
@@ -196,6 +218,10 @@ void register_conv(py::module& m) {
         py::arg("pad"), py::arg("add") = py::none(), py::arg("mask") = py::none());
   m.def("im2col_geo", &im2col_geo);
   m.def("col2im_geo", &col2im_geo);
+  m.def("bn_apply_sums", &bn_apply_sums, py::arg("x"), py::arg("ws"), py::arg("mean"),
+        py::arg("rstd"), py::arg("run_mean"), py::arg("run_var"), py::arg("gamma"),
+        py::arg("beta"), py::arg("identity"), py::arg("relu"), py::arg("y"), py::arg("eps"),
+        py::arg("momentum"));
   m.def("bn_stats", &bn_stats, py::arg("x"), py::arg("mean"), py::arg("rstd"),
         py::arg("run_mean"), py::arg("run_var"), py::arg("ws"), py::arg("eps"),
         py::arg("momentum"));

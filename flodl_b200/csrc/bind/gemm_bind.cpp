@@ -10,7 +10,8 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t M, 
           int64_t K, bool a_mn, bool b_mn, const c10::optional<at::Tensor>& bias,
           const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& aux,
           int64_t flags, double alpha, int64_t k_splits, int64_t bn,
-          const c10::optional<at::Tensor>& alpha_t, const c10::optional<at::Tensor>& colsum) {
+          const c10::optional<at::Tensor>& alpha_t, const c10::optional<at::Tensor>& colsum,
+          const c10::optional<at::Tensor>& colsumsq) {
   FL_CHECK_CUDA(A);
   FL_CHECK_CUDA(B);
   FL_CHECK_CUDA(out);
@@ -77,6 +78,14 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& out, int64_t M, 
     FL_CHECK(k_splits == 1 && !(flags & flodl::kEpiAccumulate), "colsum needs a full-K epilogue");
   }
   g.ep.colsum = opt_ptr<float>(colsum);
+  if (colsumsq) {
+    FL_CHECK_F32(*colsumsq);
+    FL_CHECK_CUDA(*colsumsq);
+    FL_CHECK(colsumsq->numel() == N && colsumsq->is_contiguous(), "colsumsq must be f32 [N]");
+    FL_CHECK(k_splits == 1 && !(flags & flodl::kEpiAccumulate),
+             "colsumsq needs a full-K epilogue");
+  }
+  g.ep.colsumsq = opt_ptr<float>(colsumsq);
   cudaStream_t st = cur_stream();
   cudaError_t e = flodl::launch_gemm(g, st);
   FL_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e), " ",
@@ -94,7 +103,7 @@ void register_gemm(py::module& m) {
         py::arg("b_mn"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("aux") = py::none(), py::arg("flags") = 0, py::arg("alpha") = 1.0,
         py::arg("k_splits") = 1, py::arg("bn") = 0, py::arg("alpha_t") = py::none(),
-        py::arg("colsum") = py::none());
+        py::arg("colsum") = py::none(), py::arg("colsumsq") = py::none());
   m.attr("EPI_GELU") = (int)flodl::kEpiGelu;
   m.attr("EPI_DGELU") = (int)flodl::kEpiDGelu;
   m.attr("EPI_ACCUMULATE") = (int)flodl::kEpiAccumulate;

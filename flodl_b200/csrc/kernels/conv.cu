@@ -349,6 +349,72 @@ __global__ void bn_apply_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, 
   }
 }
 
+// Batch norm applied from statistics a GEMM epilogue accumulated: ws[0:C]
+// holds sum(y), ws[C:2C] sum(y^2) over the M rows. Every block derives mean
+// and rstd for the channels (C <= kMaxBnC) in shared memory, block 0 writes
+// them out and updates the running statistics, and the last block to finish
+// re-zeroes the sums and the ticket for the next use.
+constexpr int kMaxBnC = 1024;
+__global__ void bn_apply_sums_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, int C,
+                                     float* __restrict__ ws, unsigned* __restrict__ ticket,
+                                     float eps, float momentum, float* __restrict__ mean_out,
+                                     float* __restrict__ rstd_out, float* __restrict__ run_mean,
+                                     float* __restrict__ run_var,
+                                     const float* __restrict__ gamma,
+                                     const float* __restrict__ beta,
+                                     const __nv_bfloat16* __restrict__ identity, int relu,
+                                     __nv_bfloat16* __restrict__ y) {
+  __shared__ float sc[kMaxBnC], sh[kMaxBnC];
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float mu = __ldcg(ws + c) / (float)M;
+    const float var = fmaxf(__ldcg(ws + C + c) / (float)M - mu * mu, 0.f);
+    const float rs = rsqrtf(var + eps);
+    const float g = gamma ? gamma[c] : 1.f;
+    sc[c] = rs * g;
+    sh[c] = (beta ? beta[c] : 0.f) - mu * rs * g;
+    if (blockIdx.x == 0) {
+      mean_out[c] = mu;
+      rstd_out[c] = rs;
+      if (run_mean) {
+        const float unbiased = M > 1 ? var * (float)M / (float)(M - 1) : var;
+        run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mu;
+        run_var[c] = (1.f - momentum) * run_var[c] + momentum * unbiased;
+      }
+    }
+  }
+  __syncthreads();
+  const int groups = C / 8;
+  const int64_t total = M * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int c0 = (int)(i % groups) * 8;
+    const int64_t r = i / groups;
+    float v[8];
+    load8(x + r * C + c0, v);
+    float id[8];
+    if (identity) load8(identity + r * C + c0, id);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float o = fmaf(v[e], sc[c0 + e], sh[c0 + e]);
+      if (identity) o += id[e];
+      v[e] = relu ? fmaxf(o, 0.f) : o;
+    }
+    store8(y + r * C + c0, v);
+  }
+  // every block read the sums at its start; the last one to get here clears them
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last) {
+    for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) ws[c] = 0.f;
+    if (threadIdx.x == 0) *ticket = 0u;
+  }
+}
+
 // sums of dz and dz * xhat per channel; the last block also accumulates
 // dgamma += sum(dz xhat), dbeta += sum(dz) and keeps both sums in out2[0:2C]
 __global__ void __launch_bounds__(kRedThreads) bn_bwd_reduce_kernel(
@@ -569,6 +635,19 @@ cudaError_t launch_bn_apply(const __nv_bfloat16* x, int64_t M, int C, const floa
   if (C % 8) return cudaErrorInvalidValue;
   bn_apply_kernel<<<blocks_for(M * (C / 8), 256, 16), 256, 0, st>>>(x, M, C, mean, rstd, gamma, beta,
                                                                      identity, relu ? 1 : 0, y);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_apply_sums(const __nv_bfloat16* x, int64_t M, int C, float* ws,
+                                 unsigned* ticket, float eps, float momentum, float* mean,
+                                 float* rstd, float* run_mean, float* run_var, const float* gamma,
+                                 const float* beta, const __nv_bfloat16* identity, bool relu,
+                                 __nv_bfloat16* y, cudaStream_t st) {
+  if (C % 8 || C > kMaxBnC || M <= 0) return cudaErrorInvalidValue;
+  bn_apply_sums_kernel<<<blocks_for(M * (C / 8), 256, 16), 256, 0, st>>>(
+      x, M, C, ws, ticket, eps, momentum, mean, rstd, run_mean, run_var, gamma, beta, identity,
+      relu ? 1 : 0, y);
   note_launch();
   return cudaGetLastError();
 }

@@ -220,7 +220,8 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
                                                    const CUtensorMap* tmOut,
                                                    const CUtensorMap* tmAux, uint8_t* slot,
                                                    int row0, int col0, int lane, int N,
-                                                   const uint32_t (&acc)[32], bool wait_slot) {
+                                                   const uint32_t (&acc)[32], bool wait_slot,
+                                                   float* cs_keep, float* cq_keep) {
   float v[32];
   if (ep.bias && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0) {
     // v = acc * alpha + bias, two columns per packed FMA
@@ -288,9 +289,26 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpilogue& ep, float
       }
     }
   }
-  if (ep.colsum) {  // bias gradient of the next layer: out-of-range rows hold zeros
+  // Column sums (bias gradient of the next layer; batch-norm statistics with
+  // the squares): out-of-range rows hold zeros. With cs_keep / cq_keep the
+  // chunk's sums are kept in the warp's registers (one column per lane) and
+  // flushed once per CTA, else one atomic per column and chunk.
+  if (ep.colsum) {
     const float s = chunk_column_sum(v, lane);
-    if (col0 + lane < N) atomicAdd(ep.colsum + col0 + lane, s);
+    if (cs_keep)
+      *cs_keep += s;
+    else if (col0 + lane < N)
+      atomicAdd(ep.colsum + col0 + lane, s);
+  }
+  if (ep.colsumsq) {
+    float sq[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sq[i] = v[i] * v[i];
+    const float s = chunk_column_sum(sq, lane);
+    if (cq_keep)
+      *cq_keep += s;
+    else if (col0 + lane < N)
+      atomicAdd(ep.colsumsq + col0 + lane, s);
   }
   slot_free();
   if (ep.out_f32) {
@@ -597,6 +615,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
+    // one N tile: every chunk cc of this warp has the same columns, so its
+    // column sums accumulate in registers and leave with one atomic per CTA
+    const bool keep_sums = (ep.colsum || ep.colsumsq) && tiles_n == 1 && k_splits == 1;
+    float cs_acc[kChunks], cq_acc[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) cs_acc[c] = cq_acc[c] = 0.f;
     bool prev_stored = false;  // chunk j-1 committed a store group (its slot may be in flight)
     uint32_t in_ph = 0;    // parity of the next completion of each slot's barrier
     uint32_t pending = 0;  // slots with an input load issued but not yet consumed
@@ -665,7 +689,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
         }
-        epilogue_chunk_tma(ep, alpha, &tmOut, &tmAux, slot, row0, col0, lane, N, r, kSlots == 1);
+        float* csk = nullptr;
+        float* cqk = nullptr;
+        if (keep_sums) {
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c)
+            if (c == cc) {
+              csk = &cs_acc[c];
+              cqk = &cq_acc[c];
+            }
+        }
+        epilogue_chunk_tma(ep, alpha, &tmOut, &tmAux, slot, row0, col0, lane, N, r, kSlots == 1,
+                           csk, cqk);
       } else {
         epilogue_chunk(ep, row0 + lane, col0, M, N, r);
       }
@@ -677,6 +712,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&in_bar[sb], (in_ph >> sb) & 1u)) {
           if (global_timer_ns() - t0 > 100000000ull) break;
+        }
+      }
+    }
+    if (keep_sums && !aborted) {
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        const int col = (half * kChunks + c) * 32 + lane;
+        if (col < N) {
+          if (ep.colsum) atomicAdd(ep.colsum + col, cs_acc[c]);
+          if (ep.colsumsq) atomicAdd(ep.colsumsq + col, cq_acc[c]);
         }
       }
     }
@@ -943,7 +988,7 @@ static cudaError_t launch_gemm_t(const GemmArgs& g, cudaStream_t stream) {
     in_kind = kInAux;
   }
   if (!use_tma) in_kind = kInNone;
-  if (g.ep.colsum && !use_tma) {
+  if ((g.ep.colsum || g.ep.colsumsq) && !use_tma) {
     g_gemm_fail = "fused column sums need the TMA-store epilogue (aligned output/aux)";
     return cudaErrorInvalidValue;
   }

@@ -25,6 +25,7 @@ struct GemmEpilogue {
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;  // optional device scalar multiplied into alpha
   float* colsum = nullptr;  // f32 [N] or null: += column sums of the output (TMA-store path)
+  float* colsumsq = nullptr;  // f32 [N] or null: += column sums of squares (batch-norm statistics)
 };
 
 struct GemmArgs {

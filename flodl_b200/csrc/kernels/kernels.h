@@ -167,6 +167,14 @@ cudaError_t launch_bn_apply(const __nv_bfloat16* x, int64_t M, int C, const floa
                             const float* rstd, const float* gamma, const float* beta,
                             const __nv_bfloat16* identity, bool relu, __nv_bfloat16* y,
                             cudaStream_t st);
+// Batch norm from statistics a GEMM epilogue accumulated (ws[0:C] = sum y,
+// ws[C:2C] = sum y^2 over M rows): writes mean/rstd, updates the running
+// statistics, applies (+ identity, ReLU) and leaves ws and *ticket zeroed.
+cudaError_t launch_bn_apply_sums(const __nv_bfloat16* x, int64_t M, int C, float* ws,
+                                 unsigned* ticket, float eps, float momentum, float* mean,
+                                 float* rstd, float* run_mean, float* run_var, const float* gamma,
+                                 const float* beta, const __nv_bfloat16* identity, bool relu,
+                                 __nv_bfloat16* y, cudaStream_t st);
 // sums: 2C f32 scratch (sum dz, sum dz*xhat); dz_out (nullable) receives the masked dy.
 cudaError_t launch_bn_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
                           const __nv_bfloat16* x, int64_t M, int C, const float* mean,

@@ -17,8 +17,10 @@ gradient) and a split-K weight-gradient GEMM that reuses the forward's column
 buffer, accumulating in packed order; one launch unpacks all of them into the
 OIHW ``param.grad`` at the end of backward.
 
-Batch norm runs as a statistics kernel (with the running-stat update) and an
-apply kernel that also adds the shortcut and applies the ReLU; its backward
+Batch norm statistics (per-channel sum and sum of squares) are added by the
+convolution GEMM's epilogue (kept in registers per CTA, one atomic per column
+and CTA); one apply kernel derives mean / rstd, updates the running
+statistics, adds the shortcut and applies the ReLU; its backward
 applies the ReLU mask of the block output and hands the masked gradient to
 the shortcut path in the same pass. Gradients accumulate in f32 straight into
 ``param.grad``; gradient-ready listeners (the DDP bucket hooks) fire per
@@ -28,8 +30,14 @@ from __future__ import annotations
 
 import torch
 
+import os
+
 from ._common import C, bf16_shadow, grad_buffer, grad_ready, splitk_for
 from .transformer import _empty
+
+# batch-norm statistics summed in the convolution GEMM's epilogue (no separate
+# statistics pass); FLODL_BN_FUSED_STATS=0 keeps the statistics kernel
+FUSED_BN_STATS = os.environ.get("FLODL_BN_FUSED_STATS", "1") != "0"
 
 
 def _ws(bn, dev):
@@ -98,8 +106,10 @@ class _Conv:
     def out_hw(self, H, W):
         return (H + 2 * self.p - self.k) // self.s + 1, (W + 2 * self.p - self.k) // self.s + 1
 
-    def forward(self, x):
-        """x NHWC bf16 -> (y [M, Cout] bf16, cols [M, K], (N, Ho, Wo))"""
+    def forward(self, x, bn=None):
+        """x NHWC bf16 -> (y [M, Cout] bf16, cols [M, K], (N, Ho, Wo)). With
+        ``bn`` (the batch norm that follows) the GEMM epilogue also adds the
+        output's per-channel sums and sums of squares into its workspace."""
         N, H, W, _ = x.shape
         Ho, Wo = self.out_hw(H, W)
         M = N * Ho * Wo
@@ -110,7 +120,12 @@ class _Conv:
             cols = _empty((M, self.K), torch.bfloat16, x.device)
             K_.im2col(x, cols, self.k, self.s, self.p)
         y = _empty((M, self.cout), torch.bfloat16, x.device)
-        K_.gemm(cols, self.packed, y, M, self.cout, self.K, False, False)
+        if bn is not None and FUSED_BN_STATS:
+            ws, _ = _ws(bn.mod, x.device)
+            K_.gemm(cols, self.packed, y, M, self.cout, self.K, False, False,
+                    colsum=ws[:self.cout], colsumsq=ws[self.cout:2 * self.cout])
+        else:
+            K_.gemm(cols, self.packed, y, M, self.cout, self.K, False, False)
         return y, cols, (N, Ho, Wo)
 
     def backward(self, dy, cols, x_shape, add=None, mask=None, need_dx=True):
@@ -158,9 +173,15 @@ class _BN:
         rstd = _empty(self.c, torch.float32, dev)
         ws, _ = _ws(self.mod, dev)
         b = self.mod
+        out = torch.empty_like(y)
+        if FUSED_BN_STATS:
+            # the convolution's GEMM epilogue left sum / sum of squares in ws
+            K_.bn_apply_sums(y, ws, mean, rstd, b.running_mean if training else None,
+                             b.running_var if training else None, b.weight.detach(),
+                             b.bias.detach(), identity, relu, out, b.eps, b.momentum)
+            return out, mean, rstd
         K_.bn_stats(y, mean, rstd, b.running_mean if training else None,
                     b.running_var if training else None, ws, b.eps, b.momentum)
-        out = torch.empty_like(y)
         K_.bn_apply(y, mean, rstd, b.weight.detach(), b.bias.detach(), identity, relu, out)
         return out, mean, rstd
 
@@ -184,12 +205,12 @@ class _Block:
         self.ds = (_Conv(blk.downsample_conv), _BN(blk.downsample_bn)) if blk.downsample_conv is not None else None
 
     def forward(self, x):
-        y1, cols1, (N, Ho, Wo) = self.conv1.forward(x)
+        y1, cols1, (N, Ho, Wo) = self.conv1.forward(x, self.bn1)
         a1, m1, r1 = self.bn1.forward(y1)
         a1 = a1.view(N, Ho, Wo, -1)
-        y2, cols2, _ = self.conv2.forward(a1)
+        y2, cols2, _ = self.conv2.forward(a1, self.bn2)
         if self.ds is not None:
-            yd, colsd, _ = self.ds[0].forward(x)
+            yd, colsd, _ = self.ds[0].forward(x, self.ds[1])
             ident, md, rd = self.ds[1].forward(yd, relu=False)
             dsv = (yd, colsd, md, rd)
         else:
@@ -225,7 +246,7 @@ class _ResNetTrainFn(torch.autograd.Function):
         plan.pack()
         x = _empty((N, H, W, stem_c.cin_pad), torch.bfloat16, dev)
         K_.nchw_to_nhwc(images.float().contiguous(), x)
-        y0, cols0, (_, Ho, Wo) = stem_c.forward(x)
+        y0, cols0, (_, Ho, Wo) = stem_c.forward(x, stem_bn)
         x0, m0, r0 = stem_bn.forward(y0)
         h = x0.view(N, Ho, Wo, -1)
         saved = []

@@ -230,3 +230,34 @@ def test_conv_transpose1d_layer_matches_fp32():
     for u, v in ((y.float(), y2), (x.grad, x2.grad), (m.weight.grad, w2.grad),
                  (m.bias.grad, b2.grad)):
         assert ((u - v).norm() / v.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 16, 144), (8192, 64, 576), (2048, 40, 96)])
+def test_gemm_column_sums_and_squares_feed_batch_norm(M, N, K):
+    """The GEMM epilogue's per-column sum and sum of squares (kept per CTA in
+    registers for a single N tile) and the batch norm applied from them match
+    fp32 batch statistics of the same product; the workspace is left zeroed."""
+    C_ = _C()
+    torch.manual_seed(12)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).bfloat16()
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ws = torch.zeros(2 * N + 1, device="cuda")
+    C_.gemm(a, w, y, M, N, K, False, False, colsum=ws[:N], colsumsq=ws[N:2 * N])
+    ref = a.float() @ w.float().t()
+    torch.testing.assert_close(ws[:N], ref.sum(0), rtol=1e-3, atol=1e-2 * M ** 0.5)
+    torch.testing.assert_close(ws[N:2 * N], (ref * ref).sum(0), rtol=1e-3, atol=1e-2 * M ** 0.5)
+    mean = torch.empty(N, device="cuda")
+    rstd = torch.empty(N, device="cuda")
+    rm, rv = torch.zeros(N, device="cuda"), torch.ones(N, device="cuda")
+    g, b = torch.rand(N, device="cuda") + 0.5, torch.randn(N, device="cuda")
+    out = torch.empty_like(y)
+    C_.bn_apply_sums(y, ws, mean, rstd, rm, rv, g, b, None, True, out, 1e-5, 0.1)
+    torch.cuda.synchronize()
+    mu, var = ref.mean(0), ref.var(0, unbiased=False)
+    torch.testing.assert_close(mean, mu, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(rstd, (var + 1e-5).rsqrt(), rtol=2e-3, atol=1e-3)
+    want = torch.relu((y.float() - mu) * (var + 1e-5).rsqrt() * g + b)
+    torch.testing.assert_close(out.float(), want, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(rm, 0.1 * mu, rtol=1e-3, atol=1e-4)
+    assert torch.count_nonzero(ws).item() == 0, "workspace not cleared for the next use"
