@@ -111,6 +111,29 @@ def case_flash(kind):
     return fn, 2.5 * f_fwd, (B * S * 3 * D * 2 + 2 * B * S * D) * 2
 
 
+def case_flash_bert(kind):
+    """BERT-base attention: 32 x 512 tokens, 12 heads of 64, bidirectional,
+    key padding (the last 10% of each sequence's keys masked)."""
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    Bb, Sb, Hb, Db = 32, 512, 12, 768
+    qkv = _bf(Bb * Sb, 3 * Db)
+    out = torch.empty(Bb * Sb, Db, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(Bb, Hb, Sb, device="cuda")
+    pad = torch.zeros(Bb, Sb, dtype=torch.bool, device="cuda")
+    pad[:, Sb - Sb // 10:] = True
+    sc = 1.0 / math.sqrt(Db // Hb)
+    C.flash_attn_fwd(qkv, out, lse, Bb, Sb, Hb, Db // Hb, False, sc, pad)
+    f_fwd = 4.0 * Bb * Hb * Sb * Sb * (Db // Hb)
+    if kind == "flash_fwd_bert":
+        fn = lambda: C.flash_attn_fwd(qkv, out, lse, Bb, Sb, Hb, Db // Hb, False, sc, pad)
+        return fn, f_fwd, (Bb * Sb * 3 * Db + Bb * Sb * Db) * 2
+    dout = _bf(Bb * Sb, Db)
+    dqkv = torch.empty_like(qkv)
+    fn = lambda: C.flash_attn_bwd(dout, qkv, out, lse, dqkv, Bb, Sb, Hb, Db // Hb, False, sc, pad)
+    return fn, 2.5 * f_fwd, (Bb * Sb * 3 * Db * 2 + 2 * Bb * Sb * Db) * 2
+
+
 def case_ln(kind):
     from ._ext import cuda_ext
     C = cuda_ext()
@@ -206,6 +229,17 @@ def case_conv(kind):
     C = cuda_ext()
     x = _bf(RN, RH, RH, RC)
     M = RN * RH * RH
+    if kind == "col2im_bn":  # col2im (+ add, * mask) with the batch-norm backward sums
+        dcols = _bf(M, 9 * RC)
+        dz = torch.empty_like(x)
+        add, mask, y = _bf(RN, RH, RH, RC), _bf(RN, RH, RH, RC), _bf(M, RC)
+        mean = torch.zeros(RC, device="cuda")
+        rstd = torch.ones(RC, device="cuda")
+        ws = torch.zeros(2 * RC + 1, device="cuda")
+        sums = torch.zeros(2 * RC, device="cuda")
+        dg, db = torch.zeros(RC, device="cuda"), torch.zeros(RC, device="cuda")
+        fn = lambda: C.col2im_bn(dcols, dz, 3, 1, 1, add, mask, y, mean, rstd, dg, db, sums, ws)
+        return fn, 0.0, M * 9 * RC * 2 + 4 * M * RC * 2
     if kind in ("im2col", "col2im"):
         cols = torch.empty(M, 9 * RC, device="cuda", dtype=torch.bfloat16)
         if kind == "im2col":
@@ -245,10 +279,11 @@ CASES = {
     "gemm_qkv": case_gemm, "gemm_fc1_gelu": case_gemm, "gemm_fc2_residual": case_gemm,
     "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm,
     "flash_fwd": case_flash, "flash_bwd": case_flash,
+    "flash_fwd_bert": case_flash_bert, "flash_bwd_bert": case_flash_bert,
     "ln_fwd": case_ln, "ln_bwd": case_ln, "adamw": case_adamw, "sgd": case_sgd,
     "softmax_ce": case_softmax_ce, "embed_fwd": case_embed, "embed_bwd": case_embed,
     "im2col": case_conv, "col2im": case_conv, "bn_stats": case_conv, "bn_apply": case_conv,
-    "bn_bwd": case_conv,
+    "bn_bwd": case_conv, "col2im_bn": case_conv,
 }
 
 

@@ -48,6 +48,39 @@ void col2im(const Tensor& dcols, Tensor& dx, int64_t k, int64_t s, int64_t p,
                                   N, H, W, C, (int)k, (int)s, (int)p, cur_stream()));
 }
 
+// col2im whose output dx (after add and mask) is the gradient dz of a batch
+// norm with input x: the same pass adds sum dz and sum dz * xhat into ws (2C+1
+// f32, zeroed), and its last block writes them to sums, accumulates dgamma /
+// dbeta and re-zeroes ws. bn_bwd_apply then finishes that batch norm.
+void col2im_bn(const Tensor& dcols, Tensor& dx, int64_t k, int64_t s, int64_t p,
+               const optional<Tensor>& add, const optional<Tensor>& mask, const Tensor& x,
+               const Tensor& mean, const Tensor& rstd, const optional<Tensor>& dgamma,
+               const optional<Tensor>& dbeta, Tensor& sums, Tensor& ws) {
+  check_nhwc(dx, "dx");
+  FL_CHECK(dcols.scalar_type() == at::kBFloat16 && dcols.dim() == 2 && dcols.stride(1) == 1,
+           "dcols must be row-major bf16 [M, >= C*k*k]");
+  const int N = (int)dx.size(0), H = (int)dx.size(1), W = (int)dx.size(2), C = (int)dx.size(3);
+  if (add) FL_CHECK(add->is_contiguous() && add->numel() == dx.numel(), "add shape");
+  if (mask) FL_CHECK(mask->is_contiguous() && mask->numel() == dx.numel() &&
+                         mask->scalar_type() == at::kBFloat16, "mask must be bf16 like dx");
+  FL_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.numel() == dx.numel(),
+           "x must be bf16 like dx");
+  FL_CHECK(C % 8 == 0 && 256 % (C / 8) == 0, "col2im_bn needs C / 8 to divide 256");
+  FL_CHECK(mean.numel() >= C && rstd.numel() >= C && sums.numel() >= 2 * C &&
+               ws.numel() >= 2 * C + 1 && ws.scalar_type() == at::kFloat,
+           "col2im_bn scratch sizes");
+  float* wsp = ptr<float>(ws);
+  const flodl::BnBwdSums bn{ptr<__nv_bfloat16>(x), ptr<float>(mean), ptr<float>(rstd),
+                            opt_ptr<float>(dgamma), opt_ptr<float>(dbeta), ptr<float>(sums), wsp,
+                            reinterpret_cast<unsigned*>(wsp + 2 * C)};
+  c10::cuda::CUDAGuard guard(dx.device());
+  FL_CUDA_OK(flodl::launch_col2im_geo(
+      ptr<__nv_bfloat16>(dcols), (int)dcols.stride(0), ptr<__nv_bfloat16>(dx),
+      add ? add->data_ptr() : nullptr, add && add->scalar_type() == at::kFloat,
+      opt_ptr<__nv_bfloat16>(mask), N, H, W, C,
+      flodl::ConvGeo{(int)k, (int)k, (int)s, (int)s, (int)p, (int)p}, cur_stream(), &bn));
+}
+
 // Rectangular-kernel forms (per-axis kernel, stride, padding).
 void im2col_geo(const Tensor& x, Tensor& cols, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
                 int64_t ph, int64_t pw) {
@@ -149,6 +182,22 @@ void bn_bwd(const Tensor& dy, const optional<Tensor>& ymask, const Tensor& x, co
       opt_ptr<__nv_bfloat16>(dz_out), cur_stream()));
 }
 
+// Elementwise half of bn_bwd, with sums [2C] already reduced (col2im_bn).
+void bn_bwd_apply(const Tensor& dy, const optional<Tensor>& ymask, const Tensor& x,
+                  const Tensor& mean, const Tensor& rstd, const optional<Tensor>& gamma,
+                  const Tensor& sums, Tensor& dx, const optional<Tensor>& dz_out) {
+  FL_CHECK(dy.scalar_type() == at::kBFloat16 && dy.is_contiguous() && x.is_contiguous() &&
+               dx.is_contiguous() && dy.numel() == x.numel() && dx.numel() == x.numel(),
+           "bn_bwd_apply layouts");
+  const int C = (int)x.size(-1);
+  FL_CHECK(sums.numel() >= 2 * C, "bn_bwd_apply sums size");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_bn_bwd_apply(
+      ptr<__nv_bfloat16>(dy), opt_ptr<const __nv_bfloat16>(ymask), ptr<__nv_bfloat16>(x),
+      x.numel() / C, C, ptr<float>(mean), ptr<float>(rstd), opt_ptr<const float>(gamma),
+      ptr<float>(sums), ptr<__nv_bfloat16>(dx), opt_ptr<__nv_bfloat16>(dz_out), cur_stream()));
+}
+
 void avgpool_fwd(const Tensor& x, Tensor& y) {
   check_nhwc(x, "x");
   const int N = (int)x.size(0), HW = (int)(x.size(1) * x.size(2)), C = (int)x.size(3);
@@ -216,6 +265,13 @@ void register_conv(py::module& m) {
         py::arg("pad"));
   m.def("col2im", &col2im, py::arg("dcols"), py::arg("dx"), py::arg("k"), py::arg("stride"),
         py::arg("pad"), py::arg("add") = py::none(), py::arg("mask") = py::none());
+  m.def("col2im_bn", &col2im_bn, py::arg("dcols"), py::arg("dx"), py::arg("k"),
+        py::arg("stride"), py::arg("pad"), py::arg("add"), py::arg("mask"), py::arg("x"),
+        py::arg("mean"), py::arg("rstd"), py::arg("dgamma"), py::arg("dbeta"), py::arg("sums"),
+        py::arg("ws"));
+  m.def("bn_bwd_apply", &bn_bwd_apply, py::arg("dy"), py::arg("ymask"), py::arg("x"),
+        py::arg("mean"), py::arg("rstd"), py::arg("gamma"), py::arg("sums"), py::arg("dx"),
+        py::arg("dz_out") = py::none());
   m.def("im2col_geo", &im2col_geo);
   m.def("col2im_geo", &col2im_geo);
   m.def("bn_apply_sums", &bn_apply_sums, py::arg("x"), py::arg("ws"), py::arg("mean"),

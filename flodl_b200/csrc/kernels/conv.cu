@@ -33,6 +33,15 @@ namespace {
 
 constexpr int kRedThreads = 256;
 
+// Launch with programmatic dependent launch (every kernel of this file starts
+// with pdl_wait, so it reads nothing before the previous kernel finished);
+// returns from the calling launcher on a launch error.
+#define FL_PDL(...)                                      \
+  do {                                                   \
+    const cudaError_t e_ = launch_pdl(__VA_ARGS__);      \
+    if (e_ != cudaSuccess) return e_;                    \
+  } while (0)
+
 int blocks_for(int64_t work, int threads, int per_sm) {
   int64_t b = (work + threads - 1) / threads;
   int64_t cap = (int64_t)num_sms() * per_sm;
@@ -45,94 +54,28 @@ int blocks_for(int64_t work, int threads, int per_sm) {
 // Thread = (output pixel, tap, group of 8 channels): one 16-byte load or zero,
 // one 16-byte store.
 __global__ void im2col_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ cols,
-                              int N, int H, int W, int C, int Ho, int Wo, ConvGeo g2) {
-  const int G = C / 8;
+                              int N, int H, int W, int C, int Ho, int Wo, ConvGeo g2, uint32_t total,
+                              FastDiv fG, FastDiv fKK, FastDiv fWo, FastDiv fHo, FastDiv fKw) {
+  pdl_wait();
+  pdl_trigger();
   const int kk = g2.kh * g2.kw;
-  const int64_t total = (int64_t)N * Ho * Wo * kk * G;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int g = (int)(i % G);
-    int64_t t = i / G;
-    const int tap = (int)(t % kk);
-    const int64_t pix = t / kk;
-    const int wo = (int)(pix % Wo);
-    t = pix / Wo;
-    const int ho = (int)(t % Ho);
-    const int n = (int)(t / Ho);
-    const int h = ho * g2.sh - g2.ph + tap / g2.kw;
-    const int w = wo * g2.sw - g2.pw + tap % g2.kw;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t t = fG.div(i);
+    const int g = (int)(i - t * fG.d);
+    const uint32_t pix = fKK.div(t);
+    const int tap = (int)(t - pix * kk);
+    const uint32_t t2 = fWo.div(pix);
+    const int wo = (int)(pix - t2 * Wo);
+    const uint32_t n = fHo.div(t2);
+    const int ho = (int)(t2 - n * Ho);
+    const int tkh = (int)fKw.div(tap);
+    const int h = ho * g2.sh - g2.ph + tkh;
+    const int w = wo * g2.sw - g2.pw + (tap - tkh * g2.kw);
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (h >= 0 && h < H && w >= 0 && w < W)
       v = *reinterpret_cast<const uint4*>(x + (((int64_t)n * H + h) * W + w) * C + g * 8);
-    *reinterpret_cast<uint4*>(cols + pix * ((int64_t)kk * C) + tap * C + g * 8) = v;
-  }
-}
-
-// dx[n, h, w, c] = sum over taps (kh, kw) whose output pixel (ho, wo) reads
-// (h, w) of dcols[pix(ho, wo), (kh*k + kw)*C + c]; then + add[...] and, with a
-// mask tensor, * [mask > 0] (the ReLU that produced the input). Thread =
-// (input pixel, group of 8 channels).
-template <typename TAdd>
-__global__ void col2im_kernel(const __nv_bfloat16* __restrict__ dcols, int ldc,
-                              __nv_bfloat16* __restrict__ dx, const TAdd* __restrict__ add,
-                              const __nv_bfloat16* __restrict__ mask, int N, int H, int W, int C,
-                              int Ho, int Wo, ConvGeo g2) {
-  const int G = C / 8;
-  const int64_t total = (int64_t)N * H * W * G;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int g = (int)(i % G);
-    const int64_t pix = i / G;
-    const int w = (int)(pix % W);
-    const int64_t t = pix / W;
-    const int h = (int)(t % H);
-    const int n = (int)(t / H);
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    for (int kh = 0; kh < g2.kh; ++kh) {
-      const int hn = h + g2.ph - kh;
-      if (hn < 0 || hn % g2.sh) continue;
-      const int ho = hn / g2.sh;
-      if (ho >= Ho) continue;
-      for (int kw = 0; kw < g2.kw; ++kw) {
-        const int wn = w + g2.pw - kw;
-        if (wn < 0 || wn % g2.sw) continue;
-        const int wo = wn / g2.sw;
-        if (wo >= Wo) continue;
-        const int64_t op = ((int64_t)n * Ho + ho) * Wo + wo;
-        const uint4 u =
-            *reinterpret_cast<const uint4*>(dcols + op * ldc + (kh * g2.kw + kw) * C + g * 8);
-        const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = unpack_bf16x2(ws[q]);
-          acc[2 * q] += f.x;
-          acc[2 * q + 1] += f.y;
-        }
-      }
-    }
-    const int64_t o = pix * C + g * 8;
-    if (add) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += to_f32(add[o + e]);
-    }
-    if (mask) {
-      const uint4 u = *reinterpret_cast<const uint4*>(mask + o);
-      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = unpack_bf16x2(ws[q]);
-        if (!(f.x > 0.f)) acc[2 * q] = 0.f;
-        if (!(f.y > 0.f)) acc[2 * q + 1] = 0.f;
-      }
-    }
-    uint4 out;
-    out.x = pack_bf16x2(acc[0], acc[1]);
-    out.y = pack_bf16x2(acc[2], acc[3]);
-    out.z = pack_bf16x2(acc[4], acc[5]);
-    out.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(dx + o) = out;
+    *reinterpret_cast<uint4*>(cols + (int64_t)pix * ((int64_t)kk * C) + tap * C + g * 8) = v;
   }
 }
 
@@ -141,6 +84,8 @@ __global__ void col2im_kernel(const __nv_bfloat16* __restrict__ dcols, int ldc,
 // and the reverse for gradients:
 //   grad[co, ci, kh, kw] += gacc[co, (kh*k + kw)*Cp + ci];  gacc <- 0
 __global__ void pack_conv_weights_kernel(const ConvPackEntry* __restrict__ tab, int n) {
+  pdl_wait();
+  pdl_trigger();
   for (int e = blockIdx.y; e < n; e += gridDim.y) {
     const ConvPackEntry t = tab[e];
     const int K = t.k * t.k * t.cin_pad;
@@ -155,6 +100,8 @@ __global__ void pack_conv_weights_kernel(const ConvPackEntry* __restrict__ tab, 
 }
 
 __global__ void unpack_conv_grads_kernel(const ConvPackEntry* __restrict__ tab, int n) {
+  pdl_wait();
+  pdl_trigger();
   for (int e = blockIdx.y; e < n; e += gridDim.y) {
     const ConvPackEntry t = tab[e];
     const int K = t.k * t.k * t.cin_pad;
@@ -284,10 +231,140 @@ __device__ bool reduce_into_workspace(const RowGroups& rg, int C, float (&a)[8],
   return last;
 }
 
+// Last block of a batch-norm backward reduction: ws[0:2C] holds the grid's
+// sum(dz) / sum(dz * xhat); keep them in out2 for the apply pass, accumulate
+// dbeta / dgamma and leave ws and the ticket zeroed for the next call.
+__device__ void bn_bwd_finish(int C, float* ws, float* out2, float* dgamma, float* dbeta,
+                              unsigned* ticket) {
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float a = __ldcg(ws + c), b = __ldcg(ws + C + c);
+    out2[c] = a;
+    out2[C + c] = b;
+    if (dbeta) dbeta[c] += a;
+    if (dgamma) dgamma[c] += b;
+    ws[c] = 0.f;
+    ws[C + c] = 0.f;
+  }
+  if (threadIdx.x == 0) *ticket = 0u;
+}
+
+// dx[n, h, w, c] = sum over taps (kh, kw) whose output pixel (ho, wo) reads
+// (h, w) of dcols[pix(ho, wo), (kh*k + kw)*C + c]; then + add[...] and, with a
+// mask tensor, * [mask > 0] (the ReLU that produced the input). Thread =
+// (input pixel, group of 8 channels).
+template <typename TAdd, bool kBn>
+__global__ void __launch_bounds__(256, kBn ? 4 : 1) col2im_kernel(
+    const __nv_bfloat16* __restrict__ dcols, int ldc, __nv_bfloat16* __restrict__ dx,
+    const TAdd* __restrict__ add, const __nv_bfloat16* __restrict__ mask, int N, int H, int W,
+    int C, int Ho, int Wo, ConvGeo g2, BnBwdSums bn, uint32_t total, FastDiv fG, FastDiv fW,
+    FastDiv fH, FastDiv fSh, FastDiv fSw) {
+  pdl_wait();
+  pdl_trigger();
+  const int G = C / 8;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  // with kBn the block size is a multiple of G, so a thread keeps its channel
+  // group (threadIdx.x % G) on every iteration and sums it in registers; the
+  // batch norm's mean / rstd wait in shared memory (C <= 2048), not registers
+  float sd[8], sdx[8];
+  __shared__ float4 s_mr[kBn ? 2 * 2048 / 4 : 1];
+  if constexpr (kBn) {
+    for (int c = threadIdx.x; c < C / 4; c += blockDim.x) {
+      s_mr[c] = reinterpret_cast<const float4*>(bn.mean)[c];
+      s_mr[512 + c] = reinterpret_cast<const float4*>(bn.rstd)[c];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sd[e] = sdx[e] = 0.f;
+    __syncthreads();
+  }
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t pix = fG.div(i);
+    const int g = (int)(i - pix * G);
+    const uint32_t t = fW.div(pix);
+    const int w = (int)(pix - t * W);
+    const uint32_t n32 = fH.div(t);
+    const int h = (int)(t - n32 * H);
+    const int n = (int)n32;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int kh = 0; kh < g2.kh; ++kh) {
+      const int hn = h + g2.ph - kh;
+      if (hn < 0) continue;
+      const int ho = (int)fSh.div((uint32_t)hn);
+      if (ho * g2.sh != hn || ho >= Ho) continue;
+      for (int kw = 0; kw < g2.kw; ++kw) {
+        const int wn = w + g2.pw - kw;
+        if (wn < 0) continue;
+        const int wo = (int)fSw.div((uint32_t)wn);
+        if (wo * g2.sw != wn || wo >= Wo) continue;
+        const int64_t op = ((int64_t)n * Ho + ho) * Wo + wo;
+        const uint4 u =
+            *reinterpret_cast<const uint4*>(dcols + op * ldc + (kh * g2.kw + kw) * C + g * 8);
+        const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ws[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
+      }
+    }
+    const int64_t o = (int64_t)pix * C + g * 8;
+    if (add) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += to_f32(add[o + e]);
+    }
+    if (mask) {
+      const uint4 u = *reinterpret_cast<const uint4*>(mask + o);
+      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(ws[q]);
+        if (!(f.x > 0.f)) acc[2 * q] = 0.f;
+        if (!(f.y > 0.f)) acc[2 * q + 1] = 0.f;
+      }
+    }
+    uint4 out;
+    out.x = pack_bf16x2(acc[0], acc[1]);
+    out.y = pack_bf16x2(acc[2], acc[3]);
+    out.z = pack_bf16x2(acc[4], acc[5]);
+    out.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(dx + o) = out;
+    if constexpr (kBn) {
+      // sums of the stored (bf16) gradient, the values the apply pass reads
+      float v[8], q[8];
+      load8(bn.x + o, v);
+      const uint32_t ow[4] = {out.x, out.y, out.z, out.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(ow[k]);
+        q[2 * k] = f.x;
+        q[2 * k + 1] = f.y;
+      }
+      const float4 m0 = s_mr[g * 2], m1 = s_mr[g * 2 + 1];
+      const float4 r0 = s_mr[512 + g * 2], r1 = s_mr[512 + g * 2 + 1];
+      const float mu[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      const float rs[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        sd[e] += q[e];
+        sdx[e] = fmaf(q[e], (v[e] - mu[e]) * rs[e], sdx[e]);
+      }
+    }
+  }
+  if constexpr (kBn) {
+    RowGroups rg(C);
+    if (!reduce_into_workspace(rg, C, sd, sdx, bn.ws, bn.ticket)) return;
+    bn_bwd_finish(C, bn.ws, bn.sums, bn.dgamma, bn.dbeta, bn.ticket);
+  }
+}
+
 __global__ void __launch_bounds__(kRedThreads) bn_stats_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t M, int C, float eps, float momentum,
     float* __restrict__ mean, float* __restrict__ rstd, float* __restrict__ run_mean,
     float* __restrict__ run_var, float* __restrict__ ws, unsigned* __restrict__ ticket) {
+  pdl_wait();
+  pdl_trigger();
   RowGroups rg(C);
   float s1[8], s2[8];
 #pragma unroll
@@ -326,13 +403,15 @@ __global__ void bn_apply_kernel(const __nv_bfloat16* __restrict__ x, int64_t M, 
                                 const float* __restrict__ mean, const float* __restrict__ rstd,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const __nv_bfloat16* __restrict__ identity, int relu,
-                                __nv_bfloat16* __restrict__ y) {
-  const int groups = C / 8;
-  const int64_t total = M * groups;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int c0 = (int)(i % groups) * 8;
-    const int64_t r = i / groups;
+                                __nv_bfloat16* __restrict__ y, FastDiv fGroups) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t total = (uint32_t)M * fGroups.d;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t r32 = fGroups.div(i);
+    const int c0 = (int)(i - r32 * fGroups.d) * 8;
+    const int64_t r = r32;
     float v[8];
     load8(x + r * C + c0, v);
     float id[8];
@@ -363,7 +442,9 @@ __global__ void bn_apply_sums_kernel(const __nv_bfloat16* __restrict__ x, int64_
                                      const float* __restrict__ gamma,
                                      const float* __restrict__ beta,
                                      const __nv_bfloat16* __restrict__ identity, int relu,
-                                     __nv_bfloat16* __restrict__ y) {
+                                     __nv_bfloat16* __restrict__ y, FastDiv fGroups) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sc[kMaxBnC], sh[kMaxBnC];
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     const float mu = __ldcg(ws + c) / (float)M;
@@ -383,12 +464,12 @@ __global__ void bn_apply_sums_kernel(const __nv_bfloat16* __restrict__ x, int64_
     }
   }
   __syncthreads();
-  const int groups = C / 8;
-  const int64_t total = M * groups;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int c0 = (int)(i % groups) * 8;
-    const int64_t r = i / groups;
+  const uint32_t total = (uint32_t)M * fGroups.d;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t r32 = fGroups.div(i);
+    const int c0 = (int)(i - r32 * fGroups.d) * 8;
+    const int64_t r = r32;
     float v[8];
     load8(x + r * C + c0, v);
     float id[8];
@@ -422,6 +503,8 @@ __global__ void __launch_bounds__(kRedThreads) bn_bwd_reduce_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t M, int C, const float* __restrict__ mean,
     const float* __restrict__ rstd, float* __restrict__ dgamma, float* __restrict__ dbeta,
     float* __restrict__ out2, float* __restrict__ ws, unsigned* __restrict__ ticket) {
+  pdl_wait();
+  pdl_trigger();
   RowGroups rg(C);
   float sd[8], sdx[8], mu[8], rs[8];
 #pragma unroll
@@ -451,16 +534,7 @@ __global__ void __launch_bounds__(kRedThreads) bn_bwd_reduce_kernel(
     }
   }
   if (!reduce_into_workspace(rg, C, sd, sdx, ws, ticket)) return;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    const float a = __ldcg(ws + c), b = __ldcg(ws + C + c);
-    out2[c] = a;
-    out2[C + c] = b;
-    if (dbeta) dbeta[c] += a;
-    if (dgamma) dgamma[c] += b;
-    ws[c] = 0.f;
-    ws[C + c] = 0.f;
-  }
-  if (threadIdx.x == 0) *ticket = 0u;
+  bn_bwd_finish(C, ws, out2, dgamma, dbeta, ticket);
 }
 
 __global__ void bn_bwd_apply_kernel(const __nv_bfloat16* __restrict__ dy,
@@ -468,14 +542,17 @@ __global__ void bn_bwd_apply_kernel(const __nv_bfloat16* __restrict__ dy,
                                     const __nv_bfloat16* __restrict__ x, int64_t M, int C,
                                     const float* __restrict__ mean, const float* __restrict__ rstd,
                                     const float* __restrict__ gamma, const float* __restrict__ sums,
-                                    __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz_out) {
-  const int groups = C / 8;
-  const int64_t total = M * groups;
+                                    __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz_out,
+                                    FastDiv fGroups) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t total = (uint32_t)M * fGroups.d;
   const float invM = 1.f / (float)M;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int c0 = (int)(i % groups) * 8;
-    const int64_t r = i / groups;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint32_t r32 = fGroups.div(i);
+    const int c0 = (int)(i - r32 * fGroups.d) * 8;
+    const int64_t r = r32;
     float g[8], v[8];
     load8(dy + r * C + c0, g);
     load8(x + r * C + c0, v);
@@ -503,6 +580,8 @@ __global__ void bn_bwd_apply_kernel(const __nv_bfloat16* __restrict__ dy,
 // y[n, c] = mean over the HW pixels of x[n, :, c]   (x NHWC bf16, y bf16)
 __global__ void avgpool_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                    int N, int HW, int C) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = (int64_t)N * C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -517,6 +596,8 @@ __global__ void avgpool_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfl
 // dx[n, p, c] = dy[n, c] / HW   (dy with row pitch ld)
 __global__ void avgpool_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int ld,
                                    __nv_bfloat16* __restrict__ dx, int N, int HW, int C) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = (int64_t)N * HW * C;
   const float inv = 1.f / (float)HW;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -530,6 +611,8 @@ __global__ void avgpool_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int ld,
 // NCHW f32 -> NHWC bf16 with Cp >= C channels (channels C..Cp-1 zero)
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                     int N, int C, int HW, int Cp) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = (int64_t)N * Cp * HW;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -544,6 +627,8 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, __nv_bfloat16* 
 // bf16 copy of an f32 [rows, cols] matrix into a [rows, ld] buffer, zero-padding columns cols..ld-1
 __global__ void cast_pad_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int rows,
                                 int cols, int ld) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = (int64_t)rows * ld;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -564,25 +649,53 @@ cudaError_t launch_im2col_geo(const __nv_bfloat16* x, __nv_bfloat16* cols, int N
   if (!geo_ok(g)) return cudaErrorInvalidValue;
   const int Ho = (H + 2 * g.ph - g.kh) / g.sh + 1, Wo = (W + 2 * g.pw - g.kw) / g.sw + 1;
   if (Ho <= 0 || Wo <= 0 || C % 8) return cudaErrorInvalidValue;
-  im2col_kernel<<<blocks_for((int64_t)N * Ho * Wo * g.kh * g.kw * (C / 8), 256, 16), 256, 0,
-                  st>>>(x, cols, N, H, W, C, Ho, Wo, g);
+  const int64_t total = (int64_t)N * Ho * Wo * g.kh * g.kw * (C / 8);
+  if (total >= kMaxFlatIndex) return cudaErrorInvalidValue;
+  FL_PDL(im2col_kernel, dim3(blocks_for(total, 256, 16)), dim3(256), 0, st, x, cols, N, H, W, C, Ho,
+      Wo, g, (uint32_t)total, FastDiv(C / 8), FastDiv(g.kh * g.kw), FastDiv(Wo), FastDiv(Ho),
+      FastDiv(g.kw));
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_col2im_geo(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx,
                               const void* add, bool add_f32, const __nv_bfloat16* mask, int N,
-                              int H, int W, int C, const ConvGeo& g, cudaStream_t st) {
+                              int H, int W, int C, const ConvGeo& g, cudaStream_t st,
+                              const BnBwdSums* bn) {
   if (!geo_ok(g)) return cudaErrorInvalidValue;
   const int Ho = (H + 2 * g.ph - g.kh) / g.sh + 1, Wo = (W + 2 * g.pw - g.kw) / g.sw + 1;
   if (C % 8) return cudaErrorInvalidValue;
-  const int blocks = blocks_for((int64_t)N * H * W * (C / 8), 256, 16);
-  if (add_f32)
-    col2im_kernel<float><<<blocks, 256, 0, st>>>(dcols, ldc, dx, (const float*)add, mask, N, H, W,
-                                                 C, Ho, Wo, g);
-  else
-    col2im_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        dcols, ldc, dx, (const __nv_bfloat16*)add, mask, N, H, W, C, Ho, Wo, g);
+  const BnBwdSums none{};
+  if (bn) {
+    // the block keeps each thread on one channel group; a few blocks per SM
+    // keep the per-block atomics into the 2C sums few
+    if (!bn->x || !bn->mean || !bn->rstd || !bn->sums || !bn->ws || !bn->ticket ||
+        256 % (C / 8) != 0 || (reinterpret_cast<uintptr_t>(bn->mean) & 15) ||
+        (reinterpret_cast<uintptr_t>(bn->rstd) & 15))
+      return cudaErrorInvalidValue;
+  }
+  const int64_t total64 = (int64_t)N * H * W * (C / 8);
+  if (total64 >= kMaxFlatIndex) return cudaErrorInvalidValue;
+  const uint32_t total = (uint32_t)total64;
+  const FastDiv fG(C / 8), fW(W), fH(H), fSh(g.sh), fSw(g.sw);
+  const int blocks = blocks_for(total64, 256, bn ? 4 : 16);
+  const BnBwdSums& b = bn ? *bn : none;
+  if (add_f32) {
+    if (bn)
+      FL_PDL(col2im_kernel<float, true>, dim3(blocks), dim3(256), 0, st, dcols, ldc, dx,
+          (const float*)add, mask, N, H, W, C, Ho, Wo, g, b, total, fG, fW, fH, fSh, fSw);
+    else
+      FL_PDL(col2im_kernel<float, false>, dim3(blocks), dim3(256), 0, st, dcols, ldc, dx,
+          (const float*)add, mask, N, H, W, C, Ho, Wo, g, b, total, fG, fW, fH, fSh, fSw);
+  } else {
+    const __nv_bfloat16* a16 = (const __nv_bfloat16*)add;
+    if (bn)
+      FL_PDL(col2im_kernel<__nv_bfloat16, true>, dim3(blocks), dim3(256), 0, st, dcols, ldc, dx,
+          a16, mask, N, H, W, C, Ho, Wo, g, b, total, fG, fW, fH, fSh, fSw);
+    else
+      FL_PDL(col2im_kernel<__nv_bfloat16, false>, dim3(blocks), dim3(256), 0, st, dcols, ldc, dx,
+          a16, mask, N, H, W, C, Ho, Wo, g, b, total, fG, fW, fH, fSh, fSw);
+  }
   note_launch();
   return cudaGetLastError();
 }
@@ -603,7 +716,7 @@ cudaError_t launch_pack_conv_weights(const ConvPackEntry* table, int n, int max_
                                      cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   dim3 grid((max_elems + 255) / 256, n);
-  pack_conv_weights_kernel<<<grid, 256, 0, st>>>(table, n);
+  FL_PDL(pack_conv_weights_kernel, dim3(grid), dim3(256), 0, st, table, n);
   note_launch();
   return cudaGetLastError();
 }
@@ -612,7 +725,7 @@ cudaError_t launch_unpack_conv_grads(const ConvPackEntry* table, int n, int max_
                                      cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   dim3 grid((max_elems + 255) / 256, n);
-  unpack_conv_grads_kernel<<<grid, 256, 0, st>>>(table, n);
+  FL_PDL(unpack_conv_grads_kernel, dim3(grid), dim3(256), 0, st, table, n);
   note_launch();
   return cudaGetLastError();
 }
@@ -622,7 +735,7 @@ cudaError_t launch_bn_stats(const __nv_bfloat16* x, int64_t M, int C, float eps,
                             unsigned* ticket, cudaStream_t st) {
   if (C % 8 || C / 8 > kRedThreads) return cudaErrorInvalidValue;
   const int lanes = kRedThreads / (C / 8);
-  bn_stats_kernel<<<blocks_for((M + lanes - 1) / lanes, 4, 2), kRedThreads, 0, st>>>(
+  FL_PDL(bn_stats_kernel, dim3(blocks_for((M + lanes - 1) / lanes, 4, 2)), dim3(kRedThreads), 0, st,
       x, M, C, eps, momentum, mean, rstd, run_mean, run_var, ws, ticket);
   note_launch();
   return cudaGetLastError();
@@ -632,9 +745,9 @@ cudaError_t launch_bn_apply(const __nv_bfloat16* x, int64_t M, int C, const floa
                             const float* rstd, const float* gamma, const float* beta,
                             const __nv_bfloat16* identity, bool relu, __nv_bfloat16* y,
                             cudaStream_t st) {
-  if (C % 8) return cudaErrorInvalidValue;
-  bn_apply_kernel<<<blocks_for(M * (C / 8), 256, 16), 256, 0, st>>>(x, M, C, mean, rstd, gamma, beta,
-                                                                     identity, relu ? 1 : 0, y);
+  if (C % 8 || M * (C / 8) >= kMaxFlatIndex) return cudaErrorInvalidValue;
+  FL_PDL(bn_apply_kernel, dim3(blocks_for(M * (C / 8), 256, 16)), dim3(256), 0, st, x, M, C, mean,
+      rstd, gamma, beta, identity, relu ? 1 : 0, y, FastDiv(C / 8));
   note_launch();
   return cudaGetLastError();
 }
@@ -644,10 +757,11 @@ cudaError_t launch_bn_apply_sums(const __nv_bfloat16* x, int64_t M, int C, float
                                  float* rstd, float* run_mean, float* run_var, const float* gamma,
                                  const float* beta, const __nv_bfloat16* identity, bool relu,
                                  __nv_bfloat16* y, cudaStream_t st) {
-  if (C % 8 || C > kMaxBnC || M <= 0) return cudaErrorInvalidValue;
-  bn_apply_sums_kernel<<<blocks_for(M * (C / 8), 256, 16), 256, 0, st>>>(
-      x, M, C, ws, ticket, eps, momentum, mean, rstd, run_mean, run_var, gamma, beta, identity,
-      relu ? 1 : 0, y);
+  if (C % 8 || C > kMaxBnC || M <= 0 || M * (C / 8) >= kMaxFlatIndex)
+    return cudaErrorInvalidValue;
+  FL_PDL(bn_apply_sums_kernel, dim3(blocks_for(M * (C / 8), 256, 16)), dim3(256), 0, st, x, M, C,
+      ws, ticket, eps, momentum, mean, rstd, run_mean, run_var, gamma, beta, identity, relu ? 1 : 0,
+      y, FastDiv(C / 8));
   note_launch();
   return cudaGetLastError();
 }
@@ -659,38 +773,51 @@ cudaError_t launch_bn_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
                           __nv_bfloat16* dz_out, cudaStream_t st) {
   if (C % 8 || C / 8 > kRedThreads) return cudaErrorInvalidValue;
   const int lanes = kRedThreads / (C / 8);
-  bn_bwd_reduce_kernel<<<blocks_for((M + lanes - 1) / lanes, 4, 2), kRedThreads, 0, st>>>(
-      dy, ymask, x, M, C, mean, rstd, dgamma, dbeta, sums, ws, ticket);
-  bn_bwd_apply_kernel<<<blocks_for(M * (C / 8), 256, 16), 256, 0, st>>>(dy, ymask, x, M, C, mean, rstd,
-                                                                         gamma, sums, dx, dz_out);
-  note_launch(2);
+  FL_PDL(bn_bwd_reduce_kernel, dim3(blocks_for((M + lanes - 1) / lanes, 4, 2)), dim3(kRedThreads),
+      0, st, dy, ymask, x, M, C, mean, rstd, dgamma, dbeta, sums, ws, ticket);
+  note_launch();
+  return launch_bn_bwd_apply(dy, ymask, x, M, C, mean, rstd, gamma, sums, dx, dz_out, st);
+}
+
+cudaError_t launch_bn_bwd_apply(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
+                                const __nv_bfloat16* x, int64_t M, int C, const float* mean,
+                                const float* rstd, const float* gamma, const float* sums,
+                                __nv_bfloat16* dx, __nv_bfloat16* dz_out, cudaStream_t st) {
+  if (C % 8 || M * (C / 8) >= kMaxFlatIndex) return cudaErrorInvalidValue;
+  FL_PDL(bn_bwd_apply_kernel, dim3(blocks_for(M * (C / 8), 256, 16)), dim3(256), 0, st, dy, ymask,
+      x, M, C, mean, rstd, gamma, sums, dx, dz_out, FastDiv(C / 8));
+  note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_avgpool_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int N, int HW, int C,
                                cudaStream_t st) {
-  avgpool_fwd_kernel<<<blocks_for((int64_t)N * C, 256, 4), 256, 0, st>>>(x, y, N, HW, C);
+  FL_PDL(avgpool_fwd_kernel, dim3(blocks_for((int64_t)N * C, 256, 4)), dim3(256), 0, st, x, y, N,
+      HW, C);
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_avgpool_bwd(const __nv_bfloat16* dy, int ld, __nv_bfloat16* dx, int N, int HW,
                                int C, cudaStream_t st) {
-  avgpool_bwd_kernel<<<blocks_for((int64_t)N * HW * C, 256, 16), 256, 0, st>>>(dy, ld, dx, N, HW, C);
+  FL_PDL(avgpool_bwd_kernel, dim3(blocks_for((int64_t)N * HW * C, 256, 16)), dim3(256), 0, st, dy,
+      ld, dx, N, HW, C);
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_nchw_to_nhwc(const float* x, __nv_bfloat16* y, int N, int C, int HW, int Cp,
                                 cudaStream_t st) {
-  nchw_to_nhwc_kernel<<<blocks_for((int64_t)N * Cp * HW, 256, 16), 256, 0, st>>>(x, y, N, C, HW, Cp);
+  FL_PDL(nchw_to_nhwc_kernel, dim3(blocks_for((int64_t)N * Cp * HW, 256, 16)), dim3(256), 0, st, x,
+      y, N, C, HW, Cp);
   note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t launch_cast_pad(const float* x, __nv_bfloat16* y, int rows, int cols, int ld,
                             cudaStream_t st) {
-  cast_pad_kernel<<<blocks_for((int64_t)rows * ld, 256, 4), 256, 0, st>>>(x, y, rows, cols, ld);
+  FL_PDL(cast_pad_kernel, dim3(blocks_for((int64_t)rows * ld, 256, 4)), dim3(256), 0, st, x, y,
+      rows, cols, ld);
   note_launch();
   return cudaGetLastError();
 }

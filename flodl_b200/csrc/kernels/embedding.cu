@@ -17,20 +17,18 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const float* _
                                  const float* __restrict__ pos, const int64_t* __restrict__ type_ids,
                                  const float* __restrict__ type_tab, float* __restrict__ out,
                                  __nv_bfloat16* __restrict__ out_bf16, int T, int S, int C, int V,
-                                 uint32_t* err) {
+                                 FastDiv fC4, FastDiv fS) {
   pdl_wait();
   pdl_trigger();
-  const int C4 = C / 4;
-  const int64_t total = (int64_t)T * C4;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / C4);
-    const int c = (int)(i % C4) * 4;
+  const uint32_t total = (uint32_t)T * fC4.d;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int t = (int)fC4.div(i);
+    const int c = (int)(i - (uint32_t)t * fC4.d) * 4;
     int64_t id = ids[t];
     if (id < 0 || id >= V) id = 0;  // out-of-range ids read row 0 (checked on the host side)
     float4 v = *reinterpret_cast<const float4*>(tok + id * C + c);
     if (pos) {
-      const int s = t % S;
+      const int s = t - (int)fS.div((uint32_t)t) * S;
       float4 p = *reinterpret_cast<const float4*>(pos + (int64_t)s * C + c);
       v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
     }
@@ -98,10 +96,11 @@ int grid_1d(int64_t work, int threads) {
 cudaError_t launch_embed_fwd(const int64_t* ids, const float* tok, const float* pos,
                              const int64_t* type_ids, const float* type_tab, float* out,
                              __nv_bfloat16* out_bf16, int T, int S, int C, int V, cudaStream_t st) {
-  if (C % 4) return cudaErrorInvalidValue;
+  if (C % 4 || (pos && S <= 0) || (int64_t)T * (C / 4) >= kMaxFlatIndex)
+    return cudaErrorInvalidValue;
   cudaError_t e = launch_pdl(embed_fwd_kernel, dim3(grid_1d((int64_t)T * C / 4, 256)), dim3(256),
                              0, st, ids, tok, pos, type_ids, type_tab, out, out_bf16, T, S, C, V,
-                             (uint32_t*)nullptr);
+                             FastDiv(C / 4), FastDiv(S > 0 ? S : 1));
   if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();

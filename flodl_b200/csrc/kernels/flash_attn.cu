@@ -878,23 +878,21 @@ __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
                                      float* __restrict__ dq_acc, int B, int S, int H) {
   pdl_wait();
   pdl_trigger();
-  const int C = H * kD;
-  const int64_t rows = (int64_t)B * S * H;
-  const int64_t warp_g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  // row rw = token * H + head is the contiguous 64-element slice at rw * kD
+  // (B * S * H < 2^31, checked by the launcher); 8 lanes per row
+  const int rows = B * S * H;
+  const int warp_g = (int)((blockIdx.x * blockDim.x + threadIdx.x) / 32);
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3, part = lane & 7;
-  const int64_t nw = (int64_t)gridDim.x * blockDim.x / 32;
+  const int nw = (int)(gridDim.x * blockDim.x / 32);
 #pragma unroll 2
-  for (int64_t base = warp_g * 4; base < rows; base += nw * 4) {
-    const int64_t rw = base + sub;
+  for (int base = warp_g * 4; base < rows; base += nw * 4) {
+    const int rw = base + sub;
     float s = 0.f;
-    int64_t tok = 0;
-    int h = 0;
     if (rw < rows) {
-      tok = rw / H;
-      h = (int)(rw % H);
-      const uint4 x = *reinterpret_cast<const uint4*>(dout + tok * C + h * kD + part * 8);
-      const uint4 y = *reinterpret_cast<const uint4*>(out + tok * C + h * kD + part * 8);
+      const int64_t off = (int64_t)rw * kD + part * 8;
+      const uint4 x = *reinterpret_cast<const uint4*>(dout + off);
+      const uint4 y = *reinterpret_cast<const uint4*>(out + off);
       const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -902,15 +900,16 @@ __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dout,
         s = fmaf(a.x, c.x, fmaf(a.y, c.y, s));
       }
       if (dq_acc != nullptr) {
-        float4* dq = reinterpret_cast<float4*>(dq_acc + tok * C + h * kD + part * 8);
+        float4* dq = reinterpret_cast<float4*>(dq_acc + off);
         dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
         dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
-    for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (rw < rows && part == 0) {
-      const int bb = (int)(tok / S), si = (int)(tok % S);
+      const int tok = rw / H, h = rw - tok * H;
+      const int bb = tok / S, si = tok - bb * S;
       delta[((int64_t)bb * H + h) * S + si] = s;
     }
   }
@@ -1848,6 +1847,7 @@ cudaError_t launch_flash_bwd(const FlashArgs& a, cudaStream_t st) {
   if (!make_map_3d(&tm_qkv, a.qkv, a.B, a.S, 3 * C)) return cudaErrorInvalidValue;
   if (!make_map_3d(&tm_do, a.dout, a.B, a.S, C)) return cudaErrorInvalidValue;
   const int64_t rows = (int64_t)a.B * a.S * a.H;
+  if (rows >= (int64_t)1 << 31) return cudaErrorInvalidValue;  // 32-bit row indices
   int pre_blocks = (int)std::min<int64_t>((rows + 31) / 32, (int64_t)num_sms() * 16);
   if (!flash_bwd_needs_dq_acc(a.S)) {
     // dQ stays in TMEM: delta only, then one kernel per (batch, head)

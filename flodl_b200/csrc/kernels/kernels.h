@@ -153,9 +153,26 @@ struct ConvGeo {
 };
 cudaError_t launch_im2col_geo(const __nv_bfloat16* x, __nv_bfloat16* cols, int N, int H, int W,
                               int C, const ConvGeo& g, cudaStream_t st);
+// Batch-norm backward sums folded into the kernel that produces the gradient
+// dz of a batch norm's output: ws[0:C] += sum dz, ws[C:2C] += sum dz * xhat
+// with xhat = (x - mean) * rstd; the last block copies both to sums[0:2C],
+// adds them to dbeta / dgamma (nullable) and zeroes ws and *ticket.
+struct BnBwdSums {
+  const __nv_bfloat16* x;
+  const float* mean;
+  const float* rstd;
+  float* dgamma;
+  float* dbeta;
+  float* sums;
+  float* ws;
+  unsigned* ticket;
+};
+// With bn, dx (after add and mask) is the dz of that batch norm; C / 8 must
+// divide 256.
 cudaError_t launch_col2im_geo(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx,
                               const void* add, bool add_f32, const __nv_bfloat16* mask, int N,
-                              int H, int W, int C, const ConvGeo& g, cudaStream_t st);
+                              int H, int W, int C, const ConvGeo& g, cudaStream_t st,
+                              const BnBwdSums* bn = nullptr);
 cudaError_t launch_col2im(const __nv_bfloat16* dcols, int ldc, __nv_bfloat16* dx, const void* add,
                           bool add_f32, const __nv_bfloat16* mask, int N, int H, int W, int C,
                           int k, int s, int p, cudaStream_t st);
@@ -181,6 +198,11 @@ cudaError_t launch_bn_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
                           const float* rstd, const float* gamma, float* dgamma, float* dbeta,
                           float* sums, float* ws, unsigned* ticket, __nv_bfloat16* dx,
                           __nv_bfloat16* dz_out, cudaStream_t st);
+// The elementwise half of launch_bn_bwd, for sums already reduced.
+cudaError_t launch_bn_bwd_apply(const __nv_bfloat16* dy, const __nv_bfloat16* ymask,
+                                const __nv_bfloat16* x, int64_t M, int C, const float* mean,
+                                const float* rstd, const float* gamma, const float* sums,
+                                __nv_bfloat16* dx, __nv_bfloat16* dz_out, cudaStream_t st);
 cudaError_t launch_avgpool_fwd(const __nv_bfloat16* x, __nv_bfloat16* y, int N, int HW, int C,
                                cudaStream_t st);
 cudaError_t launch_avgpool_bwd(const __nv_bfloat16* dy, int ld, __nv_bfloat16* dx, int N, int HW,

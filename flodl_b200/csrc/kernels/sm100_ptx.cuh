@@ -55,6 +55,25 @@ __device__ __forceinline__ void report_error(uint32_t* err, uint32_t code) {
   if (err) atomicCAS(err, 0u, code);
 }
 
+// ---------------------------------------------------------------- division by a launch constant
+// Unsigned division of dividends below 2^31 by a divisor d (1 <= d <= 2^31)
+// fixed at launch, as one multiply-high, one add and one shift: with
+// s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1, q = (umulhi(n, m) + n)
+// >> s (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, section 4; n < 2^31 keeps the add from
+// wrapping). Elementwise kernels that split a flat index into coordinates
+// spend most of their issue slots on divisions otherwise.
+struct FastDiv {
+  uint32_t d = 1, m = 1, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div) {
+    while ((1ull << s) < div) ++s;
+    m = (uint32_t)((((1ull << s) - div) << 32) / div + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> s; }
+};
+constexpr int64_t kMaxFlatIndex = (int64_t)1 << 31;  // flat indices of FastDiv kernels
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Kernels launched with launch_pdl may start (their prologue: barrier init,
 // TMEM allocation, descriptor prefetch) while the previous kernel of the
@@ -599,13 +618,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// bf16 -> f32 is exact: a bf16 is the upper half of the f32 of the same value,
+// so two shifts/masks on the integer pipe unpack a pair.
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
-  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
-  return __bfloat1622float2(b);
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
 
 __device__ __forceinline__ float to_f32(float v) { return v; }
-__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) {
+  return __uint_as_float((uint32_t)__bfloat16_as_ushort(v) << 16);
+}
 
 // Vectorised fire-and-forget fp32 add into global memory (sm_90+).
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {

@@ -38,6 +38,16 @@ from .transformer import _empty
 # batch-norm statistics summed in the convolution GEMM's epilogue (no separate
 # statistics pass); FLODL_BN_FUSED_STATS=0 keeps the statistics kernel
 FUSED_BN_STATS = os.environ.get("FLODL_BN_FUSED_STATS", "1") != "0"
+# batch-norm backward sums (sum dz, sum dz * xhat) added up by the col2im that
+# produces dz, with FLODL_BN_FUSED_BWD=1. Off by default: on B200 the block
+# reduction and ticket of the fused col2im cost more than the re-read of dz
+# they save (col2im + separate reduction: 1.725 ms per ResNet-20 step; fused:
+# 1.801 ms).
+FUSED_BN_BWD = os.environ.get("FLODL_BN_FUSED_BWD", "0") == "1"
+
+
+def _bn_bwd_fusable(c):
+    return FUSED_BN_BWD and c % 8 == 0 and 256 % (c // 8) == 0
 
 
 def _ws(bn, dev):
@@ -128,9 +138,11 @@ class _Conv:
             K_.gemm(cols, self.packed, y, M, self.cout, self.K, False, False)
         return y, cols, (N, Ho, Wo)
 
-    def backward(self, dy, cols, x_shape, add=None, mask=None, need_dx=True):
+    def backward(self, dy, cols, x_shape, add=None, mask=None, need_dx=True, bn=None):
         """dy [M, Cout] bf16 -> dx NHWC bf16 (+ add, * [mask > 0]); the weight
-        gradient accumulates (packed order) into self.gacc."""
+        gradient accumulates (packed order) into self.gacc. ``bn`` = (batch
+        norm, its input, mean, rstd) when dx is that batch norm's output
+        gradient: the col2im pass also reduces its backward sums."""
         K_ = C()
         M = dy.shape[0]
         K_.gemm(dy, cols, self.gacc, self.cout, self.K, M, True, True, flags=K_.EPI_ACCUMULATE,
@@ -140,7 +152,13 @@ class _Conv:
         dcols = _empty((M, self.K), torch.bfloat16, dy.device)
         K_.gemm(dy, self.packed, dcols, M, self.K, self.cout, False, True)
         dx = _empty(x_shape, torch.bfloat16, dy.device)
-        K_.col2im(dcols, dx, self.k, self.s, self.p, add, mask)
+        if bn is not None:
+            bno, y, mean, rstd = bn
+            ws, sums = _ws(bno.mod, dy.device)
+            K_.col2im_bn(dcols, dx, self.k, self.s, self.p, add, mask, y, mean, rstd,
+                         grad_buffer(bno.mod.weight), grad_buffer(bno.mod.bias), sums, ws)
+        else:
+            K_.col2im(dcols, dx, self.k, self.s, self.p, add, mask)
         return dx
 
 
@@ -197,6 +215,17 @@ class _BN:
         grad_ready(b.bias)
         return dx, dz
 
+    def backward_apply(self, dz, y, mean, rstd):
+        """Input gradient from sums that the producer of dz reduced (dgamma
+        and dbeta are already accumulated)."""
+        b = self.mod
+        _, sums = _ws(b, dz.device)
+        dx = torch.empty_like(y)
+        C().bn_bwd_apply(dz, None, y, mean, rstd, b.weight.detach(), sums, dx)
+        grad_ready(b.weight)
+        grad_ready(b.bias)
+        return dx
+
 
 class _Block:
     def __init__(self, blk):
@@ -217,21 +246,36 @@ class _Block:
             ident = x.view(y2.shape)
             dsv = None
         out, m2, r2 = self.bn2.forward(y2, identity=ident, relu=True)
-        saved = (x.shape, cols1, y1, m1, r1, a1, cols2, y2, m2, r2, out, dsv)
+        saved = (x, cols1, y1, m1, r1, a1, cols2, y2, m2, r2, out, dsv)
         return out.view(N, Ho, Wo, -1), saved
 
-    def backward(self, dout, saved):
-        x_shape, cols1, y1, m1, r1, a1, cols2, y2, m2, r2, out, dsv = saved
-        dy2, dz = self.bn2.backward(dout.view(y2.shape), out, y2, m2, r2, want_dz=True)
-        da1 = self.conv2.backward(dy2, cols2, a1.shape, mask=a1)
-        dy1, _ = self.bn1.backward(da1.view(y1.shape), None, y1, m1, r1)
+    def backward(self, dout, saved, reduced=False, prev=None):
+        """Gradient of the block input. ``reduced``: dout is already masked by
+        the output ReLU and bn2's backward sums are reduced. ``prev`` = (batch
+        norm, input, mean, rstd) of the batch norm whose ReLU output is this
+        block's input: the returned gradient is then masked by that ReLU with
+        the batch norm's sums reduced in the same pass."""
+        x, cols1, y1, m1, r1, a1, cols2, y2, m2, r2, out, dsv = saved
+        if reduced:
+            dz = dout.view(y2.shape)
+            dy2 = self.bn2.backward_apply(dz, y2, m2, r2)
+        else:
+            dy2, dz = self.bn2.backward(dout.view(y2.shape), out, y2, m2, r2, want_dz=True)
+        if _bn_bwd_fusable(self.bn1.c):
+            da1 = self.conv2.backward(dy2, cols2, a1.shape, mask=a1, bn=(self.bn1, y1, m1, r1))
+            dy1 = self.bn1.backward_apply(da1.view(y1.shape), y1, m1, r1)
+        else:
+            da1 = self.conv2.backward(dy2, cols2, a1.shape, mask=a1)
+            dy1, _ = self.bn1.backward(da1.view(y1.shape), None, y1, m1, r1)
         if dsv is not None:
             yd, colsd, md, rd = dsv
             dyd, _ = self.ds[1].backward(dz, None, yd, md, rd)
-            add = self.ds[0].backward(dyd, colsd, x_shape)
+            add = self.ds[0].backward(dyd, colsd, x.shape)
         else:
             add = dz
-        return self.conv1.backward(dy1, cols1, x_shape, add=add)
+        if prev is not None:
+            return self.conv1.backward(dy1, cols1, x.shape, add=add, mask=x, bn=prev)
+        return self.conv1.backward(dy1, cols1, x.shape, add=add)
 
 
 class _ResNetTrainFn(torch.autograd.Function):
@@ -293,9 +337,20 @@ class _ResNetTrainFn(torch.autograd.Function):
         K_.gemm(dlogits, bf16_shadow(fc.weight), dpooled, N, Cf, ncls, False, True, alpha_t=g)
         dh = _empty(h_shape, torch.bfloat16, pooled.device)
         K_.avgpool_bwd(dpooled, dh)
-        for b, sv in zip(reversed(blocks), reversed(ctx.saved_blocks)):
-            dh = b.backward(dh, sv)
-        dy0, _ = stem_bn.backward(dh.view(y0.shape), x0, y0, m0, r0)
+        saved = ctx.saved_blocks
+        # the batch norm feeding each block's input: the stem's, then bn2 of
+        # the block before
+        prevs = [(stem_bn, y0, m0, r0)] + [(b.bn2, sv[7], sv[8], sv[9])
+                                           for b, sv in zip(blocks[:-1], saved[:-1])]
+        reduced = False
+        for i in reversed(range(len(blocks))):
+            prev = prevs[i] if _bn_bwd_fusable(prevs[i][0].c) else None
+            dh = blocks[i].backward(dh, saved[i], reduced, prev)
+            reduced = prev is not None
+        if reduced:
+            dy0 = stem_bn.backward_apply(dh.view(y0.shape), y0, m0, r0)
+        else:
+            dy0, _ = stem_bn.backward(dh.view(y0.shape), x0, y0, m0, r0)
         stem_c.backward(dy0, cols0, x_shape, need_dx=False)
         plan.unpack()  # packed-order conv gradients -> OIHW param.grad (+ grad-ready)
         ctx.saved_blocks = None

@@ -82,6 +82,78 @@ def test_batch_norm_kernels_match_torch(Cc):
     torch.testing.assert_close(db, b_.grad, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("Cc,k,s,p", [(16, 3, 1, 1), (32, 3, 2, 1), (64, 1, 2, 0)])
+def test_col2im_with_batch_norm_sums_matches_fp32(Cc, k, s, p):
+    """col2im_bn = col2im (+ add, * mask) whose output is a batch norm's output
+    gradient, with that batch norm's backward sums reduced in the same pass;
+    bn_bwd_apply finishes the input gradient."""
+    C = _C()
+    torch.manual_seed(3)
+    N, H = 16, 16
+    Ho = (H + 2 * p - k) // s + 1
+    L, K = Ho * Ho, Cc * k * k
+    M = N * H * H
+    dcols = torch.randn(N * L, K, device="cuda").bfloat16()
+    add = torch.randn(N, H, H, Cc, device="cuda").bfloat16()
+    mask = torch.randn(N, H, H, Cc, device="cuda").bfloat16()
+    y = (torch.randn(M, Cc, device="cuda") * 2 + 0.5).bfloat16()
+    gamma = torch.rand(Cc, device="cuda") + 0.5
+    mean = y.float().mean(0)
+    rstd = torch.rsqrt(y.float().var(0, unbiased=False) + 1e-5)
+    ws = torch.zeros(2 * Cc + 1, device="cuda")
+    sums = torch.empty(2 * Cc, device="cuda")
+    dg, db = torch.zeros(Cc, device="cuda"), torch.zeros(Cc, device="cuda")
+    dz = torch.empty(N, H, H, Cc, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):  # the workspace must come back zeroed
+        C.col2im_bn(dcols, dz, k, s, p, add, mask, y, mean, rstd, dg, db, sums, ws)
+    assert ws.abs().max().item() == 0.0
+    dx = torch.empty_like(y)
+    C.bn_bwd_apply(dz.view(M, Cc), None, y, mean, rstd, gamma, sums, dx)
+    # fp32 reference: fold, add, mask, then batch-norm backward
+    dc = dcols.float().reshape(N, L, k * k, Cc).permute(0, 3, 2, 1).reshape(N, K, L)
+    fold = F.fold(dc, (H, H), k, padding=p, stride=s).permute(0, 2, 3, 1)
+    g = ((fold + add.float()) * (mask.float() > 0)).reshape(M, Cc)
+    torch.testing.assert_close(dz.float().view(M, Cc), g, rtol=2e-2, atol=5e-2)
+    xhat = (y.float() - mean) * rstd
+    sg, sgx = g.sum(0), (g * xhat).sum(0)
+    torch.testing.assert_close(sums[:Cc], sg, rtol=1e-2, atol=0.5)
+    torch.testing.assert_close(sums[Cc:], sgx, rtol=1e-2, atol=0.5)
+    torch.testing.assert_close(db, 2 * sg, rtol=1e-2, atol=1.0)
+    torch.testing.assert_close(dg, 2 * sgx, rtol=1e-2, atol=1.0)
+    ref = gamma * rstd * (g - sg / M - xhat * sgx / M)
+    torch.testing.assert_close(dx.float(), ref, rtol=3e-2, atol=3e-2)
+
+
+def test_resnet20_fused_batch_norm_backward_matches_separate_reduction(monkeypatch):
+    """The backward with batch-norm sums reduced inside col2im deviates from
+    fp32 no more than the backward with the separate reduction kernels (bf16
+    ResNet gradients are ill-conditioned: any change of summation order moves
+    them by percents, so the two bf16 runs are compared through fp32)."""
+    import flodl_b200.ops.resnet as R
+    from flodl_b200.models import ResNet20
+
+    torch.manual_seed(0)
+    cpu = ResNet20()
+    m = copy.deepcopy(cpu)
+    m.move_to_device(torch.device("cuda"))
+    x = torch.randn(64, 3, 32, 32)
+    t = torch.randint(0, 10, (64,))
+    cpu.loss(x, t).backward()
+    dev = []
+    for fused in (False, True):
+        monkeypatch.setattr(R, "FUSED_BN_BWD", fused)
+        for q in m.parameters():
+            q.grad = None
+        m.loss(x.cuda(), t.cuda()).backward()
+        torch.cuda.synchronize()
+        dev.append([((q.grad.cpu() - pc.grad).norm() / pc.grad.norm()).item()
+                    for q, pc in zip(m.parameters(), cpu.parameters())])
+    sep, fus = dev
+    for (name, _), a, b in zip(m.named_parameters(), sep, fus):
+        assert b < 2.0 * a + 0.05, f"{name}: fused {b:.3f} vs separate {a:.3f}"
+    assert sum(fus) < 1.25 * sum(sep) + 0.05, (sum(fus), sum(sep))
+
+
 def test_resnet20_fused_matches_bf16_autocast_reference():
     """bf16 training of ResNet-20 deviates from fp32 by tens of percent per
     gradient (BatchNorm backward cancels most of each gradient); the fused op
