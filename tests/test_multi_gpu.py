@@ -304,7 +304,11 @@ def test_fused_ddp_matches_single_gpu_full_batch(world, kind, clip, graph):
         assert not bad, f"rank {rank}: failed {bad}"
     ref, ref_norm = _reference(world, kind, clip)
     got = torch.from_numpy(res[0][2])
-    torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=2e-3)
+    # AdamW moves an element with a near-zero gradient by about lr per step
+    # whatever the gradient's size, so reduction-order noise can shift such
+    # elements by O(lr): the absolute tolerance follows the largest lr
+    atol = 2e-3 * (2.0 if kind == "adamw2" else 1.0)
+    torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=atol)
     if clip:
         got_norm = res[0][3]
         assert abs(got_norm - ref_norm) <= 0.03 * ref_norm, (got_norm, ref_norm)
