@@ -161,6 +161,15 @@ class Optimizer:
             self._init_fused_state(g)
         return g.arena
 
+    def adopt_arena(self, g: ParamGroup, arena: ParamArena) -> None:
+        """Make ``arena`` (e.g. parameters moved into a peer-shared region)
+        the group's fused storage. The fused optimizer state is created on the
+        group's first arena and kept across later moves (same element order)."""
+        first = g.arena is None
+        g.arena = arena
+        if first:
+            self._init_fused_state(g)
+
     def _device_scalars(self, g: ParamGroup) -> None:
         dev = g.params[0].device
         if g.lr_t is None:

@@ -175,7 +175,7 @@ class _Averager:
             arena = ParamArena(self.params)
             for g in self.opt.groups:
                 if getattr(g, "arena", None) is old_arena:
-                    g.arena = arena
+                    self.opt.adopt_arena(g, arena)
         old_comm.abandon()
 
     def _make_fused(self) -> None:
@@ -197,7 +197,7 @@ class _Averager:
         opt = self.opt
         for g in opt.groups:
             if all(any(q is p for q in arena.params) for p in g.params) and len(opt.groups) == 1:
-                g.arena = arena
+                opt.adopt_arena(g, arena)
 
     def average(self, batches: int, rnd: Optional[int] = None) -> float:
         """Average with this rank's work; returns ||pre - post|| / ||post||.

@@ -110,3 +110,25 @@ def test_schedulers():
     assert lr == 0.5
     with pytest.raises(ValueError):
         StepDecay(1.0, 0, 0.5)
+
+
+def test_adopted_arena_gets_fused_state():
+    """An arena handed over by the cluster trainer (parameters moved into a
+    peer-shared region) gets the optimizer's fused state like one the
+    optimizer built itself."""
+    from flodl_b200.optim import SGD, AdamW
+    from flodl_b200.utils.arena import ParamArena
+
+    ps = [torch.nn.Parameter(torch.randn(10, 3)), torch.nn.Parameter(torch.randn(7))]
+    sgd = SGD(ps, lr=0.1, momentum=0.9)
+    g = sgd.groups[0]
+    arena = ParamArena(g.params)
+    sgd.adopt_arena(g, arena)
+    assert g.arena is arena and g.buf is not None and g.buf.numel() == arena.numel
+    buf = g.buf
+    sgd.adopt_arena(g, ParamArena(g.params))  # a later move keeps the state
+    assert g.buf is buf
+    adam = AdamW(ps, lr=1e-3)
+    ga = adam.groups[0]
+    adam.adopt_arena(ga, arena)
+    assert ga.m.numel() == arena.numel and ga.v.numel() == arena.numel
