@@ -55,6 +55,19 @@ def case_gemm(kind):
         bias = torch.randn(N, device="cuda")
         fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False, bias=bias)
         nbytes = (M * K + N * K + M * N) * 2
+    elif kind == "gemm_qkv_nobias":  # the qkv shape without the bias (epilogue cost probe)
+        M, N, K = T, 3 * D, D
+        A, Bm = _bf(M, K), _bf(N, K)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False)
+        nbytes = (M * K + N * K + M * N) * 2
+    elif kind == "gemm_fc1_nogelu":  # the fc1 shape with bias only (GELU cost probe)
+        M, N, K = T, FF, D
+        A, Bm = _bf(M, K), _bf(N, K)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        bias = torch.randn(N, device="cuda")
+        fn = lambda: C.gemm(A, Bm, out, M, N, K, False, False, bias=bias)
+        nbytes = (M * K + N * K + M * N) * 2
     elif kind == "gemm_fc1_gelu":  # gelu(x W1^T + b1), GELU' kept (two bf16 outputs)
         M, N, K = T, FF, D
         A, Bm = _bf(M, K), _bf(N, K)
@@ -277,7 +290,8 @@ def case_conv(kind):
 
 CASES = {
     "gemm_qkv": case_gemm, "gemm_fc1_gelu": case_gemm, "gemm_fc2_residual": case_gemm,
-    "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm,
+    "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm, "gemm_qkv_nobias": case_gemm,
+    "gemm_fc1_nogelu": case_gemm,
     "flash_fwd": case_flash, "flash_bwd": case_flash,
     "flash_fwd_bert": case_flash_bert, "flash_bwd_bert": case_flash_bert,
     "ln_fwd": case_ln, "ln_bwd": case_ln, "adamw": case_adamw, "sgd": case_sgd,

@@ -710,23 +710,29 @@ __global__ void __launch_bounds__(kF2Threads, 2)
         // valid keys of this row in this tile: [k0, k0 + lim) (range and causal)
         const int lim = max(0, min((causal ? min(qi + 1, S) : S) - k0, kTile));
         const bool ranged = lim < kTile;  // warp-uniform only on tiles without masking
-        // pass 1: row maximum of the raw scores (scale > 0 commutes with max)
+        // pass 1: row maximum of the raw scores (scale > 0 commutes with max),
+        // 64 columns per tensor-memory round trip
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t raw[32];
-          tmem_ld_32cols(t_s + (uint32_t)(c * 32), raw);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t raw[2][32];
+          tmem_ld_32cols(t_s + (uint32_t)(c2 * 64), raw[0]);
+          tmem_ld_32cols(t_s + (uint32_t)(c2 * 64 + 32), raw[1]);
           tmem_ld_wait();
-          float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
-          if (ranged) {
+          for (int h = 0; h < 2; ++h) {
+            const int c = c2 * 2 + h;
+            float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = (c * 32 + i < lim) ? v[i] : -INFINITY;
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[h][i]);
+            if (ranged) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = (c * 32 + i < lim) ? v[i] : -INFINITY;
+            }
+            if (kp_row) f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
           }
-          if (kp_row) f2_pad_mask32(v, k0 + c * 32, S, kp_row);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
         }
         const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         const float mx = mraw == -INFINITY ? -INFINITY : mraw * sl2;
@@ -741,42 +747,50 @@ __global__ void __launch_bounds__(kF2Threads, 2)
         const uint64_t sl2x2 = f2_splat(sl2);
         uint64_t la = f2_splat(0.f), lb = f2_splat(0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t raw[32];
-          tmem_ld_32cols(t_s + (uint32_t)(c * 32), raw);
+        for (int c2 = 0; c2 < 2; ++c2) {
+          // 64 columns per round trip; P of these columns lands in columns
+          // [32 c2, 32 c2 + 32), which hold scores already in registers
+          uint32_t raw2[2][32];
+          tmem_ld_32cols(t_s + (uint32_t)(c2 * 64), raw2[0]);
+          tmem_ld_32cols(t_s + (uint32_t)(c2 * 64 + 32), raw2[1]);
           tmem_ld_wait();
-          float p[32];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float a0, a1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1])),
-                             sl2x2, neg_m),
-                      a0, a1);
-            p[i] = ex2_approx(a0);
-            p[i + 1] = ex2_approx(a1);
+          for (int hc = 0; hc < 2; ++hc) {
+            const int c = c2 * 2 + hc;
+            const uint32_t (&raw)[32] = raw2[hc];
+            float p[32];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              float a0, a1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(raw[i]), __uint_as_float(raw[i + 1])),
+                               sl2x2, neg_m),
+                        a0, a1);
+              p[i] = ex2_approx(a0);
+              p[i + 1] = ex2_approx(a1);
+            }
+            if (ranged) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) p[i] = (c * 32 + i < lim) ? p[i] : 0.f;
+            }
+            if (kp_row) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = 0.f;
+              f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) p[i] = v[i] == -INFINITY ? 0.f : p[i];
+            }
+            uint32_t pw[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              if (i & 2)
+                lb = f2_add(lb, f2_pack(p[i], p[i + 1]));
+              else
+                la = f2_add(la, f2_pack(p[i], p[i + 1]));
+              pw[i / 2] = pack_bf16x2(p[i], p[i + 1]);
+            }
+            tmem_st_16cols(t_s + (uint32_t)(c * 16), pw);
           }
-          if (ranged) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) p[i] = (c * 32 + i < lim) ? p[i] : 0.f;
-          }
-          if (kp_row) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-            f2_pad_mask32(v, k0 + c * 32, S, kp_row);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) p[i] = v[i] == -INFINITY ? 0.f : p[i];
-          }
-          uint32_t pw[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            if (i & 2)
-              lb = f2_add(lb, f2_pack(p[i], p[i + 1]));
-            else
-              la = f2_add(la, f2_pack(p[i], p[i + 1]));
-            pw[i / 2] = pack_bf16x2(p[i], p[i + 1]);
-          }
-          tmem_st_16cols(t_s + (uint32_t)(c * 16), pw);
         }
         float la0, la1, lb0, lb1;
         f2_unpack(la, la0, la1);

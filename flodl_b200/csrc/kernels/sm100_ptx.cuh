@@ -568,49 +568,47 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   return d;
 }
 
-// GELU and GELU' of two values with packed math: the same A&S 7.1.28 erf as
-// gelu_and_grad, with the 1/sqrt(2) argument scale folded into the
-// coefficients (b_k = a_k 2^(-k/2)), so the polynomial runs on |x| directly
-// (clamped at 8 sqrt(2), where Phi is 1 to single precision).
-//   Phi(x) = [x >= 0] - sign(x) * r / 2,  r = (1 + sum b_k |x|^k)^-16
-//   GELU(x) = x Phi(x),  GELU'(x) = Phi(x) + x exp(-x^2/2) / sqrt(2 pi)
+// GELU and GELU' of two values with packed math. erf after Abramowitz &
+// Stegun 7.1.26 (|error| <= 1.5e-7), whose exponential is the Gaussian factor
+// that GELU' needs anyway, so one ex2 serves both:
+//   z = |x| / sqrt(2),  t = 1 / (1 + p z),  e = exp(-x^2 / 2)
+//   erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e
+//   Phi(x) = 1/2 + sign(x) (1/2 - erfc(z) / 2)
+//   GELU(x) = x Phi(x),  GELU'(x) = Phi(x) + x e / sqrt(2 pi)
+// The sign is copied with integer ops; the polynomial and products run as
+// f32x2 pairs.
 __device__ __forceinline__ void gelu_and_grad2(float x0, float x1, float& g0, float& g1,
                                                float& d0, float& d1) {
-  constexpr float kR = 0.70710678118654752f;
-  constexpr float b1 = 0.0705230784f * kR, b2 = 0.0422820123f * 0.5f,
-                  b3 = 0.0092705272f * 0.5f * kR, b4 = 0.0001520143f * 0.25f,
-                  b5 = 0.0002765672f * 0.25f * kR, b6 = 0.0000430638f * 0.125f;
-  constexpr float kClamp = 8.0f * 1.41421356237309505f;
+  constexpr float kP = 0.3275911f * 0.70710678118654752f;  // p / sqrt(2): t from |x|
+  constexpr float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f,
+                  a4 = -1.453152027f, a5 = 1.061405429f;
   const uint64_t x = f2_pack(x0, x1);
-  const uint64_t ax = f2_pack(fminf(fabsf(x0), kClamp), fminf(fabsf(x1), kClamp));
-  uint64_t p = f2_fma(f2_splat(b6), ax, f2_splat(b5));
-  p = f2_fma(p, ax, f2_splat(b4));
-  p = f2_fma(p, ax, f2_splat(b3));
-  p = f2_fma(p, ax, f2_splat(b2));
-  p = f2_fma(p, ax, f2_splat(b1));
-  p = f2_fma(p, ax, f2_splat(1.0f));
-  p = f2_mul(p, p);  // ^2
-  p = f2_mul(p, p);  // ^4
-  p = f2_mul(p, p);  // ^8
-  p = f2_mul(p, p);  // ^16
-  float p0, p1, r0, r1;
-  f2_unpack(p, p0, p1);
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(p0));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(p1));
-  const uint64_t base = f2_pack(x0 >= 0.f ? 1.f : 0.f, x1 >= 0.f ? 1.f : 0.f);
-  const uint64_t nhalf = f2_pack(x0 >= 0.f ? -0.5f : 0.5f, x1 >= 0.f ? -0.5f : 0.5f);
-  const uint64_t cdf = f2_fma(nhalf, f2_pack(r0, r1), base);
+  const uint64_t den = f2_fma(f2_pack(fabsf(x0), fabsf(x1)), f2_splat(kP), f2_splat(1.0f));
+  float n0, n1, t0, t1;
+  f2_unpack(den, n0, n1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(n0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(n1));
+  const uint64_t t = f2_pack(t0, t1);
+  uint64_t poly = f2_fma(f2_splat(a5), t, f2_splat(a4));
+  poly = f2_fma(poly, t, f2_splat(a3));
+  poly = f2_fma(poly, t, f2_splat(a2));
+  poly = f2_fma(poly, t, f2_splat(a1));
+  poly = f2_mul(poly, t);
+  // exp(-x^2 / 2) = 2^(-x^2 log2(e) / 2)
+  const uint64_t arg = f2_mul(x, f2_mul(x, f2_splat(-0.72134752044448170f)));
+  float q0, q1, e0, e1;
+  f2_unpack(arg, q0, q1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(q0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(q1));
+  const uint64_t e = f2_pack(e0, e1);
+  // h = 1/2 - erfc / 2 in [0, 1/2], then Phi = 1/2 + copysign(h, x)
+  float h0, h1;
+  f2_unpack(f2_fma(f2_mul(poly, e), f2_splat(-0.5f), f2_splat(0.5f)), h0, h1);
+  const float s0 = __uint_as_float(__float_as_uint(h0) | (__float_as_uint(x0) & 0x80000000u));
+  const float s1 = __uint_as_float(__float_as_uint(h1) | (__float_as_uint(x1) & 0x80000000u));
+  const uint64_t cdf = f2_add(f2_pack(s0, s1), f2_splat(0.5f));
   f2_unpack(f2_mul(x, cdf), g0, g1);
-  // exp(-x^2/2) = 2^(-x^2 log2(e) / 2): the identity folded into one packed
-  // multiply, then the hardware base-2 exponential (the same base-2 form the
-  // attention softmax uses)
-  const uint64_t arg = f2_mul(f2_mul(x, x), f2_splat(-0.72134752044448170f));
-  float a0, a1, e0, e1;
-  f2_unpack(arg, a0, a1);
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
-  const uint64_t xe = f2_mul(x, f2_pack(e0, e1));
-  f2_unpack(f2_fma(xe, f2_splat(0.39894228040143268f), cdf), d0, d1);
+  f2_unpack(f2_fma(f2_mul(x, e), f2_splat(0.39894228040143268f), cdf), d0, d1);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
