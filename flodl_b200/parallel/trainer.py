@@ -273,6 +273,35 @@ class _Averager:
             self.fused[0].close()
 
 
+class _Bytes:
+    """A tensor pickled by value (dtype, shape, raw bytes)."""
+
+    def __init__(self, t: torch.Tensor):
+        t = t.detach().cpu().contiguous()
+        self.dtype = str(t.dtype).split(".")[-1]
+        self.shape = tuple(t.shape)
+        self.data = t.reshape(-1).view(torch.uint8).numpy().tobytes()
+
+    def tensor(self) -> torch.Tensor:
+        raw = torch.frombuffer(bytearray(self.data), dtype=torch.uint8)
+        return raw.view(getattr(torch, self.dtype)).reshape(self.shape)
+
+
+def _report_by_value(st: "TrainedState") -> "TrainedState":
+    """Tensors of a rank's report pickled by value: a queue would otherwise
+    pass them as shared-memory handles that die with the rank process, which
+    may exit before the parent reads them."""
+    st.params = [(n, _Bytes(t) if isinstance(t, torch.Tensor) else t) for n, t in st.params]
+    st.buffers = [(n, _Bytes(t) if isinstance(t, torch.Tensor) else t) for n, t in st.buffers]
+    return st
+
+
+def _report_as_tensors(st: "TrainedState") -> "TrainedState":
+    st.params = [(n, t.tensor() if isinstance(t, _Bytes) else t) for n, t in st.params]
+    st.buffers = [(n, t.tensor() if isinstance(t, _Bytes) else t) for n, t in st.buffers]
+    return st
+
+
 def _rank_main(rank: int, world: int, host: str, port: int, key: bytes, spec: dict,
                out_q) -> None:
     """One training rank process: follows the coordinator's control messages."""
@@ -284,7 +313,7 @@ def _rank_main(rank: int, world: int, host: str, port: int, key: bytes, spec: di
         log.set_label(f"rank {rank}")
         report = _RankWorker(rank, world, host, port, key, spec, device).run()
         if report is not None:
-            out_q.put(("ok", report))
+            out_q.put(("ok", _report_by_value(report)))
     except Exception as e:
         cfg = spec.get("config")
         if cfg is not None and getattr(cfg, "save_path_", None):
@@ -622,7 +651,7 @@ class DdpHandle:
                 p.join(timeout=10)
         if status != "ok":
             raise RuntimeError(payload)
-        st: TrainedState = payload
+        st: TrainedState = _report_as_tensors(payload)
         if rec is not None:
             st.world = self.coordinator.world
             st.syncs = rec["syncs"]

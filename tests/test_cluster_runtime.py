@@ -270,3 +270,18 @@ def test_elche_window_cap_scales_to_one_epoch():
     e.set_max_total(12)
     e.report_timing([100.0, 25.0], [10, 10], 1.0)
     assert sum(e.batch_counts()) == 12 and e.window_cap_binding()
+
+
+def test_rank_report_crosses_the_queue_by_value():
+    """A rank's report travels to the parent as bytes (dtype, shape, data), so
+    it survives the rank process exiting before the parent reads it."""
+    import pickle
+
+    from flodl_b200.parallel.trainer import TrainedState, _report_as_tensors, _report_by_value
+
+    p = [("w", torch.randn(3, 4)), ("h", torch.randn(5).bfloat16())]
+    st = TrainedState(params=list(p), buffers=[("n", torch.tensor(7))])
+    back = _report_as_tensors(pickle.loads(pickle.dumps(_report_by_value(st))))
+    for (n0, t0), (n1, t1) in zip(p, back.params):
+        assert n0 == n1 and t0.dtype == t1.dtype and torch.equal(t0, t1)
+    assert back.buffers[0][1].item() == 7

@@ -303,12 +303,20 @@ def test_fused_ddp_matches_single_gpu_full_batch(world, kind, clip, graph):
         bad = [k for k, v in checks.items() if not v]
         assert not bad, f"rank {rank}: failed {bad}"
     ref, ref_norm = _reference(world, kind, clip)
-    got = torch.from_numpy(res[0][2])
-    # AdamW moves an element with a near-zero gradient by about lr per step
-    # whatever the gradient's size, so reduction-order noise can shift such
-    # elements by O(lr): the absolute tolerance follows the largest lr
-    atol = 2e-3 * (2.0 if kind == "adamw2" else 1.0)
-    torch.testing.assert_close(got[:ref.numel()], ref, rtol=2e-2, atol=atol)
+    got = torch.from_numpy(res[0][2])[:ref.numel()]
+    if kind == "adamw2":
+        # AdamW moves an element with a near-zero gradient by up to lr per step
+        # whatever the gradient's size, so reduction-order noise can flip such
+        # an element's steps: a few dozen of the second group's bias / norm
+        # elements (lr 2e-3, no decay; measured up to 14 at 4 GPUs) may differ
+        # by up to 2 lr per step, the rest must agree as in the other cases (a
+        # wrong bucket or group boundary would break thousands)
+        diff = (got - ref).abs()
+        loose = diff > 2e-3 + 2e-2 * ref.abs()
+        assert int(loose.sum()) <= 48, int(loose.sum())
+        assert float(diff.max()) <= 2 * 2e-3 * STEPS + 1e-6, float(diff.max())
+    else:
+        torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-3)
     if clip:
         got_norm = res[0][3]
         assert abs(got_norm - ref_norm) <= 0.03 * ref_norm, (got_norm, ref_norm)
