@@ -557,6 +557,37 @@ __device__ __forceinline__ void f2_pad_mask32(float (&v)[32], int kc0, int S,
   }
 }
 
+// Key padding of one 128-key tile as a suffix, found once per tile by a warp:
+// lane l reads keys k0 + 4l .. k0 + 4l + 3 (keys at or past S count as
+// padded). Returns the first padded key's offset in the tile (128: none) when
+// every key from it on is padded - right-padded batches, which then need no
+// per-key mask, only a shorter row limit - and -1 when the tile mixes padded
+// and unpadded keys after the first padded one.
+__device__ __forceinline__ int f2_pad_suffix(const uint8_t* kp_row, int k0, int S, int lane) {
+  const int k = k0 + 4 * lane;
+  uint32_t word = 0;
+  if (k + 3 < S && ((reinterpret_cast<uintptr_t>(kp_row + k) & 3) == 0)) {
+    word = __ldg(reinterpret_cast<const uint32_t*>(kp_row + k));
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      word |= (uint32_t)((k + t < S) ? __ldg(kp_row + k + t) : 1) << (8 * t);
+  }
+  uint32_t pad = 0;  // bit t: key k + t padded
+#pragma unroll
+  for (int t = 0; t < 4; ++t) pad |= (((word >> (8 * t)) & 0xffu) != 0 ? 1u : 0u) << t;
+  const uint32_t any = __ballot_sync(0xffffffffu, pad != 0);
+  if (any == 0) return kTile;
+  const int L = __ffs(any) - 1;  // first lane holding a padded key
+  const uint32_t full = __ballot_sync(0xffffffffu, pad == 0xfu);
+  const int first = __ffs(__shfl_sync(0xffffffffu, pad, L)) - 1;
+  const uint32_t lpad = __shfl_sync(0xffffffffu, pad, L);
+  // lane L padded from its first padded key on, every later lane fully padded
+  const bool tail_ok = (lpad >> first) == (0xfu >> first);
+  const uint32_t later = L == 31 ? 0u : (0xffffffffu << (L + 1));
+  return (tail_ok && (full & later) == later) ? 4 * L + first : -1;
+}
+
 __global__ void __launch_bounds__(kF2Threads, 2)
     flash_fwd2_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
                       float* __restrict__ lse2, const uint8_t* __restrict__ key_pad, int B, int S,
@@ -707,8 +738,13 @@ __global__ void __launch_bounds__(kF2Threads, 2)
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
         const int k0 = j * kTile;
-        // valid keys of this row in this tile: [k0, k0 + lim) (range and causal)
-        const int lim = max(0, min((causal ? min(qi + 1, S) : S) - k0, kTile));
+        // right padding of this tile as a shorter row limit; a tile whose
+        // padding is not a suffix keeps the per-key mask
+        const int pad_from = kp_row ? f2_pad_suffix(kp_row, k0, S, lane) : kTile;
+        const uint8_t* kp_mask = pad_from < 0 ? kp_row : nullptr;
+        // valid keys of this row in this tile: [k0, k0 + lim) (range, causal, padding)
+        const int lim = max(0, min(min((causal ? min(qi + 1, S) : S) - k0, kTile),
+                                   pad_from < 0 ? kTile : pad_from));
         const bool ranged = lim < kTile;  // warp-uniform only on tiles without masking
         // pass 1: row maximum of the raw scores (scale > 0 commutes with max),
         // 64 columns per tensor-memory round trip
@@ -729,7 +765,7 @@ __global__ void __launch_bounds__(kF2Threads, 2)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = (c * 32 + i < lim) ? v[i] : -INFINITY;
             }
-            if (kp_row) f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+            if (kp_mask) f2_pad_mask32(v, k0 + c * 32, S, kp_mask);
 #pragma unroll
             for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
           }
@@ -772,11 +808,11 @@ __global__ void __launch_bounds__(kF2Threads, 2)
 #pragma unroll
               for (int i = 0; i < 32; ++i) p[i] = (c * 32 + i < lim) ? p[i] : 0.f;
             }
-            if (kp_row) {
+            if (kp_mask) {
               float v[32];
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = 0.f;
-              f2_pad_mask32(v, k0 + c * 32, S, kp_row);
+              f2_pad_mask32(v, k0 + c * 32, S, kp_mask);
 #pragma unroll
               for (int i = 0; i < 32; ++i) p[i] = v[i] == -INFINITY ? 0.f : p[i];
             }

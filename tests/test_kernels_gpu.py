@@ -107,14 +107,23 @@ def test_flash_attention_fwd_bwd(B, S, H, causal):
     torch.testing.assert_close(qkv.grad.float(), qr.grad, rtol=5e-2, atol=5e-2)
 
 
-def test_flash_attention_padding_mask():
+@pytest.mark.parametrize("kind", ["suffix", "scattered"])
+def test_flash_attention_padding_mask(kind):
+    """Right padding (taken as a shorter row limit per key tile) and padding
+    scattered through the keys (the per-key mask)."""
     torch.manual_seed(4)
     from flodl_b200.ops.attention import attention_packed
     B, S, H, D = 2, 256, 2, 64
     qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16().requires_grad_()
     pad = torch.zeros(B, S, dtype=torch.bool, device="cuda")
-    pad[0, 200:] = True
-    pad[1, 17:] = True
+    if kind == "suffix":
+        pad[0, 200:] = True
+        pad[1, 17:] = True
+    else:
+        pad[0, 40:90] = True
+        pad[0, 130:131] = True
+        pad[1] = torch.rand(S, device="cuda") < 0.3
+        pad[1, 0] = False
     out = attention_packed(qkv, B, S, H, False, pad)
     dout = torch.randn_like(out)
     out.backward(dout)
