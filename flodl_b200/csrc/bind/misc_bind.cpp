@@ -35,6 +35,38 @@ void ln_fwd(const Tensor& x, const optional<Tensor>& gamma, const optional<Tenso
   FL_CUDA_OK(flodl::launch_ln_fwd(a, cur_stream()));
 }
 
+// RMSNorm over the last dimension: y = x * rstd * w (x, y f32 or bf16).
+void rms_fwd(const Tensor& x, const optional<Tensor>& w, Tensor& y, Tensor& rstd, double eps) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(x.is_contiguous() && y.is_contiguous() && y.scalar_type() == x.scalar_type() &&
+               y.numel() == x.numel(), "rms_fwd: x, y contiguous, same dtype and size");
+  const bool bf16 = x.scalar_type() == at::kBFloat16;
+  FL_CHECK(bf16 || x.scalar_type() == at::kFloat, "rms_fwd: x must be f32 or bf16");
+  const int C = (int)x.size(-1);
+  const int rows = (int)(x.numel() / C);
+  FL_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= rows, "rms_fwd: rstd [rows] f32");
+  if (w) FL_CHECK(w->scalar_type() == at::kFloat && w->numel() == C, "rms_fwd: w [C] f32");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_rms_fwd(x.data_ptr(), bf16, opt_ptr<const float>(w), y.data_ptr(),
+                                   ptr<float>(rstd), rows, C, (float)eps, cur_stream()));
+}
+
+void rms_bwd(const Tensor& dy, const Tensor& x, const optional<Tensor>& w, const Tensor& rstd,
+             Tensor& dx, const optional<Tensor>& dw) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous() &&
+               dy.scalar_type() == x.scalar_type() && dx.scalar_type() == x.scalar_type() &&
+               dy.numel() == x.numel() && dx.numel() == x.numel(),
+           "rms_bwd: dy, x, dx contiguous, same dtype and size");
+  const int C = (int)x.size(-1);
+  const int rows = (int)(x.numel() / C);
+  if (dw) FL_CHECK(dw->scalar_type() == at::kFloat && dw->numel() == C, "rms_bwd: dw [C] f32");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_rms_bwd(dy.data_ptr(), x.data_ptr(), x.scalar_type() == at::kBFloat16,
+                                   opt_ptr<const float>(w), ptr<float>(rstd), dx.data_ptr(),
+                                   opt_ptr<float>(dw), rows, C, cur_stream()));
+}
+
 void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd,
             const optional<Tensor>& gamma, const optional<Tensor>& dres,
             const optional<Tensor>& dx_f32, const optional<Tensor>& dx_bf16,
@@ -283,6 +315,10 @@ void register_elementwise(py::module& m) {
   m.def("pos_grad", &pos_grad);
   m.def("onehot_bf16", &onehot_bf16);
   m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("rms_fwd", &rms_fwd, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("rstd"),
+        py::arg("eps"));
+  m.def("rms_bwd", &rms_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("dx"), py::arg("dw"));
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_eval_f32", &gelu_eval_f32);

@@ -41,6 +41,14 @@ struct LnBwdArgs {
 };
 cudaError_t launch_ln_fwd(const LnFwdArgs& a, cudaStream_t st);
 cudaError_t launch_ln_bwd(const LnBwdArgs& a, cudaStream_t st);
+// RMSNorm (rmsnorm.cu): y = x * rstd * w over the last dimension C; x/y/dy/dx
+// f32 or bf16 (bf16 = true), w (nullable), rstd and dw (nullable, +=) f32;
+// the backward's dw needs C <= 8192.
+cudaError_t launch_rms_fwd(const void* x, bool bf16, const float* w, void* y, float* rstd,
+                           int rows, int C, float eps, cudaStream_t st);
+cudaError_t launch_rms_bwd(const void* dy, const void* x, bool bf16, const float* w,
+                           const float* rstd, void* dx, float* dw, int rows, int C,
+                           cudaStream_t st);
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
                           const float* scale = nullptr, int ld = 0);
 // Two-stage (deterministic) column sum; partials is scratch [nblocks, C].

@@ -380,15 +380,14 @@ class LayerNorm(Module):
 class RMSNorm(Module):
     NAME = "rmsnorm"
 
-    def __init__(self, size: int, eps: float = 1e-6, device=None):
+    def __init__(self, size: int, eps: float = 1e-5, device=None):
         super().__init__()
-        self.eps = eps
+        self.eps = eps  # the reference's default (flodl/src/nn/rmsnorm.rs:39)
         self.weight = torch.nn.Parameter(torch.ones(size, device=_dev(device)))
 
     def forward(self, x):
-        xf = x.float() if x.dtype in (torch.float16, torch.bfloat16) else x  # at least f32
-        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return (y * self.weight).to(x.dtype)
+        from ..ops import rms_norm
+        return rms_norm(x, self.weight, self.eps)
 
 
 class GroupNorm(Module):

@@ -75,3 +75,40 @@ def layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[t
                 f"(got {x.dtype}, C={x.shape[-1]})")
         return F.layer_norm(x, (x.shape[-1],), weight, bias, eps)
     return _LayerNormFn.apply(x, weight, bias, float(eps), bool(out_bf16))
+
+
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        xc = x.contiguous()
+        rows = xc.numel() // xc.shape[-1]
+        rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+        y = torch.empty_like(xc)
+        C().rms_fwd(xc, weight.detach() if weight is not None else None, y, rstd, eps)
+        ctx.save_for_backward(xc, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xc, weight, rstd = ctx.saved_tensors
+        dyc = dy.contiguous().to(xc.dtype)
+        dx = torch.empty_like(xc)
+        dw = grad_buffer(weight) if wants_grad(weight) else None
+        C().rms_bwd(dyc, xc, weight.detach() if weight is not None else None, rstd, dx, dw)
+        if dw is not None:
+            grad_ready(weight)
+        return dx, None, None
+
+
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float = 1e-5) -> torch.Tensor:
+    """RMSNorm over the last dimension, ``x / sqrt(mean(x^2) + eps) * weight``
+    (flodl/src/nn/rmsnorm.rs:54-62). On CUDA one kernel forward and one
+    backward (which also accumulates ``weight.grad``); f32 and bf16 inputs keep
+    their dtype, statistics are f32."""
+    if not use_kernels(x) or x.dtype not in (torch.float32, torch.bfloat16) or (
+            x.shape[-1] > 8192 and wants_grad(weight)):
+        xf = x.float() if x.dtype in (torch.float16, torch.bfloat16) else x  # at least f32
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+        y = y * weight if weight is not None else y
+        return y.to(x.dtype) if x.dtype in (torch.float16, torch.bfloat16) else y
+    return _RMSNormFn.apply(x, weight, float(eps))

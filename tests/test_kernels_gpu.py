@@ -340,3 +340,28 @@ def test_flash_attention_previous_kernels_still_match():
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        timeout=300, cwd=root)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("C,dtype", [(512, torch.float32), (1000, torch.float32),
+                                     (4096, torch.bfloat16), (768, torch.bfloat16)])
+def test_rms_norm_kernel_matches_fp32(C, dtype):
+    """RMSNorm forward/backward kernels (weight gradient included) against
+    the fp32 composition of the reference formula."""
+    from flodl_b200.ops import rms_norm
+    torch.manual_seed(7)
+    rows = 333
+    x = (torch.randn(rows, C, device="cuda") * 1.5 + 0.2).to(dtype).requires_grad_()
+    w = (torch.rand(C, device="cuda") + 0.5).requires_grad_()
+    y = rms_norm(x, w, 1e-5)
+    assert y.dtype == dtype
+    dy = torch.randn(rows, C, device="cuda").to(dtype)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    ref = xr / torch.sqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr
+    ref.backward(dy.float())
+    tol = dict(rtol=1e-4, atol=1e-4) if dtype == torch.float32 else dict(rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(y.float(), ref, **tol)
+    torch.testing.assert_close(x.grad.float(), xr.grad, **tol)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=2e-3 if dtype == torch.float32 else 3e-2,
+                               atol=2e-3 if dtype == torch.float32 else 0.5)
