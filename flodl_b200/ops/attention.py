@@ -83,15 +83,22 @@ def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
                                  dropout_p: float = 0.0) -> torch.Tensor:
     """Functional SDPA on ``[B, H, S, D]`` tensors (floDl's functional API).
 
-    Self-attention shapes with no additive mask and D in {32, 64, 128} run the
-    flash kernel through the packed layout; anything else uses the composed
-    (explicit softmax) form, which is also the CPU path.
+    Self-attention with head size 64 (the flash kernel's) runs the kernel
+    through the packed layout when there is no mask or the mask only hides
+    keys (boolean, broadcast over heads and queries: ``[B, 1, 1, S]`` with
+    True = attend, the padding mask of encoder batches); anything else uses
+    the composed (explicit softmax) form, which is also the CPU path.
     """
     B, H, S, D = q.shape
-    if (q.is_cuda and attn_mask is None and dropout_p == 0.0 and k.shape == q.shape
-            and v.shape == q.shape and D in (32, 64, 128)):
+    key_padding = None
+    if (attn_mask is not None and attn_mask.dtype == torch.bool and attn_mask.dim() == 4
+            and attn_mask.shape[1] == 1 and attn_mask.shape[2] == 1
+            and attn_mask.shape[0] in (1, B) and attn_mask.shape[3] == S and not is_causal):
+        key_padding = (~attn_mask[:, 0, 0, :]).expand(B, S).contiguous()
+    if (q.is_cuda and (attn_mask is None or key_padding is not None) and dropout_p == 0.0
+            and k.shape == q.shape and v.shape == q.shape and D == 64):
         qkv = torch.stack([q, k, v], dim=0).permute(1, 3, 0, 2, 4).reshape(B * S, 3 * H * D)
-        o = attention_packed(qkv.to(torch.bfloat16), B, S, H, is_causal)
+        o = attention_packed(qkv.to(torch.bfloat16), B, S, H, is_causal, key_padding)
         return o.view(B, S, H, D).permute(0, 2, 1, 3).to(q.dtype)
     scale = 1.0 / math.sqrt(D)
     s = torch.matmul(q, k.transpose(-2, -1)) * scale
