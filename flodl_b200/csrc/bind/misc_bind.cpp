@@ -67,6 +67,42 @@ void rms_bwd(const Tensor& dy, const Tensor& x, const optional<Tensor>& w, const
                                    opt_ptr<float>(dw), rows, C, cur_stream()));
 }
 
+// GroupNorm over x [N, C, *] contiguous (f32 or bf16), G groups.
+void gn_fwd(const Tensor& x, const optional<Tensor>& gamma, const optional<Tensor>& beta,
+            Tensor& y, Tensor& mean, Tensor& rstd, int64_t G, double eps) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(x.dim() >= 2 && x.is_contiguous() && y.is_contiguous() &&
+               y.scalar_type() == x.scalar_type() && y.numel() == x.numel(),
+           "gn_fwd: x, y contiguous [N, C, *], same dtype and size");
+  const bool bf16 = x.scalar_type() == at::kBFloat16;
+  FL_CHECK(bf16 || x.scalar_type() == at::kFloat, "gn_fwd: x must be f32 or bf16");
+  const int N = (int)x.size(0), Cc = (int)x.size(1);
+  const int HW = (int)(x.numel() / ((int64_t)N * Cc));
+  FL_CHECK(G > 0 && Cc % G == 0, "gn_fwd: C must divide into G groups");
+  FL_CHECK(mean.numel() >= N * G && rstd.numel() >= N * G, "gn_fwd: mean/rstd [N*G] f32");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_gn_fwd(x.data_ptr(), bf16, opt_ptr<const float>(gamma),
+                                  opt_ptr<const float>(beta), y.data_ptr(), ptr<float>(mean),
+                                  ptr<float>(rstd), N, Cc, HW, (int)G, (float)eps, cur_stream()));
+}
+
+void gn_bwd(const Tensor& dy, const Tensor& x, const optional<Tensor>& gamma, const Tensor& mean,
+            const Tensor& rstd, Tensor& dx, const optional<Tensor>& dgamma,
+            const optional<Tensor>& dbeta, int64_t G) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous() &&
+               dy.scalar_type() == x.scalar_type() && dx.scalar_type() == x.scalar_type() &&
+               dy.numel() == x.numel() && dx.numel() == x.numel(),
+           "gn_bwd: dy, x, dx contiguous, same dtype and size");
+  const int N = (int)x.size(0), Cc = (int)x.size(1);
+  const int HW = (int)(x.numel() / ((int64_t)N * Cc));
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_gn_bwd(dy.data_ptr(), x.data_ptr(), x.scalar_type() == at::kBFloat16,
+                                  opt_ptr<const float>(gamma), ptr<float>(mean), ptr<float>(rstd),
+                                  dx.data_ptr(), opt_ptr<float>(dgamma), opt_ptr<float>(dbeta), N,
+                                  Cc, HW, (int)G, cur_stream()));
+}
+
 void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd,
             const optional<Tensor>& gamma, const optional<Tensor>& dres,
             const optional<Tensor>& dx_f32, const optional<Tensor>& dx_bf16,
@@ -319,6 +355,10 @@ void register_elementwise(py::module& m) {
         py::arg("eps"));
   m.def("rms_bwd", &rms_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("dx"), py::arg("dw"));
+  m.def("gn_fwd", &gn_fwd, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("y"),
+        py::arg("mean"), py::arg("rstd"), py::arg("groups"), py::arg("eps"));
+  m.def("gn_bwd", &gn_bwd, py::arg("dy"), py::arg("x"), py::arg("gamma"), py::arg("mean"),
+        py::arg("rstd"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"), py::arg("groups"));
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_eval_f32", &gelu_eval_f32);

@@ -61,27 +61,50 @@ __global__ void embed_bwd_atomic_kernel(const int64_t* __restrict__ ids, const f
   }
 }
 
-// dpos[s, c] += sum_b dy[b, s, c]
+// dpos[s, c] += sum_b dy[b, s, c]; four independent partial sums keep four
+// loads in flight per thread
 __global__ void pos_grad_kernel(const float* __restrict__ dy, float* __restrict__ dpos, int B, int S,
                                 int C) {
   const int64_t total = (int64_t)S * C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < B; ++b) s += dy[(int64_t)b * total + i];
-    dpos[i] += s;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    int b = 0;
+    for (; b + 4 <= B; b += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[u] += __ldg(dy + (int64_t)(b + u) * total + i);
+    }
+    for (; b < B; ++b) s[0] += __ldg(dy + (int64_t)b * total + i);
+    dpos[i] += (s[0] + s[1]) + (s[2] + s[3]);
   }
 }
 
+// one_hot[t, v] = (ids[t] == v), eight columns (one 16-byte store) per
+// thread; V % 8 == 0 and T * V / 8 < 2^31 (checked by the launcher)
 __global__ void onehot_kernel(const int64_t* __restrict__ ids, __nv_bfloat16* __restrict__ out,
-                              int T, int V) {
+                              int T, int V, FastDiv fV8) {
+  const uint32_t total = (uint32_t)T * fV8.d;
+  const uint32_t one = 0x3f80u;  // bf16 1.0
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t t = fV8.div(i);
+    const int v0 = (int)(i - t * fV8.d) * 8;
+    const int64_t id = __ldg(ids + t);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      w[q] = (id == v0 + 2 * q ? one : 0u) | ((id == v0 + 2 * q + 1 ? one : 0u) << 16);
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void onehot_scalar_kernel(const int64_t* __restrict__ ids,
+                                     __nv_bfloat16* __restrict__ out, int T, int V) {
   const int64_t total = (int64_t)T * V;
   const __nv_bfloat16 one = __float2bfloat16_rn(1.f), zero = __float2bfloat16_rn(0.f);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / V);
-    const int v = (int)(i % V);
-    out[i] = (ids[t] == v) ? one : zero;
+    out[i] = (ids[t] == (int)(i % V)) ? one : zero;
   }
 }
 
@@ -122,7 +145,11 @@ cudaError_t launch_pos_grad(const float* dy, float* dpos, int B, int S, int C, c
 
 cudaError_t launch_onehot_bf16(const int64_t* ids, __nv_bfloat16* out, int T, int V,
                                cudaStream_t st) {
-  onehot_kernel<<<grid_1d((int64_t)T * V, 256), 256, 0, st>>>(ids, out, T, V);
+  if (V % 8 || (int64_t)T * (V / 8) >= kMaxFlatIndex || (reinterpret_cast<uintptr_t>(out) & 15))
+    onehot_scalar_kernel<<<grid_1d((int64_t)T * V, 256), 256, 0, st>>>(ids, out, T, V);
+  else
+    onehot_kernel<<<grid_1d((int64_t)T * V / 8, 256), 256, 0, st>>>(ids, out, T, V,
+                                                                     FastDiv(V / 8));
   note_launch();
   return cudaGetLastError();
 }

@@ -49,6 +49,15 @@ cudaError_t launch_rms_fwd(const void* x, bool bf16, const float* w, void* y, fl
 cudaError_t launch_rms_bwd(const void* dy, const void* x, bool bf16, const float* w,
                            const float* rstd, void* dx, float* dw, int rows, int C,
                            cudaStream_t st);
+// GroupNorm (groupnorm.cu) over x [N, C, HW] contiguous, G groups (C % G == 0);
+// x/y/dy/dx f32 or bf16, gamma/beta/dgamma/dbeta (nullable, += ) and the
+// per-(sample, group) mean/rstd f32.
+cudaError_t launch_gn_fwd(const void* x, bool bf16, const float* gamma, const float* beta,
+                          void* y, float* mean, float* rstd, int N, int C, int HW, int G,
+                          float eps, cudaStream_t st);
+cudaError_t launch_gn_bwd(const void* dy, const void* x, bool bf16, const float* gamma,
+                          const float* mean, const float* rstd, void* dx, float* dgamma,
+                          float* dbeta, int N, int C, int HW, int G, cudaStream_t st);
 cudaError_t launch_colsum(const void* m, bool bf16, float* out, int rows, int C, cudaStream_t st,
                           const float* scale = nullptr, int ld = 0);
 // Two-stage (deterministic) column sum; partials is scratch [nblocks, C].

@@ -4,7 +4,7 @@ from .linear import linear  # noqa: F401
 from .loss import cross_entropy  # noqa: F401
 from .misc import (batch_norm2d, conv1d, conv2d, conv_transpose1d, conv_transpose2d,  # noqa: F401
                    embedding, gelu)
-from .norm import layer_norm, rms_norm  # noqa: F401
+from .norm import group_norm, layer_norm, rms_norm  # noqa: F401
 from .transformer import lm_train_loss  # noqa: F401,E402
 from .bert import bert_mlm_train_loss  # noqa: F401,E402
 from .resnet import resnet_train_loss  # noqa: F401,E402

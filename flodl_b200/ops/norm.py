@@ -112,3 +112,43 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float = 1e-5)
         y = y * weight if weight is not None else y
         return y.to(x.dtype) if x.dtype in (torch.float16, torch.bfloat16) else y
     return _RMSNormFn.apply(x, weight, float(eps))
+
+
+class _GroupNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, groups, weight, bias, eps):
+        xc = x.contiguous()
+        n = xc.shape[0] * groups
+        mean = torch.empty(n, device=x.device, dtype=torch.float32)
+        rstd = torch.empty(n, device=x.device, dtype=torch.float32)
+        y = torch.empty_like(xc)
+        C().gn_fwd(xc, weight.detach() if weight is not None else None,
+                   bias.detach() if bias is not None else None, y, mean, rstd, groups, eps)
+        ctx.groups = groups
+        ctx.save_for_backward(xc, weight, bias, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xc, weight, bias, mean, rstd = ctx.saved_tensors
+        dx = torch.empty_like(xc)
+        dg = grad_buffer(weight) if wants_grad(weight) else None
+        db = grad_buffer(bias) if wants_grad(bias) else None
+        C().gn_bwd(dy.contiguous().to(xc.dtype), xc, weight.detach() if weight is not None else None,
+                   mean, rstd, dx, dg, db, ctx.groups)
+        if dg is not None:
+            grad_ready(weight)
+        if db is not None:
+            grad_ready(bias)
+        return dx, None, None, None, None
+
+
+def group_norm(x: torch.Tensor, groups: int, weight: Optional[torch.Tensor] = None,
+               bias: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """GroupNorm over ``x [N, C, *]`` (flodl/src/nn/groupnorm.rs:62-70): one
+    kernel forward, one backward that also accumulates the affine gradients,
+    on CUDA for f32 and bf16; elsewhere PyTorch's."""
+    if (not use_kernels(x) or x.dtype not in (torch.float32, torch.bfloat16) or x.dim() < 2
+            or x.shape[1] % groups):
+        return F.group_norm(x, groups, weight, bias, eps)
+    return _GroupNormFn.apply(x, int(groups), weight, bias, float(eps))

@@ -365,3 +365,68 @@ def test_rms_norm_kernel_matches_fp32(C, dtype):
     torch.testing.assert_close(x.grad.float(), xr.grad, **tol)
     torch.testing.assert_close(w.grad, wr.grad, rtol=2e-3 if dtype == torch.float32 else 3e-2,
                                atol=2e-3 if dtype == torch.float32 else 0.5)
+
+
+@pytest.mark.parametrize("D,masked", [(64, False), (64, True), (128, False)])
+def test_sdpa_routes_and_matches_torch(D, masked):
+    """Functional SDPA: head size 64 with no mask or a key-padding mask runs
+    the flash kernel, other head sizes the composed form; both match torch's
+    fp32 attention."""
+    from flodl_b200.ops.attention import scaled_dot_product_attention as sdpa
+    torch.manual_seed(11)
+    B, H, S = 2, 3, 200
+    q, k, v = (torch.randn(B, H, S, D, device="cuda") for _ in range(3))
+    mask = None
+    if masked:
+        mask = torch.ones(B, 1, 1, S, dtype=torch.bool, device="cuda")
+        mask[0, ..., 150:] = False
+        mask[1, ..., 37:] = False
+    out = sdpa(q, k, v, attn_mask=mask)
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+    torch.testing.assert_close(out.float(), ref, rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("V", [256, 100])
+def test_onehot_and_position_gradient_kernels(V):
+    """One-hot rows of the embedding-gradient GEMM (16-byte stores when V is
+    a multiple of 8, element stores otherwise) and the position-table
+    gradient (a sum over the batch)."""
+    from flodl_b200._ext import cuda_ext
+    C = cuda_ext()
+    torch.manual_seed(5)
+    T = 1000
+    ids = torch.randint(0, V, (T,), device="cuda")
+    oh = torch.full((T, V), 7.0, device="cuda", dtype=torch.bfloat16)
+    C.onehot_bf16(ids, oh)
+    torch.testing.assert_close(oh.float(), torch.nn.functional.one_hot(ids, V).float())
+    B, S, D = 5, 37, 64
+    dy = torch.randn(B, S, D, device="cuda")
+    dpos = torch.ones(S, D, device="cuda")
+    C.pos_grad(dy, dpos, B, S)
+    torch.testing.assert_close(dpos, 1.0 + dy.sum(0), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("N,C,HW,G,dtype", [(4, 32, 64, 8, torch.float32),
+                                            (3, 48, 17 * 9, 6, torch.float32),
+                                            (2, 64, 256, 32, torch.bfloat16)])
+def test_group_norm_kernel_matches_fp32(N, C, HW, G, dtype):
+    """GroupNorm forward/backward kernels (affine gradients included) against
+    PyTorch's fp32 group_norm."""
+    from flodl_b200.ops import group_norm
+    torch.manual_seed(9)
+    x = (torch.randn(N, C, HW, device="cuda") * 2 + 0.3).to(dtype).requires_grad_()
+    w = (torch.rand(C, device="cuda") + 0.5).requires_grad_()
+    b = torch.randn(C, device="cuda").requires_grad_()
+    y = group_norm(x, G, w, b, 1e-5)
+    dy = torch.randn(N, C, HW, device="cuda").to(dtype)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_()
+    wr, br = w.detach().clone().requires_grad_(), b.detach().clone().requires_grad_()
+    ref = torch.nn.functional.group_norm(xr, G, wr, br, 1e-5)
+    ref.backward(dy.float())
+    tol = dict(rtol=1e-4, atol=1e-4) if dtype == torch.float32 else dict(rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(y.float(), ref, **tol)
+    torch.testing.assert_close(x.grad.float(), xr.grad, **tol)
+    gt = dict(rtol=1e-3, atol=1e-3) if dtype == torch.float32 else dict(rtol=3e-2, atol=0.3)
+    torch.testing.assert_close(w.grad, wr.grad, **gt)
+    torch.testing.assert_close(b.grad, br.grad, **gt)
