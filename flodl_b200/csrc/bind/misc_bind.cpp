@@ -103,6 +103,42 @@ void gn_bwd(const Tensor& dy, const Tensor& x, const optional<Tensor>& gamma, co
                                   Cc, HW, (int)G, cur_stream()));
 }
 
+// Max pooling of x [planes, H, W] (f32 or bf16) into y [planes, Ho, Wo] with
+// the argmax index per output (int32).
+void maxpool_fwd(const Tensor& x, Tensor& y, Tensor& idx, int64_t kh, int64_t kw, int64_t sh,
+                 int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(x.is_contiguous() && y.is_contiguous() && idx.is_contiguous() && x.dim() >= 2 &&
+               y.scalar_type() == x.scalar_type() && idx.scalar_type() == at::kInt &&
+               idx.numel() == y.numel(),
+           "maxpool_fwd: contiguous x, y (same dtype) and int32 idx like y");
+  const bool bf16 = x.scalar_type() == at::kBFloat16;
+  FL_CHECK(bf16 || x.scalar_type() == at::kFloat, "maxpool_fwd: x must be f32 or bf16");
+  const int H = (int)x.size(-2), W = (int)x.size(-1);
+  const int Ho = (int)y.size(-2), Wo = (int)y.size(-1);
+  const int planes = (int)(x.numel() / ((int64_t)H * W));
+  FL_CHECK(y.numel() == (int64_t)planes * Ho * Wo, "maxpool_fwd: y shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_maxpool_fwd(
+      x.data_ptr(), bf16, y.data_ptr(), ptr<int32_t>(idx), planes, H, W, Ho, Wo,
+      flodl::PoolGeo{(int)kh, (int)kw, (int)sh, (int)sw, (int)ph, (int)pw, (int)dh, (int)dw},
+      cur_stream()));
+}
+
+void maxpool_bwd(const Tensor& dy, const Tensor& idx, Tensor& dx) {
+  FL_CHECK_CUDA(dy);
+  FL_CHECK(dy.is_contiguous() && idx.is_contiguous() && dx.is_contiguous() &&
+               dy.scalar_type() == dx.scalar_type() && idx.numel() == dy.numel(),
+           "maxpool_bwd: contiguous dy, dx (same dtype), idx like dy");
+  const int H = (int)dx.size(-2), W = (int)dx.size(-1);
+  const int Ho = (int)dy.size(-2), Wo = (int)dy.size(-1);
+  const int planes = (int)(dx.numel() / ((int64_t)H * W));
+  c10::cuda::CUDAGuard guard(dy.device());
+  FL_CUDA_OK(flodl::launch_maxpool_bwd(dy.data_ptr(), dy.scalar_type() == at::kBFloat16,
+                                       ptr<int32_t>(idx), dx.data_ptr(), planes, H, W, Ho, Wo,
+                                       cur_stream()));
+}
+
 void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd,
             const optional<Tensor>& gamma, const optional<Tensor>& dres,
             const optional<Tensor>& dx_f32, const optional<Tensor>& dx_bf16,
@@ -359,6 +395,8 @@ void register_elementwise(py::module& m) {
         py::arg("mean"), py::arg("rstd"), py::arg("groups"), py::arg("eps"));
   m.def("gn_bwd", &gn_bwd, py::arg("dy"), py::arg("x"), py::arg("gamma"), py::arg("mean"),
         py::arg("rstd"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"), py::arg("groups"));
+  m.def("maxpool_fwd", &maxpool_fwd);
+  m.def("maxpool_bwd", &maxpool_bwd);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_eval_f32", &gelu_eval_f32);

@@ -49,6 +49,16 @@ cudaError_t launch_rms_fwd(const void* x, bool bf16, const float* w, void* y, fl
 cudaError_t launch_rms_bwd(const void* dy, const void* x, bool bf16, const float* w,
                            const float* rstd, void* dx, float* dw, int rows, int C,
                            cudaStream_t st);
+// Max pooling over NCHW planes (pool.cu): kernel, stride, padding, dilation.
+struct PoolGeo {
+  int kh, kw, sh, sw, ph, pw, dh, dw;
+};
+// y [planes, Ho, Wo] and idx (flat in-plane index of each maximum, -1 for an
+// empty window); the backward adds dy at idx into dx (zeroed by the caller).
+cudaError_t launch_maxpool_fwd(const void* x, bool bf16, void* y, int32_t* idx, int planes, int H,
+                               int W, int Ho, int Wo, const PoolGeo& g, cudaStream_t st);
+cudaError_t launch_maxpool_bwd(const void* dy, bool bf16, const int32_t* idx, void* dx, int planes,
+                               int H, int W, int Ho, int Wo, cudaStream_t st);
 // GroupNorm (groupnorm.cu) over x [N, C, HW] contiguous, G groups (C % G == 0);
 // x/y/dy/dx f32 or bf16, gamma/beta/dgamma/dbeta (nullable, += ) and the
 // per-(sample, group) mean/rstd f32.

@@ -199,16 +199,18 @@ class MaxPool2d(Module):
                      ceil_mode)
 
     def forward(self, x):
+        from ..ops import max_pool2d
         k, s, p, d, c = self.args
-        return F.max_pool2d(x, k, s, p, d, c)
+        return max_pool2d(x, k, s, p, d, c)
 
 
 class MaxPool1d(MaxPool2d):
     NAME = "maxpool1d"
 
     def forward(self, x):
+        from ..ops import max_pool1d
         k, s, p, d, c = self.args
-        return F.max_pool1d(x, k, s, p, d, c)
+        return max_pool1d(x, k, s, p, d, c)
 
 
 class AvgPool2d(Module):

@@ -306,3 +306,55 @@ def batch_norm2d(x, running_mean, running_var, weight, bias, training, momentum,
             and x.shape[1] <= 2048):
         return _BatchNorm2dFn.apply(x, weight, bias, running_mean, running_var, momentum, eps)
     return F.batch_norm(x, running_mean, running_var, weight, bias, training, momentum, eps)
+
+
+def _pool_out(n, k, s, p, d, ceil_mode):
+    span = n + 2 * p - d * (k - 1) - 1
+    o = (-(-span // s) if ceil_mode else span // s) + 1
+    if ceil_mode and (o - 1) * s >= n + p:  # the last window must start inside the input
+        o -= 1
+    return o
+
+
+class _MaxPool2dFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, k, s, p, d, ceil_mode):
+        xc = x.contiguous()
+        H, W = xc.shape[-2:]
+        Ho = _pool_out(H, k[0], s[0], p[0], d[0], ceil_mode)
+        Wo = _pool_out(W, k[1], s[1], p[1], d[1], ceil_mode)
+        y = torch.empty(xc.shape[:-2] + (Ho, Wo), device=x.device, dtype=x.dtype)
+        idx = torch.empty(y.shape, device=x.device, dtype=torch.int32)
+        C().maxpool_fwd(xc, y, idx, k[0], k[1], s[0], s[1], p[0], p[1], d[0], d[1])
+        ctx.save_for_backward(idx)
+        ctx.in_shape = xc.shape
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (idx,) = ctx.saved_tensors
+        dx = torch.zeros(ctx.in_shape, device=dy.device, dtype=dy.dtype)
+        C().maxpool_bwd(dy.contiguous(), idx, dx)
+        return dx, None, None, None, None, None
+
+
+def max_pool2d(x, kernel_size, stride=None, padding=0, dilation=1, ceil_mode=False):
+    """Max pooling over the last two dimensions (flodl/src/nn/pooling.rs): one
+    kernel forward (with the argmax of each window), one scatter backward, for
+    f32 and bf16 on CUDA; PyTorch's elsewhere."""
+    k = _pair(kernel_size)
+    s = _pair(stride if stride is not None else kernel_size)
+    p, d = _pair(padding), _pair(dilation)
+    if not use_kernels(x) or x.dtype not in (torch.float32, torch.bfloat16) or x.dim() < 3:
+        return F.max_pool2d(x, k, s, p, d, ceil_mode)
+    return _MaxPool2dFn.apply(x, k, s, p, d, bool(ceil_mode))
+
+
+def max_pool1d(x, kernel_size, stride=None, padding=0, dilation=1, ceil_mode=False):
+    """Max pooling over the last dimension through the 2-D kernel (H = 1)."""
+    if not use_kernels(x) or x.dtype not in (torch.float32, torch.bfloat16) or x.dim() < 2:
+        return F.max_pool1d(x, kernel_size, stride, padding, dilation, ceil_mode)
+    st = stride if stride is not None else kernel_size
+    y = max_pool2d(x.unsqueeze(-2), (1, kernel_size), (1, st), (0, padding), (1, dilation),
+                   ceil_mode)
+    return y.squeeze(-2)

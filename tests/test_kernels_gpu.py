@@ -430,3 +430,31 @@ def test_group_norm_kernel_matches_fp32(N, C, HW, G, dtype):
     gt = dict(rtol=1e-3, atol=1e-3) if dtype == torch.float32 else dict(rtol=3e-2, atol=0.3)
     torch.testing.assert_close(w.grad, wr.grad, **gt)
     torch.testing.assert_close(b.grad, br.grad, **gt)
+
+
+@pytest.mark.parametrize("shape,k,s,p,d,ceil,dtype", [
+    ((2, 3, 28, 28), 2, 2, 0, 1, False, torch.float32),
+    ((2, 4, 17, 13), 3, 2, 1, 1, True, torch.float32),
+    ((1, 8, 16, 16), 3, 1, 1, 2, False, torch.bfloat16),
+])
+def test_max_pool2d_kernel_matches_torch(shape, k, s, p, d, ceil, dtype):
+    """Max pooling forward (values) and backward (gradient routed to each
+    window's maximum) against PyTorch's."""
+    from flodl_b200.ops import max_pool1d, max_pool2d
+    torch.manual_seed(2)
+    x = torch.randn(*shape, device="cuda").to(dtype).requires_grad_()
+    y = max_pool2d(x, k, s, p, d, ceil)
+    xr = x.detach().clone().requires_grad_()
+    yr = torch.nn.functional.max_pool2d(xr, k, s, p, d, ceil)
+    assert y.shape == yr.shape
+    torch.testing.assert_close(y, yr)
+    dy = torch.randn_like(yr)
+    y.backward(dy)
+    # reference gradient in fp32 (bf16 gradients accumulate overlapping windows
+    # with bf16 atomic adds: a few ulps per overlap)
+    xf = x.detach().float().requires_grad_()
+    torch.nn.functional.max_pool2d(xf, k, s, p, d, ceil).backward(dy.float())
+    tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=5e-2, atol=5e-2)
+    torch.testing.assert_close(x.grad.float(), xf.grad, **tol)
+    x1 = torch.randn(3, 5, 40, device="cuda")
+    torch.testing.assert_close(max_pool1d(x1, 3, 2, 1), torch.nn.functional.max_pool1d(x1, 3, 2, 1))
