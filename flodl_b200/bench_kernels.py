@@ -288,6 +288,50 @@ def case_conv(kind):
     return fn, 0.0, 2 * (3 * M * RC * 2) + M * RC * 2
 
 
+def case_norms(kind):
+    """RMSNorm (BERT-width rows), GroupNorm and max pooling (ResNet-like
+    activations), forward + backward per launch pair."""
+    from ._ext import cuda_ext
+    C = cuda_ext()
+    if kind == "rmsnorm":
+        rows, Cd = T, 768
+        x = torch.randn(rows, Cd, device="cuda")
+        w = torch.rand(Cd, device="cuda") + 0.5
+        y, dx = torch.empty_like(x), torch.empty_like(x)
+        rstd = torch.empty(rows, device="cuda")
+        dy = torch.randn_like(x)
+        dw = torch.zeros(Cd, device="cuda")
+
+        def fn():
+            C.rms_fwd(x, w, y, rstd, 1e-5)
+            C.rms_bwd(dy, x, w, rstd, dx, dw)
+        return fn, 0.0, (2 + 3) * rows * Cd * 4  # fwd: x, y; bwd: dy, x, dx
+    if kind == "groupnorm":
+        N, Cc, HW, G = 128, 64, 32 * 32, 32
+        x = torch.randn(N, Cc, HW, device="cuda")
+        w, b = torch.rand(Cc, device="cuda") + 0.5, torch.randn(Cc, device="cuda")
+        y, dx = torch.empty_like(x), torch.empty_like(x)
+        mean, rstd = torch.empty(N * G, device="cuda"), torch.empty(N * G, device="cuda")
+        dy = torch.randn_like(x)
+        dg, db = torch.zeros(Cc, device="cuda"), torch.zeros(Cc, device="cuda")
+
+        def fn():
+            C.gn_fwd(x, w, b, y, mean, rstd, G, 1e-5)
+            C.gn_bwd(dy, x, w, mean, rstd, dx, dg, db, G)
+        return fn, 0.0, (2 + 3) * x.numel() * 4
+    N, Cc, H = 128, 64, 64  # max pooling 2x2 / 2
+    x = torch.randn(N, Cc, H, H, device="cuda")
+    y = torch.empty(N, Cc, H // 2, H // 2, device="cuda")
+    idx = torch.empty(y.shape, device="cuda", dtype=torch.int32)
+    dx = torch.zeros_like(x)
+    dy = torch.randn_like(y)
+
+    def fn():
+        C.maxpool_fwd(x, y, idx, 2, 2, 2, 2, 0, 0, 1, 1)
+        C.maxpool_bwd(dy, idx, dx)
+    return fn, 0.0, x.numel() * 4 + y.numel() * 8 + y.numel() * 8 + x.numel() * 4
+
+
 CASES = {
     "gemm_qkv": case_gemm, "gemm_fc1_gelu": case_gemm, "gemm_fc2_residual": case_gemm,
     "gemm_dgrad_dgelu": case_gemm, "gemm_wgrad": case_gemm, "gemm_qkv_nobias": case_gemm,
@@ -298,6 +342,7 @@ CASES = {
     "softmax_ce": case_softmax_ce, "embed_fwd": case_embed, "embed_bwd": case_embed,
     "im2col": case_conv, "col2im": case_conv, "bn_stats": case_conv, "bn_apply": case_conv,
     "bn_bwd": case_conv, "col2im_bn": case_conv,
+    "rmsnorm": case_norms, "groupnorm": case_norms, "maxpool": case_norms,
 }
 
 

@@ -8,7 +8,8 @@
 // backward:
 //   g = dy * w,  xhat = x * rstd
 //   dx = rstd * (g - xhat * mean(g * xhat))
-//   dw += sum_rows dy * xhat   (per-block shared-memory partials, one global
+//   dw += sum_rows dy * xhat   (per-lane register partials for rows up to 1024
+//                               wide, else shared-memory atomics; one global
 //                               atomic per column and block)
 // x, y, dy and dx are f32 or bf16 (the same type); w, rstd and dw are f32.
 #include "sm100_ptx.cuh"
@@ -58,29 +59,49 @@ __global__ void __launch_bounds__(kRmsThreads) rms_fwd_kernel(const T* __restric
   }
 }
 
-template <typename T>
+// kRegDw: dw partials of a lane's columns (C <= 1024: at most 32) stay in
+// registers across the warp's rows and meet in shared memory once per block;
+// wider rows add into a shared-memory row with atomics.
+template <typename T, bool kRegDw>
 __global__ void __launch_bounds__(kRmsThreads) rms_bwd_kernel(
     const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
     const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw, int rows, int C) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float s_dw[kRmsMaxC];
-  if (dw) {
+  constexpr int kWarps = kRmsThreads / 32;
+  __shared__ float s_dw[kRegDw ? kWarps * 1024 : kRmsMaxC];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  float acc[32];
+  if constexpr (kRegDw) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+  } else if (dw) {
     for (int c = threadIdx.x; c < C; c += blockDim.x) s_dw[c] = 0.f;
     __syncthreads();
   }
-  const int lane = threadIdx.x & 31;
-  const int wpb = blockDim.x / 32;
-  for (int r = blockIdx.x * wpb + threadIdx.x / 32; r < rows; r += gridDim.x * wpb) {
+  for (int r = blockIdx.x * kWarps + warp; r < rows; r += gridDim.x * kWarps) {
     const T* xr = x + (int64_t)r * C;
     const T* gr = dy + (int64_t)r * C;
     const float rs = rstd[r];
     float dot = 0.f;  // sum of g * xhat
-    for (int c = lane; c < C; c += 32) {
-      const float xh = ld_f32(xr, c) * rs;
-      const float d = ld_f32(gr, c);
-      dot = fmaf(d * (w ? __ldg(w + c) : 1.f), xh, dot);
-      if (dw) atomicAdd(&s_dw[c], d * xh);
+    if constexpr (kRegDw) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int c = lane + 32 * k;
+        if (c < C) {
+          const float xh = ld_f32(xr, c) * rs;
+          const float d = ld_f32(gr, c);
+          dot = fmaf(d * (w ? __ldg(w + c) : 1.f), xh, dot);
+          acc[k] = fmaf(d, xh, acc[k]);
+        }
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) {
+        const float xh = ld_f32(xr, c) * rs;
+        const float d = ld_f32(gr, c);
+        dot = fmaf(d * (w ? __ldg(w + c) : 1.f), xh, dot);
+        if (dw) atomicAdd(&s_dw[c], d * xh);
+      }
     }
     const float m = warp_sum(dot) / (float)C;
     T* dr = dx + (int64_t)r * C;
@@ -90,7 +111,19 @@ __global__ void __launch_bounds__(kRmsThreads) rms_bwd_kernel(
       st_out(dr, c, rs * (g - xh * m));
     }
   }
-  if (dw) {
+  if (!dw) return;
+  if constexpr (kRegDw) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (lane + 32 * k < C) s_dw[warp * 1024 + lane + 32 * k] = acc[k];
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int v = 0; v < kWarps; ++v) t += s_dw[v * 1024 + c];
+      atomicAdd(dw + c, t);
+    }
+  } else {
     __syncthreads();
     for (int c = threadIdx.x; c < C; c += blockDim.x) atomicAdd(dw + c, s_dw[c]);
   }
@@ -124,16 +157,19 @@ cudaError_t launch_rms_bwd(const void* dy, const void* x, bool bf16, const float
                            const float* rstd, void* dx, float* dw, int rows, int C,
                            cudaStream_t st) {
   if (rows <= 0 || C <= 0 || (dw && C > kRmsMaxC)) return cudaErrorInvalidValue;
-  // fewer blocks when dw is accumulated: one shared-memory flush per block
-  const int grid = rms_grid(rows, dw ? 2 : 8);
+  const bool reg = C <= 1024;
+  // with dw in shared-memory atomics, fewer blocks (one flush each)
+  const int grid = rms_grid(rows, (dw && !reg) ? 2 : 8);
   cudaError_t e;
-  if (bf16)
-    e = launch_pdl(rms_bwd_kernel<__nv_bfloat16>, dim3(grid), dim3(kRmsThreads), 0, st,
-                   (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
-                   (__nv_bfloat16*)dx, dw, rows, C);
-  else
-    e = launch_pdl(rms_bwd_kernel<float>, dim3(grid), dim3(kRmsThreads), 0, st, (const float*)dy,
-                   (const float*)x, w, rstd, (float*)dx, dw, rows, C);
+  if (bf16) {
+    auto k = reg ? rms_bwd_kernel<__nv_bfloat16, true> : rms_bwd_kernel<__nv_bfloat16, false>;
+    e = launch_pdl(k, dim3(grid), dim3(kRmsThreads), 0, st, (const __nv_bfloat16*)dy,
+                   (const __nv_bfloat16*)x, w, rstd, (__nv_bfloat16*)dx, dw, rows, C);
+  } else {
+    auto k = reg ? rms_bwd_kernel<float, true> : rms_bwd_kernel<float, false>;
+    e = launch_pdl(k, dim3(grid), dim3(kRmsThreads), 0, st, (const float*)dy, (const float*)x, w,
+                   rstd, (float*)dx, dw, rows, C);
+  }
   if (e != cudaSuccess) return e;
   note_launch();
   return cudaGetLastError();
