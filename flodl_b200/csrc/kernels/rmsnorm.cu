@@ -85,16 +85,29 @@ __global__ void __launch_bounds__(kRmsThreads) rms_bwd_kernel(
     const float rs = rstd[r];
     float dot = 0.f;  // sum of g * xhat
     if constexpr (kRegDw) {
+      // the row stays in registers between the two passes
+      float xv[32], gv[32];
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
         const int c = lane + 32 * k;
-        if (c < C) {
-          const float xh = ld_f32(xr, c) * rs;
-          const float d = ld_f32(gr, c);
-          dot = fmaf(d * (w ? __ldg(w + c) : 1.f), xh, dot);
-          acc[k] = fmaf(d, xh, acc[k]);
-        }
+        xv[k] = c < C ? ld_f32(xr, c) : 0.f;
+        gv[k] = c < C ? ld_f32(gr, c) : 0.f;
       }
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int c = lane + 32 * k;
+        const float xh = xv[k] * rs;
+        dot = fmaf(gv[k] * (c < C && w ? __ldg(w + c) : 1.f), xh, dot);
+        acc[k] = fmaf(gv[k], xh, acc[k]);
+      }
+      const float m = warp_sum(dot) / (float)C;
+      T* dr = dx + (int64_t)r * C;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int c = lane + 32 * k;
+        if (c < C) st_out(dr, c, rs * (gv[k] * (w ? __ldg(w + c) : 1.f) - xv[k] * rs * m));
+      }
+      continue;
     } else {
       for (int c = lane; c < C; c += 32) {
         const float xh = ld_f32(xr, c) * rs;
