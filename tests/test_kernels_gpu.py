@@ -408,7 +408,8 @@ def test_onehot_and_position_gradient_kernels(V):
 
 @pytest.mark.parametrize("N,C,HW,G,dtype", [(4, 32, 64, 8, torch.float32),
                                             (3, 48, 17 * 9, 6, torch.float32),
-                                            (2, 64, 256, 32, torch.bfloat16)])
+                                            (2, 64, 256, 32, torch.bfloat16),
+                                            (2, 16, 1024, 2, torch.float32)])
 def test_group_norm_kernel_matches_fp32(N, C, HW, G, dtype):
     """GroupNorm forward/backward kernels (affine gradients included) against
     PyTorch's fp32 group_norm."""
