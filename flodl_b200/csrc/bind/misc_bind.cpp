@@ -139,6 +139,19 @@ void maxpool_bwd(const Tensor& dy, const Tensor& idx, Tensor& dx) {
                                        cur_stream()));
 }
 
+// Dropout with a counter-based mask (same seed and offset: same mask).
+void dropout(const Tensor& x, Tensor& y, double p, int64_t seed, int64_t offset) {
+  FL_CHECK_CUDA(x);
+  FL_CHECK(x.is_contiguous() && y.is_contiguous() && y.scalar_type() == x.scalar_type() &&
+               y.numel() == x.numel(), "dropout: x, y contiguous, same dtype and size");
+  const bool bf16 = x.scalar_type() == at::kBFloat16;
+  FL_CHECK(bf16 || x.scalar_type() == at::kFloat, "dropout: x must be f32 or bf16");
+  FL_CHECK(p >= 0.0 && p < 1.0, "dropout: 0 <= p < 1");
+  c10::cuda::CUDAGuard guard(x.device());
+  FL_CUDA_OK(flodl::launch_dropout(x.data_ptr(), y.data_ptr(), bf16, x.numel(), (float)p,
+                                   (uint64_t)seed, (uint64_t)offset, cur_stream()));
+}
+
 void ln_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd,
             const optional<Tensor>& gamma, const optional<Tensor>& dres,
             const optional<Tensor>& dx_f32, const optional<Tensor>& dx_bf16,
@@ -397,6 +410,8 @@ void register_elementwise(py::module& m) {
         py::arg("rstd"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"), py::arg("groups"));
   m.def("maxpool_fwd", &maxpool_fwd);
   m.def("maxpool_bwd", &maxpool_bwd);
+  m.def("dropout", &dropout, py::arg("x"), py::arg("y"), py::arg("p"), py::arg("seed"),
+        py::arg("offset"));
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_eval_f32", &gelu_eval_f32);

@@ -49,6 +49,11 @@ cudaError_t launch_rms_fwd(const void* x, bool bf16, const float* w, void* y, fl
 cudaError_t launch_rms_bwd(const void* dy, const void* x, bool bf16, const float* w,
                            const float* rstd, void* dx, float* dw, int rows, int C,
                            cudaStream_t st);
+// Dropout (dropout.cu): y = x * keep / (1 - p), keep drawn from Philox-4x32-10
+// on (element, offset) with the key seed; the same seed and offset give the
+// same mask (the backward calls it on dy). x/y f32 or bf16, 0 <= p < 1.
+cudaError_t launch_dropout(const void* x, void* y, bool bf16, int64_t n, float p, uint64_t seed,
+                           uint64_t offset, cudaStream_t st);
 // Max pooling over NCHW planes (pool.cu): kernel, stride, padding, dilation.
 struct PoolGeo {
   int kh, kw, sh, sw, ph, pw, dh, dw;

@@ -3,7 +3,7 @@ from .attention import attention_packed, scaled_dot_product_attention  # noqa: F
 from .linear import linear  # noqa: F401
 from .loss import cross_entropy  # noqa: F401
 from .misc import (batch_norm2d, conv1d, conv2d, conv_transpose1d, conv_transpose2d,  # noqa: F401
-                   embedding, gelu, max_pool1d, max_pool2d)
+                   dropout, embedding, gelu, max_pool1d, max_pool2d)
 from .norm import group_norm, layer_norm, rms_norm  # noqa: F401
 from .transformer import lm_train_loss  # noqa: F401,E402
 from .bert import bert_mlm_train_loss  # noqa: F401,E402

@@ -358,3 +358,40 @@ def max_pool1d(x, kernel_size, stride=None, padding=0, dilation=1, ceil_mode=Fal
     y = max_pool2d(x.unsqueeze(-2), (1, kernel_size), (1, st), (0, padding), (1, dilation),
                    ceil_mode)
     return y.squeeze(-2)
+
+
+_DROPOUT_CALLS = [0]
+
+
+class _DropoutFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, p, seed, offset):
+        xc = x.contiguous()
+        y = torch.empty_like(xc)
+        C().dropout(xc, y, p, seed, offset)
+        ctx.args = (p, seed, offset)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        p, seed, offset = ctx.args
+        dyc = dy.contiguous()
+        dx = torch.empty_like(dyc)
+        C().dropout(dyc, dx, p, seed, offset)  # the same mask and scale
+        return dx, None, None, None
+
+
+def dropout(x: torch.Tensor, p: float = 0.5, training: bool = True) -> torch.Tensor:
+    """Dropout (flodl/src/nn/dropout.rs). On CUDA (f32/bf16, outside CUDA-graph
+    capture) one kernel draws the mask from a counter-based generator keyed by
+    a seed from torch's generator, so the backward regenerates it instead of
+    keeping it; under capture, and elsewhere, PyTorch's (which advances its
+    generator per graph replay)."""
+    if not training or p == 0.0:
+        return x
+    if (not use_kernels(x) or x.dtype not in (torch.float32, torch.bfloat16) or p >= 1.0
+            or torch.cuda.is_current_stream_capturing()):
+        return F.dropout(x, p, training)
+    seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    _DROPOUT_CALLS[0] += 1
+    return _DropoutFn.apply(x, float(p), seed, _DROPOUT_CALLS[0])

@@ -459,3 +459,27 @@ def test_max_pool2d_kernel_matches_torch(shape, k, s, p, d, ceil, dtype):
     torch.testing.assert_close(x.grad.float(), xf.grad, **tol)
     x1 = torch.randn(3, 5, 40, device="cuda")
     torch.testing.assert_close(max_pool1d(x1, 3, 2, 1), torch.nn.functional.max_pool1d(x1, 3, 2, 1))
+
+
+@pytest.mark.parametrize("dtype,p", [(torch.float32, 0.1), (torch.float32, 0.5),
+                                     (torch.bfloat16, 0.3)])
+def test_dropout_kernel_mask_scale_and_backward(dtype, p):
+    """Dropout kernel: the kept fraction is 1 - p, kept values are scaled by
+    1/(1-p), the backward applies the forward's mask (regenerated from the
+    same seed and offset), and two calls draw different masks."""
+    from flodl_b200.ops import dropout
+    torch.manual_seed(12)
+    n = 1 << 20
+    x = (torch.rand(n, device="cuda") + 0.5).to(dtype).requires_grad_()
+    y = dropout(x, p, True)
+    kept = y != 0
+    frac = kept.float().mean().item()
+    assert abs(frac - (1 - p)) < 5e-3, frac
+    torch.testing.assert_close(y[kept].float(), (x[kept].float() / (1 - p)).to(dtype).float(),
+                               rtol=1e-2 if dtype == torch.bfloat16 else 1e-6, atol=0)
+    dy = torch.ones_like(y)
+    y.backward(dy)
+    assert torch.equal(x.grad != 0, kept)
+    y2 = dropout(x.detach(), p, True)
+    assert not torch.equal(y2 != 0, kept)
+    assert torch.equal(dropout(x.detach(), p, False), x.detach())
