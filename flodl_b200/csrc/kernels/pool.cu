@@ -59,6 +59,38 @@ __global__ void maxpool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
   }
 }
 
+// The common 2x2 window, stride 2, no padding or dilation, every window
+// inside the input: four loads per output and no bounds checks.
+template <typename T>
+__global__ void maxpool2x2_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                      int32_t* __restrict__ idx, int planes, int H, int W, int Ho,
+                                      int Wo, FastDiv fWo, FastDiv fHo) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t total = (uint32_t)planes * Ho * Wo;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t t = fWo.div(i);
+    const int ow = (int)(i - t * Wo);
+    const uint32_t pl = fHo.div(t);
+    const int oh = (int)(t - pl * Ho);
+    const int j0 = 2 * oh * W + 2 * ow;
+    const T* xp = x + (int64_t)pl * H * W;
+    const int js[4] = {j0, j0 + 1, j0 + W, j0 + W + 1};
+    float best = mp_ld(xp, js[0]);
+    int bi = js[0];
+#pragma unroll
+    for (int q = 1; q < 4; ++q) {
+      const float v = mp_ld(xp, js[q]);
+      if ((v > best || v != v) && !(best != best)) {  // first maximum; the first NaN wins
+        best = v;
+        bi = js[q];
+      }
+    }
+    mp_st(y, i, best);
+    idx[i] = bi;
+  }
+}
+
 template <typename T>
 __global__ void maxpool_bwd_kernel(const T* __restrict__ dy, const int32_t* __restrict__ idx,
                                    T* __restrict__ dx, int planes, int HW, int HoWo,
@@ -89,8 +121,17 @@ cudaError_t launch_maxpool_fwd(const void* x, bool bf16, void* y, int32_t* idx, 
       (int64_t)H * W >= kMaxFlatIndex)
     return cudaErrorInvalidValue;
   const int grid = pool_grid((int64_t)planes * Ho * Wo);
+  const bool k2s2 = g.kh == 2 && g.kw == 2 && g.sh == 2 && g.sw == 2 && g.ph == 0 && g.pw == 0 &&
+                    g.dh == 1 && g.dw == 1 && 2 * Ho <= H && 2 * Wo <= W;
   cudaError_t e;
-  if (bf16)
+  if (k2s2 && bf16)
+    e = launch_pdl(maxpool2x2_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st,
+                   (const __nv_bfloat16*)x, (__nv_bfloat16*)y, idx, planes, H, W, Ho, Wo,
+                   FastDiv(Wo), FastDiv(Ho));
+  else if (k2s2)
+    e = launch_pdl(maxpool2x2_fwd_kernel<float>, dim3(grid), dim3(256), 0, st, (const float*)x,
+                   (float*)y, idx, planes, H, W, Ho, Wo, FastDiv(Wo), FastDiv(Ho));
+  else if (bf16)
     e = launch_pdl(maxpool_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st,
                    (const __nv_bfloat16*)x, (__nv_bfloat16*)y, idx, planes, H, W, Ho, Wo, g,
                    FastDiv(Wo), FastDiv(Ho));
